@@ -1,0 +1,56 @@
+"""crukx_sync_b200: exact, compact bf16 weight updates for RL weight sync, on B200 (sm_100a).
+
+    update = encode_update(prev, cur)   # trainer: dicts of name -> bf16 torch tensors
+    apply_update(weights, update)       # worker: writes the new values into `weights` in place
+
+A drop-in for crukx-sync's public API (src/crukx_sync/__init__.py:28-57 of the reference):
+same signatures, same wire format (version 2, byte-identical updates), same all-or-nothing
+``CorruptUpdate`` semantics and the same checksum-cache rules:
+- Sender: ``checksums`` maps name -> checksum of the last `cur`; it is updated only once the
+  update exists, and a wrong cache produces an update the receiver rejects, never wrong weights.
+- Receiver: ``checksums`` maps name -> (checksum, tensor._version); a cached checksum is used
+  only while the tensor's ``_version`` is unchanged since this library last wrote it.
+All arithmetic runs in hand-written CUDA kernels (libcrukx_b200.so, C ABI in
+include/crukx_b200.h); there is no CPU implementation and no other backend.
+"""
+
+from __future__ import annotations
+
+from collections.abc import Mapping
+from dataclasses import dataclass
+
+import torch
+
+from . import codec
+from .wire import CorruptUpdate, parse, serialize
+
+__all__ = ["encode_update", "apply_update", "UpdateStats", "CorruptUpdate"]
+
+
+@dataclass
+class UpdateStats:
+    tensors: int
+    changed: int
+    bytes: int
+
+
+def encode_update(old: Mapping[str, torch.Tensor], new: Mapping[str, torch.Tensor],
+                  checksums: dict | None = None) -> bytes:
+    """Bytes that turn `old` into `new` exactly. Same names and shapes; tensors are bf16 or int16."""
+    if old.keys() != new.keys():
+        raise ValueError(f"old and new differ in tensor names: {sorted(old.keys() ^ new.keys())[:5]}")
+    with torch.no_grad():
+        update = codec.encode(old, new, checksums)
+    data = serialize(update)
+    if checksums is not None:  # commit only once the update exists
+        checksums.update(update.checksums)
+    return data
+
+
+def apply_update(weights: Mapping[str, torch.Tensor], update: bytes,
+                 checksums: dict | None = None) -> UpdateStats:
+    """Write the update into `weights` in place; on any error nothing is written."""
+    u = parse(update)
+    with torch.no_grad():
+        changed = codec.apply(weights, u, checksums)
+    return UpdateStats(len(u.tensors), changed, len(update))

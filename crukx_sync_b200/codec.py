@@ -1,0 +1,162 @@
+"""Torch-facing side of encode/apply: argument checks with the reference's error rules, device
+placement, checksum caches, and the calls into the CUDA library.
+
+Reference behaviour kept (paths relative to the crukx-sync project):
+  bits16 rules (dtype bf16/int16, contiguous)            src/crukx_sync/codec.py:35-41
+  same names/shapes, one device                          codec.py:284-293, __init__.py:41-42
+  sender cache: cached + delta, else a full checksum     codec.py:344-352
+  receiver checks (name, numel) before anything else     codec.py:582-592
+  receiver cache trusted only while _version unchanged   codec.py:457-460, 702-705, 715-716
+CPU tensors are accepted the way the reference accepts them, but the work always runs on a CUDA
+device: they are copied to the current CUDA device and, on apply, the result is copied back in
+place.  Without a CUDA device these functions raise; there is no CPU implementation here.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from collections.abc import Mapping
+
+import torch
+
+from . import _ext
+from .wire import CorruptUpdate, EncodedUpdate, ParsedUpdate
+
+
+def bits16(name: str, t) -> torch.Tensor:
+    """Flat int16 view of a bf16 (or int16 bit-pattern) tensor."""
+    if not isinstance(t, torch.Tensor) or t.dtype not in (torch.bfloat16, torch.int16):
+        raise ValueError(f"{name}: expected a bfloat16 or int16 torch tensor, got {getattr(t, 'dtype', type(t))}")
+    if not t.is_contiguous():
+        raise ValueError(f"{name}: tensor must be contiguous")
+    return t.view(torch.int16).view(-1)
+
+
+def _cuda_device(dev: torch.device) -> torch.device:
+    if not torch.cuda.is_available():
+        raise RuntimeError("crukx_sync_b200 runs on CUDA (sm_100a) only and no CUDA device is available")
+    if dev.type == "cuda":
+        return dev if dev.index is not None else torch.device("cuda", torch.cuda.current_device())
+    return torch.device("cuda", torch.cuda.current_device())
+
+
+def _raise(status: int, err) -> None:
+    msg = err.value.decode(errors="replace")
+    if status == _ext.CRX_CORRUPT:
+        raise CorruptUpdate(msg)
+    if status == _ext.CRX_VALUE_ERROR:
+        raise ValueError(msg)
+    if status == _ext.CRX_NO_MEMORY:
+        raise MemoryError(msg)
+    raise RuntimeError(f"crukx_sync_b200: status {status}: {msg}")
+
+
+def encode(old: Mapping[str, torch.Tensor], new: Mapping[str, torch.Tensor],
+           checksums: dict | None = None) -> EncodedUpdate:
+    """The encoded update (not yet bytes); ``.checksums`` holds what the sender cache commits."""
+    pairs = []
+    for name in old:
+        a, b = bits16(name, old[name]), bits16(name, new[name])
+        if a.shape != b.shape:
+            raise ValueError(f"{name}: old and new differ in shape")
+        pairs.append((name, a, b))
+    if not pairs:
+        return _encode_on(torch.device("cpu"), [], None)
+    devs = {t.device for _, a, b in pairs for t in (a, b)}
+    if len(devs) != 1:
+        raise ValueError("all tensors must be on one device")
+    return _encode_on(next(iter(devs)), pairs, checksums)
+
+
+def _encode_on(dev, pairs, checksums) -> EncodedUpdate:
+    cdev = _cuda_device(dev)
+    if dev.type != "cuda":
+        pairs = [(n, a.to(cdev), b.to(cdev)) for n, a, b in pairs]
+    L = _ext.load()
+    names = [n for n, _, _ in pairs]
+    raw = [n.encode("utf-8") for n in names]
+    k = len(pairs)
+    prev = _ext.ptr_array([a.data_ptr() for _, a, _ in pairs])
+    cur = _ext.ptr_array([b.data_ptr() for _, _, b in pairs])
+    numel = (ctypes.c_int64 * max(k, 1))(*[a.numel() for _, a, _ in pairs])
+    name_bufs = [ctypes.create_string_buffer(r, len(r) or 1) for r in raw]
+    name_ptrs = _ext.ptr_array([ctypes.addressof(b) for b in name_bufs])
+    name_len = (ctypes.c_int64 * max(k, 1))(*[len(r) for r in raw])
+    cache = (ctypes.c_uint64 * max(k, 1))(*[int(checksums[n]) & (2**64 - 1) if checksums is not None and n in checksums
+                                            else 0 for n in names])
+    has = (ctypes.c_uint8 * max(k, 1))(*[1 if checksums is not None and n in checksums else 0 for n in names])
+    h = ctypes.c_void_p()
+    err = ctypes.create_string_buffer(1024)
+    with torch.cuda.device(cdev):
+        stream = torch.cuda.current_stream(cdev).cuda_stream
+        st = L.crx_encode(_ext.context(cdev.index), k, prev, cur, numel, name_ptrs, name_len, cache, has,
+                          ctypes.c_void_p(stream), ctypes.byref(h), err, 1024)
+    if st != _ext.CRX_OK:
+        _raise(st, err)
+    return EncodedUpdate(h, names)
+
+
+def _cache_get(checksums, name, t):
+    """A cached checksum, trusted only if the tensor was not modified since it was recorded."""
+    hit = checksums.get(name) if checksums is not None else None
+    return hit[0] if isinstance(hit, tuple) and hit[1] == t._version else None
+
+
+def apply(weights: Mapping[str, torch.Tensor], u: ParsedUpdate, checksums: dict | None = None) -> int:
+    """Verify ``u`` against ``weights``, then write the new values in place; returns changes."""
+    headers = u.tensors
+    if not headers:
+        return 0
+    targets = []
+    for h in headers:
+        if h.name not in weights:
+            raise ValueError(f"update has tensor {h.name!r} that the receiver does not have")
+        a = bits16(h.name, weights[h.name])
+        if a.numel() != h.numel:
+            raise ValueError(f"{h.name}: update is for {h.numel} elements, receiver has {a.numel()}")
+        targets.append(a)
+    dev = targets[0].device
+    if any(a.device != dev for a in targets):
+        raise ValueError("all updated tensors must be on one device")
+    cdev = _cuda_device(dev)
+    work = targets if dev.type == "cuda" else [a.to(cdev) for a in targets]
+    k = len(headers)
+    cached = [_cache_get(checksums, h.name, weights[h.name]) for h in headers]
+    cache = (ctypes.c_uint64 * k)(*[c if c is not None else 0 for c in cached])
+    has = (ctypes.c_uint8 * k)(*[1 if c is not None else 0 for c in cached])
+    ptrs = _ext.ptr_array([a.data_ptr() for a in work])
+    changed = ctypes.c_int64()
+    err = ctypes.create_string_buffer(1024)
+    L = _ext.load()
+    with torch.cuda.device(cdev):
+        stream = torch.cuda.current_stream(cdev).cuda_stream
+        st = L.crx_apply(_ext.context(cdev.index), u.handle, ptrs, cache, has, ctypes.c_void_p(stream),
+                         ctypes.byref(changed), err, 1024)
+    if st != _ext.CRX_OK:
+        _raise(st, err)
+    if dev.type == "cuda":
+        for h in headers:   # the commit wrote through raw pointers: move the version like a[idx] = v
+            torch.autograd.graph.increment_version(weights[h.name])
+    else:
+        for a, wk in zip(targets, work):
+            a.copy_(wk)     # in-place copy back: bumps the version and reaches every view
+    if checksums is not None:   # record the version after our own write
+        checksums.update({h.name: (h.checksum, weights[h.name]._version) for h in headers})
+    return int(changed.value)
+
+
+def checksum(t: torch.Tensor) -> int:
+    """sum(u_i * w_i) mod 2^64 over the uint16 bits u_i, computed on the GPU."""
+    a = bits16("tensor", t)
+    cdev = _cuda_device(a.device)
+    if a.device.type != "cuda":
+        a = a.to(cdev)
+    out = ctypes.c_uint64()
+    err = ctypes.create_string_buffer(512)
+    with torch.cuda.device(cdev):
+        stream = torch.cuda.current_stream(cdev).cuda_stream
+        st = _ext.load().crx_checksum(_ext.context(cdev.index), ctypes.c_void_p(a.data_ptr()), a.numel(),
+                                      ctypes.c_void_p(stream), ctypes.byref(out), err, 512)
+    if st != _ext.CRX_OK:
+        _raise(st, err)
+    return int(out.value)

@@ -1,0 +1,658 @@
+// Apply: verify a parsed crukx-sync update against the receiver's bf16 weights and commit it in
+// place, all or nothing (reference src/crukx_sync/codec.py:578-717).
+//
+//   k_app_hist     old-exponent histogram per super-tile (+ full checksum when the receiver has no
+//                  trusted cached checksum, codec.py:702-705); column scans give every
+//                  super-tile its per-exponent offset and every group its exact size.
+//   k_decode       one thread per 256-change block: Golomb-Rice gap + canonical Huffman residual,
+//                  with the reference's validation (codec.py:504-575, _triton.py:34-88): overrun,
+//                  q > q_max, no code, block not consumed exactly.  Unary runs longer than one
+//                  64-bit window are followed inside the block's own bits only.
+//   k_locals       group-local index = running sum of gap + 1 (codec.py:640-642), range checks
+//                  (codec.py:696-697).
+//   k_map          per super-tile: in-CTA stable counting sort of the old exponents, then every
+//                  change is placed by (exponent, local rank) -> position (codec.py:654-694), the
+//                  new value staged and the checksum delta accumulated (codec.py:698-700).
+//   host verdict   one synchronisation: decode/range flags and per-tensor checksums.
+//   k_commit       scatter of the staged values, only after the verdict (codec.py:713-714).
+#include <algorithm>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "capi_internal.h"
+#include "common.cuh"
+
+namespace crx {
+
+namespace {
+
+constexpr uint32_t FULL = 0xffffffffu;
+constexpr int LUT_BITS = 10;
+
+struct AppTensor {
+    int16_t* w;
+    int64_t numel;
+    int64_t super_begin;
+    int32_t want_full;
+    int32_t g_begin;
+    int32_t g_end;
+    int32_t pad;
+};
+
+struct AppGroup {
+    uint64_t start;      // first change of the group (update-wide index)
+    uint64_t count;
+    int32_t tensor;
+    int32_t exp;
+    int32_t rice;
+    int32_t table;
+};
+
+struct DecTable {
+    uint32_t first[kMaxCodeLen + 1];
+    uint32_t base[kMaxCodeLen + 1];
+    uint32_t limit[kMaxCodeLen + 1];
+    uint32_t sym_off;
+    uint32_t nsym;
+    uint32_t lut[1 << LUT_BITS];   // len << 24 | symbol index for codes of <= LUT_BITS bits, else 0
+};
+
+__device__ __forceinline__ int tensor_of_super(const AppTensor* T, int nT, int64_t s) {
+    int lo = 0, hi = nT - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (T[mid].super_begin <= s) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+__device__ __forceinline__ int64_t last_le(const uint64_t* __restrict__ a, int64_t n, uint64_t v) {
+    int64_t lo = 0, hi = n - 1;
+    while (lo < hi) {
+        const int64_t mid = (lo + hi + 1) >> 1;
+        if (a[mid] <= v) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+__device__ __forceinline__ uint64_t bswap64(uint64_t x) {
+    const uint32_t lo = uint32_t(x), hi = uint32_t(x >> 32);
+    return (uint64_t(bswap32(lo)) << 32) | bswap32(hi);
+}
+
+// 64 payload bits starting at bit `pos`, MSB first.  The buffer carries >= 16 zero bytes past the
+// payload, so every read the decoder makes (pos <= block end) stays inside it.
+__device__ __forceinline__ uint64_t read64(const uint64_t* __restrict__ W, uint64_t pos) {
+    const uint64_t w = pos >> 6;
+    const int s = int(pos & 63);
+    const uint64_t hi = bswap64(__ldg(W + w));
+    if (!s) return hi;
+    const uint64_t lo = bswap64(__ldg(W + w + 1));
+    return (hi << s) | (lo >> (64 - s));
+}
+
+// ------------------------------------------------------------------ histogram of old exponents
+
+constexpr int HIST_THREADS = 512;
+
+__global__ void __launch_bounds__(HIST_THREADS) k_app_hist(const AppTensor* __restrict__ T, int nT, uint32_t* __restrict__ HS,
+                                                           unsigned long long* __restrict__ chk_full) {
+    __shared__ uint32_t hist[HIST_THREADS / 32][256];
+    __shared__ uint64_t red[HIST_THREADS / 32];
+    const int64_t s = blockIdx.x;
+    const int t = tensor_of_super(T, nT, s);
+    const AppTensor tt = T[t];
+    const int64_t e0 = (s - tt.super_begin) * SUPER_N;
+    const int64_t e1 = min(tt.numel, e0 + SUPER_N);
+    const int w = threadIdx.x >> 5;
+    for (int k = threadIdx.x; k < (HIST_THREADS / 32) * 256; k += HIST_THREADS) (&hist[0][0])[k] = 0;
+    __syncthreads();
+    uint64_t full = 0;
+    const int16_t* p = tt.w + e0;
+    const int64_t n = e1 - e0;
+    if ((reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+        const uint4* v = reinterpret_cast<const uint4*>(p);
+        const int64_t nv = n / 8;
+        for (int64_t k = threadIdx.x; k < nv; k += HIST_THREADS) {
+            const uint4 q = __ldcs(v + k);
+            const uint32_t ws[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                atomicAdd(&hist[w][(ws[h] >> 7) & 0xFF], 1u);
+                atomicAdd(&hist[w][(ws[h] >> 23) & 0xFF], 1u);
+            }
+            if (tt.want_full) {
+                const uint64_t i0 = uint64_t(e0 + 8 * k);
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    full += uint64_t(ws[h] & 0xFFFF) * splitmix_weight(i0 + 2 * h);
+                    full += uint64_t(ws[h] >> 16) * splitmix_weight(i0 + 2 * h + 1);
+                }
+            }
+        }
+        for (int64_t i = nv * 8 + threadIdx.x; i < n; i += HIST_THREADS) {
+            const uint32_t x = uint16_t(p[i]);
+            atomicAdd(&hist[w][(x >> 7) & 0xFF], 1u);
+            if (tt.want_full) full += uint64_t(x) * splitmix_weight(uint64_t(e0 + i));
+        }
+    } else {
+        for (int64_t i = threadIdx.x; i < n; i += HIST_THREADS) {
+            const uint32_t x = uint16_t(p[i]);
+            atomicAdd(&hist[w][(x >> 7) & 0xFF], 1u);
+            if (tt.want_full) full += uint64_t(x) * splitmix_weight(uint64_t(e0 + i));
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x < 256) {
+        uint32_t a = 0;
+        for (int ww = 0; ww < HIST_THREADS / 32; ++ww) a += hist[ww][threadIdx.x];
+        HS[s * 256 + threadIdx.x] = a;
+    }
+    if (tt.want_full) block_add_u64<HIST_THREADS>(full, &chk_full[t], red);
+}
+
+// ------------------------------------------------------------------ block decoder
+
+__global__ void __launch_bounds__(128) k_decode(const uint64_t* __restrict__ W, const uint32_t* __restrict__ bb,
+                                                const uint64_t* __restrict__ boff, int64_t n_blocks,
+                                                const AppGroup* __restrict__ G, const uint64_t* __restrict__ gblock, int64_t ng,
+                                                const DecTable* __restrict__ TB, const uint32_t* __restrict__ SYMS,
+                                                const uint64_t* __restrict__ GS, uint32_t* __restrict__ gaps,
+                                                uint32_t* __restrict__ zz, uint64_t* __restrict__ bsum,
+                                                unsigned long long* __restrict__ counters) {
+    const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (b >= n_blocks) return;
+    const int64_t g = last_le(gblock, ng, uint64_t(b));
+    const AppGroup grp = G[g];
+    const uint64_t k = uint64_t(b) - gblock[g];
+    const int cnt = int(tmin<uint64_t>(kBlock, grp.count - k * kBlock));
+    const uint64_t ebase = grp.start + k * kBlock;
+    uint64_t cur = boff[b];
+    const uint64_t end = cur + bb[b];
+    const uint64_t size = GS[int64_t(grp.tensor) * 256 + grp.exp];
+    const int rice = grp.rice;
+    const uint64_t qmax = size >> rice;
+    const DecTable* tab = TB + grp.table;
+    bool bad = false;
+    uint64_t sum = 0;
+    for (int step = 0; step < cnt; ++step) {
+        if (cur >= end) { bad = true; break; }
+        uint64_t y = ~read64(W, cur);
+        uint64_t q;
+        if (y) {
+            q = uint64_t(__clzll(y));
+        } else {
+            // a run of more than 64 ones: follow it window by window, never past this block's end
+            // or past q_max, so hostile updates cost at most their own bits
+            q = 64;
+            while (q <= qmax && cur + q < end) {
+                y = ~read64(W, cur + q);
+                if (y) { q += uint64_t(__clzll(y)); break; }
+                q += 64;
+            }
+        }
+        if (q > qmax || cur + q >= end) { bad = true; break; }
+        const uint64_t c = cur + q + 1;
+        const uint64_t x = read64(W, c);
+        const uint64_t rem = rice ? (x >> (64 - rice)) : 0;
+        const uint32_t peek = uint32_t((x << rice) >> (64 - kMaxCodeLen));
+        const uint32_t lv = tab->lut[peek >> (kMaxCodeLen - LUT_BITS)];
+        int L;
+        uint32_t idx;
+        if (lv) {
+            L = int(lv >> 24);
+            idx = lv & 0xFFFFFFu;
+        } else {
+            L = 1;
+            while (L <= kMaxCodeLen && peek >= tab->limit[L]) ++L;
+            if (L > kMaxCodeLen) { bad = true; break; }
+            idx = tab->base[L] + (peek >> (kMaxCodeLen - L)) - tab->first[L];
+        }
+        const uint32_t sym = SYMS[tab->sym_off + min(idx, tab->nsym - 1)];
+        const uint64_t gap = (q << rice) | rem;
+        gaps[ebase + step] = gap > 0xFFFFFFFFull ? 0xFFFFFFFFu : uint32_t(gap);
+        zz[ebase + step] = sym;
+        sum += gap + 1;
+        cur = c + uint64_t(rice) + uint64_t(L);
+    }
+    if (!bad && cur != end) bad = true;
+    bsum[b] = bad ? 0 : sum;
+    if (bad) atomicOr(&counters[1], (unsigned long long)ERR_DECODE);
+}
+
+// group-local index of every change: running sum of gap + 1 within its group
+__global__ void __launch_bounds__(256) k_locals(const uint64_t* __restrict__ bscan, int64_t n_blocks,
+                                                const AppGroup* __restrict__ G, const uint64_t* __restrict__ gblock, int64_t ng,
+                                                const uint64_t* __restrict__ GS, const uint32_t* __restrict__ gaps,
+                                                uint32_t* __restrict__ local, unsigned long long* __restrict__ counters) {
+    const int64_t b = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (b >= n_blocks) return;
+    const int64_t g = last_le(gblock, ng, uint64_t(b));
+    const AppGroup grp = G[g];
+    const uint64_t k = uint64_t(b) - gblock[g];
+    const uint64_t cnt = tmin<uint64_t>(kBlock, grp.count - k * kBlock);
+    const uint64_t ebase = grp.start + k * kBlock;
+    const uint64_t size = GS[int64_t(grp.tensor) * 256 + grp.exp];
+    uint64_t base = bscan[b] - bscan[gblock[g]];
+    bool bad = false;
+    for (uint64_t i0 = 0; i0 < cnt; i0 += 32) {
+        const uint64_t i = i0 + lane;
+        const uint64_t gp = i < cnt ? gaps[ebase + i] : 0;
+        uint64_t incl = i < cnt ? gp + 1 : 0;
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint64_t y = __shfl_up_sync(FULL, incl, o);
+            if (lane >= o) incl += y;
+        }
+        if (i < cnt) {
+            const uint64_t loc = base + incl - 1;
+            if (gp >= size || loc >= size) bad = true;
+            local[ebase + i] = loc > 0xFFFFFFFFull ? 0xFFFFFFFFu : uint32_t(loc);
+        }
+        base += __shfl_sync(FULL, incl, 31);
+    }
+    if (__any_sync(FULL, bad) && lane == 0) atomicOr(&counters[1], (unsigned long long)ERR_RANGE);
+}
+
+// ------------------------------------------------------------------ (exponent, rank) -> position
+
+struct MapSmem {
+    uint16_t tile[SUB_N];
+    uint16_t order[SUB_N];
+    uint16_t cnt[RANK_WARPS][256];
+    uint32_t tot[256], estart[256], pcur[256];
+    uint64_t cursor[256], gend[256];
+    int32_t gexp[256];
+    uint64_t red[RANK_WARPS];
+};
+
+__global__ void __launch_bounds__(RANK_THREADS, 2)
+k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, const uint32_t* __restrict__ PS,
+      const uint32_t* __restrict__ local, const uint32_t* __restrict__ zz, unsigned long long* __restrict__ caddr,
+      uint16_t* __restrict__ cval, unsigned long long* __restrict__ chk_delta, unsigned long long* __restrict__ mapped) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    MapSmem& S = *reinterpret_cast<MapSmem*>(smem_raw);
+    const int64_t s = blockIdx.x;
+    const int t = tensor_of_super(T, nT, s);
+    const AppTensor tt = T[t];
+    const int64_t e_begin = (s - tt.super_begin) * SUPER_N;
+    const int64_t e_end = min(tt.numel, e_begin + SUPER_N);
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const uint32_t lt = lanemask_lt();
+    const int ngt = tt.g_end - tt.g_begin;
+    if (tid < 256) S.pcur[tid] = PS[s * 256 + tid];
+    __syncthreads();
+    if (tid < ngt) {
+        const AppGroup grp = G[tt.g_begin + tid];
+        const uint32_t p0 = S.pcur[grp.exp];
+        uint64_t lo = grp.start, hi = grp.start + grp.count;      // first change with local >= p0
+        while (lo < hi) {
+            const uint64_t mid = (lo + hi) >> 1;
+            if (local[mid] < p0) lo = mid + 1; else hi = mid;
+        }
+        S.cursor[tid] = lo;
+        S.gend[tid] = grp.start + grp.count;
+        S.gexp[tid] = grp.exp;
+    }
+    uint64_t delta = 0, n_mapped = 0;
+    for (int64_t base = e_begin; base < e_end; base += SUB_N) {
+        const int n = int(tmin<int64_t>(SUB_N, e_end - base));
+        const int16_t* p = tt.w + base;
+        if (n == SUB_N && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+            const uint4* v = reinterpret_cast<const uint4*>(p);
+            uint4* d = reinterpret_cast<uint4*>(S.tile);
+            for (int k = tid; k < SUB_N / 8; k += RANK_THREADS) d[k] = __ldcs(v + k);
+        } else {
+            for (int i = tid; i < n; i += RANK_THREADS) S.tile[i] = uint16_t(p[i]);
+        }
+        for (int k = tid; k < RANK_WARPS * 256; k += RANK_THREADS) (&S.cnt[0][0])[k] = 0;
+        __syncthreads();
+        // pass 1: per-warp exponent counts
+        for (int c = 0; c < CHUNKS_PER_WARP; ++c) {
+            const int i0 = w * WARP_SPAN + c * 32;
+            if (i0 >= n) break;
+            const int i = i0 + lane;
+            const bool act = i < n;
+            const uint32_t e = act ? exp_of(S.tile[i]) : 0u;
+            const uint32_t peers = __match_any_sync(FULL, act ? e : 0x100u + lane);
+            if (act && (peers & lt) == 0) S.cnt[w][e] += uint16_t(__popc(peers));
+            __syncwarp();
+        }
+        __syncthreads();
+        if (tid < 256) {
+            uint32_t a = 0;
+            for (int ww = 0; ww < RANK_WARPS; ++ww) {
+                const uint32_t v = S.cnt[ww][tid];
+                S.cnt[ww][tid] = uint16_t(a);
+                a += v;
+            }
+            S.tot[tid] = a;
+        }
+        __syncthreads();
+        if (w == 0) {                       // exclusive scan of the 256 totals -> bucket starts
+            uint32_t v[8], sum = 0;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) { v[k] = S.tot[lane * 8 + k]; sum += v[k]; }
+            uint32_t incl = sum;
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(FULL, incl, o);
+                if (lane >= o) incl += y;
+            }
+            uint32_t run = incl - sum;
+#pragma unroll
+            for (int k = 0; k < 8; ++k) { S.estart[lane * 8 + k] = run; run += v[k]; }
+        }
+        __syncthreads();
+        // pass 2: stable counting sort of the sub-tile by exponent
+        for (int c = 0; c < CHUNKS_PER_WARP; ++c) {
+            const int i0 = w * WARP_SPAN + c * 32;
+            if (i0 >= n) break;
+            const int i = i0 + lane;
+            const bool act = i < n;
+            const uint32_t e = act ? exp_of(S.tile[i]) : 0u;
+            const uint32_t peers = __match_any_sync(FULL, act ? e : 0x100u + lane);
+            if (act) S.order[S.estart[e] + S.cnt[w][e] + __popc(peers & lt)] = uint16_t(i);
+            __syncwarp();
+            if (act && (peers & lt) == 0) S.cnt[w][e] += uint16_t(__popc(peers));
+            __syncwarp();
+        }
+        __syncthreads();
+        // place this sub-tile's changes, group by group
+        for (int k = w; k < ngt; k += RANK_WARPS) {
+            const int e = S.gexp[k];
+            const uint32_t lo = S.pcur[e], tot = S.tot[e];
+            const uint64_t ge = S.gend[k];
+            uint64_t cur = S.cursor[k];
+            for (;;) {
+                const uint64_t j = cur + lane;
+                uint32_t lc = 0;
+                bool valid = j < ge;
+                if (valid) { lc = local[j]; valid = lc - lo < tot && lc >= lo; }
+                if (valid) {
+                    const uint32_t i = S.order[S.estart[e] + (lc - lo)];
+                    const uint32_t old = S.tile[i];
+                    const uint32_t z = zz[j];
+                    const int32_t res = int32_t(z >> 1) ^ -int32_t(z & 1);
+                    const uint32_t nv = uint32_t(int32_t(old) + res) & 0xFFFFu;
+                    const int64_t pos = base + i;
+                    caddr[j] = (unsigned long long)(reinterpret_cast<uintptr_t>(tt.w + pos));
+                    cval[j] = uint16_t(nv);
+                    delta += (uint64_t(nv) - uint64_t(old)) * splitmix_weight(uint64_t(pos));
+                    ++n_mapped;
+                }
+                const uint32_t m = __ballot_sync(FULL, valid);
+                // consumed changes are a prefix: stop at the first one beyond this sub-tile
+                const int taken = __popc(~m) ? __ffs(~m) - 1 : 32;
+                cur += uint64_t(taken);
+                if (taken < 32) break;
+            }
+            if (lane == 0) S.cursor[k] = cur;
+        }
+        __syncthreads();
+        if (tid < 256) S.pcur[tid] += S.tot[tid];
+        __syncthreads();
+    }
+    block_add_u64<RANK_THREADS>(delta, &chk_delta[t], S.red);
+    block_add_u64<RANK_THREADS>(n_mapped, mapped, S.red);
+}
+
+// Runs only after the host verdict, which requires every change to have been mapped exactly once;
+// a null address (never mapped) is skipped all the same.
+__global__ void __launch_bounds__(256) k_commit(const unsigned long long* __restrict__ caddr, const uint16_t* __restrict__ cval,
+                                                uint64_t n) {
+    const uint64_t j = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (j >= n) return;
+    const unsigned long long a = caddr[j];
+    if (a) *reinterpret_cast<uint16_t*>(uintptr_t(a)) = cval[j];
+}
+
+__global__ void k_widen(const uint32_t* __restrict__ a, uint64_t* __restrict__ b, int64_t n) {
+    const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (i < n) b[i] = a[i];
+}
+
+__global__ void __launch_bounds__(512) k_checksum(const int16_t* __restrict__ p, int64_t n, unsigned long long* __restrict__ out) {
+    __shared__ uint64_t red[16];
+    uint64_t s = 0;
+    for (int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += int64_t(gridDim.x) * blockDim.x)
+        s += uint64_t(uint16_t(p[i])) * splitmix_weight(uint64_t(i));
+    block_add_u64<512>(s, out, red);
+}
+
+template <class T>
+T* dev(Ctx& c, Slot s) { return reinterpret_cast<T*>(c.b[s].p); }
+
+void build_lut(const DecodeTable& d, uint32_t* lut) {
+    for (uint32_t p = 0; p < (1u << LUT_BITS); ++p) {
+        const uint32_t lo = p << (kMaxCodeLen - LUT_BITS);
+        int L = 1;
+        while (L <= kMaxCodeLen && lo >= d.limit[L]) ++L;
+        if (L <= LUT_BITS) lut[p] = (uint32_t(L) << 24) | (d.base[L] + (lo >> (kMaxCodeLen - L)) - d.first[L]);
+        else lut[p] = 0;
+    }
+}
+
+}  // namespace
+
+Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64_t* old_chk, const uint8_t* has_chk,
+                  cudaStream_t st, int64_t* changed, std::string* err) {
+    *changed = 0;
+    const int nt = int(u.tensors.size());
+    if (nt == 0) return kOk;
+    // ---- host tables
+    std::vector<AppTensor> T(static_cast<size_t>(nt));
+    std::vector<AppGroup> G;
+    std::vector<uint64_t> gblock(1, 0);
+    std::vector<int64_t> row_begin(static_cast<size_t>(nt) + 1), chunk_begin(static_cast<size_t>(nt) + 1, 0);
+    int64_t n_super = 0;
+    uint64_t start = 0;
+    for (int t = 0; t < nt; ++t) {
+        const TensorHeader& h = u.tensors[size_t(t)];
+        if (h.numel >= (int64_t(1) << 32)) { *err = "tensors of 2^32 or more elements are not supported"; return kValueError; }
+        AppTensor& d = T[size_t(t)];
+        d.w = weights[t];
+        d.numel = h.numel;
+        d.super_begin = n_super;
+        d.want_full = has_chk && has_chk[t] ? 0 : 1;
+        d.g_begin = int32_t(G.size());
+        for (const Group& g : h.groups) {
+            AppGroup ag{};
+            ag.start = start;
+            ag.count = uint64_t(g.count);
+            ag.tensor = t;
+            ag.exp = g.exponent;
+            ag.rice = g.rice;
+            ag.table = u.table_of_exp[g.exponent];
+            G.push_back(ag);
+            start += uint64_t(g.count);
+            gblock.push_back(gblock.back() + (uint64_t(g.count) + kBlock - 1) / kBlock);
+        }
+        d.g_end = int32_t(G.size());
+        row_begin[size_t(t)] = n_super;
+        const int64_t rows = (h.numel + SUPER_N - 1) / SUPER_N;
+        n_super += rows;
+        chunk_begin[size_t(t) + 1] = chunk_begin[size_t(t)] + (rows + SCAN_CHUNK - 1) / SCAN_CHUNK;
+    }
+    row_begin[size_t(nt)] = n_super;
+    const int64_t n_chunks = chunk_begin[size_t(nt)];
+    const int64_t ng = int64_t(G.size());
+    const uint64_t total = start;
+    const int64_t n_blocks = u.n_blocks;
+    if (int64_t(gblock.back()) != n_blocks) { *err = "internal: block count mismatch"; return kCudaError; }
+    std::vector<DecTable> TB(u.tables.size());
+    std::vector<uint32_t> syms;
+    for (size_t k = 0; k < u.tables.size(); ++k) {
+        DecodeTable d;
+        const size_t off = syms.size();
+        syms.resize(off + u.tables[k].symbols.size());
+        build_decode_table(u.tables[k], &d, syms.data() + off);
+        DecTable& x = TB[k];
+        std::memcpy(x.first, d.first, sizeof(x.first));
+        std::memcpy(x.base, d.base, sizeof(x.base));
+        std::memcpy(x.limit, d.limit, sizeof(x.limit));
+        x.sym_off = uint32_t(off);
+        x.nsym = uint32_t(u.tables[k].symbols.size());
+        build_lut(d, x.lut);
+    }
+
+    // ---- device buffers
+    const size_t cells = size_t(nt) * 256;
+    const size_t payload_alloc = size_t(u.payload_len) + 64;
+    CRX_CUDA(ensure_dev(C.b[S_A_TENS], sizeof(AppTensor) * size_t(nt), st));
+    CRX_CUDA(ensure_dev(C.b[S_A_GROUPS], sizeof(AppGroup) * size_t(ng) + sizeof(uint64_t) * (size_t(ng) + 1), st));
+    CRX_CUDA(ensure_dev(C.b[S_A_TABLES], sizeof(DecTable) * TB.size(), st));
+    CRX_CUDA(ensure_dev(C.b[S_A_SYMS], sizeof(uint32_t) * syms.size(), st));
+    CRX_CUDA(ensure_dev(C.b[S_A_PAYLOAD], payload_alloc, st));
+    CRX_CUDA(ensure_dev(C.b[S_A_BB], sizeof(uint32_t) * size_t(n_blocks), st));
+    CRX_CUDA(ensure_dev(C.b[S_A_BOFF], sizeof(uint64_t) * size_t(n_blocks), st));
+    CRX_CUDA(ensure_dev(C.b[S_A_BSUM], sizeof(uint64_t) * size_t(n_blocks), st));
+    CRX_CUDA(ensure_dev(C.b[S_A_SCAN_TMP], sizeof(uint64_t) * (exclusive_scan_tmp_elems(n_blocks) + 2), st));
+    CRX_CUDA(ensure_dev(C.b[S_A_GAPS], sizeof(uint32_t) * total, st));
+    CRX_CUDA(ensure_dev(C.b[S_A_ZZ], sizeof(uint32_t) * total, st));
+    CRX_CUDA(ensure_dev(C.b[S_A_LOCAL], sizeof(uint32_t) * total, st));
+    CRX_CUDA(ensure_dev(C.b[S_A_CADDR], sizeof(uint64_t) * total, st));
+    CRX_CUDA(ensure_dev(C.b[S_A_CVAL], sizeof(uint16_t) * total, st));
+    CRX_CUDA(ensure_dev(C.b[S_A_HS], sizeof(uint32_t) * 256 * size_t(n_super), st));
+    CRX_CUDA(ensure_dev(C.b[S_A_TOT], sizeof(uint64_t) * cells, st));
+    CRX_CUDA(ensure_dev(C.b[S_A_CHUNK_ROWS], sizeof(int64_t) * 2 * (size_t(nt) + 1), st));
+    CRX_CUDA(ensure_dev(C.b[S_A_CHUNK_SUMS], sizeof(uint32_t) * 256 * size_t(n_chunks), st));
+    CRX_CUDA(ensure_dev(C.b[S_A_COUNTERS], sizeof(uint64_t) * (16 + 2 * size_t(nt)), st));
+
+    // ---- uploads: metadata through pinned staging, the payload straight from the caller's buffer
+    const size_t up = sizeof(AppTensor) * nt + sizeof(AppGroup) * ng + 8 * (ng + 1) + sizeof(DecTable) * TB.size() +
+                      4 * syms.size() + 16 * (nt + 1) + 4 * size_t(n_blocks) + 256;
+    CRX_CUDA(ensure_host(C, up, st));
+    uint8_t* h = static_cast<uint8_t*>(C.host);
+    size_t o = 0;
+    auto upload = [&](void* dst, const void* src, size_t bytes) -> cudaError_t {
+        if (!bytes) return cudaSuccess;
+        std::memcpy(h + o, src, bytes);
+        const cudaError_t e = cudaMemcpyAsync(dst, h + o, bytes, cudaMemcpyHostToDevice, st);
+        o += (bytes + 15) & ~size_t(15);
+        return e;
+    };
+    auto* dG = dev<AppGroup>(C, S_A_GROUPS);
+    auto* dgblock = reinterpret_cast<uint64_t*>(dG + ng);
+    auto* drows = dev<int64_t>(C, S_A_CHUNK_ROWS);
+    CRX_CUDA(upload(C.b[S_A_TENS].p, T.data(), sizeof(AppTensor) * size_t(nt)));
+    CRX_CUDA(upload(dG, G.data(), sizeof(AppGroup) * size_t(ng)));
+    CRX_CUDA(upload(dgblock, gblock.data(), 8 * (size_t(ng) + 1)));
+    CRX_CUDA(upload(C.b[S_A_TABLES].p, TB.data(), sizeof(DecTable) * TB.size()));
+    CRX_CUDA(upload(C.b[S_A_SYMS].p, syms.data(), 4 * syms.size()));
+    CRX_CUDA(upload(drows, row_begin.data(), 8 * (size_t(nt) + 1)));
+    CRX_CUDA(upload(drows + nt + 1, chunk_begin.data(), 8 * (size_t(nt) + 1)));
+    CRX_CUDA(upload(C.b[S_A_BB].p, u.block_table, 4 * size_t(n_blocks)));
+    CRX_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(C.b[S_A_PAYLOAD].p) + u.payload_len, 0, 64, st));
+    if (u.payload_len)
+        CRX_CUDA(cudaMemcpyAsync(C.b[S_A_PAYLOAD].p, u.payload, size_t(u.payload_len), cudaMemcpyHostToDevice, st));
+    auto* counters = dev<unsigned long long>(C, S_A_COUNTERS);
+    auto* chk_delta = counters + 16;
+    auto* chk_full = chk_delta + nt;
+    CRX_CUDA(cudaMemsetAsync(counters, 0, sizeof(uint64_t) * (16 + 2 * size_t(nt)), st));
+
+    // ---- exponent histograms, per-super-tile offsets and group sizes
+    const AppTensor* dT = dev<AppTensor>(C, S_A_TENS);
+    { KernelScope ks_(C, "k_app_hist", st);
+    k_app_hist<<<unsigned(n_super), HIST_THREADS, 0, st>>>(dT, nt, dev<uint32_t>(C, S_A_HS), chk_full);
+    }
+    CRX_CUDA(cudaGetLastError());
+    launch_column_scan(C, dev<uint32_t>(C, S_A_HS), n_super, drows, nt, drows + nt + 1, n_chunks,
+                       dev<uint32_t>(C, S_A_CHUNK_SUMS), dev<uint64_t>(C, S_A_TOT), st);
+    // ---- block offsets and decode
+    uint64_t* boff = dev<uint64_t>(C, S_A_BOFF);
+    uint64_t* scan_tmp = dev<uint64_t>(C, S_A_SCAN_TMP);
+    uint64_t* d_total = scan_tmp + exclusive_scan_tmp_elems(n_blocks);
+    { KernelScope ks_(C, "k_widen", st);
+    k_widen<<<unsigned((n_blocks + 255) / 256), 256, 0, st>>>(dev<uint32_t>(C, S_A_BB), boff, n_blocks);
+    }
+    launch_exclusive_scan_u64(C, boff, n_blocks, scan_tmp, d_total, st);
+    { KernelScope ks_(C, "k_decode", st);
+    k_decode<<<unsigned((n_blocks + 127) / 128), 128, 0, st>>>(
+        dev<uint64_t>(C, S_A_PAYLOAD), dev<uint32_t>(C, S_A_BB), boff, n_blocks, dG, dgblock, ng, dev<DecTable>(C, S_A_TABLES),
+        dev<uint32_t>(C, S_A_SYMS), dev<uint64_t>(C, S_A_TOT), dev<uint32_t>(C, S_A_GAPS), dev<uint32_t>(C, S_A_ZZ),
+        dev<uint64_t>(C, S_A_BSUM), counters);
+    }
+    CRX_CUDA(cudaGetLastError());
+    launch_exclusive_scan_u64(C, dev<uint64_t>(C, S_A_BSUM), n_blocks, scan_tmp, d_total, st);
+    { KernelScope ks_(C, "k_locals", st);
+    k_locals<<<unsigned((n_blocks * 32 + 255) / 256), 256, 0, st>>>(dev<uint64_t>(C, S_A_BSUM), n_blocks, dG, dgblock, ng,
+                                                                   dev<uint64_t>(C, S_A_TOT), dev<uint32_t>(C, S_A_GAPS),
+                                                                   dev<uint32_t>(C, S_A_LOCAL), counters);
+    }
+    CRX_CUDA(cudaGetLastError());
+    // ---- positions, staged values, checksum deltas
+    CRX_CUDA(cudaMemsetAsync(C.b[S_A_CADDR].p, 0, sizeof(uint64_t) * total, st));
+    const size_t map_smem = sizeof(MapSmem);
+    CRX_CUDA(cudaFuncSetAttribute(k_map, cudaFuncAttributeMaxDynamicSharedMemorySize, int(map_smem)));
+    { KernelScope ks_(C, "k_map", st);
+    k_map<<<unsigned(n_super), RANK_THREADS, map_smem, st>>>(dT, nt, dG, dev<uint32_t>(C, S_A_HS), dev<uint32_t>(C, S_A_LOCAL),
+                                                            dev<uint32_t>(C, S_A_ZZ), dev<unsigned long long>(C, S_A_CADDR),
+                                                            dev<uint16_t>(C, S_A_CVAL), chk_delta, counters + 2);
+    }
+    CRX_CUDA(cudaGetLastError());
+    // ---- verdict (one synchronisation for the whole update)
+    uint64_t* hc = C.small;
+    const size_t nsmall = 16 + 2 * size_t(nt);
+    std::vector<uint64_t> hv(nsmall);
+    if (nsmall <= 512) {
+        CRX_CUDA(cudaMemcpyAsync(hc, counters, 8 * nsmall, cudaMemcpyDeviceToHost, st));
+        CRX_CUDA(cudaStreamSynchronize(st));
+        std::memcpy(hv.data(), hc, 8 * nsmall);
+    } else {
+        CRX_CUDA(ensure_host(C, 8 * nsmall, st));
+        CRX_CUDA(cudaMemcpyAsync(C.host, counters, 8 * nsmall, cudaMemcpyDeviceToHost, st));
+        CRX_CUDA(cudaStreamSynchronize(st));
+        std::memcpy(hv.data(), C.host, 8 * nsmall);
+    }
+    if (hv[1] & (ERR_DECODE | ERR_RANGE)) {
+        *err = "payload positions outside their exponent groups";
+        return kCorrupt;
+    }
+    if (hv[2] != total) {   // every in-range change lands in exactly one sub-tile
+        *err = "internal: not every change was placed";
+        return kCudaError;
+    }
+    std::string bad_names;
+    int n_bad = 0;
+    for (int t = 0; t < nt; ++t) {
+        const uint64_t base = T[size_t(t)].want_full ? hv[16 + size_t(nt) + size_t(t)] : old_chk[t];
+        if (base + hv[16 + size_t(t)] != u.tensors[size_t(t)].checksum) {
+            if (n_bad < 3) {
+                if (n_bad) bad_names += ", ";
+                bad_names.append(reinterpret_cast<const char*>(u.tensors[size_t(t)].name), size_t(u.tensors[size_t(t)].name_len));
+            }
+            ++n_bad;
+        }
+    }
+    if (n_bad) {
+        *err = "update does not verify (checksum mismatch: " + bad_names + ")";
+        return kCorrupt;
+    }
+    { KernelScope ks_(C, "k_commit", st);
+    k_commit<<<unsigned((total + 255) / 256), 256, 0, st>>>(dev<unsigned long long>(C, S_A_CADDR), dev<uint16_t>(C, S_A_CVAL),
+                                                           total);
+    }
+    CRX_CUDA(cudaGetLastError());
+    *changed = int64_t(total);
+    return kOk;
+}
+
+Status checksum_impl(Ctx& C, const int16_t* data, int64_t n, cudaStream_t st, uint64_t* out, std::string* err) {
+    CRX_CUDA(ensure_dev(C.b[S_CHK], 64, st));
+    auto* acc = dev<unsigned long long>(C, S_CHK);
+    CRX_CUDA(cudaMemsetAsync(acc, 0, 8, st));
+    if (n > 0) {
+        const int64_t blocks = std::min<int64_t>((n + 511) / 512, 148 * 8);
+        { KernelScope ks_(C, "k_checksum", st);
+        k_checksum<<<unsigned(blocks), 512, 0, st>>>(data, n, acc);
+        }
+        CRX_CUDA(cudaGetLastError());
+    }
+    CRX_CUDA(cudaMemcpyAsync(C.small, acc, 8, cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaStreamSynchronize(st));
+    *out = C.small[0];
+    return kOk;
+}
+
+}  // namespace crx

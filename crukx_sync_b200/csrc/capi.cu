@@ -1,0 +1,383 @@
+// extern "C" entry points (include/crukx_b200.h) over the C++ drivers; no exception crosses.
+#include <cstdio>
+#include <cstring>
+#include <new>
+#include <string>
+
+#include "../../include/crukx_b200.h"
+#include "capi_internal.h"
+
+struct crx_ctx {
+    crx::Ctx c;
+};
+struct crx_encoded {
+    crx::Encoded e;
+};
+struct crx_update {
+    crx::Update u;
+};
+
+namespace crx {
+
+static cudaEvent_t pooled_event(Ctx& c) {
+    if (c.ev_used == c.ev_pool.size()) {
+        cudaEvent_t e = nullptr;
+        if (cudaEventCreate(&e) != cudaSuccess) { cudaGetLastError(); return nullptr; }
+        c.ev_pool.push_back(e);
+    }
+    return c.ev_pool[c.ev_used++];
+}
+
+KernelScope::KernelScope(Ctx& ctx, const char* name, cudaStream_t st) : c(ctx), s(st) {
+    ++c.launches;
+    if (c.profile) {
+        m.name = name;
+        m.a = pooled_event(c);
+        m.b = pooled_event(c);
+        if (m.a) cudaEventRecord(m.a, s);
+    }
+}
+
+KernelScope::~KernelScope() {
+    if (c.profile && m.a && m.b) {
+        cudaEventRecord(m.b, s);
+        c.marks.push_back(m);
+    }
+}
+
+Ctx::~Ctx() {
+    int prev = -1;
+    cudaGetDevice(&prev);
+    cudaSetDevice(device);
+    cudaDeviceSynchronize();
+    for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
+    for (auto& d : b)
+        if (d.p) cudaFree(d.p);
+    if (host) cudaFreeHost(host);
+    if (small) cudaFreeHost(small);
+    if (prev >= 0) cudaSetDevice(prev);
+}
+
+cudaError_t ensure_dev(DevBuf& buf, size_t bytes, cudaStream_t s) {
+    if (bytes <= buf.cap) return cudaSuccess;
+    size_t cap = buf.cap ? buf.cap : 4096;
+    while (cap < bytes) cap += cap / 2 + 4096;
+    if (buf.p) {
+        cudaError_t e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return e;
+        cudaFree(buf.p);
+        buf.p = nullptr;
+        buf.cap = 0;
+    }
+    cudaError_t e = cudaMalloc(&buf.p, cap);
+    if (e != cudaSuccess) {
+        cudaGetLastError();
+        e = cudaMalloc(&buf.p, bytes);   // retry without headroom
+        if (e != cudaSuccess) { buf.p = nullptr; return e; }
+        cap = bytes;
+    }
+    buf.cap = cap;
+    return cudaSuccess;
+}
+
+cudaError_t ensure_host(Ctx& c, size_t bytes, cudaStream_t s) {
+    if (bytes <= c.host_cap) return cudaSuccess;
+    size_t cap = c.host_cap ? c.host_cap : (1 << 20);
+    while (cap < bytes) cap *= 2;
+    if (c.host) {
+        cudaError_t e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return e;
+        cudaFreeHost(c.host);
+        c.host = nullptr;
+        c.host_cap = 0;
+    }
+    cudaError_t e = cudaMallocHost(&c.host, cap);
+    if (e != cudaSuccess) { c.host = nullptr; return e; }
+    c.host_cap = cap;
+    return cudaSuccess;
+}
+
+}  // namespace crx
+
+namespace {
+
+void put_err(char* err, size_t n, const std::string& m) {
+    if (err && n) std::snprintf(err, n, "%s", m.c_str());
+}
+
+struct DeviceGuard {
+    int prev = -1;
+    explicit DeviceGuard(int dev) {
+        cudaGetDevice(&prev);
+        if (prev != dev) cudaSetDevice(dev);
+    }
+    ~DeviceGuard() {
+        int cur = -1;
+        cudaGetDevice(&cur);
+        if (prev >= 0 && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+}  // namespace
+
+extern "C" {
+
+int crx_wire_version(void) { return 2; }
+
+int crx_ctx_create(int device, crx_ctx** out, char* err, size_t errlen) {
+    if (!out) return CRX_BAD_ARGUMENT;
+    *out = nullptr;
+    crx_ctx* c = new (std::nothrow) crx_ctx;
+    if (!c) return CRX_NO_MEMORY;
+    c->c.device = device;
+    DeviceGuard g(device);
+    cudaError_t e = cudaSetDevice(device);
+    if (e == cudaSuccess) e = cudaMallocHost(reinterpret_cast<void**>(&c->c.small), 4096);
+    if (e != cudaSuccess) {
+        put_err(err, errlen, std::string("crx_ctx_create: ") + cudaGetErrorString(e));
+        cudaGetLastError();
+        c->c.small = nullptr;
+        delete c;
+        return CRX_CUDA_ERROR;
+    }
+    *out = c;
+    return CRX_OK;
+}
+
+void crx_ctx_destroy(crx_ctx* ctx) { delete ctx; }
+
+int crx_encode(crx_ctx* ctx, int32_t n_tensors, const int16_t* const* prev, const int16_t* const* cur,
+               const int64_t* numel, const uint8_t* const* names, const int64_t* name_len,
+               const uint64_t* cached_checksums, const uint8_t* has_cached, void* stream,
+               crx_encoded** out, char* err, size_t errlen) {
+    if (!ctx || !out || n_tensors < 0 || (n_tensors && (!prev || !cur || !numel || !names || !name_len))) {
+        put_err(err, errlen, "crx_encode: bad argument");
+        return CRX_BAD_ARGUMENT;
+    }
+    *out = nullptr;
+    try {
+        std::lock_guard<std::mutex> lock(ctx->c.mu);
+        DeviceGuard g(ctx->c.device);
+        crx_encoded* e = new crx_encoded;
+        std::string msg;
+        const crx::Status s = crx::encode_impl(ctx->c, n_tensors, prev, cur, numel, names, name_len, cached_checksums,
+                                               has_cached, static_cast<cudaStream_t>(stream), &e->e, &msg);
+        if (s != crx::kOk) {
+            delete e;
+            put_err(err, errlen, msg);
+            return int(s);
+        }
+        *out = e;
+        return CRX_OK;
+    } catch (const std::bad_alloc&) {
+        put_err(err, errlen, "crx_encode: out of host memory");
+        return CRX_NO_MEMORY;
+    } catch (const std::exception& ex) {
+        put_err(err, errlen, std::string("crx_encode: ") + ex.what());
+        return CRX_CUDA_ERROR;
+    }
+}
+
+int64_t crx_encoded_size(const crx_encoded* enc) { return enc ? int64_t(enc->e.bytes.size()) : -1; }
+
+int crx_encoded_copy(const crx_encoded* enc, uint8_t* dst, int64_t cap) {
+    if (!enc || !dst || cap < int64_t(enc->e.bytes.size())) return CRX_BAD_ARGUMENT;
+    std::memcpy(dst, enc->e.bytes.data(), enc->e.bytes.size());
+    return CRX_OK;
+}
+
+int64_t crx_encoded_changes(const crx_encoded* enc) { return enc ? int64_t(enc->e.changes) : -1; }
+
+void crx_encoded_checksums(const crx_encoded* enc, uint64_t* checksums, uint8_t* present) {
+    if (!enc) return;
+    for (size_t i = 0; i < enc->e.checksums.size(); ++i) {
+        if (checksums) checksums[i] = enc->e.checksums[i];
+        if (present) present[i] = enc->e.present[i];
+    }
+}
+
+void crx_encoded_free(crx_encoded* enc) { delete enc; }
+
+int crx_parse(const uint8_t* data, int64_t len, crx_update** out, char* err, size_t errlen) {
+    if (!out || len < 0 || (len && !data)) return CRX_BAD_ARGUMENT;
+    *out = nullptr;
+    try {
+        crx_update* u = new crx_update;
+        std::string msg;
+        const crx::Status s = crx::parse_update(data, len, &u->u, &msg);
+        if (s != crx::kOk) {
+            delete u;
+            put_err(err, errlen, msg);
+            return int(s);
+        }
+        *out = u;
+        return CRX_OK;
+    } catch (const std::bad_alloc&) {
+        put_err(err, errlen, "crx_parse: out of host memory");
+        return CRX_NO_MEMORY;
+    }
+}
+
+int64_t crx_update_n_tensors(const crx_update* u) { return u ? int64_t(u->u.tensors.size()) : -1; }
+int64_t crx_update_changes(const crx_update* u) { return u ? u->u.total_changes : -1; }
+
+int crx_update_tensor(const crx_update* u, int64_t i, const uint8_t** name, int64_t* name_len, int64_t* numel,
+                      uint64_t* checksum, int32_t* n_groups) {
+    if (!u || i < 0 || i >= int64_t(u->u.tensors.size())) return CRX_BAD_ARGUMENT;
+    const crx::TensorHeader& h = u->u.tensors[size_t(i)];
+    if (name) *name = h.name;
+    if (name_len) *name_len = h.name_len;
+    if (numel) *numel = h.numel;
+    if (checksum) *checksum = h.checksum;
+    if (n_groups) *n_groups = int32_t(h.groups.size());
+    return CRX_OK;
+}
+
+int crx_update_group(const crx_update* u, int64_t i, int32_t k, int32_t* exponent, int64_t* count, int32_t* rice) {
+    if (!u || i < 0 || i >= int64_t(u->u.tensors.size())) return CRX_BAD_ARGUMENT;
+    const auto& gs = u->u.tensors[size_t(i)].groups;
+    if (k < 0 || k >= int32_t(gs.size())) return CRX_BAD_ARGUMENT;
+    if (exponent) *exponent = gs[size_t(k)].exponent;
+    if (count) *count = gs[size_t(k)].count;
+    if (rice) *rice = gs[size_t(k)].rice;
+    return CRX_OK;
+}
+
+int32_t crx_update_n_tables(const crx_update* u) { return u ? int32_t(u->u.tables.size()) : -1; }
+
+int crx_update_table(const crx_update* u, int32_t k, int32_t* exponent, int64_t* n_symbols) {
+    if (!u || k < 0 || k >= int32_t(u->u.tables.size())) return CRX_BAD_ARGUMENT;
+    if (exponent) *exponent = u->u.tables[size_t(k)].exponent;
+    if (n_symbols) *n_symbols = int64_t(u->u.tables[size_t(k)].symbols.size());
+    return CRX_OK;
+}
+
+int crx_update_table_entries(const crx_update* u, int32_t k, uint32_t* symbols, uint8_t* lengths) {
+    if (!u || k < 0 || k >= int32_t(u->u.tables.size())) return CRX_BAD_ARGUMENT;
+    const crx::Table& t = u->u.tables[size_t(k)];
+    if (symbols) std::memcpy(symbols, t.symbols.data(), 4 * t.symbols.size());
+    if (lengths) std::memcpy(lengths, t.lengths.data(), t.lengths.size());
+    return CRX_OK;
+}
+
+int64_t crx_update_n_blocks(const crx_update* u) { return u ? u->u.n_blocks : -1; }
+
+int crx_update_block_bits(const crx_update* u, uint32_t* out) {
+    if (!u || !out) return CRX_BAD_ARGUMENT;
+    std::memcpy(out, u->u.block_table, 4 * size_t(u->u.n_blocks));
+    return CRX_OK;
+}
+
+int crx_update_payload(const crx_update* u, const uint8_t** data, int64_t* len) {
+    if (!u) return CRX_BAD_ARGUMENT;
+    if (data) *data = u->u.payload;
+    if (len) *len = u->u.payload_len;
+    return CRX_OK;
+}
+
+void crx_update_free(crx_update* u) { delete u; }
+
+int crx_apply(crx_ctx* ctx, const crx_update* u, int16_t* const* weights, const uint64_t* cached_checksums,
+              const uint8_t* has_cached, void* stream, int64_t* changed, char* err, size_t errlen) {
+    if (!ctx || !u || !changed || (!u->u.tensors.empty() && !weights)) {
+        put_err(err, errlen, "crx_apply: bad argument");
+        return CRX_BAD_ARGUMENT;
+    }
+    if (has_cached && !cached_checksums) {
+        put_err(err, errlen, "crx_apply: has_cached without cached_checksums");
+        return CRX_BAD_ARGUMENT;
+    }
+    try {
+        std::lock_guard<std::mutex> lock(ctx->c.mu);
+        DeviceGuard g(ctx->c.device);
+        std::string msg;
+        const crx::Status s = crx::apply_impl(ctx->c, u->u, weights, cached_checksums, has_cached,
+                                              static_cast<cudaStream_t>(stream), changed, &msg);
+        if (s != crx::kOk) {
+            put_err(err, errlen, msg);
+            return int(s);
+        }
+        return CRX_OK;
+    } catch (const std::bad_alloc&) {
+        put_err(err, errlen, "crx_apply: out of host memory");
+        return CRX_NO_MEMORY;
+    } catch (const std::exception& ex) {
+        put_err(err, errlen, std::string("crx_apply: ") + ex.what());
+        return CRX_CUDA_ERROR;
+    }
+}
+
+int crx_huffman_lengths(const uint64_t* counts, int64_t n, uint8_t* lengths) {
+    if (n <= 0 || !counts || !lengths) return CRX_BAD_ARGUMENT;
+    try {
+        crx::huffman_lengths(counts, n, lengths);
+        return CRX_OK;
+    } catch (const std::bad_alloc&) {
+        return CRX_NO_MEMORY;
+    }
+}
+
+uint64_t crx_ctx_launches(crx_ctx* ctx) { return ctx ? ctx->c.launches : 0; }
+
+int crx_ctx_profile(crx_ctx* ctx, int enable) {
+    if (!ctx) return CRX_BAD_ARGUMENT;
+    std::lock_guard<std::mutex> lock(ctx->c.mu);
+    ctx->c.profile = enable != 0;
+    if (enable) {
+        ctx->c.marks.clear();
+        ctx->c.ev_used = 0;
+    }
+    return CRX_OK;
+}
+
+int32_t crx_ctx_kernel_times(crx_ctx* ctx, char* names, size_t names_len, double* ms, int32_t* counts, int32_t max) {
+    if (!ctx) return -1;
+    std::lock_guard<std::mutex> lock(ctx->c.mu);
+    DeviceGuard g(ctx->c.device);
+    std::vector<std::string> order;
+    std::vector<double> tot;
+    std::vector<int32_t> cnt;
+    for (const crx::ProfMark& m : ctx->c.marks) {
+        float t = 0.f;
+        if (cudaEventSynchronize(m.b) != cudaSuccess || cudaEventElapsedTime(&t, m.a, m.b) != cudaSuccess) {
+            cudaGetLastError();
+            continue;
+        }
+        size_t k = 0;
+        while (k < order.size() && order[k] != m.name) ++k;
+        if (k == order.size()) { order.push_back(m.name); tot.push_back(0.0); cnt.push_back(0); }
+        tot[k] += t;
+        cnt[k] += 1;
+    }
+    std::string joined;
+    for (size_t k = 0; k < order.size(); ++k) {
+        if (int32_t(k) < max) {
+            if (ms) ms[k] = tot[k];
+            if (counts) counts[k] = cnt[k];
+        }
+        joined += order[k];
+        joined += '\n';
+    }
+    if (names && names_len) std::snprintf(names, names_len, "%s", joined.c_str());
+    return int32_t(order.size());
+}
+
+int crx_checksum(crx_ctx* ctx, const int16_t* data, int64_t n, void* stream, uint64_t* out, char* err, size_t errlen) {
+    if (!ctx || !out || n < 0 || (n && !data)) return CRX_BAD_ARGUMENT;
+    try {
+        std::lock_guard<std::mutex> lock(ctx->c.mu);
+        DeviceGuard g(ctx->c.device);
+        std::string msg;
+        const crx::Status s = crx::checksum_impl(ctx->c, data, n, static_cast<cudaStream_t>(stream), out, &msg);
+        if (s != crx::kOk) {
+            put_err(err, errlen, msg);
+            return int(s);
+        }
+        return CRX_OK;
+    } catch (const std::exception& ex) {
+        put_err(err, errlen, std::string("crx_checksum: ") + ex.what());
+        return CRX_CUDA_ERROR;
+    }
+}
+
+}  // extern "C"

@@ -1,0 +1,79 @@
+// Per-device context: grow-only device workspace, pinned host staging and the lock that
+// serializes calls on one context.  Library-owned scratch; callers own every weight buffer.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "host_codec.h"
+
+namespace crx {
+
+struct DevBuf {
+    void* p = nullptr;
+    size_t cap = 0;
+};
+
+struct Ctx;
+
+// Grow `buf` to at least `bytes` (contents not preserved).  Synchronizes `s` before freeing.
+cudaError_t ensure_dev(DevBuf& buf, size_t bytes, cudaStream_t s);
+cudaError_t ensure_host(Ctx& c, size_t bytes, cudaStream_t s);
+
+// Named slots of Ctx::b.
+enum Slot : int {
+    S_TENS = 0, S_HS, S_CS, S_CHUNK_ROWS, S_CHUNK_SUMS, S_TOTALS_A, S_TOTALS_C, S_COUNTERS, S_REC_KEY, S_REC_VAL,
+    S_GIDX, S_GROUPS, S_LOCAL, S_VALS, S_COSTS, S_DENSE_HIST, S_RARE_HIST, S_RARE_FLAG, S_RARE_OUT, S_RARE_CNT,
+    S_DENSE_CODE, S_BIG_CODE, S_RICE, S_GBLOCK, S_BLOCK_BITS, S_BLOCK_OFF, S_SCAN_TMP, S_PAYLOAD, S_BB32, S_RARE_CODES,
+    // apply
+    S_A_TENS, S_A_GROUPS, S_A_TABLES, S_A_SYMS, S_A_PAYLOAD, S_A_BB, S_A_BOFF, S_A_GAPS, S_A_ZZ, S_A_BSUM,
+    S_A_LOCAL, S_A_CADDR, S_A_CVAL, S_A_HS, S_A_TOT, S_A_CHUNK_ROWS, S_A_CHUNK_SUMS, S_A_COUNTERS, S_A_SCAN_TMP,
+    S_CHK,
+    S_NSLOTS
+};
+
+struct ProfMark {
+    const char* name;
+    cudaEvent_t a, b;
+};
+
+struct Ctx {
+    int device = 0;
+    std::mutex mu;
+    DevBuf b[S_NSLOTS];
+    void* host = nullptr;       // pinned host staging (metadata both ways, payload down)
+    size_t host_cap = 0;
+    uint64_t* small = nullptr;  // fixed pinned words for counters and verdicts (never moves)
+    uint64_t launches = 0;      // kernels launched by this context since creation
+    // optional per-kernel timing with CUDA events on the caller's stream
+    bool profile = false;
+    std::vector<cudaEvent_t> ev_pool;
+    size_t ev_used = 0;
+    std::vector<ProfMark> marks;
+    ~Ctx();
+};
+
+// Brackets one kernel launch: counts it and, while profiling is on, records events around it.
+struct KernelScope {
+    Ctx& c;
+    cudaStream_t s;
+    ProfMark m{nullptr, nullptr, nullptr};
+    KernelScope(Ctx& ctx, const char* name, cudaStream_t st);
+    ~KernelScope();
+};
+
+#define CRX_CUDA(call)                                                               \
+    do {                                                                             \
+        cudaError_t e_ = (call);                                                     \
+        if (e_ != cudaSuccess) {                                                     \
+            if (err) *err = std::string(#call ": ") + cudaGetErrorString(e_);        \
+            return kCudaError;                                                       \
+        }                                                                            \
+    } while (0)
+
+}  // namespace crx

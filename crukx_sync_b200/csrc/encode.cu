@@ -1,0 +1,989 @@
+// Encoder: bf16 prev/cur -> crukx-sync update bytes (wire format version 2), byte-identical to
+// the reference's encode_update (src/crukx_sync/codec.py:278-420, wire.py:64-89).
+//
+// Pipeline (one CUDA stream, three small host round trips):
+//   k_enc_rank     one pass over prev+cur.  Per super-tile: old-exponent histogram and changed
+//                  count per exponent; every changed element becomes a record holding its rank
+//                  among same-exponent elements and among same-exponent changes, both local to
+//                  the super-tile.  Checksum delta (and the full checksum when no cache) fused.
+//                  Replaces the reference's stable argsort ranking (codec.py:124-194).
+//   column scans   per tensor and exponent, exclusive prefix over super-tiles (scan.cu).
+//   k_groups       (tensor, exponent) groups in the reference's order, change offsets.
+//   k_place        records -> group order: local index and old|new bits per change.
+//   k_r0 / k_stats Golomb-Rice candidate costs per group (codec.py:268-275) and the
+//                  (exponent, zigzag residual) symbol histogram (codec.py:355-367).
+//   host           Rice choice, length-limited Huffman per exponent (codec.py:71-111, 369-392).
+//   k_block_bits   bits per 256-change block (codec.py:411-416), then an exclusive scan.
+//   k_pack         one warp per block writes its bits MSB-first (codec.py:218-257).
+#include <algorithm>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "capi_internal.h"
+#include "common.cuh"
+
+namespace crx {
+
+namespace {
+
+constexpr uint32_t FULL = 0xffffffffu;
+constexpr int DENSE_SYM = 64;          // residual symbols below this are counted per CTA in smem
+constexpr int STATS_PER_CTA = 8192;    // changes per k_stats CTA
+constexpr int STATS_LOCAL_GROUPS = 64; // groups a k_stats CTA accumulates in smem
+
+struct EncTensor {
+    const int16_t* prev;
+    const int16_t* cur;
+    int64_t numel;
+    int64_t super_begin;
+    int32_t want_full;
+    int32_t pad;
+};
+
+__device__ __forceinline__ int tensor_of_super(const EncTensor* T, int nT, int64_t s) {
+    int lo = 0, hi = nT - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (T[mid].super_begin <= s) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+__device__ __forceinline__ int64_t group_of(const uint64_t* __restrict__ start, int64_t ng, uint64_t j) {
+    int64_t lo = 0, hi = ng - 1;             // last g with start[g] <= j
+    while (lo < hi) {
+        const int64_t mid = (lo + hi + 1) >> 1;
+        if (start[mid] <= j) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+// ------------------------------------------------------------------ k_enc_rank
+
+struct RankSmem {
+    uint32_t tile[SUB_N];                 // prev | cur << 16
+    uint16_t cntA[RANK_WARPS][256];       // per-warp counts, then per-warp exclusive bases
+    uint16_t cntC[RANK_WARPS][256];
+    uint32_t runA[256], runC[256];        // super-tile running totals (ranks local to the super-tile)
+    uint32_t totA[256], totC[256];
+    uint32_t wchg[RANK_WARPS], wbase[RANK_WARPS];
+    unsigned long long rec_base;
+    uint64_t red[RANK_WARPS];
+};
+
+__global__ void __launch_bounds__(RANK_THREADS, 2)
+k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_key, uint32_t* __restrict__ rec_val,
+           uint64_t rec_cap, unsigned long long* __restrict__ counters, uint32_t* __restrict__ HS,
+           uint32_t* __restrict__ CS, unsigned long long* __restrict__ chk_delta, unsigned long long* __restrict__ chk_full) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    RankSmem& S = *reinterpret_cast<RankSmem*>(smem_raw);
+    const int64_t s = blockIdx.x;
+    const int t = tensor_of_super(T, nT, s);
+    const EncTensor tt = T[t];
+    const int64_t s_local = s - tt.super_begin;
+    const int64_t e_begin = s_local * SUPER_N;
+    const int64_t e_end = min(tt.numel, e_begin + SUPER_N);
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    const uint32_t lt = lanemask_lt();
+    uint64_t delta = 0, full = 0;
+
+    if (tid < 256) { S.runA[tid] = 0; S.runC[tid] = 0; }
+
+    for (int64_t base = e_begin; base < e_end; base += SUB_N) {
+        const int n = int(tmin<int64_t>(SUB_N, e_end - base));
+        const int16_t* pp = tt.prev + base;
+        const int16_t* cp = tt.cur + base;
+        // ---- stage prev|cur into shared memory (128-bit streaming loads when aligned)
+        if (n == SUB_N && ((reinterpret_cast<uintptr_t>(pp) | reinterpret_cast<uintptr_t>(cp)) & 15) == 0) {
+            const uint4* pv = reinterpret_cast<const uint4*>(pp);
+            const uint4* cv = reinterpret_cast<const uint4*>(cp);
+#pragma unroll
+            for (int k = 0; k < SUB_N / 8 / RANK_THREADS; ++k) {
+                const int v = tid + k * RANK_THREADS;
+                const uint4 a = __ldcs(pv + v);
+                const uint4 b = __ldcs(cv + v);
+                uint4* dst = reinterpret_cast<uint4*>(S.tile + 8 * v);
+                dst[0] = make_uint4(__byte_perm(a.x, b.x, 0x5410), __byte_perm(a.x, b.x, 0x7632),
+                                    __byte_perm(a.y, b.y, 0x5410), __byte_perm(a.y, b.y, 0x7632));
+                dst[1] = make_uint4(__byte_perm(a.z, b.z, 0x5410), __byte_perm(a.z, b.z, 0x7632),
+                                    __byte_perm(a.w, b.w, 0x5410), __byte_perm(a.w, b.w, 0x7632));
+            }
+        } else {
+            for (int i = tid; i < n; i += RANK_THREADS)
+                S.tile[i] = uint32_t(uint16_t(pp[i])) | (uint32_t(uint16_t(cp[i])) << 16);
+        }
+        for (int k = tid; k < RANK_WARPS * 256; k += RANK_THREADS) {
+            (&S.cntA[0][0])[k] = 0;
+            (&S.cntC[0][0])[k] = 0;
+        }
+        __syncthreads();
+
+        // ---- pass 1: per-warp counts per exponent (all elements, changed elements)
+        uint32_t wc = 0;
+        for (int c = 0; c < CHUNKS_PER_WARP; ++c) {
+            const int i0 = w * WARP_SPAN + c * 32;
+            if (i0 >= n) break;
+            const int i = i0 + lane;
+            const bool act = i < n;
+            const uint32_t x = act ? S.tile[i] : 0u;
+            const uint32_t e = (x >> 7) & 0xFFu;
+            const uint32_t peers = __match_any_sync(FULL, act ? e : 0x100u + lane);
+            const bool ch = act && ((x & 0xFFFFu) != (x >> 16));
+            const uint32_t chb = __ballot_sync(FULL, ch);
+            if (act && (peers & lt) == 0) {
+                S.cntA[w][e] += uint16_t(__popc(peers));
+                S.cntC[w][e] += uint16_t(__popc(peers & chb));
+            }
+            if (ch) {
+                const uint64_t gi = uint64_t(base + i);
+                delta += (uint64_t(x >> 16) - uint64_t(x & 0xFFFFu)) * splitmix_weight(gi);
+            }
+            if (tt.want_full && act) full += uint64_t(x >> 16) * splitmix_weight(uint64_t(base + i));
+            wc += __popc(chb);
+            __syncwarp();
+        }
+        if (lane == 0) S.wchg[w] = wc;
+        __syncthreads();
+
+        // ---- per exponent: exclusive bases over warps; per tile: record slots
+        if (tid < 256) {
+            uint32_t a = 0, cc = 0;
+            for (int ww = 0; ww < RANK_WARPS; ++ww) {
+                const uint32_t va = S.cntA[ww][tid], vc = S.cntC[ww][tid];
+                S.cntA[ww][tid] = uint16_t(a);
+                S.cntC[ww][tid] = uint16_t(cc);
+                a += va;
+                cc += vc;
+            }
+            S.totA[tid] = a;
+            S.totC[tid] = cc;
+        } else if (tid == 256) {
+            uint32_t r = 0;
+            for (int ww = 0; ww < RANK_WARPS; ++ww) { S.wbase[ww] = r; r += S.wchg[ww]; }
+            S.rec_base = r ? atomicAdd(&counters[0], (unsigned long long)r) : 0ull;
+        }
+        __syncthreads();
+
+        // ---- pass 2: ranks of changed elements -> records
+        if (S.wchg[w]) {
+            uint32_t rc = S.wbase[w];
+            const uint32_t rend = rc + S.wchg[w];
+            const uint64_t rbase = S.rec_base;
+            for (int c = 0; c < CHUNKS_PER_WARP && rc < rend; ++c) {
+                const int i = w * WARP_SPAN + c * 32 + lane;
+                const bool act = i < n;
+                const uint32_t x = act ? S.tile[i] : 0u;
+                const uint32_t e = (x >> 7) & 0xFFu;
+                const uint32_t peers = __match_any_sync(FULL, act ? e : 0x100u + lane);
+                const bool ch = act && ((x & 0xFFFFu) != (x >> 16));
+                const uint32_t chb = __ballot_sync(FULL, ch);
+                if (ch) {
+                    const uint32_t rankA = S.runA[e] + S.cntA[w][e] + __popc(peers & lt);
+                    const uint32_t rankC = S.runC[e] + S.cntC[w][e] + __popc(peers & chb & lt);
+                    const uint64_t j = rbase + rc + __popc(chb & lt);
+                    if (j < rec_cap) {
+                        rec_key[j] = (uint64_t(s) << 36) | (uint64_t(rankA) << 18) | uint64_t(rankC);
+                        rec_val[j] = x;
+                    }
+                }
+                rc += __popc(chb);
+                __syncwarp();
+                if (act && (peers & lt) == 0) {
+                    S.cntA[w][e] += uint16_t(__popc(peers));
+                    S.cntC[w][e] += uint16_t(__popc(peers & chb));
+                }
+                __syncwarp();
+            }
+        }
+        __syncthreads();
+        if (tid < 256) { S.runA[tid] += S.totA[tid]; S.runC[tid] += S.totC[tid]; }
+        __syncthreads();
+    }
+    if (tid < 256) {
+        HS[s * 256 + tid] = S.runA[tid];
+        CS[s * 256 + tid] = S.runC[tid];
+    }
+    block_add_u64<RANK_THREADS>(delta, &chk_delta[t], S.red);
+    if (tt.want_full) block_add_u64<RANK_THREADS>(full, &chk_full[t], S.red);
+}
+
+// ------------------------------------------------------------------ groups in reference order
+
+__device__ __forceinline__ uint32_t block_scan_u32(uint32_t v, uint32_t* sh, uint32_t* total) {
+    const int l = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    uint32_t x = v;
+    for (int o = 1; o < 32; o <<= 1) { const uint32_t y = __shfl_up_sync(FULL, x, o); if (l >= o) x += y; }
+    if (l == 31) sh[w] = x;
+    __syncthreads();
+    if (w == 0) {
+        uint32_t q = l < nw ? sh[l] : 0;
+        for (int o = 1; o < 32; o <<= 1) { const uint32_t y = __shfl_up_sync(FULL, q, o); if (l >= o) q += y; }
+        sh[l] = q;
+    }
+    __syncthreads();
+    const uint32_t ex = (w ? sh[w - 1] : 0) + x - v;
+    *total = sh[nw - 1];
+    __syncthreads();
+    return ex;
+}
+
+__device__ __forceinline__ uint64_t block_scan_u64(uint64_t v, uint64_t* sh, uint64_t* total) {
+    const int l = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    uint64_t x = v;
+    for (int o = 1; o < 32; o <<= 1) { const uint64_t y = __shfl_up_sync(FULL, x, o); if (l >= o) x += y; }
+    if (l == 31) sh[w] = x;
+    __syncthreads();
+    if (w == 0) {
+        uint64_t q = l < nw ? sh[l] : 0;
+        for (int o = 1; o < 32; o <<= 1) { const uint64_t y = __shfl_up_sync(FULL, q, o); if (l >= o) q += y; }
+        sh[l] = q;
+    }
+    __syncthreads();
+    const uint64_t ex = (w ? sh[w - 1] : 0) + x - v;
+    *total = sh[nw - 1];
+    __syncthreads();
+    return ex;
+}
+
+// Groups are the (tensor, exponent) cells with changes, tensors in caller order, exponents
+// ascending (codec.py:146, :317-323): one CTA scans the cells.
+__global__ void __launch_bounds__(1024) k_groups(const uint64_t* __restrict__ GC, int64_t n_cells, int32_t* __restrict__ gidx,
+                                                 int32_t* __restrict__ g_tensor, int32_t* __restrict__ g_exp,
+                                                 uint64_t* __restrict__ g_start, uint64_t* __restrict__ g_count,
+                                                 unsigned long long* __restrict__ counters) {
+    __shared__ uint32_t sh32[32];
+    __shared__ uint64_t sh64[32];
+    uint32_t gbase = 0;
+    uint64_t cbase = 0;
+    for (int64_t b = 0; b < n_cells; b += 1024) {
+        const int64_t cell = b + threadIdx.x;
+        const uint64_t cnt = cell < n_cells ? GC[cell] : 0;
+        const uint32_t f = cnt ? 1u : 0u;
+        uint32_t nf;
+        uint64_t nc;
+        const uint32_t exf = block_scan_u32(f, sh32, &nf);
+        const uint64_t exc = block_scan_u64(cnt, sh64, &nc);
+        if (cell < n_cells) {
+            if (f) {
+                const uint32_t g = gbase + exf;
+                gidx[cell] = int32_t(g);
+                g_tensor[g] = int32_t(cell >> 8);
+                g_exp[g] = int32_t(cell & 255);
+                g_start[g] = cbase + exc;
+                g_count[g] = cnt;
+            } else {
+                gidx[cell] = -1;
+            }
+        }
+        gbase += nf;
+        cbase += nc;
+    }
+    if (threadIdx.x == 0) {
+        g_start[gbase] = cbase;           // sentinel: start of the (absent) next group
+        counters[2] = gbase;
+        counters[3] = cbase;
+    }
+}
+
+// records (any order) -> changes in group order
+__global__ void __launch_bounds__(256) k_place(const EncTensor* __restrict__ T, int nT, const uint64_t* __restrict__ rec_key,
+                                               const uint32_t* __restrict__ rec_val, uint64_t n_rec,
+                                               const uint32_t* __restrict__ HSP, const uint32_t* __restrict__ CSP,
+                                               const int32_t* __restrict__ gidx, const uint64_t* __restrict__ g_start,
+                                               uint32_t* __restrict__ local, uint32_t* __restrict__ vals,
+                                               uint64_t total, unsigned long long* __restrict__ counters) {
+    const uint64_t j = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (j >= n_rec) return;
+    const uint64_t key = rec_key[j];
+    const uint32_t x = rec_val[j];
+    const int64_t s = int64_t(key >> 36);
+    const uint32_t rankA = uint32_t(key >> 18) & 0x3FFFFu;
+    const uint32_t rankC = uint32_t(key) & 0x3FFFFu;
+    const int e = exp_of(x & 0xFFFFu);
+    const int t = tensor_of_super(T, nT, s);
+    const int32_t g = gidx[int64_t(t) * 256 + e];
+    if (g < 0) { atomicOr(&counters[1], (unsigned long long)ERR_INTERNAL); return; }
+    const uint64_t dest = g_start[g] + CSP[s * 256 + e] + rankC;
+    if (dest >= total) { atomicOr(&counters[1], (unsigned long long)ERR_INTERNAL); return; }
+    local[dest] = HSP[s * 256 + e] + rankA;
+    vals[dest] = x;
+}
+
+// floor(log2(max(mean gap, 1))) clamped to [0, 30], by exact integer comparison: the mean is
+// sum/count with sum < 2^33, so double rounding can never cross a power of two (codec.py:271-272)
+__global__ void k_r0(const uint64_t* __restrict__ g_start, const uint64_t* __restrict__ g_count, int64_t ng,
+                     const uint32_t* __restrict__ local, uint32_t* __restrict__ g_cand) {
+    const int64_t g = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (g >= ng) return;
+    const uint64_t cnt = g_count[g];
+    const uint64_t last = local[g_start[g] + cnt - 1];
+    const uint64_t sum = last - (cnt - 1);        // gaps telescope: sum = last local - (count - 1)
+    int r0 = 0;
+    while (r0 < 30 && (cnt << (r0 + 1)) <= sum) ++r0;
+    const int c0 = max(r0 - 1, 0), c1 = r0, c2 = min(r0 + 1, 30);
+    g_cand[g] = uint32_t(c0) | (uint32_t(c1) << 8) | (uint32_t(c2) << 16);
+}
+
+__device__ __forceinline__ uint32_t zigzag_of(uint32_t x) {
+    const int32_t res = int32_t(int16_t(x >> 16)) - int32_t(int16_t(x & 0xFFFFu));
+    return uint32_t((res << 1) ^ (res >> 31));
+}
+
+struct StatsSmem {
+    uint32_t hist[STATS_LOCAL_GROUPS][DENSE_SYM];
+    unsigned long long cost[STATS_LOCAL_GROUPS][3];
+    int32_t gexp[STATS_LOCAL_GROUPS];
+    int64_t g0;
+};
+
+// Rice candidate costs sum((gap >> c) + 1 + c) per group and (exponent, zigzag) counts
+__global__ void __launch_bounds__(256) k_stats(const uint64_t* __restrict__ g_start, const int32_t* __restrict__ g_exp,
+                                               const uint32_t* __restrict__ g_cand, int64_t ng, uint64_t total,
+                                               const uint32_t* __restrict__ local, const uint32_t* __restrict__ vals,
+                                               unsigned long long* __restrict__ costs, unsigned long long* __restrict__ dense_hist,
+                                               uint32_t* __restrict__ rare_hist, uint32_t* __restrict__ rare_flag) {
+    __shared__ StatsSmem S;
+    const uint64_t j0 = uint64_t(blockIdx.x) * STATS_PER_CTA;
+    const uint64_t j1 = tmin<uint64_t>(j0 + STATS_PER_CTA, total);
+    if (threadIdx.x == 0) S.g0 = group_of(g_start, ng, j0);
+    for (int k = threadIdx.x; k < STATS_LOCAL_GROUPS * DENSE_SYM; k += blockDim.x) (&S.hist[0][0])[k] = 0;
+    for (int k = threadIdx.x; k < STATS_LOCAL_GROUPS * 3; k += blockDim.x) (&S.cost[0][0])[k] = 0;
+    __syncthreads();
+    const int64_t g0 = S.g0;
+    if (threadIdx.x < STATS_LOCAL_GROUPS && g0 + threadIdx.x < ng) S.gexp[threadIdx.x] = g_exp[g0 + threadIdx.x];
+    __syncthreads();
+    constexpr int PER = STATS_PER_CTA / 256;
+    const uint64_t a = j0 + uint64_t(threadIdx.x) * PER;
+    const uint64_t b = tmin<uint64_t>(a + PER, j1);
+    if (a < b) {
+        int64_t g = group_of(g_start, ng, a);
+        uint64_t gs = g_start[g], ge = g_start[g + 1];
+        uint32_t cand = g_cand[g];
+        int e = g_exp[g];
+        uint64_t acc0 = 0, acc1 = 0, acc2 = 0;
+        auto flush = [&]() {
+            const int64_t lg = g - g0;
+            if (lg < STATS_LOCAL_GROUPS) {
+                atomicAdd(&S.cost[lg][0], (unsigned long long)acc0);
+                atomicAdd(&S.cost[lg][1], (unsigned long long)acc1);
+                atomicAdd(&S.cost[lg][2], (unsigned long long)acc2);
+            } else {
+                atomicAdd(&costs[3 * g + 0], (unsigned long long)acc0);
+                atomicAdd(&costs[3 * g + 1], (unsigned long long)acc1);
+                atomicAdd(&costs[3 * g + 2], (unsigned long long)acc2);
+            }
+            acc0 = acc1 = acc2 = 0;
+        };
+        uint32_t prev_local = a > gs ? local[a - 1] : 0;
+        for (uint64_t j = a; j < b; ++j) {
+            while (j >= ge) {
+                flush();
+                ++g;
+                gs = g_start[g];
+                ge = g_start[g + 1];
+                cand = g_cand[g];
+                e = g_exp[g];
+            }
+            const uint32_t loc = local[j];
+            const uint64_t gap = j == gs ? loc : uint64_t(loc) - prev_local - 1;
+            prev_local = loc;
+            const uint32_t c0 = cand & 255, c1 = (cand >> 8) & 255, c2 = (cand >> 16) & 255;
+            acc0 += (gap >> c0) + 1 + c0;
+            acc1 += (gap >> c1) + 1 + c1;
+            acc2 += (gap >> c2) + 1 + c2;
+            const uint32_t z = zigzag_of(vals[j]);
+            const int64_t lg = g - g0;
+            if (z < DENSE_SYM) {
+                if (lg < STATS_LOCAL_GROUPS) atomicAdd(&S.hist[lg][z], 1u);
+                else atomicAdd(&dense_hist[e * DENSE_SYM + z], 1ull);
+            } else {
+                atomicAdd(&rare_hist[int64_t(e) * kSymSpace + z], 1u);
+                if (!rare_flag[e]) rare_flag[e] = 1;
+            }
+        }
+        flush();
+    }
+    __syncthreads();
+    for (int k = threadIdx.x; k < STATS_LOCAL_GROUPS * DENSE_SYM; k += blockDim.x) {
+        const int lg = k / DENSE_SYM;
+        const uint32_t v = (&S.hist[0][0])[k];
+        if (v && g0 + lg < ng) atomicAdd(&dense_hist[S.gexp[lg] * DENSE_SYM + (k % DENSE_SYM)], (unsigned long long)v);
+    }
+    for (int k = threadIdx.x; k < STATS_LOCAL_GROUPS * 3; k += blockDim.x) {
+        const int lg = k / 3;
+        const unsigned long long v = (&S.cost[0][0])[k];
+        if (v && g0 + lg < ng) atomicAdd(&costs[3 * (g0 + lg) + (k % 3)], v);
+    }
+}
+
+// Rare symbols of one exponent, ascending, as (symbol << 32 | count); the histogram row is
+// zeroed again so the buffer stays clean between calls.
+__global__ void __launch_bounds__(1024) k_rare_compact(uint32_t* __restrict__ rare_hist, uint32_t* __restrict__ rare_flag,
+                                                       uint64_t* __restrict__ out, uint64_t out_cap,
+                                                       unsigned long long* __restrict__ rare_total,
+                                                       uint64_t* __restrict__ rare_base, uint32_t* __restrict__ rare_cnt) {
+    __shared__ uint32_t sh[32];
+    __shared__ uint64_t base_sh;
+    const int e = blockIdx.x;
+    if (!rare_flag[e]) { if (threadIdx.x == 0) rare_cnt[e] = 0; return; }
+    uint32_t* row = rare_hist + int64_t(e) * kSymSpace;
+    uint32_t nz = 0;
+    for (uint32_t i = threadIdx.x; i < kSymSpace; i += 1024) nz += row[i] != 0;
+    uint32_t tot;
+    block_scan_u32(nz, sh, &tot);
+    if (threadIdx.x == 0) {
+        base_sh = atomicAdd(rare_total, (unsigned long long)tot);
+        rare_base[e] = base_sh;
+        rare_cnt[e] = tot;
+        rare_flag[e] = 0;
+    }
+    __syncthreads();
+    uint64_t pos = base_sh;
+    for (uint32_t b = 0; b < kSymSpace; b += 1024) {
+        const uint32_t i = b + threadIdx.x;
+        const uint32_t v = i < kSymSpace ? row[i] : 0;
+        uint32_t t2;
+        const uint32_t ex = block_scan_u32(v ? 1u : 0u, sh, &t2);
+        if (v) {
+            if (pos + ex < out_cap) out[pos + ex] = (uint64_t(i) << 32) | v;
+            row[i] = 0;
+        }
+        pos += t2;
+    }
+}
+
+__global__ void k_scatter_codes(const uint64_t* __restrict__ list, int64_t n, uint32_t* __restrict__ big_code) {
+    const int64_t k = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (k >= n) return;
+    const uint64_t v = list[k];   // (exp << 17 | sym) << 32 | (code | len << 24)
+    const uint32_t key = uint32_t(v >> 32);
+    big_code[int64_t(key >> 17) * kSymSpace + (key & 0x1FFFFu)] = uint32_t(v);
+}
+
+__device__ __forceinline__ uint32_t code_of(const uint32_t* __restrict__ dense_code, const uint32_t* __restrict__ big_code,
+                                            int e, uint32_t z) {
+    return z < DENSE_SYM ? dense_code[e * DENSE_SYM + z] : big_code[int64_t(e) * kSymSpace + z];
+}
+
+// bits of each 256-change block; one warp per block
+__global__ void __launch_bounds__(256) k_block_bits(const uint64_t* __restrict__ g_start, const int32_t* __restrict__ g_exp,
+                                                    const uint8_t* __restrict__ g_rice, const uint64_t* __restrict__ g_block,
+                                                    int64_t ng, int64_t n_blocks, const uint32_t* __restrict__ local,
+                                                    const uint32_t* __restrict__ vals, const uint32_t* __restrict__ dense_code,
+                                                    const uint32_t* __restrict__ big_code, uint64_t* __restrict__ bb64,
+                                                    uint32_t* __restrict__ bb32, unsigned long long* __restrict__ counters) {
+    const int64_t b = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (b >= n_blocks) return;
+    const int64_t g = group_of(g_block, ng, uint64_t(b));
+    const uint64_t gs = g_start[g], ge = g_start[g + 1];
+    const uint64_t j0 = gs + uint64_t(b - int64_t(g_block[g])) * kBlock;
+    const uint64_t j1 = tmin<uint64_t>(j0 + kBlock, ge);
+    const int r = g_rice[g];
+    const int e = g_exp[g];
+    uint64_t sum = 0;
+    for (uint64_t j = j0 + lane; j < j1; j += 32) {
+        const uint32_t loc = local[j];
+        const uint64_t gap = j == gs ? loc : uint64_t(loc) - local[j - 1] - 1;
+        const uint32_t cl = code_of(dense_code, big_code, e, zigzag_of(vals[j]));
+        sum += (gap >> r) + 1 + r + (cl >> 24);
+    }
+    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(FULL, sum, o);
+    if (lane == 0) {
+        bb64[b] = sum;
+        bb32[b] = uint32_t(sum);
+        if (sum >> 32) atomicOr(&counters[1], (unsigned long long)ERR_BLOCK_TOO_LONG);
+    }
+}
+
+__device__ __forceinline__ void or_word(uint32_t* words, uint64_t w, uint32_t v) {
+    if (v) atomicOr(&words[w], bswap32(v));
+}
+
+// write `len` (<= 64) low bits of v at bit position pos (MSB-first stream)
+__device__ __forceinline__ void put_bits(uint32_t* words, uint64_t pos, uint64_t v, int len) {
+    if (len == 0) return;
+    const int o = int(pos & 31);
+    const uint64_t w0 = pos >> 5;
+    const unsigned __int128 win = (unsigned __int128)v << (96 - o - len);
+    or_word(words, w0, uint32_t(win >> 64));
+    if (o + len > 32) or_word(words, w0 + 1, uint32_t(win >> 32));
+    if (o + len > 64) or_word(words, w0 + 2, uint32_t(win));
+}
+
+// q one-bits starting at pos: partial edge words by atomicOr, whole words by plain stores
+__device__ void put_ones(uint32_t* words, uint64_t pos, uint64_t q) {
+    const uint64_t end = pos + q;
+    while (pos < end && (pos & 31)) {
+        const int o = int(pos & 31);
+        const int k = int(tmin<uint64_t>(32 - o, end - pos));
+        const uint32_t m = (k == 32 ? FULL : ((1u << k) - 1u)) << (32 - o - k);
+        or_word(words, pos >> 5, m);
+        pos += k;
+    }
+    while (end - pos >= 32) { words[pos >> 5] = FULL; pos += 32; }
+    if (pos < end) {
+        const int k = int(end - pos);
+        or_word(words, pos >> 5, ((1u << k) - 1u) << (32 - k));
+    }
+}
+
+// one warp per block: Rice gap then canonical Huffman code per change, MSB first
+__global__ void __launch_bounds__(256) k_pack(const uint64_t* __restrict__ g_start, const int32_t* __restrict__ g_exp,
+                                              const uint8_t* __restrict__ g_rice, const uint64_t* __restrict__ g_block,
+                                              int64_t ng, int64_t n_blocks, const uint32_t* __restrict__ local,
+                                              const uint32_t* __restrict__ vals, const uint32_t* __restrict__ dense_code,
+                                              const uint32_t* __restrict__ big_code, const uint64_t* __restrict__ block_off,
+                                              uint32_t* __restrict__ words) {
+    const int64_t b = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (b >= n_blocks) return;
+    const int64_t g = group_of(g_block, ng, uint64_t(b));
+    const uint64_t gs = g_start[g], ge = g_start[g + 1];
+    const uint64_t j0 = gs + uint64_t(b - int64_t(g_block[g])) * kBlock;
+    const uint64_t j1 = tmin<uint64_t>(j0 + kBlock, ge);
+    const int r = g_rice[g];
+    const int e = g_exp[g];
+    uint64_t pos = block_off[b];
+    for (uint64_t jb = j0; jb < j1; jb += 32) {
+        const uint64_t j = jb + lane;
+        uint64_t L = 0, gap = 0;
+        uint32_t cl = 0;
+        if (j < j1) {
+            const uint32_t loc = local[j];
+            gap = j == gs ? loc : uint64_t(loc) - local[j - 1] - 1;
+            cl = code_of(dense_code, big_code, e, zigzag_of(vals[j]));
+            L = (gap >> r) + 1 + r + (cl >> 24);
+        }
+        uint64_t incl = L;
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint64_t y = __shfl_up_sync(FULL, incl, o);
+            if (lane >= o) incl += y;
+        }
+        const uint64_t at = pos + incl - L;
+        if (j < j1) {
+            const uint64_t q = gap >> r;
+            const int hl = int(cl >> 24);
+            const uint64_t code = cl & 0xFFFFFFu;
+            const uint64_t rem = r ? (gap & ((1ull << r) - 1)) : 0;
+            const int tail_len = 1 + r + hl;                          // the 0, r remainder bits, code
+            const uint64_t tail = (rem << hl) | code;                 // leading 0 is implicit
+            if (q + tail_len <= 64) {
+                const uint64_t v = q ? ((((1ull << q) - 1) << tail_len) | tail) : tail;
+                put_bits(words, at, v, int(q) + tail_len);
+            } else {
+                put_ones(words, at, q);
+                put_bits(words, at + q, tail, tail_len);
+            }
+        }
+        pos += __shfl_sync(FULL, incl, 31);
+    }
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ host driver
+
+namespace {
+
+template <class T>
+T* dev(Ctx& c, Slot s) { return reinterpret_cast<T*>(c.b[s].p); }
+
+struct HostTables {
+    // per exponent: ascending symbols, their counts, lengths and codes
+    std::vector<uint32_t> sym[256];
+    std::vector<uint64_t> cnt[256];
+    std::vector<uint8_t> len[256];
+    std::vector<uint32_t> code[256];
+};
+
+}  // namespace
+
+Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* const* cur, const int64_t* numel,
+                   const uint8_t* const* names, const int64_t* name_len, const uint64_t* cache_chk,
+                   const uint8_t* has_cache, cudaStream_t st, Encoded* out, std::string* err) {
+    out->bytes.clear();
+    out->checksums.assign(size_t(nT), 0);
+    out->present.assign(size_t(nT), 0);
+    // ---- tensor descriptors
+    std::vector<EncTensor> T;
+    std::vector<int> tmap;  // index into caller arrays
+    int64_t n_super = 0;
+    for (int t = 0; t < nT; ++t) {
+        if (numel[t] < 0) { *err = "negative numel"; return kBadArgument; }
+        if (numel[t] >= (int64_t(1) << 32)) { *err = "tensors of 2^32 or more elements are not supported"; return kValueError; }
+        if (numel[t] == 0) continue;
+        EncTensor d{};
+        d.prev = prev[t];
+        d.cur = cur[t];
+        d.numel = numel[t];
+        d.super_begin = n_super;
+        d.want_full = has_cache && has_cache[t] ? 0 : 1;
+        n_super += (numel[t] + SUPER_N - 1) / SUPER_N;
+        T.push_back(d);
+        tmap.push_back(t);
+    }
+    const int nt = int(T.size());
+    auto empty_update = [&]() {
+        static const uint8_t kEmpty[8] = {'C', 'R', 'X', 'S', 2, 0, 0, 0};
+        out->bytes.assign(kEmpty, kEmpty + 8);
+        return kOk;
+    };
+    if (nt == 0) return empty_update();
+    if (n_super >= (int64_t(1) << 28)) { *err = "update too large for one call"; return kValueError; }
+
+    // ---- buffers
+    const size_t cells = size_t(nt) * 256;
+    std::vector<int64_t> row_begin(static_cast<size_t>(nt) + 1), chunk_begin(static_cast<size_t>(nt) + 1);
+    for (int t = 0; t < nt; ++t) {
+        row_begin[size_t(t)] = T[size_t(t)].super_begin;
+        const int64_t rows = (T[size_t(t)].numel + SUPER_N - 1) / SUPER_N;
+        chunk_begin[size_t(t) + 1] = chunk_begin[size_t(t)] + (rows + SCAN_CHUNK - 1) / SCAN_CHUNK;
+    }
+    row_begin[size_t(nt)] = n_super;
+    const int64_t n_chunks = chunk_begin[size_t(nt)];
+    CRX_CUDA(ensure_dev(C.b[S_TENS], sizeof(EncTensor) * size_t(nt), st));
+    CRX_CUDA(ensure_dev(C.b[S_HS], sizeof(uint32_t) * 256 * size_t(n_super), st));
+    CRX_CUDA(ensure_dev(C.b[S_CS], sizeof(uint32_t) * 256 * size_t(n_super), st));
+    CRX_CUDA(ensure_dev(C.b[S_CHUNK_ROWS], sizeof(int64_t) * 2 * (size_t(nt) + 1), st));
+    CRX_CUDA(ensure_dev(C.b[S_CHUNK_SUMS], sizeof(uint32_t) * 256 * size_t(n_chunks), st));
+    CRX_CUDA(ensure_dev(C.b[S_TOTALS_A], sizeof(uint64_t) * cells, st));
+    CRX_CUDA(ensure_dev(C.b[S_TOTALS_C], sizeof(uint64_t) * cells, st));
+    CRX_CUDA(ensure_dev(C.b[S_COUNTERS], sizeof(uint64_t) * 16, st));
+    CRX_CUDA(ensure_dev(C.b[S_CHK], sizeof(uint64_t) * 2 * size_t(nt), st));
+    CRX_CUDA(ensure_dev(C.b[S_GIDX], sizeof(int32_t) * cells, st));
+    // groups: tensor, exp (i32), start (cells+1), count, cand (u32), costs (3 u64), rice (u8), block start
+    CRX_CUDA(ensure_dev(C.b[S_GROUPS], (4 + 4 + 8 + 8 + 4 + 24 + 1 + 8) * (cells + 1) + 64, st));
+    int64_t total_el = 0;
+    for (auto& d : T) total_el += d.numel;
+    uint64_t rec_cap = C.b[S_REC_KEY].cap / sizeof(uint64_t);
+    const uint64_t want_cap = std::max<uint64_t>(uint64_t(total_el / 16) + 4096, rec_cap);
+    CRX_CUDA(ensure_dev(C.b[S_REC_KEY], sizeof(uint64_t) * want_cap, st));
+    CRX_CUDA(ensure_dev(C.b[S_REC_VAL], sizeof(uint32_t) * want_cap, st));
+    rec_cap = want_cap;
+
+    const size_t meta_bytes = sizeof(EncTensor) * size_t(nt) + sizeof(int64_t) * 2 * (size_t(nt) + 1);
+    CRX_CUDA(ensure_host(C, std::max<size_t>(meta_bytes, 1 << 20), st));
+    {
+        uint8_t* h = static_cast<uint8_t*>(C.host);
+        std::memcpy(h, T.data(), sizeof(EncTensor) * size_t(nt));
+        CRX_CUDA(cudaMemcpyAsync(C.b[S_TENS].p, h, sizeof(EncTensor) * size_t(nt), cudaMemcpyHostToDevice, st));
+        int64_t* rb = reinterpret_cast<int64_t*>(h + sizeof(EncTensor) * size_t(nt));
+        std::memcpy(rb, row_begin.data(), sizeof(int64_t) * (size_t(nt) + 1));
+        std::memcpy(rb + nt + 1, chunk_begin.data(), sizeof(int64_t) * (size_t(nt) + 1));
+        CRX_CUDA(cudaMemcpyAsync(C.b[S_CHUNK_ROWS].p, rb, sizeof(int64_t) * 2 * (size_t(nt) + 1), cudaMemcpyHostToDevice, st));
+    }
+    const int64_t* d_row_begin = dev<int64_t>(C, S_CHUNK_ROWS);
+    const int64_t* d_chunk_begin = d_row_begin + nt + 1;
+    auto* counters = dev<unsigned long long>(C, S_COUNTERS);
+    auto* chk_delta = dev<unsigned long long>(C, S_CHK);
+    auto* chk_full = chk_delta + nt;
+    const size_t rank_smem = sizeof(RankSmem);
+    CRX_CUDA(cudaFuncSetAttribute(k_enc_rank, cudaFuncAttributeMaxDynamicSharedMemorySize, int(rank_smem)));
+
+    uint64_t* hostc = C.small;
+    for (int attempt = 0; attempt < 2; ++attempt) {
+        CRX_CUDA(cudaMemsetAsync(counters, 0, sizeof(uint64_t) * 16, st));
+        CRX_CUDA(cudaMemsetAsync(chk_delta, 0, sizeof(uint64_t) * 2 * size_t(nt), st));
+        { KernelScope ks_(C, "k_enc_rank", st);
+        k_enc_rank<<<unsigned(n_super), RANK_THREADS, rank_smem, st>>>(
+            dev<EncTensor>(C, S_TENS), nt, dev<uint64_t>(C, S_REC_KEY), dev<uint32_t>(C, S_REC_VAL), rec_cap, counters,
+            dev<uint32_t>(C, S_HS), dev<uint32_t>(C, S_CS), chk_delta, chk_full);
+        }
+        CRX_CUDA(cudaGetLastError());
+        CRX_CUDA(cudaMemcpyAsync(hostc, counters, sizeof(uint64_t) * 2, cudaMemcpyDeviceToHost, st));
+        CRX_CUDA(cudaStreamSynchronize(st));
+        if (hostc[0] <= rec_cap) break;
+        const uint64_t need = hostc[0] + 4096;
+        CRX_CUDA(ensure_dev(C.b[S_REC_KEY], sizeof(uint64_t) * need, st));
+        CRX_CUDA(ensure_dev(C.b[S_REC_VAL], sizeof(uint32_t) * need, st));
+        rec_cap = need;
+    }
+    const uint64_t n_rec = hostc[0];
+    if (n_rec == 0) return empty_update();
+
+    // ---- per tensor column scans and the group table
+    launch_column_scan(C, dev<uint32_t>(C, S_HS), n_super, d_row_begin, nt, d_chunk_begin, n_chunks,
+                       dev<uint32_t>(C, S_CHUNK_SUMS), dev<uint64_t>(C, S_TOTALS_A), st);
+    launch_column_scan(C, dev<uint32_t>(C, S_CS), n_super, d_row_begin, nt, d_chunk_begin, n_chunks,
+                       dev<uint32_t>(C, S_CHUNK_SUMS), dev<uint64_t>(C, S_TOTALS_C), st);
+    uint8_t* gb = dev<uint8_t>(C, S_GROUPS);
+    const size_t gcap = cells + 1;
+    auto* g_start = reinterpret_cast<uint64_t*>(gb);
+    auto* g_count = reinterpret_cast<uint64_t*>(gb + 8 * gcap);
+    auto* costs = reinterpret_cast<unsigned long long*>(gb + 16 * gcap);
+    auto* g_block = reinterpret_cast<uint64_t*>(gb + 40 * gcap);
+    auto* g_tensor = reinterpret_cast<int32_t*>(gb + 48 * gcap);
+    auto* g_exp = reinterpret_cast<int32_t*>(gb + 52 * gcap);
+    auto* g_cand = reinterpret_cast<uint32_t*>(gb + 56 * gcap);
+    auto* g_rice = reinterpret_cast<uint8_t*>(gb + 60 * gcap);
+    { KernelScope ks_(C, "k_groups", st);
+    k_groups<<<1, 1024, 0, st>>>(dev<uint64_t>(C, S_TOTALS_C), int64_t(cells), dev<int32_t>(C, S_GIDX), g_tensor, g_exp,
+                                g_start, g_count, counters);
+    }
+    CRX_CUDA(cudaGetLastError());
+    CRX_CUDA(cudaMemcpyAsync(hostc, counters, sizeof(uint64_t) * 4, cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaStreamSynchronize(st));
+    const int64_t ng = int64_t(hostc[2]);
+    const uint64_t total = hostc[3];
+    if (total != n_rec || (hostc[1] & ERR_INTERNAL)) { *err = "internal: change count mismatch"; return kCudaError; }
+
+    CRX_CUDA(ensure_dev(C.b[S_LOCAL], sizeof(uint32_t) * total, st));
+    CRX_CUDA(ensure_dev(C.b[S_VALS], sizeof(uint32_t) * total, st));
+    auto* local = dev<uint32_t>(C, S_LOCAL);
+    auto* vals = dev<uint32_t>(C, S_VALS);
+    { KernelScope ks_(C, "k_place", st);
+    k_place<<<unsigned((n_rec + 255) / 256), 256, 0, st>>>(dev<EncTensor>(C, S_TENS), nt, dev<uint64_t>(C, S_REC_KEY),
+                                                           dev<uint32_t>(C, S_REC_VAL), n_rec, dev<uint32_t>(C, S_HS),
+                                                           dev<uint32_t>(C, S_CS), dev<int32_t>(C, S_GIDX), g_start, local,
+                                                           vals, total, counters);
+    }
+    CRX_CUDA(cudaGetLastError());
+    { KernelScope ks_(C, "k_r0", st);
+    k_r0<<<unsigned((ng + 255) / 256), 256, 0, st>>>(g_start, g_count, ng, local, g_cand);
+    }
+    CRX_CUDA(cudaGetLastError());
+
+    // ---- symbol histogram + Rice costs
+    CRX_CUDA(ensure_dev(C.b[S_DENSE_HIST], sizeof(uint64_t) * 256 * DENSE_SYM, st));
+    CRX_CUDA(ensure_dev(C.b[S_RARE_FLAG], sizeof(uint32_t) * 256 * 2 + sizeof(uint64_t) * 256, st));
+    if (C.b[S_RARE_HIST].cap < sizeof(uint32_t) * 256 * size_t(kSymSpace)) {
+        CRX_CUDA(ensure_dev(C.b[S_RARE_HIST], sizeof(uint32_t) * 256 * size_t(kSymSpace), st));
+        CRX_CUDA(cudaMemsetAsync(C.b[S_RARE_HIST].p, 0, C.b[S_RARE_HIST].cap, st));
+        CRX_CUDA(cudaMemsetAsync(C.b[S_RARE_FLAG].p, 0, sizeof(uint32_t) * 256, st));
+    }
+    auto* rare_flag = dev<uint32_t>(C, S_RARE_FLAG);
+    auto* rare_cnt = rare_flag + 256;
+    auto* rare_base = reinterpret_cast<uint64_t*>(rare_flag + 512);
+    CRX_CUDA(cudaMemsetAsync(C.b[S_DENSE_HIST].p, 0, sizeof(uint64_t) * 256 * DENSE_SYM, st));
+    CRX_CUDA(cudaMemsetAsync(costs, 0, sizeof(uint64_t) * 3 * size_t(ng), st));
+    { KernelScope ks_(C, "k_stats", st);
+    k_stats<<<unsigned((total + STATS_PER_CTA - 1) / STATS_PER_CTA), 256, 0, st>>>(
+        g_start, g_exp, g_cand, ng, total, local, vals, costs, dev<unsigned long long>(C, S_DENSE_HIST),
+        dev<uint32_t>(C, S_RARE_HIST), rare_flag);
+    }
+    CRX_CUDA(cudaGetLastError());
+    const uint64_t rare_cap = std::min<uint64_t>(total, uint64_t(256) * kSymSpace);
+    CRX_CUDA(ensure_dev(C.b[S_RARE_OUT], sizeof(uint64_t) * rare_cap, st));
+    { KernelScope ks_(C, "k_rare_compact", st);
+    k_rare_compact<<<256, 1024, 0, st>>>(dev<uint32_t>(C, S_RARE_HIST), rare_flag, dev<uint64_t>(C, S_RARE_OUT), rare_cap,
+                                         counters + 4, rare_base, rare_cnt);
+    }
+    CRX_CUDA(cudaGetLastError());
+
+    // ---- download what the host needs for headers and Huffman tables
+    const size_t off_gt = 0, off_ge = off_gt + 4 * size_t(ng), off_gc = off_ge + 4 * size_t(ng);
+    const size_t off_cost = off_gc + 8 * size_t(ng), off_dense = off_cost + 24 * size_t(ng);
+    const size_t off_rc = off_dense + 8 * 256 * DENSE_SYM, off_rb = off_rc + 4 * 256, off_chk = off_rb + 8 * 256;
+    const size_t off_ctr = off_chk + 16 * size_t(nt), off_cand = off_ctr + 8 * 16;
+    const size_t down1 = off_cand + 4 * size_t(ng);
+    CRX_CUDA(ensure_host(C, down1, st));
+    uint8_t* h = static_cast<uint8_t*>(C.host);
+    CRX_CUDA(cudaMemcpyAsync(h + off_gt, g_tensor, 4 * size_t(ng), cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaMemcpyAsync(h + off_ge, g_exp, 4 * size_t(ng), cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaMemcpyAsync(h + off_gc, g_count, 8 * size_t(ng), cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaMemcpyAsync(h + off_cost, costs, 24 * size_t(ng), cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaMemcpyAsync(h + off_dense, C.b[S_DENSE_HIST].p, 8 * 256 * DENSE_SYM, cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaMemcpyAsync(h + off_rc, rare_cnt, 4 * 256, cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaMemcpyAsync(h + off_rb, rare_base, 8 * 256, cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaMemcpyAsync(h + off_chk, chk_delta, 16 * size_t(nt), cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaMemcpyAsync(h + off_ctr, counters, 8 * 16, cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaMemcpyAsync(h + off_cand, g_cand, 4 * size_t(ng), cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaStreamSynchronize(st));
+    std::vector<uint32_t> hcand(static_cast<size_t>(ng));
+    std::memcpy(hcand.data(), h + off_cand, 4 * size_t(ng));
+    std::vector<int32_t> hg_tensor(static_cast<size_t>(ng)), hg_exp(static_cast<size_t>(ng));
+    std::vector<uint64_t> hg_count(static_cast<size_t>(ng)), hcost(3 * static_cast<size_t>(ng)), hdense(256 * DENSE_SYM), hrb(256), hchk(2 * static_cast<size_t>(nt));
+    std::vector<uint32_t> hrc(256);
+    std::memcpy(hg_tensor.data(), h + off_gt, 4 * size_t(ng));
+    std::memcpy(hg_exp.data(), h + off_ge, 4 * size_t(ng));
+    std::memcpy(hg_count.data(), h + off_gc, 8 * size_t(ng));
+    std::memcpy(hcost.data(), h + off_cost, 24 * size_t(ng));
+    std::memcpy(hdense.data(), h + off_dense, 8 * 256 * DENSE_SYM);
+    std::memcpy(hrc.data(), h + off_rc, 4 * 256);
+    std::memcpy(hrb.data(), h + off_rb, 8 * 256);
+    std::memcpy(hchk.data(), h + off_chk, 16 * size_t(nt));
+    uint64_t hctr[16];
+    std::memcpy(hctr, h + off_ctr, 8 * 16);
+    if (hctr[1] & ERR_INTERNAL) { *err = "internal: a change has no group"; return kCudaError; }
+    const uint64_t rare_total = hctr[4];
+    if (rare_total > rare_cap) { *err = "internal: rare symbol overflow"; return kCudaError; }
+    std::vector<uint64_t> hrare(rare_total);
+    if (rare_total) {
+        CRX_CUDA(ensure_host(C, 8 * rare_total, st));
+        CRX_CUDA(cudaMemcpyAsync(C.host, C.b[S_RARE_OUT].p, 8 * rare_total, cudaMemcpyDeviceToHost, st));
+        CRX_CUDA(cudaStreamSynchronize(st));
+        std::memcpy(hrare.data(), C.host, 8 * rare_total);
+    }
+
+    // ---- Rice per group: first cheapest of the three candidates (codec.py:273-275)
+    std::vector<uint8_t> rice(static_cast<size_t>(ng));
+    std::vector<uint64_t> gblock(static_cast<size_t>(ng) + 1, 0);
+    for (int64_t g = 0; g < ng; ++g) {
+        const uint64_t* cst = &hcost[3 * size_t(g)];
+        int best = 0;
+        for (int k = 1; k < 3; ++k) if (cst[k] < cst[best]) best = k;
+        rice[size_t(g)] = uint8_t((hcand[size_t(g)] >> (8 * best)) & 255);
+        gblock[size_t(g) + 1] = gblock[size_t(g)] + (hg_count[size_t(g)] + kBlock - 1) / kBlock;
+    }
+    const int64_t n_blocks = int64_t(gblock[size_t(ng)]);
+
+    // ---- one Huffman table per exponent over the whole update (codec.py:369-392)
+    HostTables tabs;
+    for (int e = 0; e < 256; ++e) {
+        for (int z = 0; z < DENSE_SYM; ++z) {
+            const uint64_t c = hdense[size_t(e) * DENSE_SYM + size_t(z)];
+            if (c) { tabs.sym[e].push_back(uint32_t(z)); tabs.cnt[e].push_back(c); }
+        }
+        for (uint32_t k = 0; k < hrc[size_t(e)]; ++k) {
+            const uint64_t v = hrare[size_t(hrb[size_t(e)] + k)];
+            tabs.sym[e].push_back(uint32_t(v >> 32));
+            tabs.cnt[e].push_back(v & 0xFFFFFFFFull);
+        }
+        const size_t ns = tabs.sym[e].size();
+        if (!ns) continue;
+        tabs.len[e].resize(ns);
+        tabs.code[e].resize(ns);
+        huffman_lengths(tabs.cnt[e].data(), int64_t(ns), tabs.len[e].data());
+        canonical_codes(tabs.len[e].data(), int64_t(ns), tabs.code[e].data());
+    }
+
+    // ---- upload rice, block starts, code tables
+    std::vector<uint32_t> dense_code(256 * DENSE_SYM, 0);
+    std::vector<uint64_t> rare_codes;
+    for (int e = 0; e < 256; ++e) {
+        for (size_t k = 0; k < tabs.sym[e].size(); ++k) {
+            const uint32_t z = tabs.sym[e][k];
+            const uint32_t cl = tabs.code[e][k] | (uint32_t(tabs.len[e][k]) << 24);
+            if (z < DENSE_SYM) dense_code[size_t(e) * DENSE_SYM + z] = cl;
+            else rare_codes.push_back((uint64_t((uint32_t(e) << 17) | z) << 32) | cl);
+        }
+    }
+    CRX_CUDA(ensure_dev(C.b[S_DENSE_CODE], sizeof(uint32_t) * 256 * DENSE_SYM, st));
+    if (!rare_codes.empty()) {
+        if (C.b[S_BIG_CODE].cap < sizeof(uint32_t) * 256 * size_t(kSymSpace))
+            CRX_CUDA(ensure_dev(C.b[S_BIG_CODE], sizeof(uint32_t) * 256 * size_t(kSymSpace), st));
+        CRX_CUDA(ensure_dev(C.b[S_RARE_CODES], sizeof(uint64_t) * rare_codes.size(), st));
+    }
+    const size_t up_bytes = ng + 8 * (size_t(ng) + 1) + 4 * 256 * DENSE_SYM + 8 * rare_codes.size() + 64;
+    CRX_CUDA(ensure_host(C, up_bytes, st));
+    h = static_cast<uint8_t*>(C.host);
+    size_t o = 0;
+    std::memcpy(h + o, gblock.data(), 8 * (size_t(ng) + 1));
+    CRX_CUDA(cudaMemcpyAsync(g_block, h + o, 8 * (size_t(ng) + 1), cudaMemcpyHostToDevice, st));
+    o += 8 * (size_t(ng) + 1);
+    std::memcpy(h + o, dense_code.data(), 4 * 256 * DENSE_SYM);
+    CRX_CUDA(cudaMemcpyAsync(C.b[S_DENSE_CODE].p, h + o, 4 * 256 * DENSE_SYM, cudaMemcpyHostToDevice, st));
+    o += 4 * 256 * DENSE_SYM;
+    if (!rare_codes.empty()) {
+        std::memcpy(h + o, rare_codes.data(), 8 * rare_codes.size());
+        CRX_CUDA(cudaMemcpyAsync(C.b[S_RARE_CODES].p, h + o, 8 * rare_codes.size(), cudaMemcpyHostToDevice, st));
+        o += 8 * rare_codes.size();
+        { KernelScope ks_(C, "k_scatter_codes", st);
+        k_scatter_codes<<<unsigned((rare_codes.size() + 255) / 256), 256, 0, st>>>(
+            dev<uint64_t>(C, S_RARE_CODES), int64_t(rare_codes.size()), dev<uint32_t>(C, S_BIG_CODE));
+        }
+        CRX_CUDA(cudaGetLastError());
+    }
+    std::memcpy(h + o, rice.data(), size_t(ng));
+    CRX_CUDA(cudaMemcpyAsync(g_rice, h + o, size_t(ng), cudaMemcpyHostToDevice, st));
+    o += size_t(ng);
+
+    // ---- block lengths, offsets, payload
+    CRX_CUDA(ensure_dev(C.b[S_BLOCK_BITS], sizeof(uint64_t) * size_t(n_blocks), st));
+    CRX_CUDA(ensure_dev(C.b[S_BB32], sizeof(uint32_t) * size_t(n_blocks), st));
+    CRX_CUDA(ensure_dev(C.b[S_SCAN_TMP], sizeof(uint64_t) * (exclusive_scan_tmp_elems(n_blocks) + 2), st));
+    const uint32_t* big_code = rare_codes.empty() ? dev<uint32_t>(C, S_DENSE_CODE) : dev<uint32_t>(C, S_BIG_CODE);
+    const unsigned warps_grid = unsigned((n_blocks * 32 + 255) / 256);
+    { KernelScope ks_(C, "k_block_bits", st);
+    k_block_bits<<<warps_grid, 256, 0, st>>>(g_start, g_exp, g_rice, g_block, ng, n_blocks, local, vals,
+                                             dev<uint32_t>(C, S_DENSE_CODE), big_code, dev<uint64_t>(C, S_BLOCK_BITS),
+                                             dev<uint32_t>(C, S_BB32), counters);
+    }
+    CRX_CUDA(cudaGetLastError());
+    uint64_t* scan_tmp = dev<uint64_t>(C, S_SCAN_TMP);
+    uint64_t* d_total_bits = scan_tmp + exclusive_scan_tmp_elems(n_blocks);
+    launch_exclusive_scan_u64(C, dev<uint64_t>(C, S_BLOCK_BITS), n_blocks, scan_tmp, d_total_bits, st);
+    CRX_CUDA(cudaMemcpyAsync(hostc, d_total_bits, 8, cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaMemcpyAsync(hostc + 1, counters + 1, 8, cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaStreamSynchronize(st));
+    const uint64_t total_bits = hostc[0];
+    if (hostc[1] & ERR_BLOCK_TOO_LONG) {
+        *err = "a block exceeds 2^32 bits; the update cannot be represented";
+        return kValueError;
+    }
+    const uint64_t payload_len = (total_bits + 7) / 8;
+    const size_t n_words = size_t((total_bits + 31) / 32) + 4;
+    CRX_CUDA(ensure_dev(C.b[S_PAYLOAD], 4 * n_words, st));
+    CRX_CUDA(cudaMemsetAsync(C.b[S_PAYLOAD].p, 0, 4 * n_words, st));
+    { KernelScope ks_(C, "k_pack", st);
+    k_pack<<<warps_grid, 256, 0, st>>>(g_start, g_exp, g_rice, g_block, ng, n_blocks, local, vals,
+                                       dev<uint32_t>(C, S_DENSE_CODE), big_code, dev<uint64_t>(C, S_BLOCK_BITS),
+                                       dev<uint32_t>(C, S_PAYLOAD));
+    }
+    CRX_CUDA(cudaGetLastError());
+
+    // ---- header (wire.py:64-89), block table and payload
+    std::vector<uint8_t>& ob = out->bytes;
+    ob.reserve(size_t(64 + 4 * n_blocks + payload_len) + 1024);
+    const uint8_t magic[5] = {'C', 'R', 'X', 'S', 2};
+    ob.insert(ob.end(), magic, magic + 5);
+    int n_tables = 0;
+    for (int e = 0; e < 256; ++e) n_tables += !tabs.sym[e].empty();
+    put_varint(ob, uint64_t(n_tables));
+    for (int e = 0; e < 256; ++e) {
+        if (tabs.sym[e].empty()) continue;
+        ob.push_back(uint8_t(e));
+        put_varint(ob, tabs.sym[e].size());
+        for (size_t k = 0; k < tabs.sym[e].size(); ++k) {
+            put_varint(ob, tabs.sym[e][k]);
+            ob.push_back(tabs.len[e][k]);
+        }
+    }
+    // tensors present = those with groups, in caller order
+    std::vector<int64_t> t_first(static_cast<size_t>(nt), -1), t_ng(static_cast<size_t>(nt), 0);
+    for (int64_t g = 0; g < ng; ++g) {
+        const int t = hg_tensor[size_t(g)];
+        if (t_first[size_t(t)] < 0) t_first[size_t(t)] = g;
+        t_ng[size_t(t)]++;
+    }
+    int n_present = 0;
+    for (int t = 0; t < nt; ++t) n_present += t_ng[size_t(t)] > 0;
+    put_varint(ob, uint64_t(n_present));
+    for (int t = 0; t < nt; ++t) {
+        if (!t_ng[size_t(t)]) continue;
+        const int ct = tmap[size_t(t)];
+        const uint64_t chk = T[size_t(t)].want_full ? hchk[size_t(nt + t)] : cache_chk[ct] + hchk[size_t(t)];
+        out->checksums[size_t(ct)] = chk;
+        out->present[size_t(ct)] = 1;
+        put_varint(ob, uint64_t(name_len[ct]));
+        ob.insert(ob.end(), names[ct], names[ct] + name_len[ct]);
+        put_varint(ob, uint64_t(numel[ct]));
+        for (int k = 0; k < 8; ++k) ob.push_back(uint8_t(chk >> (8 * k)));
+        put_varint(ob, uint64_t(t_ng[size_t(t)]));
+        for (int64_t g = t_first[size_t(t)]; g < t_first[size_t(t)] + t_ng[size_t(t)]; ++g) {
+            ob.push_back(uint8_t(hg_exp[size_t(g)]));
+            put_varint(ob, hg_count[size_t(g)]);
+            ob.push_back(rice[size_t(g)]);
+        }
+    }
+    const size_t bt_at = ob.size();
+    ob.resize(bt_at + 4 * size_t(n_blocks));
+    put_varint(ob, payload_len);
+    const size_t pl_at = ob.size();
+    ob.resize(pl_at + payload_len);
+    const size_t down2 = 4 * size_t(n_blocks) + payload_len;
+    CRX_CUDA(ensure_host(C, down2 + 16, st));
+    h = static_cast<uint8_t*>(C.host);
+    CRX_CUDA(cudaMemcpyAsync(h, C.b[S_BB32].p, 4 * size_t(n_blocks), cudaMemcpyDeviceToHost, st));
+    if (payload_len)
+        CRX_CUDA(cudaMemcpyAsync(h + 4 * size_t(n_blocks), C.b[S_PAYLOAD].p, payload_len, cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaStreamSynchronize(st));
+    std::memcpy(ob.data() + bt_at, h, 4 * size_t(n_blocks));
+    std::memcpy(ob.data() + pl_at, h + 4 * size_t(n_blocks), payload_len);
+    out->changes = total;
+    return kOk;
+}
+
+}  // namespace crx

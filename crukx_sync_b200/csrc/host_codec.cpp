@@ -1,0 +1,300 @@
+// Host-side wire-format code: parse (with every receiver limit), Huffman lengths with the
+// reference's tie order, canonical codes and decode tables.  See host_codec.h for the
+// reference lines each function restates.
+#include "host_codec.h"
+
+#include <algorithm>
+#include <cstring>
+
+namespace crx {
+
+namespace {
+
+// Sequential reader: any overrun is a corrupt update (wire.py:92-123).
+struct Reader {
+    const uint8_t* d;
+    int64_t n;
+    int64_t pos = 0;
+    bool take(int64_t k, const uint8_t** p) {
+        if (k < 0 || k > n - pos) return false;
+        *p = d + pos;
+        pos += k;
+        return true;
+    }
+    bool u8(int* v) {
+        if (pos >= n) return false;
+        *v = d[pos++];
+        return true;
+    }
+    // LEB128 below 2^63 and at most 10 bytes (wire.py:109-120): a set bit at or above bit 63 is
+    // corrupt as soon as it is read, a continuation past shift 63 likewise.
+    bool varint(int64_t* out) {
+        uint64_t v = 0;
+        int shift = 0;
+        for (;;) {
+            int b;
+            if (!u8(&b)) return false;
+            uint64_t part = uint64_t(b & 0x7F);
+            if (part) {
+                if (shift >= 63) return false;
+                if (shift > 56 && (part >> (63 - shift)) != 0) return false;
+                v |= part << shift;
+            }
+            if (!(b & 0x80)) { *out = int64_t(v); return true; }
+            shift += 7;
+            if (shift > 63) return false;
+        }
+    }
+    int64_t remaining() const { return n - pos; }
+};
+
+// Strict UTF-8 as Python decodes it: no overlong forms, no surrogates, at most U+10FFFF.
+bool valid_utf8(const uint8_t* s, int64_t n) {
+    int64_t i = 0;
+    while (i < n) {
+        const uint32_t c = s[i];
+        if (c < 0x80) { ++i; continue; }
+        int extra;
+        uint32_t cp, lo;
+        if (c >= 0xC2 && c <= 0xDF) { extra = 1; cp = c & 0x1F; lo = 0x80; }
+        else if (c >= 0xE0 && c <= 0xEF) { extra = 2; cp = c & 0x0F; lo = 0x800; }
+        else if (c >= 0xF0 && c <= 0xF4) { extra = 3; cp = c & 0x07; lo = 0x10000; }
+        else return false;
+        if (n - i <= extra) return false;
+        for (int k = 1; k <= extra; ++k) {
+            const uint32_t cc = s[i + k];
+            if ((cc & 0xC0) != 0x80) return false;
+            cp = (cp << 6) | (cc & 0x3F);
+        }
+        if (cp < lo || cp > 0x10FFFF || (cp >= 0xD800 && cp <= 0xDFFF)) return false;
+        i += extra + 1;
+    }
+    return true;
+}
+
+}  // namespace
+
+Status parse_update(const uint8_t* data, int64_t len, Update* u, std::string* err) {
+    auto bad = [&](const char* m) { if (err) *err = m; return kCorrupt; };
+    Reader r{data, len};
+    const uint8_t* p;
+    int v;
+    int64_t x;
+    for (int e = 0; e < 256; ++e) u->table_of_exp[e] = -1;
+    if (!r.take(4, &p)) return bad("update is truncated");
+    if (std::memcmp(p, "CRXS", 4) != 0) return bad("not a crukx-sync update");
+    if (!r.u8(&v)) return bad("update is truncated");
+    if (v != 2) return bad("unsupported format version");
+
+    int64_t n_tables;
+    if (!r.varint(&n_tables)) return bad("update is truncated or has a bad varint");
+    if (n_tables > 256) return bad("too many tables");
+    u->tables.resize(size_t(n_tables));
+    std::vector<uint8_t> seen_sym;
+    for (int64_t t = 0; t < n_tables; ++t) {
+        int e;
+        int64_t n_sym;
+        if (!r.u8(&e) || !r.varint(&n_sym)) return bad("update is truncated or has a bad varint");
+        const int64_t cap = std::min<int64_t>(kMaxSymbol + 1, r.remaining() / 2);
+        if (u->table_of_exp[e] >= 0 || !(n_sym > 0 && n_sym <= cap)) return bad("bad table header");
+        u->table_of_exp[e] = int(t);
+        Table& tb = u->tables[size_t(t)];
+        tb.exponent = e;
+        tb.symbols.resize(size_t(n_sym));
+        tb.lengths.resize(size_t(n_sym));
+        bool sym_range_ok = true;
+        for (int64_t k = 0; k < n_sym; ++k) {
+            int64_t s;
+            int L;
+            if (!r.varint(&s) || !r.u8(&L)) return bad("update is truncated or has a bad varint");
+            if (s > int64_t(kMaxSymbol)) sym_range_ok = false;
+            tb.symbols[size_t(k)] = uint32_t(std::min<int64_t>(s, kMaxSymbol + 1));
+            tb.lengths[size_t(k)] = uint8_t(L);
+        }
+        // symbols unique and <= MAX_SYMBOL (either failure is the same error)
+        if (!sym_range_ok) return bad("bad table symbols");
+        if (seen_sym.empty()) seen_sym.assign(kSymSpace, 0);
+        bool dup = false;
+        for (uint32_t s : tb.symbols) { dup |= seen_sym[s] != 0; seen_sym[s] = 1; }
+        for (uint32_t s : tb.symbols) seen_sym[s] = 0;
+        if (dup) return bad("bad table symbols");
+        // lengths 1..17 and Kraft sum <= 1; each term is a multiple of 2^-17, so the float test
+        // with its 1e-12 slack (wire.py:149) is this exact integer test
+        uint64_t kraft = 0;
+        for (uint8_t L : tb.lengths) {
+            if (L < 1 || L > kMaxCodeLen) return bad("bad Huffman code lengths");
+            kraft += uint64_t(1) << (kMaxCodeLen - L);
+        }
+        if (kraft > (uint64_t(1) << kMaxCodeLen)) return bad("bad Huffman code lengths");
+    }
+
+    int64_t n_tensors;
+    if (!r.varint(&n_tensors)) return bad("update is truncated or has a bad varint");
+    if (n_tensors > r.remaining()) return bad("too many tensors");
+    u->tensors.resize(size_t(n_tensors));
+    unsigned __int128 total_blocks = 0;
+    unsigned __int128 per_exp[256] = {};
+    for (int64_t t = 0; t < n_tensors; ++t) {
+        TensorHeader& h = u->tensors[size_t(t)];
+        int64_t nl;
+        if (!r.varint(&nl) || !r.take(nl, &p)) return bad("update is truncated");
+        if (!valid_utf8(p, nl)) return bad("tensor name is not valid UTF-8");
+        h.name = p;
+        h.name_len = nl;
+        for (int64_t s = 0; s < t; ++s) {
+            const TensorHeader& o = u->tensors[size_t(s)];
+            if (o.name_len == nl && std::memcmp(o.name, p, size_t(nl)) == 0) return bad("tensor appears twice");
+        }
+        if (!r.varint(&h.numel)) return bad("update is truncated or has a bad varint");
+        if (!r.take(8, &p)) return bad("update is truncated");
+        h.checksum = 0;
+        for (int k = 7; k >= 0; --k) h.checksum = (h.checksum << 8) | p[k];
+        int64_t ng;
+        if (!r.varint(&ng)) return bad("update is truncated or has a bad varint");
+        if (!(ng > 0 && ng <= 256)) return bad("bad group count");
+        h.groups.resize(size_t(ng));
+        bool used[256] = {};
+        unsigned __int128 sum = 0;
+        for (int64_t k = 0; k < ng; ++k) {
+            int e, rice;
+            int64_t c;
+            if (!r.u8(&e) || !r.varint(&c) || !r.u8(&rice)) return bad("update is truncated or has a bad varint");
+            if (used[e] || u->table_of_exp[e] < 0) return bad("bad group exponent");
+            if (!(c > 0 && c <= h.numel) || rice > kMaxRice) return bad("bad group header");
+            used[e] = true;
+            h.groups[size_t(k)] = Group{e, c, rice};
+            total_blocks += (unsigned __int128)((c + kBlock - 1) / kBlock);
+            sum += (unsigned __int128)c;
+            per_exp[e] += (unsigned __int128)c;
+        }
+        if (sum > (unsigned __int128)h.numel) return bad("more changes than elements");
+    }
+    for (const Table& tb : u->tables)
+        if ((unsigned __int128)tb.symbols.size() > per_exp[tb.exponent]) return bad("table unused or larger than its changes");
+    if (total_blocks * 4 > (unsigned __int128)r.remaining()) return bad("block table longer than the update");
+    u->n_blocks = int64_t(total_blocks);
+    if (!r.take(4 * u->n_blocks, &u->block_table)) return bad("update is truncated");
+    int64_t pl;
+    if (!r.varint(&pl) || !r.take(pl, &u->payload)) return bad("update is truncated");
+    u->payload_len = pl;
+    if (r.remaining() != 0) return bad("trailing bytes after the payload");
+    uint64_t total_bits = 0;
+    const uint8_t* bt = u->block_table;
+    for (int64_t b = 0; b < u->n_blocks; ++b) {
+        uint32_t w;
+        std::memcpy(&w, bt + 4 * b, 4);
+        total_bits += w;
+    }
+    if ((total_bits + 7) / 8 != uint64_t(pl)) return bad("payload length does not match its block table");
+    if ((total_bits & 7) && (u->payload[pl - 1] & ((1u << (8 - (total_bits & 7))) - 1))) return bad("non-zero padding bits");
+    // every change costs at least 2 + rice bits (wire.py:204-211)
+    int64_t b = 0;
+    int64_t changes = 0;
+    for (const TensorHeader& h : u->tensors) {
+        for (const Group& g : h.groups) {
+            changes += g.count;
+            for (int64_t k = 0; k * kBlock < g.count; ++k, ++b) {
+                uint32_t w;
+                std::memcpy(&w, bt + 4 * b, 4);
+                const int64_t m = std::min<int64_t>(kBlock, g.count - k * kBlock);
+                if (uint64_t(w) < uint64_t(m) * uint64_t(2 + g.rice)) return bad("block shorter than its symbols could be");
+            }
+        }
+    }
+    u->total_bits = total_bits;
+    u->total_changes = changes;
+    return kOk;
+}
+
+// ---------------------------------------------------------------- Huffman
+
+namespace {
+
+struct Item {
+    uint64_t count;
+    int64_t id;
+    bool operator<(const Item& o) const { return count != o.count ? count < o.count : id < o.id; }
+};
+
+// Code lengths of an unlimited Huffman code, popping (count, id) pairs in the order a binary
+// min-heap would (codec.py:81-98): leaves are ids 0..n-1, merged nodes n, n+1, ...  Merged
+// counts never decrease, so two FIFO queues (sorted leaves, merged nodes) reproduce the heap.
+void huffman_unlimited(const std::vector<uint64_t>& counts, std::vector<int>& depth_out) {
+    const int64_t n = int64_t(counts.size());
+    depth_out.assign(size_t(n), 1);
+    if (n == 1) return;
+    std::vector<Item> leaves(static_cast<size_t>(n));
+    for (int64_t i = 0; i < n; ++i) leaves[size_t(i)] = Item{counts[size_t(i)], i};
+    std::sort(leaves.begin(), leaves.end());
+    std::vector<Item> merged;
+    merged.reserve(size_t(n));
+    std::vector<int64_t> parent(static_cast<size_t>(2 * n - 1), 0);
+    size_t li = 0, mi = 0;
+    int64_t next_id = n;
+    auto pop = [&]() -> Item {
+        if (li < leaves.size() && (mi >= merged.size() || leaves[li] < merged[mi])) return leaves[li++];
+        return merged[mi++];
+    };
+    for (int64_t k = 0; k < n - 1; ++k) {
+        const Item a = pop(), b = pop();
+        parent[size_t(a.id)] = next_id;
+        parent[size_t(b.id)] = next_id;
+        merged.push_back(Item{a.count + b.count, next_id});
+        ++next_id;
+    }
+    std::vector<int> depth(static_cast<size_t>(2 * n - 1), 0);
+    for (int64_t node = 2 * n - 3; node >= 0; --node) depth[size_t(node)] = depth[size_t(parent[size_t(node)])] + 1;
+    for (int64_t i = 0; i < n; ++i) depth_out[size_t(i)] = depth[size_t(i)];
+}
+
+}  // namespace
+
+void huffman_lengths(const uint64_t* counts_in, int64_t n, uint8_t* lengths) {
+    std::vector<uint64_t> c(counts_in, counts_in + n);
+    std::vector<int> d;
+    for (int round = 0; round < 8; ++round) {          // codec.py:71-78
+        huffman_unlimited(c, d);
+        if (*std::max_element(d.begin(), d.end()) <= kMaxCodeLen) {
+            for (int64_t i = 0; i < n; ++i) lengths[i] = uint8_t(d[size_t(i)]);
+            return;
+        }
+        for (auto& x : c) x = std::max<uint64_t>(1, x >> 2);
+    }
+    int bl = 0;
+    for (uint64_t v = uint64_t(n - 1); v; v >>= 1) ++bl;
+    bl = std::max(bl, 1);
+    for (int64_t i = 0; i < n; ++i) lengths[i] = uint8_t(bl);
+}
+
+void canonical_codes(const uint8_t* lengths, int64_t n, uint32_t* codes) {
+    uint32_t per[kMaxCodeLen + 1] = {};
+    for (int64_t i = 0; i < n; ++i) per[lengths[i]]++;
+    // first code of each length in canonical order; codes of one length follow table position
+    uint32_t next[kMaxCodeLen + 1] = {};
+    uint32_t code = 0;
+    for (int L = 1; L <= kMaxCodeLen; ++L) {
+        next[L] = code;
+        code = (code + per[L]) << 1;
+    }
+    for (int64_t i = 0; i < n; ++i) codes[i] = next[lengths[i]]++;
+}
+
+void build_decode_table(const Table& t, DecodeTable* d, uint32_t* sorted_syms) {
+    uint32_t per[kMaxCodeLen + 1] = {};
+    for (uint8_t L : t.lengths) per[L]++;
+    uint32_t code = 0, idx = 0;
+    d->first[0] = d->count[0] = d->base[0] = d->limit[0] = 0;
+    for (int L = 1; L <= kMaxCodeLen; ++L) {
+        d->first[L] = code;
+        d->count[L] = per[L];
+        d->base[L] = idx;
+        d->limit[L] = (code + per[L]) << (kMaxCodeLen - L);
+        code = (code + per[L]) << 1;
+        idx += per[L];
+    }
+    uint32_t fill[kMaxCodeLen + 1];
+    for (int L = 1; L <= kMaxCodeLen; ++L) fill[L] = d->base[L];
+    for (size_t k = 0; k < t.symbols.size(); ++k) sorted_syms[fill[t.lengths[k]]++] = t.symbols[k];
+}
+
+}  // namespace crx

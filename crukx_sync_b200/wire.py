@@ -1,0 +1,240 @@
+"""The update container (wire format version 2): types, constants, varint writer, and parsing.
+
+Mirrors the reference module src/crukx_sync/wire.py (constants :8-13, ``CorruptUpdate`` :16-17,
+dataclasses :20-48, ``write_varint`` :55-61, ``serialize`` :64-89, ``parse`` :126-212).  Parsing
+and validation run in the C++ host code of libcrukx_b200.so (``crx_parse``); ``parse`` returns a
+``ParsedUpdate`` that holds that handle and exposes the reference's dataclass view lazily.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import struct
+from dataclasses import dataclass, field
+
+from . import _ext
+
+MAGIC = b"CRXS"
+VERSION = 2
+MAX_CODE_LEN = 17
+MAX_SYMBOL = 131070
+MAX_RICE = 30
+BLOCK = 256
+
+
+class CorruptUpdate(ValueError):
+    """The update bytes are malformed, truncated, or do not reproduce the expected weights."""
+
+
+@dataclass
+class Table:
+    """Canonical Huffman table for residual symbols of one old-weight exponent."""
+    exponent: int
+    symbols: list[int]
+    lengths: list[int]
+
+
+@dataclass
+class Group:
+    exponent: int
+    count: int
+    rice_r: int
+
+
+@dataclass
+class TensorHeader:
+    name: str
+    numel: int
+    checksum: int
+    groups: list[Group]
+
+
+@dataclass
+class Update:
+    tables: list[Table]
+    tensors: list[TensorHeader]
+    block_bits: list[int] = field(default_factory=list)
+    payload: bytes = b""
+
+
+def n_blocks(count: int) -> int:
+    return -(-count // BLOCK)
+
+
+def write_varint(out: bytearray, v: int) -> None:
+    if not 0 <= v < 1 << 63:
+        raise ValueError(f"varint out of range: {v}")
+    while v >= 0x80:
+        out.append((v & 0x7F) | 0x80)
+        v >>= 7
+    out.append(v)
+
+
+def _serialize_update(u: Update) -> bytes:
+    out = bytearray(MAGIC)
+    out.append(VERSION)
+    write_varint(out, len(u.tables))
+    for t in u.tables:
+        out.append(t.exponent)
+        write_varint(out, len(t.symbols))
+        for s, L in zip(t.symbols, t.lengths):
+            write_varint(out, s)
+            out.append(L)
+    write_varint(out, len(u.tensors))
+    for t in u.tensors:
+        raw = t.name.encode()
+        write_varint(out, len(raw))
+        out += raw
+        write_varint(out, t.numel)
+        out += struct.pack("<Q", t.checksum)
+        write_varint(out, len(t.groups))
+        for g in t.groups:
+            out.append(g.exponent)
+            write_varint(out, g.count)
+            out.append(g.rice_r)
+    out += struct.pack(f"<{len(u.block_bits)}I", *u.block_bits)
+    write_varint(out, len(u.payload))
+    out += u.payload
+    return bytes(out)
+
+
+_PyBytes_FromStringAndSize = ctypes.pythonapi.PyBytes_FromStringAndSize
+_PyBytes_FromStringAndSize.restype = ctypes.py_object
+_PyBytes_FromStringAndSize.argtypes = [ctypes.c_void_p, ctypes.c_ssize_t]
+_PyBytes_AsString = ctypes.pythonapi.PyBytes_AsString
+_PyBytes_AsString.restype = ctypes.c_void_p
+_PyBytes_AsString.argtypes = [ctypes.py_object]
+
+
+class EncodedUpdate:
+    """An update produced by the CUDA encoder, not yet serialized to ``bytes``."""
+
+    def __init__(self, handle, names):
+        self._h = handle
+        self.names = names
+        L = _ext.load()
+        chk = (ctypes.c_uint64 * max(len(names), 1))()
+        present = (ctypes.c_uint8 * max(len(names), 1))()
+        L.crx_encoded_checksums(handle, chk, present)
+        self.checksums = {n: int(chk[i]) for i, n in enumerate(names) if present[i]}
+        self.changes = int(L.crx_encoded_changes(handle))
+
+    def to_bytes(self) -> bytes:
+        L = _ext.load()
+        n = int(L.crx_encoded_size(self._h))
+        out = _PyBytes_FromStringAndSize(None, n)   # a fresh bytes object, filled in place once
+        if n and L.crx_encoded_copy(self._h, _PyBytes_AsString(out), n) != _ext.CRX_OK:
+            raise RuntimeError("crukx_sync_b200: encoded update copy failed")
+        return out
+
+    def close(self):
+        if self._h:
+            _ext.load().crx_encoded_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def serialize(u) -> bytes:
+    """Bytes of an update: an EncodedUpdate from the CUDA encoder, or an Update dataclass."""
+    if isinstance(u, EncodedUpdate):
+        return u.to_bytes()
+    return _serialize_update(u)
+
+
+class ParsedUpdate:
+    """A validated update (C handle).  Borrows ``data``; attribute views match wire.Update."""
+
+    def __init__(self, data: bytes):
+        L = _ext.load()
+        self._data = data if isinstance(data, bytes) else bytes(data)
+        self._h = ctypes.c_void_p()
+        err = ctypes.create_string_buffer(512)
+        buf = ctypes.cast(ctypes.c_char_p(self._data), ctypes.c_void_p)
+        st = L.crx_parse(buf, len(self._data), ctypes.byref(self._h), err, 512)
+        if st == _ext.CRX_CORRUPT:
+            raise CorruptUpdate(err.value.decode(errors="replace"))
+        if st != _ext.CRX_OK:
+            raise RuntimeError(f"crukx_sync_b200: parse failed ({st}): {err.value.decode(errors='replace')}")
+        self._tensors = None
+        self._tables = None
+
+    @property
+    def handle(self):
+        return self._h
+
+    @property
+    def tensors(self) -> list[TensorHeader]:
+        if self._tensors is None:
+            L = _ext.load()
+            out = []
+            for t in range(int(L.crx_update_n_tensors(self._h))):
+                p, nl, ne, ck, ng = (ctypes.c_void_p(), ctypes.c_int64(), ctypes.c_int64(), ctypes.c_uint64(),
+                                     ctypes.c_int32())
+                L.crx_update_tensor(self._h, t, ctypes.byref(p), ctypes.byref(nl), ctypes.byref(ne), ctypes.byref(ck),
+                                    ctypes.byref(ng))
+                name = ctypes.string_at(p, nl.value).decode("utf-8")
+                groups = []
+                for k in range(ng.value):
+                    e, c, r = ctypes.c_int32(), ctypes.c_int64(), ctypes.c_int32()
+                    L.crx_update_group(self._h, t, k, ctypes.byref(e), ctypes.byref(c), ctypes.byref(r))
+                    groups.append(Group(e.value, c.value, r.value))
+                out.append(TensorHeader(name, ne.value, ck.value, groups))
+            self._tensors = out
+        return self._tensors
+
+    @property
+    def tables(self) -> list[Table]:
+        if self._tables is None:
+            L = _ext.load()
+            out = []
+            for k in range(int(L.crx_update_n_tables(self._h))):
+                e, n = ctypes.c_int32(), ctypes.c_int64()
+                L.crx_update_table(self._h, k, ctypes.byref(e), ctypes.byref(n))
+                syms = (ctypes.c_uint32 * max(n.value, 1))()
+                lens = (ctypes.c_uint8 * max(n.value, 1))()
+                L.crx_update_table_entries(self._h, k, syms, lens)
+                out.append(Table(e.value, list(syms)[: n.value], list(lens)[: n.value]))
+            self._tables = out
+        return self._tables
+
+    @property
+    def block_bits(self) -> list[int]:
+        L = _ext.load()
+        n = int(L.crx_update_n_blocks(self._h))
+        arr = (ctypes.c_uint32 * max(n, 1))()
+        L.crx_update_block_bits(self._h, arr)
+        return list(arr)[:n]
+
+    @property
+    def payload(self) -> bytes:
+        p, n = ctypes.c_void_p(), ctypes.c_int64()
+        _ext.load().crx_update_payload(self._h, ctypes.byref(p), ctypes.byref(n))
+        return ctypes.string_at(p, n.value) if n.value else b""
+
+    @property
+    def changes(self) -> int:
+        return int(_ext.load().crx_update_changes(self._h))
+
+    def to_update(self) -> Update:
+        return Update(self.tables, self.tensors, self.block_bits, self.payload)
+
+    def close(self):
+        if self._h:
+            _ext.load().crx_update_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def parse(data: bytes) -> ParsedUpdate:
+    """Parse and structurally validate an update (every limit of the format); CorruptUpdate if not."""
+    return ParsedUpdate(data)

@@ -1,0 +1,117 @@
+/*
+ * crukx_b200.h -- C ABI of the B200-native crukx-sync encode/apply path.
+ *
+ * Plain pointers, sizes and an opaque CUDA stream (cudaStream_t passed as void*); no C++ or torch
+ * types cross this boundary and no exceptions escape it.  Every call returns a status code:
+ *
+ *   CRX_OK            success
+ *   CRX_VALUE_ERROR   caller mistake / unrepresentable update      -> Python ValueError
+ *   CRX_CORRUPT       malformed update or one that does not verify -> Python CorruptUpdate
+ *   CRX_CUDA_ERROR    CUDA runtime failure
+ *   CRX_NO_MEMORY     host allocation failure
+ *   CRX_BAD_ARGUMENT  null/negative arguments
+ *
+ * and writes a NUL-terminated message into err[0..errlen) on failure.
+ *
+ * Device pointers are owned by the caller; scratch memory is owned by the context (one per
+ * device, grown on demand, reused across calls).  Calls on one context are serialized by an
+ * internal lock; work is ordered on the caller's stream.  The reference interfaces each entry
+ * point replaces are cited beside it (paths relative to the crukx-sync project).
+ */
+#ifndef CRUKX_B200_H
+#define CRUKX_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CRX_OK 0
+#define CRX_VALUE_ERROR 1
+#define CRX_CORRUPT 2
+#define CRX_CUDA_ERROR 3
+#define CRX_NO_MEMORY 4
+#define CRX_BAD_ARGUMENT 5
+
+typedef struct crx_ctx crx_ctx;
+typedef struct crx_encoded crx_encoded;
+typedef struct crx_update crx_update;
+
+/* Wire format version produced and accepted (src/crukx_sync/wire.py:9: VERSION = 2). */
+int crx_wire_version(void);
+
+/* Per-device context.  No reference counterpart: the reference allocates through torch. */
+int crx_ctx_create(int device, crx_ctx** out, char* err, size_t errlen);
+void crx_ctx_destroy(crx_ctx* ctx);
+/* Kernels launched by this context so far (no reference counterpart: instrumentation). */
+uint64_t crx_ctx_launches(crx_ctx* ctx);
+/* Per-kernel timing with CUDA events on the caller's stream while enabled (instrumentation, no
+ * reference counterpart).  Enabling clears earlier records.  crx_ctx_kernel_times returns the
+ * number of distinct kernels, writes their names ('\n'-separated) and total ms / launch counts
+ * for the first `max` of them. */
+int crx_ctx_profile(crx_ctx* ctx, int enable);
+int32_t crx_ctx_kernel_times(crx_ctx* ctx, char* names, size_t names_len, double* ms, int32_t* counts, int32_t max);
+
+/*
+ * Encode old -> new for n tensors of bf16/int16 bits on the context's device.
+ * Replaces codec.encode + wire.serialize (src/crukx_sync/codec.py:278-420, wire.py:64-89) as
+ * called by encode_update (src/crukx_sync/__init__.py:38-48).  Tensor order = update order;
+ * names are UTF-8 (name_len bytes each).  cached_checksums/has_cached (may be NULL) hold the
+ * sender's cached checksum of prev[i] (codec.py:345-352).  On success *out holds the update.
+ */
+int crx_encode(crx_ctx* ctx, int32_t n_tensors, const int16_t* const* prev, const int16_t* const* cur,
+               const int64_t* numel, const uint8_t* const* names, const int64_t* name_len,
+               const uint64_t* cached_checksums, const uint8_t* has_cached, void* stream,
+               crx_encoded** out, char* err, size_t errlen);
+int64_t crx_encoded_size(const crx_encoded* enc);
+/* Copy the serialized update into dst (cap >= crx_encoded_size). */
+int crx_encoded_copy(const crx_encoded* enc, uint8_t* dst, int64_t cap);
+int64_t crx_encoded_changes(const crx_encoded* enc);
+/* Per input tensor: the checksum of new[i] to commit to the sender cache, present[i] = 1 when
+ * tensor i is in the update (the reference commits only those, __init__.py:46-47). */
+void crx_encoded_checksums(const crx_encoded* enc, uint64_t* checksums, uint8_t* present);
+void crx_encoded_free(crx_encoded* enc);
+
+/*
+ * Parse and validate an update on the host: every limit of wire.parse
+ * (src/crukx_sync/wire.py:126-212).  The handle borrows data[0..len), which must outlive it.
+ */
+int crx_parse(const uint8_t* data, int64_t len, crx_update** out, char* err, size_t errlen);
+int64_t crx_update_n_tensors(const crx_update* u);
+int64_t crx_update_changes(const crx_update* u);
+int crx_update_tensor(const crx_update* u, int64_t i, const uint8_t** name, int64_t* name_len, int64_t* numel,
+                      uint64_t* checksum, int32_t* n_groups);
+int crx_update_group(const crx_update* u, int64_t i, int32_t k, int32_t* exponent, int64_t* count, int32_t* rice);
+int32_t crx_update_n_tables(const crx_update* u);
+int crx_update_table(const crx_update* u, int32_t k, int32_t* exponent, int64_t* n_symbols);
+int crx_update_table_entries(const crx_update* u, int32_t k, uint32_t* symbols, uint8_t* lengths);
+int64_t crx_update_n_blocks(const crx_update* u);
+int crx_update_block_bits(const crx_update* u, uint32_t* out);
+int crx_update_payload(const crx_update* u, const uint8_t** data, int64_t* len);
+void crx_update_free(crx_update* u);
+
+/*
+ * Verify a parsed update against the receiver's weights and write it in place, all or nothing.
+ * Replaces codec.apply (src/crukx_sync/codec.py:578-717) as called by apply_update
+ * (src/crukx_sync/__init__.py:51-57).  weights[i] is the device buffer of update tensor i (the
+ * caller matched names and sizes first, codec.py:582-592).  cached_checksums/has_cached (may be
+ * NULL): the receiver's trusted checksum of weights[i] (codec.py:457-460, 702-705).  On
+ * CRX_CORRUPT nothing was written; on CRX_OK the commit is enqueued on `stream`.
+ */
+int crx_apply(crx_ctx* ctx, const crx_update* u, int16_t* const* weights, const uint64_t* cached_checksums,
+              const uint8_t* has_cached, void* stream, int64_t* changed, char* err, size_t errlen);
+
+/* Length-limited canonical Huffman code lengths for n symbol counts, with the reference's tie
+ * order (src/crukx_sync/codec.py:71-98).  Host only; the encoder uses the same routine. */
+int crx_huffman_lengths(const uint64_t* counts, int64_t n, uint8_t* lengths);
+
+/* Full checksum of n int16 elements on the device (src/crukx_sync/codec.py:61-68). */
+int crx_checksum(crx_ctx* ctx, const int16_t* data, int64_t n, void* stream, uint64_t* out, char* err, size_t errlen);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CRUKX_B200_H */
