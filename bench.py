@@ -227,6 +227,11 @@ def time_oracle(prev, cur, steps=1):
     return t_enc / steps, t_app / steps, len(upd)
 
 
+def log(*a):
+    if os.environ.get("CRUKX_B200_TRACE"):
+        print(f"[bench {time.strftime('%H:%M:%S')}]", *a, file=sys.stderr, flush=True)
+
+
 def run_ours(args, rank, world, dist):
     import crukx_sync_b200 as crx
     from crukx_sync_b200 import _ext
@@ -239,7 +244,9 @@ def run_ours(args, rank, world, dist):
     shapes = {k: v for k, v in shapes_all.items() if owner[k] == rank}
     total_params = sum(int(torch.tensor(s).prod()) for s in shapes_all.values())
     my_params = sum(int(torch.tensor(s).prod()) for s in shapes.values())
-    A, B = make_states(shapes, cfg["lr"], dev, seed=rank * 0 + 0)
+    log("generating", len(shapes), "tensors,", my_params, "params")
+    A, B = make_states(shapes, cfg["lr"], dev, seed=0)
+    log("generated")
     changed = sum(int((A[k].view(torch.int16) != B[k].view(torch.int16)).sum()) for k in A)
     recv = {k: v.clone() for k, v in A.items()}
     sender, receiver = {}, {}
@@ -285,7 +292,8 @@ def run_ours(args, rank, world, dist):
         state["src"], state["dst"] = dst, src
         return upd, st
 
-    for _ in range(args.warmup):
+    for i in range(args.warmup):
+        log("warmup step", i)
         step()
     barrier()
     # correctness of the warm state before timing

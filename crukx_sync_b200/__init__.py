@@ -16,6 +16,7 @@ include/crukx_b200.h); there is no CPU implementation and no other backend.
 
 from __future__ import annotations
 
+import time
 from collections.abc import Mapping
 from dataclasses import dataclass
 
@@ -39,9 +40,13 @@ def encode_update(old: Mapping[str, torch.Tensor], new: Mapping[str, torch.Tenso
     """Bytes that turn `old` into `new` exactly. Same names and shapes; tensors are bf16 or int16."""
     if old.keys() != new.keys():
         raise ValueError(f"old and new differ in tensor names: {sorted(old.keys() ^ new.keys())[:5]}")
+    t0 = time.perf_counter()
     with torch.no_grad():
         update = codec.encode(old, new, checksums)
+    codec._trace("encode (C-ABI call)", t0)
+    t1 = time.perf_counter()
     data = serialize(update)
+    codec._trace("serialize to bytes", t1)
     if checksums is not None:  # commit only once the update exists
         checksums.update(update.checksums)
     return data
@@ -50,7 +55,11 @@ def encode_update(old: Mapping[str, torch.Tensor], new: Mapping[str, torch.Tenso
 def apply_update(weights: Mapping[str, torch.Tensor], update: bytes,
                  checksums: dict | None = None) -> UpdateStats:
     """Write the update into `weights` in place; on any error nothing is written."""
+    t0 = time.perf_counter()
     u = parse(update)
+    codec._trace("parse", t0)
+    t1 = time.perf_counter()
     with torch.no_grad():
         changed = codec.apply(weights, u, checksums)
-    return UpdateStats(len(u.tensors), changed, len(update))
+    codec._trace("apply (C-ABI call)", t1)
+    return UpdateStats(u.n_tensors, changed, len(update))

@@ -19,13 +19,13 @@ EXPORTS = [
     "crx_wire_version", "crx_ctx_create", "crx_ctx_destroy", "crx_ctx_launches", "crx_ctx_profile",
     "crx_ctx_kernel_times", "crx_encode", "crx_encoded_size", "crx_encoded_copy",
     "crx_encoded_changes", "crx_encoded_checksums", "crx_encoded_free", "crx_parse", "crx_update_n_tensors",
-    "crx_update_changes", "crx_update_tensor", "crx_update_group", "crx_update_n_tables", "crx_update_table",
+    "crx_update_changes", "crx_update_tensor", "crx_update_group", "crx_update_tensor_table", "crx_update_n_tables", "crx_update_table",
     "crx_update_table_entries", "crx_update_n_blocks", "crx_update_block_bits", "crx_update_payload",
     "crx_update_free", "crx_apply", "crx_huffman_lengths", "crx_checksum",
 ]
 
 _lib = None
-_lock = threading.Lock()
+_lock = threading.RLock()   # context() calls load() while holding it
 
 
 def load():
@@ -60,6 +60,7 @@ def load():
             "crx_update_changes": ([P], I64),
             "crx_update_tensor": ([P, I64, P, P, P, P, P], ctypes.c_int),
             "crx_update_group": ([P, I64, I32, P, P, P], ctypes.c_int),
+            "crx_update_tensor_table": ([P, P, P, P, P], ctypes.c_int),
             "crx_update_n_tables": ([P], I32),
             "crx_update_table": ([P, I32, P, P], ctypes.c_int),
             "crx_update_table_entries": ([P, I32, P, P], ctypes.c_int),

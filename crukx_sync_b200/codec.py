@@ -15,12 +15,23 @@ place.  Without a CUDA device these functions raise; there is no CPU implementat
 from __future__ import annotations
 
 import ctypes
+import os
+import sys
+import time
 from collections.abc import Mapping
 
 import torch
 
 from . import _ext
 from .wire import CorruptUpdate, EncodedUpdate, ParsedUpdate
+
+
+_TRACE = bool(os.environ.get("CRUKX_B200_TRACE"))
+
+
+def _trace(what: str, t0: float) -> None:
+    if _TRACE:
+        print(f"[crx-py] {what:<28} {1e3 * (time.perf_counter() - t0):9.3f} ms", file=sys.stderr, flush=True)
 
 
 def bits16(name: str, t) -> torch.Tensor:
@@ -104,16 +115,16 @@ def _cache_get(checksums, name, t):
 
 def apply(weights: Mapping[str, torch.Tensor], u: ParsedUpdate, checksums: dict | None = None) -> int:
     """Verify ``u`` against ``weights``, then write the new values in place; returns changes."""
-    headers = u.tensors
+    headers = u.tensor_table()
     if not headers:
         return 0
     targets = []
-    for h in headers:
-        if h.name not in weights:
-            raise ValueError(f"update has tensor {h.name!r} that the receiver does not have")
-        a = bits16(h.name, weights[h.name])
-        if a.numel() != h.numel:
-            raise ValueError(f"{h.name}: update is for {h.numel} elements, receiver has {a.numel()}")
+    for name, numel, _ in headers:
+        if name not in weights:
+            raise ValueError(f"update has tensor {name!r} that the receiver does not have")
+        a = bits16(name, weights[name])
+        if a.numel() != numel:
+            raise ValueError(f"{name}: update is for {numel} elements, receiver has {a.numel()}")
         targets.append(a)
     dev = targets[0].device
     if any(a.device != dev for a in targets):
@@ -121,7 +132,7 @@ def apply(weights: Mapping[str, torch.Tensor], u: ParsedUpdate, checksums: dict 
     cdev = _cuda_device(dev)
     work = targets if dev.type == "cuda" else [a.to(cdev) for a in targets]
     k = len(headers)
-    cached = [_cache_get(checksums, h.name, weights[h.name]) for h in headers]
+    cached = [_cache_get(checksums, name, weights[name]) for name, _, _ in headers]
     cache = (ctypes.c_uint64 * k)(*[c if c is not None else 0 for c in cached])
     has = (ctypes.c_uint8 * k)(*[1 if c is not None else 0 for c in cached])
     ptrs = _ext.ptr_array([a.data_ptr() for a in work])
@@ -135,13 +146,13 @@ def apply(weights: Mapping[str, torch.Tensor], u: ParsedUpdate, checksums: dict 
     if st != _ext.CRX_OK:
         _raise(st, err)
     if dev.type == "cuda":
-        for h in headers:   # the commit wrote through raw pointers: move the version like a[idx] = v
-            torch.autograd.graph.increment_version(weights[h.name])
+        for name, _, _ in headers:   # the commit wrote through raw pointers: move the version like a[idx] = v
+            torch.autograd.graph.increment_version(weights[name])
     else:
         for a, wk in zip(targets, work):
             a.copy_(wk)     # in-place copy back: bumps the version and reaches every view
     if checksums is not None:   # record the version after our own write
-        checksums.update({h.name: (h.checksum, weights[h.name]._version) for h in headers})
+        checksums.update({name: (chk, weights[name]._version) for name, _, chk in headers})
     return int(changed.value)
 
 

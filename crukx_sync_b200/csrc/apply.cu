@@ -154,31 +154,28 @@ __global__ void __launch_bounds__(HIST_THREADS) k_app_hist(const AppTensor* __re
 
 // ------------------------------------------------------------------ block decoder
 
-__global__ void __launch_bounds__(128) k_decode(const uint64_t* __restrict__ W, const uint32_t* __restrict__ bb,
-                                                const uint64_t* __restrict__ boff, int64_t n_blocks,
-                                                const AppGroup* __restrict__ G, const uint64_t* __restrict__ gblock, int64_t ng,
-                                                const DecTable* __restrict__ TB, const uint32_t* __restrict__ SYMS,
-                                                const uint64_t* __restrict__ GS, uint32_t* __restrict__ gaps,
-                                                uint32_t* __restrict__ zz, uint64_t* __restrict__ bsum,
-                                                unsigned long long* __restrict__ counters) {
-    const int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (b >= n_blocks) return;
-    const int64_t g = last_le(gblock, ng, uint64_t(b));
-    const AppGroup grp = G[g];
-    const uint64_t k = uint64_t(b) - gblock[g];
-    const int cnt = int(tmin<uint64_t>(kBlock, grp.count - k * kBlock));
-    const uint64_t ebase = grp.start + k * kBlock;
-    uint64_t cur = boff[b];
-    const uint64_t end = cur + bb[b];
-    const uint64_t size = GS[int64_t(grp.tensor) * 256 + grp.exp];
-    const int rice = grp.rice;
-    const uint64_t qmax = size >> rice;
-    const DecTable* tab = TB + grp.table;
-    bool bad = false;
+constexpr int DEC_WARPS = 4;                 // warps per CTA; a warp decodes 32 consecutive blocks
+constexpr int DEC_WORDS = 1536;              // payload words a warp stages in shared memory (12 KB)
+
+// 64 payload bits starting at bit `pos` from words staged in shared memory (w0 = first word)
+__device__ __forceinline__ uint64_t read64s(const uint64_t* W, uint64_t w0, uint64_t pos) {
+    const uint64_t w = (pos >> 6) - w0;
+    const int s = int(pos & 63);
+    const uint64_t hi = W[w];
+    if (!s) return hi;
+    return (hi << s) | (W[w + 1] >> (64 - s));
+}
+
+template <bool kShared>
+__device__ __forceinline__ bool decode_block(const uint64_t* Wsrc, uint64_t w0, uint64_t cur, const uint64_t end, int cnt,
+                                             uint64_t ebase, uint64_t qmax, int rice, const DecTable* __restrict__ tab,
+                                             const uint32_t* __restrict__ SYMS, uint32_t* __restrict__ gaps,
+                                             uint32_t* __restrict__ zz, uint64_t* sum_out) {
+    auto rd = [&](uint64_t p) { return kShared ? read64s(Wsrc, w0, p) : read64(Wsrc, p); };
     uint64_t sum = 0;
     for (int step = 0; step < cnt; ++step) {
-        if (cur >= end) { bad = true; break; }
-        uint64_t y = ~read64(W, cur);
+        if (cur >= end) return false;
+        uint64_t y = ~rd(cur);
         uint64_t q;
         if (y) {
             q = uint64_t(__clzll(y));
@@ -187,14 +184,14 @@ __global__ void __launch_bounds__(128) k_decode(const uint64_t* __restrict__ W, 
             // or past q_max, so hostile updates cost at most their own bits
             q = 64;
             while (q <= qmax && cur + q < end) {
-                y = ~read64(W, cur + q);
+                y = ~rd(cur + q);
                 if (y) { q += uint64_t(__clzll(y)); break; }
                 q += 64;
             }
         }
-        if (q > qmax || cur + q >= end) { bad = true; break; }
+        if (q > qmax || cur + q >= end) return false;
         const uint64_t c = cur + q + 1;
-        const uint64_t x = read64(W, c);
+        const uint64_t x = rd(c);
         const uint64_t rem = rice ? (x >> (64 - rice)) : 0;
         const uint32_t peek = uint32_t((x << rice) >> (64 - kMaxCodeLen));
         const uint32_t lv = tab->lut[peek >> (kMaxCodeLen - LUT_BITS)];
@@ -206,19 +203,58 @@ __global__ void __launch_bounds__(128) k_decode(const uint64_t* __restrict__ W, 
         } else {
             L = 1;
             while (L <= kMaxCodeLen && peek >= tab->limit[L]) ++L;
-            if (L > kMaxCodeLen) { bad = true; break; }
+            if (L > kMaxCodeLen) return false;
             idx = tab->base[L] + (peek >> (kMaxCodeLen - L)) - tab->first[L];
         }
-        const uint32_t sym = SYMS[tab->sym_off + min(idx, tab->nsym - 1)];
+        const uint32_t sym = SYMS[tab->sym_off + tmin(idx, tab->nsym - 1)];
         const uint64_t gap = (q << rice) | rem;
         gaps[ebase + step] = gap > 0xFFFFFFFFull ? 0xFFFFFFFFu : uint32_t(gap);
         zz[ebase + step] = sym;
         sum += gap + 1;
         cur = c + uint64_t(rice) + uint64_t(L);
     }
-    if (!bad && cur != end) bad = true;
-    bsum[b] = bad ? 0 : sum;
-    if (bad) atomicOr(&counters[1], (unsigned long long)ERR_DECODE);
+    *sum_out = sum;
+    return cur == end;
+}
+
+__global__ void __launch_bounds__(DEC_WARPS * 32) k_decode(const uint64_t* __restrict__ W, const uint32_t* __restrict__ bb,
+                                                           const uint64_t* __restrict__ boff, int64_t n_blocks,
+                                                           const AppGroup* __restrict__ G, const uint64_t* __restrict__ gblock,
+                                                           int64_t ng, const DecTable* __restrict__ TB,
+                                                           const uint32_t* __restrict__ SYMS, const uint64_t* __restrict__ GS,
+                                                           uint32_t* __restrict__ gaps, uint32_t* __restrict__ zz,
+                                                           uint64_t* __restrict__ bsum, unsigned long long* __restrict__ counters) {
+    __shared__ uint64_t stage[DEC_WARPS][DEC_WORDS];
+    const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
+    const int64_t b0 = (int64_t(blockIdx.x) * DEC_WARPS + wi) * 32;
+    if (b0 >= n_blocks) return;
+    const int64_t b_last = tmin<int64_t>(b0 + 31, n_blocks - 1);
+    const int64_t b = b0 + lane;
+    // this warp's blocks are consecutive in the payload: stage their words when they fit
+    const uint64_t w0 = boff[b0] >> 6;
+    const uint64_t w1 = ((boff[b_last] + bb[b_last]) >> 6) + 2;   // + the window a read can reach
+    const bool staged = w1 - w0 <= DEC_WORDS;
+    if (staged) {
+        for (uint64_t k = lane; k < w1 - w0; k += 32) stage[wi][k] = bswap64(__ldg(W + w0 + k));
+        __syncwarp();
+    }
+    if (b > b_last) return;
+    const int64_t g = last_le(gblock, ng, uint64_t(b));
+    const AppGroup grp = G[g];
+    const uint64_t k = uint64_t(b) - gblock[g];
+    const int cnt = int(tmin<uint64_t>(kBlock, grp.count - k * kBlock));
+    const uint64_t ebase = grp.start + k * kBlock;
+    const uint64_t cur = boff[b];
+    const uint64_t end = cur + bb[b];
+    const uint64_t size = GS[int64_t(grp.tensor) * 256 + grp.exp];
+    const int rice = grp.rice;
+    const uint64_t qmax = size >> rice;
+    const DecTable* tab = TB + grp.table;
+    uint64_t sum = 0;
+    const bool ok = staged ? decode_block<true>(stage[wi], w0, cur, end, cnt, ebase, qmax, rice, tab, SYMS, gaps, zz, &sum)
+                           : decode_block<false>(W, 0, cur, end, cnt, ebase, qmax, rice, tab, SYMS, gaps, zz, &sum);
+    bsum[b] = ok ? sum : 0;
+    if (!ok) atomicOr(&counters[1], (unsigned long long)ERR_DECODE);
 }
 
 // group-local index of every change: running sum of gap + 1 within its group
@@ -256,32 +292,57 @@ __global__ void __launch_bounds__(256) k_locals(const uint64_t* __restrict__ bsc
 }
 
 // ------------------------------------------------------------------ (exponent, rank) -> position
+//
+// Per sub-tile a stable counting sort of the old exponents built the same way as the encoder's
+// ranks (lane runs with private counters over a 16-exponent window, warp matching below it), then
+// every change is placed by (exponent, group-local rank) and its new value staged in position order.
+
+constexpr int MP_THREADS = 256;
+constexpr int MP_WARPS = MP_THREADS / 32;
+constexpr int MP_SUB = 8192;
+constexpr int MP_SPAN = MP_SUB / MP_WARPS;   // 1024
+constexpr int MP_RUN = MP_SPAN / 32;         // 32
+constexpr int MWIN = 16;
+static_assert(MP_SUB * 32 == SUPER_N, "32 sub-tiles per super-tile");
+
+__device__ __forceinline__ int mpidx(int i) { return i + (i >> 5); }
 
 struct MapSmem {
-    uint16_t tile[SUB_N];
-    uint16_t order[SUB_N];
-    uint16_t cnt[RANK_WARPS][256];
-    uint32_t tot[256], estart[256], pcur[256];
+    uint32_t tile[MP_SUB + MP_SUB / 32];  // old bits | (own rank, later the new bits) << 16, padded
+    uint16_t order[MP_SUB];               // sub-tile index of the k-th element in (exponent, index) order
+    uint32_t mark[MP_SUB / 32];           // changed positions (unpadded index)
+    uint16_t cnt[MP_WARPS][MWIN][34];     // per-lane counts, then exclusive prefixes over lanes
+    uint32_t ocnt[MP_WARPS][256];         // out-of-window per-warp counts, then warp bases
+    uint32_t wwin[MP_WARPS][MWIN];        // per-warp window totals, then warp bases
+    uint16_t tot[256], estart[256];
+    uint32_t pcur[256];
     uint64_t cursor[256], gend[256];
-    int32_t gexp[256];
-    uint64_t red[RANK_WARPS];
+    uint32_t nextloc[256];                // group-local index of each group's next change (~0: none)
+    uint8_t gexp[256];
+    uint32_t oow[MP_WARPS], wcnt[MP_WARPS], wbase[MP_WARPS];
+    unsigned long long stage_base;
+    int emax;
+    uint64_t red[MP_WARPS];
 };
 
-__global__ void __launch_bounds__(RANK_THREADS, 2)
+__global__ void __launch_bounds__(MP_THREADS, 3)
 k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, const uint32_t* __restrict__ PS,
       const uint32_t* __restrict__ local, const uint32_t* __restrict__ zz, unsigned long long* __restrict__ caddr,
-      uint16_t* __restrict__ cval, unsigned long long* __restrict__ chk_delta, unsigned long long* __restrict__ mapped) {
+      uint16_t* __restrict__ cval, uint64_t stage_cap, unsigned long long* __restrict__ chk_delta,
+      unsigned long long* __restrict__ staged) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     MapSmem& S = *reinterpret_cast<MapSmem*>(smem_raw);
     const int64_t s = blockIdx.x;
     const int t = tensor_of_super(T, nT, s);
     const AppTensor tt = T[t];
     const int64_t e_begin = (s - tt.super_begin) * SUPER_N;
-    const int64_t e_end = min(tt.numel, e_begin + SUPER_N);
+    const int64_t e_end = tmin(tt.numel, e_begin + SUPER_N);
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const uint32_t lt = lanemask_lt();
     const int ngt = tt.g_end - tt.g_begin;
-    if (tid < 256) S.pcur[tid] = PS[s * 256 + tid];
+    const int span0 = w * MP_SPAN;
+    S.pcur[tid] = PS[s * 256 + tid];
+    if (tid == 0) S.emax = 0;
     __syncthreads();
     if (tid < ngt) {
         const AppGroup grp = G[tt.g_begin + tid];
@@ -293,41 +354,105 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
         }
         S.cursor[tid] = lo;
         S.gend[tid] = grp.start + grp.count;
-        S.gexp[tid] = grp.exp;
+        S.gexp[tid] = uint8_t(grp.exp);
+        S.nextloc[tid] = lo < grp.start + grp.count ? local[lo] : 0xFFFFFFFFu;
     }
-    uint64_t delta = 0, n_mapped = 0;
-    for (int64_t base = e_begin; base < e_end; base += SUB_N) {
-        const int n = int(tmin<int64_t>(SUB_N, e_end - base));
+    uint64_t delta = 0;
+    for (int64_t base = e_begin; base < e_end; base += MP_SUB) {
+        const int n = int(tmin<int64_t>(MP_SUB, e_end - base));
         const int16_t* p = tt.w + base;
-        if (n == SUB_N && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+        uint32_t mx = 0;
+        if (n == MP_SUB && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
             const uint4* v = reinterpret_cast<const uint4*>(p);
-            uint4* d = reinterpret_cast<uint4*>(S.tile);
-            for (int k = tid; k < SUB_N / 8; k += RANK_THREADS) d[k] = __ldcs(v + k);
-        } else {
-            for (int i = tid; i < n; i += RANK_THREADS) S.tile[i] = uint16_t(p[i]);
-        }
-        for (int k = tid; k < RANK_WARPS * 256; k += RANK_THREADS) (&S.cnt[0][0])[k] = 0;
-        __syncthreads();
-        // pass 1: per-warp exponent counts
-        for (int c = 0; c < CHUNKS_PER_WARP; ++c) {
-            const int i0 = w * WARP_SPAN + c * 32;
-            if (i0 >= n) break;
-            const int i = i0 + lane;
-            const bool act = i < n;
-            const uint32_t e = act ? exp_of(S.tile[i]) : 0u;
-            const uint32_t peers = __match_any_sync(FULL, act ? e : 0x100u + lane);
-            if (act && (peers & lt) == 0) S.cnt[w][e] += uint16_t(__popc(peers));
-            __syncwarp();
-        }
-        __syncthreads();
-        if (tid < 256) {
-            uint32_t a = 0;
-            for (int ww = 0; ww < RANK_WARPS; ++ww) {
-                const uint32_t v = S.cnt[ww][tid];
-                S.cnt[ww][tid] = uint16_t(a);
-                a += v;
+#pragma unroll
+            for (int k = 0; k < MP_SUB / 8 / MP_THREADS; ++k) {
+                const int vi = tid + k * MP_THREADS;
+                const uint4 q = __ldcs(v + vi);
+                const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
+                const int pi = mpidx(8 * vi);
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    S.tile[pi + 2 * h] = wd[h] & 0xFFFFu;
+                    S.tile[pi + 2 * h + 1] = wd[h] >> 16;
+                    mx = tmax(mx, tmax((wd[h] >> 7) & 0xFFu, (wd[h] >> 23) & 0xFFu));
+                }
             }
-            S.tot[tid] = a;
+        } else {
+            for (int i = tid; i < n; i += MP_THREADS) {
+                const uint32_t x = uint16_t(p[i]);
+                S.tile[mpidx(i)] = x;
+                mx = tmax(mx, (x >> 7) & 0xFFu);
+            }
+        }
+        mx = __reduce_max_sync(FULL, mx);
+        if (lane == 0) atomicMax(&S.emax, int(mx));
+        for (int k = tid; k < MP_WARPS * MWIN * 34 / 2; k += MP_THREADS) reinterpret_cast<uint32_t*>(&S.cnt[0][0][0])[k] = 0;
+        for (int k = tid; k < MP_WARPS * 256; k += MP_THREADS) (&S.ocnt[0][0])[k] = 0;
+        S.mark[tid] = 0;
+        if (tid < MP_WARPS) S.oow[tid] = 0;
+        __syncthreads();
+        const int ebase = tmax(S.emax - (MWIN - 1), 0);
+        const int span_n = tmax(0, tmin(MP_SPAN, n - span0));
+        const int r0 = lane * MP_RUN;
+        const int vn = tmax(0, tmin(MP_RUN, span_n - r0));
+        const int pb = mpidx(span0 + r0);
+        // ---- lane walk: own ranks with private counters
+        {
+            uint16_t* myc = &S.cnt[w][0][lane];
+            bool any_oow = false;
+            for (int k = 0; k < vn; ++k) {
+                const uint32_t x = S.tile[pb + k];
+                const int d = int((x >> 7) & 0xFFu) - ebase;
+                if (unsigned(d) < unsigned(MWIN)) {
+                    const uint32_t c = myc[d * 34];
+                    S.tile[pb + k] = x | (c << 16);
+                    myc[d * 34] = uint16_t(c + 1);
+                } else {
+                    any_oow = true;
+                }
+            }
+            if (any_oow) atomicOr(&S.oow[w], 1u << lane);
+        }
+        __syncwarp();
+        for (uint32_t m = S.oow[w]; m; m &= m - 1) {      // below the window: match, in index order
+            const int run = __ffs(m) - 1;
+            const int ii = run * MP_RUN + lane;
+            const bool valid = ii < span_n;
+            const uint32_t x = valid ? S.tile[mpidx(span0 + ii)] : 0u;
+            const uint32_t e = (x >> 7) & 0xFFu;
+            const bool oow = valid && int(e) < ebase;
+            const uint32_t r = warp_rank(S.ocnt[w], e, oow, lt, lane);
+            if (oow) S.tile[mpidx(span0 + ii)] = x | (r << 16);
+        }
+        if (lane < MWIN) {
+            uint32_t run = 0;
+            for (int col = 0; col < 32; ++col) {
+                const uint32_t v = S.cnt[w][lane][col];
+                S.cnt[w][lane][col] = uint16_t(run);
+                run += v;
+            }
+            S.wwin[w][lane] = run;
+        }
+        __syncthreads();
+        {
+            const int e = tid;
+            uint32_t o = 0;
+            for (int ww = 0; ww < MP_WARPS; ++ww) {
+                const uint32_t v = S.ocnt[ww][e];
+                S.ocnt[ww][e] = o;
+                o += v;
+            }
+            const int d = e - ebase;
+            if (unsigned(d) < unsigned(MWIN)) {
+                uint32_t a = 0;
+                for (int ww = 0; ww < MP_WARPS; ++ww) {
+                    const uint32_t v = S.wwin[ww][d];
+                    S.wwin[ww][d] = a;
+                    a += v;
+                }
+                o += a;
+            }
+            S.tot[e] = uint16_t(o);
         }
         __syncthreads();
         if (w == 0) {                       // exclusive scan of the 256 totals -> bucket starts
@@ -341,64 +466,87 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             }
             uint32_t run = incl - sum;
 #pragma unroll
-            for (int k = 0; k < 8; ++k) { S.estart[lane * 8 + k] = run; run += v[k]; }
+            for (int k = 0; k < 8; ++k) { S.estart[lane * 8 + k] = uint16_t(run); run += v[k]; }
         }
         __syncthreads();
-        // pass 2: stable counting sort of the sub-tile by exponent
-        for (int c = 0; c < CHUNKS_PER_WARP; ++c) {
-            const int i0 = w * WARP_SPAN + c * 32;
-            if (i0 >= n) break;
-            const int i = i0 + lane;
-            const bool act = i < n;
-            const uint32_t e = act ? exp_of(S.tile[i]) : 0u;
-            const uint32_t peers = __match_any_sync(FULL, act ? e : 0x100u + lane);
-            if (act) S.order[S.estart[e] + S.cnt[w][e] + __popc(peers & lt)] = uint16_t(i);
-            __syncwarp();
-            if (act && (peers & lt) == 0) S.cnt[w][e] += uint16_t(__popc(peers));
-            __syncwarp();
+        // ---- second lane walk: every element to its sorted slot
+        for (int k = 0; k < vn; ++k) {
+            const uint32_t x = S.tile[pb + k];
+            const uint32_t e = (x >> 7) & 0xFFu;
+            const int d = int(e) - ebase;
+            const uint32_t sp = S.estart[e] + (x >> 16) +
+                                (unsigned(d) < unsigned(MWIN) ? S.wwin[w][d] + S.cnt[w][d][lane] : S.ocnt[w][e]);
+            S.order[sp] = uint16_t(span0 + r0 + k);
         }
         __syncthreads();
-        // place this sub-tile's changes, group by group
-        for (int k = w; k < ngt; k += RANK_WARPS) {
+        // ---- place this sub-tile's changes group by group; new bits go to the tile's upper half.
+        //      Groups whose next change lies beyond this sub-tile are skipped from shared memory.
+        for (int k = w; k < ngt; k += MP_WARPS) {
             const int e = S.gexp[k];
             const uint32_t lo = S.pcur[e], tot = S.tot[e];
+            if (S.nextloc[k] - lo >= tot) continue;
             const uint64_t ge = S.gend[k];
             uint64_t cur = S.cursor[k];
             for (;;) {
                 const uint64_t j = cur + lane;
                 uint32_t lc = 0;
                 bool valid = j < ge;
-                if (valid) { lc = local[j]; valid = lc - lo < tot && lc >= lo; }
+                if (valid) { lc = local[j]; valid = lc >= lo && lc - lo < tot; }
                 if (valid) {
                     const uint32_t i = S.order[S.estart[e] + (lc - lo)];
-                    const uint32_t old = S.tile[i];
+                    const int pi = mpidx(int(i));
+                    const uint32_t old = S.tile[pi] & 0xFFFFu;
                     const uint32_t z = zz[j];
                     const int32_t res = int32_t(z >> 1) ^ -int32_t(z & 1);
                     const uint32_t nv = uint32_t(int32_t(old) + res) & 0xFFFFu;
-                    const int64_t pos = base + i;
-                    caddr[j] = (unsigned long long)(reinterpret_cast<uintptr_t>(tt.w + pos));
-                    cval[j] = uint16_t(nv);
-                    delta += (uint64_t(nv) - uint64_t(old)) * splitmix_weight(uint64_t(pos));
-                    ++n_mapped;
+                    S.tile[pi] = old | (nv << 16);
+                    atomicOr(&S.mark[i >> 5], 1u << (i & 31));
+                    delta += (uint64_t(nv) - uint64_t(old)) * splitmix_weight(uint64_t(base + i));
                 }
                 const uint32_t m = __ballot_sync(FULL, valid);
-                // consumed changes are a prefix: stop at the first one beyond this sub-tile
-                const int taken = __popc(~m) ? __ffs(~m) - 1 : 32;
+                const int taken = __popc(~m) ? __ffs(~m) - 1 : 32;   // consumed changes are a prefix
                 cur += uint64_t(taken);
                 if (taken < 32) break;
             }
-            if (lane == 0) S.cursor[k] = cur;
+            if (lane == 0) {
+                S.cursor[k] = cur;
+                S.nextloc[k] = cur < ge ? local[cur] : 0xFFFFFFFFu;
+            }
         }
         __syncthreads();
-        if (tid < 256) S.pcur[tid] += S.tot[tid];
+        // ---- stage the sub-tile's new values in position order (one atomic per sub-tile): lane l
+        //      owns mark word l of its warp's span
+        const uint32_t bits = S.mark[(span0 >> 5) + lane];
+        uint32_t incl = __popc(bits);
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(FULL, incl, o);
+            if (lane >= o) incl += y;
+        }
+        if (lane == 31) S.wcnt[w] = incl;
+        __syncthreads();
+        if (tid == 0) {
+            uint32_t r = 0;
+            for (int ww = 0; ww < MP_WARPS; ++ww) { S.wbase[ww] = r; r += S.wcnt[ww]; }
+            S.stage_base = r ? atomicAdd(staged, (unsigned long long)r) : 0ull;
+        }
+        __syncthreads();
+        uint64_t at = S.stage_base + S.wbase[w] + incl - __popc(bits);
+        for (uint32_t b = bits; b; b &= b - 1, ++at) {
+            const int i = span0 + lane * 32 + (__ffs(b) - 1);
+            if (at < stage_cap) {
+                caddr[at] = (unsigned long long)(reinterpret_cast<uintptr_t>(tt.w + base + i));
+                cval[at] = uint16_t(S.tile[mpidx(i)] >> 16);
+            }
+        }
+        __syncthreads();
+        S.pcur[tid] += S.tot[tid];
+        if (tid == 0) S.emax = 0;
         __syncthreads();
     }
-    block_add_u64<RANK_THREADS>(delta, &chk_delta[t], S.red);
-    block_add_u64<RANK_THREADS>(n_mapped, mapped, S.red);
+    block_add_u64<MP_THREADS>(delta, &chk_delta[t], S.red);
 }
 
-// Runs only after the host verdict, which requires every change to have been mapped exactly once;
-// a null address (never mapped) is skipped all the same.
+// Runs only after the host verdict, which requires every change to have been staged exactly once.
 __global__ void __launch_bounds__(256) k_commit(const unsigned long long* __restrict__ caddr, const uint16_t* __restrict__ cval,
                                                 uint64_t n) {
     const uint64_t j = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -440,6 +588,7 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     *changed = 0;
     const int nt = int(u.tensors.size());
     if (nt == 0) return kOk;
+    trace_phase(C, "apply: start");
     // ---- host tables
     std::vector<AppTensor> T(static_cast<size_t>(nt));
     std::vector<AppGroup> G;
@@ -496,6 +645,7 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
         build_lut(d, x.lut);
     }
 
+    trace_phase(C, "apply: host tables");
     // ---- device buffers
     const size_t cells = size_t(nt) * 256;
     const size_t payload_alloc = size_t(u.payload_len) + 64;
@@ -521,7 +671,7 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
 
     // ---- uploads: metadata through pinned staging, the payload straight from the caller's buffer
     const size_t up = sizeof(AppTensor) * nt + sizeof(AppGroup) * ng + 8 * (ng + 1) + sizeof(DecTable) * TB.size() +
-                      4 * syms.size() + 16 * (nt + 1) + 4 * size_t(n_blocks) + 256;
+                      4 * syms.size() + 16 * (nt + 1) + 256;
     CRX_CUDA(ensure_host(C, up, st));
     uint8_t* h = static_cast<uint8_t*>(C.host);
     size_t o = 0;
@@ -542,10 +692,7 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     CRX_CUDA(upload(C.b[S_A_SYMS].p, syms.data(), 4 * syms.size()));
     CRX_CUDA(upload(drows, row_begin.data(), 8 * (size_t(nt) + 1)));
     CRX_CUDA(upload(drows + nt + 1, chunk_begin.data(), 8 * (size_t(nt) + 1)));
-    CRX_CUDA(upload(C.b[S_A_BB].p, u.block_table, 4 * size_t(n_blocks)));
     CRX_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(C.b[S_A_PAYLOAD].p) + u.payload_len, 0, 64, st));
-    if (u.payload_len)
-        CRX_CUDA(cudaMemcpyAsync(C.b[S_A_PAYLOAD].p, u.payload, size_t(u.payload_len), cudaMemcpyHostToDevice, st));
     auto* counters = dev<unsigned long long>(C, S_A_COUNTERS);
     auto* chk_delta = counters + 16;
     auto* chk_full = chk_delta + nt;
@@ -559,6 +706,14 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     CRX_CUDA(cudaGetLastError());
     launch_column_scan(C, dev<uint32_t>(C, S_A_HS), n_super, drows, nt, drows + nt + 1, n_chunks,
                        dev<uint32_t>(C, S_A_CHUNK_SUMS), dev<uint64_t>(C, S_A_TOT), st);
+    trace_phase(C, "apply: uploads + hist launched");
+    // ---- block table and payload: chunked multithreaded copies into pinned memory, each chunk's
+    //      DMA overlapping the next chunk's copy (and the histogram pass already running)
+    const size_t bt_bytes = 4 * size_t(n_blocks);
+    CRX_CUDA(ensure_pinned(C.in_host, bt_bytes + size_t(u.payload_len) + 16, st));
+    uint8_t* ih = static_cast<uint8_t*>(C.in_host.p);
+    CRX_CUDA(upload_pipelined(C, C.b[S_A_BB].p, u.block_table, ih, bt_bytes, st));
+    CRX_CUDA(upload_pipelined(C, C.b[S_A_PAYLOAD].p, u.payload, ih + bt_bytes, size_t(u.payload_len), st));
     // ---- block offsets and decode
     uint64_t* boff = dev<uint64_t>(C, S_A_BOFF);
     uint64_t* scan_tmp = dev<uint64_t>(C, S_A_SCAN_TMP);
@@ -568,7 +723,7 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     }
     launch_exclusive_scan_u64(C, boff, n_blocks, scan_tmp, d_total, st);
     { KernelScope ks_(C, "k_decode", st);
-    k_decode<<<unsigned((n_blocks + 127) / 128), 128, 0, st>>>(
+    k_decode<<<unsigned((n_blocks + DEC_WARPS * 32 - 1) / (DEC_WARPS * 32)), DEC_WARPS * 32, 0, st>>>(
         dev<uint64_t>(C, S_A_PAYLOAD), dev<uint32_t>(C, S_A_BB), boff, n_blocks, dG, dgblock, ng, dev<DecTable>(C, S_A_TABLES),
         dev<uint32_t>(C, S_A_SYMS), dev<uint64_t>(C, S_A_TOT), dev<uint32_t>(C, S_A_GAPS), dev<uint32_t>(C, S_A_ZZ),
         dev<uint64_t>(C, S_A_BSUM), counters);
@@ -582,13 +737,12 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     }
     CRX_CUDA(cudaGetLastError());
     // ---- positions, staged values, checksum deltas
-    CRX_CUDA(cudaMemsetAsync(C.b[S_A_CADDR].p, 0, sizeof(uint64_t) * total, st));
     const size_t map_smem = sizeof(MapSmem);
     CRX_CUDA(cudaFuncSetAttribute(k_map, cudaFuncAttributeMaxDynamicSharedMemorySize, int(map_smem)));
     { KernelScope ks_(C, "k_map", st);
-    k_map<<<unsigned(n_super), RANK_THREADS, map_smem, st>>>(dT, nt, dG, dev<uint32_t>(C, S_A_HS), dev<uint32_t>(C, S_A_LOCAL),
+    k_map<<<unsigned(n_super), MP_THREADS, map_smem, st>>>(dT, nt, dG, dev<uint32_t>(C, S_A_HS), dev<uint32_t>(C, S_A_LOCAL),
                                                             dev<uint32_t>(C, S_A_ZZ), dev<unsigned long long>(C, S_A_CADDR),
-                                                            dev<uint16_t>(C, S_A_CVAL), chk_delta, counters + 2);
+                                                            dev<uint16_t>(C, S_A_CVAL), total, chk_delta, counters + 2);
     }
     CRX_CUDA(cudaGetLastError());
     // ---- verdict (one synchronisation for the whole update)
@@ -605,6 +759,7 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
         CRX_CUDA(cudaStreamSynchronize(st));
         std::memcpy(hv.data(), C.host, 8 * nsmall);
     }
+    trace_phase(C, "apply: verdict (sync)");
     if (hv[1] & (ERR_DECODE | ERR_RANGE)) {
         *err = "payload positions outside their exponent groups";
         return kCorrupt;

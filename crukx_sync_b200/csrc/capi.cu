@@ -1,5 +1,8 @@
 // extern "C" entry points (include/crukx_b200.h) over the C++ drivers; no exception crosses.
+#include <algorithm>
+#include <chrono>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <new>
 #include <string>
@@ -28,8 +31,24 @@ static cudaEvent_t pooled_event(Ctx& c) {
     return c.ev_pool[c.ev_used++];
 }
 
+static double now_ms() {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+void trace_phase(Ctx& c, const char* name) {
+    if (!c.trace) return;
+    const double t = now_ms();
+    std::fprintf(stderr, "[crx-host] %-28s +%9.3f ms\n", name, c.phase_t > 0 ? t - c.phase_t : 0.0);
+    c.phase_t = t;
+}
+
 KernelScope::KernelScope(Ctx& ctx, const char* name, cudaStream_t st) : c(ctx), s(st) {
     ++c.launches;
+    m.name = name;
+    if (c.trace) {
+        cudaStreamSynchronize(s);
+        t0 = now_ms();
+    }
     if (c.profile) {
         m.name = name;
         m.a = pooled_event(c);
@@ -43,6 +62,10 @@ KernelScope::~KernelScope() {
         cudaEventRecord(m.b, s);
         c.marks.push_back(m);
     }
+    if (c.trace) {
+        const cudaError_t e = cudaStreamSynchronize(s);
+        std::fprintf(stderr, "[crx] %-16s %10.3f ms  %s\n", m.name, now_ms() - t0, cudaGetErrorString(e));
+    }
 }
 
 Ctx::~Ctx() {
@@ -51,9 +74,12 @@ Ctx::~Ctx() {
     cudaSetDevice(device);
     cudaDeviceSynchronize();
     for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
+    for (cudaEvent_t e : copy_ev) cudaEventDestroy(e);
     for (auto& d : b)
         if (d.p) cudaFree(d.p);
     if (host) cudaFreeHost(host);
+    if (out_host.p) cudaFreeHost(out_host.p);
+    if (in_host.p) cudaFreeHost(in_host.p);
     if (small) cudaFreeHost(small);
     if (prev >= 0) cudaSetDevice(prev);
 }
@@ -97,6 +123,95 @@ cudaError_t ensure_host(Ctx& c, size_t bytes, cudaStream_t s) {
     return cudaSuccess;
 }
 
+cudaError_t ensure_pinned(DevBuf& buf, size_t bytes, cudaStream_t s) {
+    if (bytes <= buf.cap) return cudaSuccess;
+    size_t cap = buf.cap ? buf.cap : (size_t(1) << 20);
+    while (cap < bytes) cap += cap / 2;
+    if (buf.p) {
+        cudaError_t e = cudaStreamSynchronize(s);
+        if (e != cudaSuccess) return e;
+        cudaFreeHost(buf.p);
+        buf.p = nullptr;
+        buf.cap = 0;
+    }
+    cudaError_t e = cudaMallocHost(&buf.p, cap);
+    if (e != cudaSuccess) { buf.p = nullptr; return e; }
+    buf.cap = cap;
+    return cudaSuccess;
+}
+
+static constexpr size_t kCopyChunk = size_t(32) << 20;
+
+static cudaError_t chunk_events(Ctx& c, size_t n_chunks) {
+    while (c.copy_ev.size() < n_chunks) {
+        cudaEvent_t e = nullptr;
+        const cudaError_t r = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
+        if (r != cudaSuccess) return r;
+        c.copy_ev.push_back(e);
+    }
+    return cudaSuccess;
+}
+
+cudaError_t upload_pipelined(Ctx& c, void* dev_dst, const void* host_src, uint8_t* pinned, size_t n, cudaStream_t s) {
+    for (size_t off = 0; off < n; off += kCopyChunk) {
+        const size_t len = std::min(kCopyChunk, n - off);
+        parallel_copy(pinned + off, static_cast<const uint8_t*>(host_src) + off, len);
+        const cudaError_t e = cudaMemcpyAsync(static_cast<uint8_t*>(dev_dst) + off, pinned + off, len, cudaMemcpyHostToDevice, s);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+cudaError_t download_pipelined(Ctx& c, void* host_dst, const void* dev_src, uint8_t* pinned, size_t n, cudaStream_t s) {
+    const size_t nc = (n + kCopyChunk - 1) / kCopyChunk;
+    cudaError_t e = chunk_events(c, nc);
+    if (e != cudaSuccess) return e;
+    for (size_t k = 0; k < nc; ++k) {
+        const size_t off = k * kCopyChunk, len = std::min(kCopyChunk, n - off);
+        e = cudaMemcpyAsync(pinned + off, static_cast<const uint8_t*>(dev_src) + off, len, cudaMemcpyDeviceToHost, s);
+        if (e == cudaSuccess) e = cudaEventRecord(c.copy_ev[k], s);
+        if (e != cudaSuccess) return e;
+    }
+    for (size_t k = 0; k < nc; ++k) {
+        const size_t off = k * kCopyChunk, len = std::min(kCopyChunk, n - off);
+        e = cudaEventSynchronize(c.copy_ev[k]);
+        if (e != cudaSuccess) return e;
+        parallel_copy(static_cast<uint8_t*>(host_dst) + off, pinned + off, len);
+    }
+    return cudaSuccess;
+}
+
+cudaError_t Encoded::write(uint8_t* dst) const {
+    std::memcpy(dst, head.data(), head.size());
+    dst += head.size();
+    const size_t bt = 4 * size_t(n_blocks);
+    if (bt) parallel_copy(dst, table, bt);
+    dst += bt;
+    std::memcpy(dst, len_varint.data(), len_varint.size());
+    dst += len_varint.size();
+    if (!payload_len) return cudaSuccess;
+    if (!dpay) {
+        parallel_copy(dst, own.data() + bt, payload_len);
+        return cudaSuccess;
+    }
+    return download_pipelined(*ctx, dst, dpay, static_cast<uint8_t*>(ctx->out_host.p) + bt, payload_len, stream);
+}
+
+cudaError_t Encoded::detach() {
+    const size_t bt = 4 * size_t(n_blocks);
+    std::vector<uint8_t> tmp(bt + payload_len);
+    if (bt) std::memcpy(tmp.data(), table, bt);
+    if (dpay && payload_len) {
+        cudaError_t e = cudaMemcpyAsync(tmp.data() + bt, dpay, payload_len, cudaMemcpyDeviceToHost, stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) return e;
+    }
+    own.swap(tmp);
+    table = own.data();
+    dpay = nullptr;
+    return cudaSuccess;
+}
+
 }  // namespace crx
 
 namespace {
@@ -130,6 +245,8 @@ int crx_ctx_create(int device, crx_ctx** out, char* err, size_t errlen) {
     crx_ctx* c = new (std::nothrow) crx_ctx;
     if (!c) return CRX_NO_MEMORY;
     c->c.device = device;
+    const char* tr = std::getenv("CRUKX_B200_TRACE");
+    c->c.trace = tr && *tr && *tr != '0';
     DeviceGuard g(device);
     cudaError_t e = cudaSetDevice(device);
     if (e == cudaSuccess) e = cudaMallocHost(reinterpret_cast<void**>(&c->c.small), 4096);
@@ -178,12 +295,19 @@ int crx_encode(crx_ctx* ctx, int32_t n_tensors, const int16_t* const* prev, cons
     }
 }
 
-int64_t crx_encoded_size(const crx_encoded* enc) { return enc ? int64_t(enc->e.bytes.size()) : -1; }
+int64_t crx_encoded_size(const crx_encoded* enc) { return enc ? int64_t(enc->e.size()) : -1; }
 
 int crx_encoded_copy(const crx_encoded* enc, uint8_t* dst, int64_t cap) {
-    if (!enc || !dst || cap < int64_t(enc->e.bytes.size())) return CRX_BAD_ARGUMENT;
-    std::memcpy(dst, enc->e.bytes.data(), enc->e.bytes.size());
-    return CRX_OK;
+    if (!enc || !dst || cap < int64_t(enc->e.size())) return CRX_BAD_ARGUMENT;
+    cudaError_t e;
+    if (enc->e.ctx) {   // the context lock keeps the next encode from reusing the buffers meanwhile
+        std::lock_guard<std::mutex> lock(enc->e.ctx->mu);
+        DeviceGuard g(enc->e.ctx->device);
+        e = enc->e.write(dst);
+    } else {
+        e = enc->e.write(dst);
+    }
+    return e == cudaSuccess ? CRX_OK : CRX_CUDA_ERROR;
 }
 
 int64_t crx_encoded_changes(const crx_encoded* enc) { return enc ? int64_t(enc->e.changes) : -1; }
@@ -196,7 +320,14 @@ void crx_encoded_checksums(const crx_encoded* enc, uint64_t* checksums, uint8_t*
     }
 }
 
-void crx_encoded_free(crx_encoded* enc) { delete enc; }
+void crx_encoded_free(crx_encoded* enc) {
+    if (!enc) return;
+    if (enc->e.ctx) {
+        std::lock_guard<std::mutex> lock(enc->e.ctx->mu);
+        if (enc->e.ctx->live == &enc->e) enc->e.ctx->live = nullptr;
+    }
+    delete enc;
+}
 
 int crx_parse(const uint8_t* data, int64_t len, crx_update** out, char* err, size_t errlen) {
     if (!out || len < 0 || (len && !data)) return CRX_BAD_ARGUMENT;
@@ -230,6 +361,19 @@ int crx_update_tensor(const crx_update* u, int64_t i, const uint8_t** name, int6
     if (numel) *numel = h.numel;
     if (checksum) *checksum = h.checksum;
     if (n_groups) *n_groups = int32_t(h.groups.size());
+    return CRX_OK;
+}
+
+int crx_update_tensor_table(const crx_update* u, const uint8_t** names, int64_t* name_lens, int64_t* numels,
+                            uint64_t* checksums) {
+    if (!u) return CRX_BAD_ARGUMENT;
+    for (size_t i = 0; i < u->u.tensors.size(); ++i) {
+        const crx::TensorHeader& h = u->u.tensors[i];
+        if (names) names[i] = h.name;
+        if (name_lens) name_lens[i] = h.name_len;
+        if (numels) numels[i] = h.numel;
+        if (checksums) checksums[i] = h.checksum;
+    }
     return CRX_OK;
 }
 

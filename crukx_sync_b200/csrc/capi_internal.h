@@ -4,6 +4,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstring>
 #include <string>
 #include <vector>
 
@@ -12,11 +13,28 @@
 
 namespace crx {
 
+// A serialized update, kept in pieces so the large part is copied once, straight into the
+// caller's buffer: header bytes (host); the block table (in the context's pinned output buffer);
+// the payload, still in device memory until write() streams it down chunk by chunk, overlapping
+// each chunk's DMA with the host copy of the previous one.  The next encode on the same context
+// first moves block table and payload into `own` (detach()).
 struct Encoded {
-    std::vector<uint8_t> bytes;        // the complete serialized update
+    Ctx* ctx = nullptr;
+    cudaStream_t stream = nullptr;
+    std::vector<uint8_t> head;         // magic .. last group header
+    const uint8_t* table = nullptr;    // 4 * n_blocks block-table bytes (pinned, or own)
+    const uint8_t* dpay = nullptr;     // payload in device memory (context workspace) until detached
+    std::vector<uint8_t> own;          // block table + payload after detach()
+    int64_t n_blocks = 0;
+    uint64_t payload_len = 0;
+    std::vector<uint8_t> len_varint;   // payload_len as LEB128
     std::vector<uint64_t> checksums;   // per caller tensor: checksum of `cur` (when present)
     std::vector<uint8_t> present;      // per caller tensor: 1 when the tensor is in the update
     uint64_t changes = 0;
+
+    size_t size() const { return head.size() + 4 * size_t(n_blocks) + len_varint.size() + payload_len; }
+    cudaError_t write(uint8_t* dst) const;   // capi.cu
+    cudaError_t detach();                    // capi.cu
 };
 
 // Encode n tensors (device pointers).  cache_chk/has_cache may be null.

@@ -17,10 +17,10 @@ namespace crx {
 
 struct Ctx;
 
-constexpr int SUB_N = 16384;                 // elements per sub-tile (held in shared memory)
-constexpr int SUPER = 16;                    // sub-tiles per super-tile
-constexpr int64_t SUPER_N = int64_t(SUB_N) * SUPER;
-constexpr int RANK_THREADS = 512;            // 16 warps; each warp owns SUB_N/16 = 1024 elements
+constexpr int SUB_N = 8192;                  // elements per sub-tile (held in shared memory)
+constexpr int SUPER = 32;                    // sub-tiles per super-tile
+constexpr int64_t SUPER_N = int64_t(SUB_N) * SUPER;   // 2^18: ranks local to a super-tile fit 18 bits
+constexpr int RANK_THREADS = 512;            // 16 warps; each warp owns SUB_N/16 = 512 elements
 constexpr int RANK_WARPS = RANK_THREADS / 32;
 constexpr int WARP_SPAN = SUB_N / RANK_WARPS;
 constexpr int CHUNKS_PER_WARP = WARP_SPAN / 32;
@@ -54,6 +54,20 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
 }
 
 __device__ __forceinline__ uint32_t bswap32(uint32_t x) { return __byte_perm(x, 0, 0x0123); }
+
+// Stable rank of this lane's key (0..255) among the same-key lanes of this chunk and of every
+// earlier chunk this warp ranked with the same counters.  The lowest lane of each peer group adds
+// the group's size to the warp's counter with one shared-memory atomic and broadcasts the old
+// value; the next chunk's atomics are issued only after that value came back, so each counter
+// sees its updates in chunk order.  Inactive lanes (act = false) get a key no other lane has.
+__device__ __forceinline__ uint32_t warp_rank(uint32_t* cnt, uint32_t key, bool act, uint32_t lt, int lane) {
+    const uint32_t peers = __match_any_sync(0xffffffffu, act ? key : 0x100u + uint32_t(lane));
+    const int leader = __ffs(peers) - 1;
+    uint32_t base = 0;
+    if (act && lane == leader) base = atomicAdd(&cnt[key], uint32_t(__popc(peers)));
+    base = __shfl_sync(0xffffffffu, base, leader);
+    return base + __popc(peers & lt);
+}
 
 __device__ __forceinline__ int exp_of(uint32_t bits16) { return int((bits16 >> 7) & 0xFFu); }
 

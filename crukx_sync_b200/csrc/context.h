@@ -24,6 +24,14 @@ struct Ctx;
 // Grow `buf` to at least `bytes` (contents not preserved).  Synchronizes `s` before freeing.
 cudaError_t ensure_dev(DevBuf& buf, size_t bytes, cudaStream_t s);
 cudaError_t ensure_host(Ctx& c, size_t bytes, cudaStream_t s);
+cudaError_t ensure_pinned(DevBuf& buf, size_t bytes, cudaStream_t s);
+// memcpy split over threads (large copies; also spreads first-touch page faults)
+void parallel_copy(void* dst, const void* src, size_t n);
+// host -> device through pinned staging, chunk by chunk: the host copy of chunk k+1 overlaps the
+// DMA of chunk k.  `pinned` holds at least n bytes.
+cudaError_t upload_pipelined(Ctx& c, void* dev_dst, const void* host_src, uint8_t* pinned, size_t n, cudaStream_t s);
+// device -> host the same way, into pageable memory
+cudaError_t download_pipelined(Ctx& c, void* host_dst, const void* dev_src, uint8_t* pinned, size_t n, cudaStream_t s);
 
 // Named slots of Ctx::b.
 enum Slot : int {
@@ -33,7 +41,7 @@ enum Slot : int {
     // apply
     S_A_TENS, S_A_GROUPS, S_A_TABLES, S_A_SYMS, S_A_PAYLOAD, S_A_BB, S_A_BOFF, S_A_GAPS, S_A_ZZ, S_A_BSUM,
     S_A_LOCAL, S_A_CADDR, S_A_CVAL, S_A_HS, S_A_TOT, S_A_CHUNK_ROWS, S_A_CHUNK_SUMS, S_A_COUNTERS, S_A_SCAN_TMP,
-    S_CHK,
+    S_CHK, S_REC_POS, S_SUPER_T,
     S_NSLOTS
 };
 
@@ -42,6 +50,8 @@ struct ProfMark {
     cudaEvent_t a, b;
 };
 
+struct Encoded;
+
 struct Ctx {
     int device = 0;
     std::mutex mu;
@@ -49,20 +59,30 @@ struct Ctx {
     void* host = nullptr;       // pinned host staging (metadata both ways, payload down)
     size_t host_cap = 0;
     uint64_t* small = nullptr;  // fixed pinned words for counters and verdicts (never moves)
+    DevBuf out_host;            // pinned: block table + payload of the last encode (see Encoded)
+    DevBuf in_host;             // pinned: block table + payload of the update being applied
+    Encoded* live = nullptr;    // the encode result still reading out_host, if any
     uint64_t launches = 0;      // kernels launched by this context since creation
     // optional per-kernel timing with CUDA events on the caller's stream
     bool profile = false;
+    bool trace = false;         // CRUKX_B200_TRACE=1: synchronize after every kernel and log its time
     std::vector<cudaEvent_t> ev_pool;
     size_t ev_used = 0;
     std::vector<ProfMark> marks;
+    double phase_t = 0.0;
+    std::vector<cudaEvent_t> copy_ev;   // chunk events of the pipelined host <-> device copies
     ~Ctx();
 };
+
+// Host-phase timestamps on stderr while tracing (CRUKX_B200_TRACE=1); no synchronisation.
+void trace_phase(Ctx& c, const char* name);
 
 // Brackets one kernel launch: counts it and, while profiling is on, records events around it.
 struct KernelScope {
     Ctx& c;
     cudaStream_t s;
     ProfMark m{nullptr, nullptr, nullptr};
+    double t0 = 0.0;
     KernelScope(Ctx& ctx, const char* name, cudaStream_t st);
     ~KernelScope();
 };

@@ -60,19 +60,84 @@ __device__ __forceinline__ int64_t group_of(const uint64_t* __restrict__ start, 
 }
 
 // ------------------------------------------------------------------ k_enc_rank
+//
+// Stable rank by old exponent without a sort and without per-element warp matching: every lane
+// walks its own contiguous run of 32 elements with private counters (one per exponent of a
+// 16-exponent window ending at the sub-tile's largest exponent), so an element's rank is
+//   running total of earlier sub-tiles + earlier warps + earlier lanes of its warp + its own count.
+// Elements below the window (zeros, tiny weights) take a side path with warp matching, in index
+// order; a sub-tile with too many changes for the record buffers is re-ranked by matching.
+
+constexpr int ER_THREADS = 256;
+constexpr int ER_WARPS = ER_THREADS / 32;
+constexpr int ER_SUB = 8192;                 // elements per sub-tile
+constexpr int ER_SPAN = ER_SUB / ER_WARPS;   // 1024 per warp
+constexpr int ER_RUN = ER_SPAN / 32;         // 32 per lane
+constexpr int WIN = 16;                      // exponents counted in registers-of-shared-memory per lane
+constexpr int WREC = 128;                    // in-window change records per warp (12.5% of its span)
+constexpr int OREC = 32;                     // out-of-window change records per warp
+static_assert(ER_SUB * 32 == SUPER_N, "32 sub-tiles per super-tile");
+
+__device__ __forceinline__ int pidx(int i) { return i + (i >> 5); }   // one pad word per 32: no bank conflicts
 
 struct RankSmem {
-    uint32_t tile[SUB_N];                 // prev | cur << 16
-    uint16_t cntA[RANK_WARPS][256];       // per-warp counts, then per-warp exclusive bases
-    uint16_t cntC[RANK_WARPS][256];
-    uint32_t runA[256], runC[256];        // super-tile running totals (ranks local to the super-tile)
-    uint32_t totA[256], totC[256];
-    uint32_t wchg[RANK_WARPS], wbase[RANK_WARPS];
+    uint32_t tile[ER_SUB + ER_SUB / 32];  // prev | cur << 16, padded layout
+    uint32_t cnt[ER_WARPS][WIN][33];      // per-lane counts A | C << 16, then exclusive prefixes over lanes
+    uint32_t ocnt[ER_WARPS][256];         // per-warp counts A | C << 16 of out-of-window elements, then warp bases
+    uint32_t wwin[ER_WARPS][WIN];         // per-warp window totals, then exclusive bases over warps
+    uint32_t rec[ER_WARPS][WREC];         // span index << 16 | window row << 12 | own count A << 6 | own count C
+    uint64_t orec[ER_WARPS][OREC];        // span index | exponent << 10 | warp rank A << 18 | warp rank C << 29
+    uint32_t runA[256], runC[256];        // super-tile running totals
+    uint32_t tot[256];                    // this sub-tile's totals A | C << 16
+    uint32_t cstart[256];                 // exclusive scan of the changed totals: records sorted by exponent
+    uint32_t nrec[ER_WARPS], norec[ER_WARPS], oow[ER_WARPS], wbase[ER_WARPS];
     unsigned long long rec_base;
-    uint64_t red[RANK_WARPS];
+    int emax, dense;
+    uint64_t red[ER_WARPS];
 };
 
-__global__ void __launch_bounds__(RANK_THREADS, 2)
+__device__ __forceinline__ void put_record(uint64_t* rec_key, uint32_t* rec_val, uint64_t rec_cap, uint64_t j, int64_t s,
+                                           uint32_t rankA, uint32_t rankC, uint32_t x) {
+    if (j < rec_cap) {
+        rec_key[j] = (uint64_t(s) << 36) | (uint64_t(rankA) << 18) | uint64_t(rankC);
+        rec_val[j] = x;
+    }
+}
+
+// (new - old) * w(position), the change's term of the checksum delta (codec.py:325)
+__device__ __forceinline__ uint64_t change_delta(uint32_t x, int64_t pos) {
+    return (uint64_t(x >> 16) - uint64_t(x & 0xFFFFu)) * splitmix_weight(uint64_t(pos));
+}
+
+// warp_rank with counters packed as A | C << 16: adds to the half selected by `shift`
+__device__ __forceinline__ uint32_t warp_rank_packed(uint32_t* cnt, uint32_t key, bool act, int shift, uint32_t lt, int lane) {
+    const uint32_t peers = __match_any_sync(0xffffffffu, act ? key : 0x100u + uint32_t(lane));
+    const int leader = __ffs(peers) - 1;
+    uint32_t base = 0;
+    if (act && lane == leader) base = atomicAdd(&cnt[key], uint32_t(__popc(peers)) << shift);
+    base = __shfl_sync(0xffffffffu, base, leader);
+    return ((base >> shift) & 0xFFFFu) + __popc(peers & lt);
+}
+
+__device__ __forceinline__ bool changed_bits(uint32_t x) { return ((x ^ (x >> 16)) & 0xFFFFu) != 0; }
+
+// warp 0: cstart[e] = number of this sub-tile's changed elements with a smaller exponent, so each
+// sub-tile's records land sorted by (exponent, rank) and k_place writes runs of consecutive changes
+__device__ __forceinline__ void scan_change_starts(const uint32_t* tot, uint32_t* cstart, int lane) {
+    uint32_t v[8], sum = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) { v[k] = tot[lane * 8 + k] >> 16; sum += v[k]; }
+    uint32_t incl = sum;
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    uint32_t run = incl - sum;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) { cstart[lane * 8 + k] = run; run += v[k]; }
+}
+
+__global__ void __launch_bounds__(ER_THREADS, 3)
 k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_key, uint32_t* __restrict__ rec_val,
            uint64_t rec_cap, unsigned long long* __restrict__ counters, uint32_t* __restrict__ HS,
            uint32_t* __restrict__ CS, unsigned long long* __restrict__ chk_delta, unsigned long long* __restrict__ chk_full) {
@@ -81,131 +146,228 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
     const int64_t s = blockIdx.x;
     const int t = tensor_of_super(T, nT, s);
     const EncTensor tt = T[t];
-    const int64_t s_local = s - tt.super_begin;
-    const int64_t e_begin = s_local * SUPER_N;
-    const int64_t e_end = min(tt.numel, e_begin + SUPER_N);
+    const int64_t e_begin = (s - tt.super_begin) * SUPER_N;
+    const int64_t e_end = tmin(tt.numel, e_begin + SUPER_N);
     const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
     const uint32_t lt = lanemask_lt();
-    uint64_t delta = 0, full = 0;
+    const int span0 = w * ER_SPAN;
+    uint64_t full = 0, delta = 0;   // checksum of cur (no cache) / checksum delta of the changes
 
-    if (tid < 256) { S.runA[tid] = 0; S.runC[tid] = 0; }
+    S.runA[tid] = 0;
+    S.runC[tid] = 0;
+    if (tid == 0) { S.emax = 0; S.dense = 0; }
+    __syncthreads();
 
-    for (int64_t base = e_begin; base < e_end; base += SUB_N) {
-        const int n = int(tmin<int64_t>(SUB_N, e_end - base));
+    for (int64_t base = e_begin; base < e_end; base += ER_SUB) {
+        const int n = int(tmin<int64_t>(ER_SUB, e_end - base));
         const int16_t* pp = tt.prev + base;
         const int16_t* cp = tt.cur + base;
-        // ---- stage prev|cur into shared memory (128-bit streaming loads when aligned)
-        if (n == SUB_N && ((reinterpret_cast<uintptr_t>(pp) | reinterpret_cast<uintptr_t>(cp)) & 15) == 0) {
+        // ---- stage prev|cur (padded) and find the largest old exponent
+        uint32_t mx = 0;
+        if (n == ER_SUB && ((reinterpret_cast<uintptr_t>(pp) | reinterpret_cast<uintptr_t>(cp)) & 15) == 0) {
             const uint4* pv = reinterpret_cast<const uint4*>(pp);
             const uint4* cv = reinterpret_cast<const uint4*>(cp);
 #pragma unroll
-            for (int k = 0; k < SUB_N / 8 / RANK_THREADS; ++k) {
-                const int v = tid + k * RANK_THREADS;
+            for (int k = 0; k < ER_SUB / 8 / ER_THREADS; ++k) {
+                const int v = tid + k * ER_THREADS;
                 const uint4 a = __ldcs(pv + v);
                 const uint4 b = __ldcs(cv + v);
-                uint4* dst = reinterpret_cast<uint4*>(S.tile + 8 * v);
-                dst[0] = make_uint4(__byte_perm(a.x, b.x, 0x5410), __byte_perm(a.x, b.x, 0x7632),
-                                    __byte_perm(a.y, b.y, 0x5410), __byte_perm(a.y, b.y, 0x7632));
-                dst[1] = make_uint4(__byte_perm(a.z, b.z, 0x5410), __byte_perm(a.z, b.z, 0x7632),
-                                    __byte_perm(a.w, b.w, 0x5410), __byte_perm(a.w, b.w, 0x7632));
+                const uint32_t wd[8] = {__byte_perm(a.x, b.x, 0x5410), __byte_perm(a.x, b.x, 0x7632),
+                                        __byte_perm(a.y, b.y, 0x5410), __byte_perm(a.y, b.y, 0x7632),
+                                        __byte_perm(a.z, b.z, 0x5410), __byte_perm(a.z, b.z, 0x7632),
+                                        __byte_perm(a.w, b.w, 0x5410), __byte_perm(a.w, b.w, 0x7632)};
+                const int p = pidx(8 * v);
+#pragma unroll
+                for (int h = 0; h < 8; ++h) {
+                    S.tile[p + h] = wd[h];
+                    mx = tmax(mx, (wd[h] >> 7) & 0xFFu);
+                    if (tt.want_full) full += uint64_t(wd[h] >> 16) * splitmix_weight(uint64_t(base + 8 * v + h));
+                }
             }
         } else {
-            for (int i = tid; i < n; i += RANK_THREADS)
-                S.tile[i] = uint32_t(uint16_t(pp[i])) | (uint32_t(uint16_t(cp[i])) << 16);
-        }
-        for (int k = tid; k < RANK_WARPS * 256; k += RANK_THREADS) {
-            (&S.cntA[0][0])[k] = 0;
-            (&S.cntC[0][0])[k] = 0;
-        }
-        __syncthreads();
-
-        // ---- pass 1: per-warp counts per exponent (all elements, changed elements)
-        uint32_t wc = 0;
-        for (int c = 0; c < CHUNKS_PER_WARP; ++c) {
-            const int i0 = w * WARP_SPAN + c * 32;
-            if (i0 >= n) break;
-            const int i = i0 + lane;
-            const bool act = i < n;
-            const uint32_t x = act ? S.tile[i] : 0u;
-            const uint32_t e = (x >> 7) & 0xFFu;
-            const uint32_t peers = __match_any_sync(FULL, act ? e : 0x100u + lane);
-            const bool ch = act && ((x & 0xFFFFu) != (x >> 16));
-            const uint32_t chb = __ballot_sync(FULL, ch);
-            if (act && (peers & lt) == 0) {
-                S.cntA[w][e] += uint16_t(__popc(peers));
-                S.cntC[w][e] += uint16_t(__popc(peers & chb));
+            for (int i = tid; i < n; i += ER_THREADS) {
+                const uint32_t x = uint32_t(uint16_t(pp[i])) | (uint32_t(uint16_t(cp[i])) << 16);
+                S.tile[pidx(i)] = x;
+                mx = tmax(mx, (x >> 7) & 0xFFu);
+                if (tt.want_full) full += uint64_t(x >> 16) * splitmix_weight(uint64_t(base + i));
             }
-            if (ch) {
-                const uint64_t gi = uint64_t(base + i);
-                delta += (uint64_t(x >> 16) - uint64_t(x & 0xFFFFu)) * splitmix_weight(gi);
-            }
-            if (tt.want_full && act) full += uint64_t(x >> 16) * splitmix_weight(uint64_t(base + i));
-            wc += __popc(chb);
-            __syncwarp();
         }
-        if (lane == 0) S.wchg[w] = wc;
+        mx = __reduce_max_sync(FULL, mx);
+        if (lane == 0) atomicMax(&S.emax, int(mx));
+        for (int k = tid; k < ER_WARPS * WIN * 33; k += ER_THREADS) (&S.cnt[0][0][0])[k] = 0;
+        for (int k = tid; k < ER_WARPS * 256; k += ER_THREADS) (&S.ocnt[0][0])[k] = 0;
+        if (tid < ER_WARPS) { S.nrec[tid] = 0; S.norec[tid] = 0; S.oow[tid] = 0; }
         __syncthreads();
+        const int ebase = tmax(S.emax - (WIN - 1), 0);
+        const int span_n = tmax(0, tmin(ER_SPAN, n - span0));
 
-        // ---- per exponent: exclusive bases over warps; per tile: record slots
-        if (tid < 256) {
-            uint32_t a = 0, cc = 0;
-            for (int ww = 0; ww < RANK_WARPS; ++ww) {
-                const uint32_t va = S.cntA[ww][tid], vc = S.cntC[ww][tid];
-                S.cntA[ww][tid] = uint16_t(a);
-                S.cntC[ww][tid] = uint16_t(cc);
-                a += va;
-                cc += vc;
-            }
-            S.totA[tid] = a;
-            S.totC[tid] = cc;
-        } else if (tid == 256) {
-            uint32_t r = 0;
-            for (int ww = 0; ww < RANK_WARPS; ++ww) { S.wbase[ww] = r; r += S.wchg[ww]; }
-            S.rec_base = r ? atomicAdd(&counters[0], (unsigned long long)r) : 0ull;
-        }
-        __syncthreads();
-
-        // ---- pass 2: ranks of changed elements -> records
-        if (S.wchg[w]) {
-            uint32_t rc = S.wbase[w];
-            const uint32_t rend = rc + S.wchg[w];
-            const uint64_t rbase = S.rec_base;
-            for (int c = 0; c < CHUNKS_PER_WARP && rc < rend; ++c) {
-                const int i = w * WARP_SPAN + c * 32 + lane;
-                const bool act = i < n;
-                const uint32_t x = act ? S.tile[i] : 0u;
-                const uint32_t e = (x >> 7) & 0xFFu;
-                const uint32_t peers = __match_any_sync(FULL, act ? e : 0x100u + lane);
-                const bool ch = act && ((x & 0xFFFFu) != (x >> 16));
-                const uint32_t chb = __ballot_sync(FULL, ch);
-                if (ch) {
-                    const uint32_t rankA = S.runA[e] + S.cntA[w][e] + __popc(peers & lt);
-                    const uint32_t rankC = S.runC[e] + S.cntC[w][e] + __popc(peers & chb & lt);
-                    const uint64_t j = rbase + rc + __popc(chb & lt);
-                    if (j < rec_cap) {
-                        rec_key[j] = (uint64_t(s) << 36) | (uint64_t(rankA) << 18) | uint64_t(rankC);
-                        rec_val[j] = x;
+        // ---- lane walk: private counters, in-window change records
+        {
+            const int r0 = lane * ER_RUN;
+            const int vn = tmax(0, tmin(ER_RUN, span_n - r0));
+            const int pb = pidx(span0 + r0);
+            uint32_t* myc = &S.cnt[w][0][lane];
+            bool any_oow = false;
+            for (int k = 0; k < vn; ++k) {
+                const uint32_t x = S.tile[pb + k];
+                const int d = int((x >> 7) & 0xFFu) - ebase;
+                const bool ch = changed_bits(x);
+                if (unsigned(d) < unsigned(WIN)) {
+                    const uint32_t c = myc[d * 33];
+                    if (ch) {
+                        const uint32_t slot = atomicAdd(&S.nrec[w], 1u);
+                        if (slot < WREC)
+                            S.rec[w][slot] = (uint32_t(r0 + k) << 16) | (uint32_t(d) << 12) | ((c & 0xFFFFu) << 6) | (c >> 16);
                     }
+                    myc[d * 33] = c + (ch ? 0x10001u : 1u);
+                } else {
+                    any_oow = true;
                 }
-                rc += __popc(chb);
-                __syncwarp();
-                if (act && (peers & lt) == 0) {
-                    S.cntA[w][e] += uint16_t(__popc(peers));
-                    S.cntC[w][e] += uint16_t(__popc(peers & chb));
+            }
+            if (any_oow) atomicOr(&S.oow[w], 1u << lane);
+        }
+        __syncwarp();
+        // ---- out-of-window elements, run by run in index order (rare)
+        for (uint32_t m = S.oow[w]; m; m &= m - 1) {
+            const int run = __ffs(m) - 1;
+            const int ii = run * ER_RUN + lane;
+            const bool valid = ii < span_n;
+            const uint32_t x = valid ? S.tile[pidx(span0 + ii)] : 0u;
+            const uint32_t e = (x >> 7) & 0xFFu;
+            const bool oow = valid && int(e) < ebase;
+            const bool ch = oow && changed_bits(x);
+            const uint32_t rA = warp_rank_packed(S.ocnt[w], e, oow, 0, lt, lane);
+            const uint32_t rC = warp_rank_packed(S.ocnt[w], e, ch, 16, lt, lane);
+            if (ch) {
+                const uint32_t slot = atomicAdd(&S.norec[w], 1u);
+                if (slot < OREC)
+                    S.orec[w][slot] = uint64_t(ii) | (uint64_t(e) << 10) | (uint64_t(rA) << 18) | (uint64_t(rC) << 29);
+            }
+        }
+        // ---- lane prefixes: lane d scans window row d (rows are padded to 33 words)
+        if (lane < WIN) {
+            uint32_t run = 0;
+            for (int col = 0; col < 32; ++col) {
+                const uint32_t v = S.cnt[w][lane][col];
+                S.cnt[w][lane][col] = run;
+                run += v;
+            }
+            S.wwin[w][lane] = run;
+        }
+        __syncthreads();
+
+        // ---- warp bases per exponent, sub-tile totals, record slots
+        {
+            const int e = tid;
+            uint32_t o = 0;
+            for (int ww = 0; ww < ER_WARPS; ++ww) {
+                const uint32_t v = S.ocnt[ww][e];
+                S.ocnt[ww][e] = o;
+                o += v;
+            }
+            const int d = e - ebase;
+            if (unsigned(d) < unsigned(WIN)) {
+                uint32_t a = 0;
+                for (int ww = 0; ww < ER_WARPS; ++ww) {
+                    const uint32_t v = S.wwin[ww][d];
+                    S.wwin[ww][d] = a;
+                    a += v;
                 }
-                __syncwarp();
+                o += a;
+            }
+            S.tot[e] = o;
+            if (tid == 0) {
+                uint32_t r = 0;
+                int dense = 0;
+                for (int ww = 0; ww < ER_WARPS; ++ww) {
+                    S.wbase[ww] = r;
+                    r += S.nrec[ww] + S.norec[ww];
+                    dense |= S.nrec[ww] > WREC || S.norec[ww] > OREC;
+                }
+                S.dense = dense;
+                S.rec_base = r ? atomicAdd(&counters[0], (unsigned long long)r) : 0ull;
             }
         }
         __syncthreads();
-        if (tid < 256) { S.runA[tid] += S.totA[tid]; S.runC[tid] += S.totC[tid]; }
+        if (w == 0) scan_change_starts(S.tot, S.cstart, lane);
+        __syncthreads();
+
+        if (!S.dense) {
+            const uint64_t rb = S.rec_base;
+            const uint32_t nr = S.nrec[w];
+            for (uint32_t k = lane; k < nr; k += 32) {
+                const uint32_t r = S.rec[w][k];
+                const int ii = int(r >> 16), d = int((r >> 12) & 15u);
+                const uint32_t e = uint32_t(ebase + d);
+                const uint32_t lp = S.cnt[w][d][ii >> 5], wb = S.wwin[w][d];
+                const uint32_t x = S.tile[pidx(span0 + ii)];
+                const uint32_t rc = (wb >> 16) + (lp >> 16) + (r & 63u);   // rank among the sub-tile's changes
+                put_record(rec_key, rec_val, rec_cap, rb + S.cstart[e] + rc, s,
+                           S.runA[e] + (wb & 0xFFFFu) + (lp & 0xFFFFu) + ((r >> 6) & 63u), S.runC[e] + rc, x);
+                delta += change_delta(x, base + span0 + ii);
+            }
+            const uint32_t no = S.norec[w];
+            for (uint32_t k = lane; k < no; k += 32) {
+                const uint64_t q = S.orec[w][k];
+                const int ii = int(q & 1023u);
+                const uint32_t e = uint32_t(q >> 10) & 0xFFu;
+                const uint32_t wb = S.ocnt[w][e];
+                const uint32_t x = S.tile[pidx(span0 + ii)];
+                const uint32_t rc = (wb >> 16) + (uint32_t(q >> 29) & 2047u);
+                put_record(rec_key, rec_val, rec_cap, rb + S.cstart[e] + rc, s,
+                           S.runA[e] + (wb & 0xFFFFu) + (uint32_t(q >> 18) & 2047u), S.runC[e] + rc, x);
+                delta += change_delta(x, base + span0 + ii);
+            }
+        } else {
+            // ---- too many changes for the buffers: count per warp and exponent, then rank again
+            for (int k = tid; k < ER_WARPS * 256; k += ER_THREADS) (&S.ocnt[0][0])[k] = 0;
+            __syncthreads();
+            for (int c = 0; c * 32 < span_n; ++c) {
+                const int ii = c * 32 + lane;
+                const bool valid = ii < span_n;
+                const uint32_t x = valid ? S.tile[pidx(span0 + ii)] : 0u;
+                const uint32_t e = (x >> 7) & 0xFFu;
+                warp_rank_packed(S.ocnt[w], e, valid, 0, lt, lane);
+                warp_rank_packed(S.ocnt[w], e, valid && changed_bits(x), 16, lt, lane);
+            }
+            __syncthreads();
+            {
+                uint32_t o = 0;
+                for (int ww = 0; ww < ER_WARPS; ++ww) {
+                    const uint32_t v = S.ocnt[ww][tid];
+                    S.ocnt[ww][tid] = o;
+                    o += v;
+                }
+                S.tot[tid] = o;
+            }
+            __syncthreads();
+            if (w == 0) scan_change_starts(S.tot, S.cstart, lane);
+            __syncthreads();
+            const uint64_t rb = S.rec_base;
+            for (int c = 0; c * 32 < span_n; ++c) {
+                const int ii = c * 32 + lane;
+                const bool valid = ii < span_n;
+                const uint32_t x = valid ? S.tile[pidx(span0 + ii)] : 0u;
+                const uint32_t e = (x >> 7) & 0xFFu;
+                const bool ch = valid && changed_bits(x);
+                const uint32_t rA = warp_rank_packed(S.ocnt[w], e, valid, 0, lt, lane);
+                const uint32_t rC = warp_rank_packed(S.ocnt[w], e, ch, 16, lt, lane);
+                if (ch) {
+                    put_record(rec_key, rec_val, rec_cap, rb + S.cstart[e] + rC, s, S.runA[e] + rA, S.runC[e] + rC, x);
+                    delta += change_delta(x, base + span0 + ii);
+                }
+            }
+        }
+        __syncthreads();
+        S.runA[tid] += S.tot[tid] & 0xFFFFu;
+        S.runC[tid] += S.tot[tid] >> 16;
+        if (tid == 0) { S.emax = 0; S.dense = 0; }
         __syncthreads();
     }
-    if (tid < 256) {
-        HS[s * 256 + tid] = S.runA[tid];
-        CS[s * 256 + tid] = S.runC[tid];
-    }
-    block_add_u64<RANK_THREADS>(delta, &chk_delta[t], S.red);
-    if (tt.want_full) block_add_u64<RANK_THREADS>(full, &chk_full[t], S.red);
+    HS[s * 256 + tid] = S.runA[tid];
+    CS[s * 256 + tid] = S.runC[tid];
+    block_add_u64<ER_THREADS>(delta, &chk_delta[t], S.red);
+    if (tt.want_full) block_add_u64<ER_THREADS>(full, &chk_full[t], S.red);
 }
 
 // ------------------------------------------------------------------ groups in reference order
@@ -248,7 +410,7 @@ __device__ __forceinline__ uint64_t block_scan_u64(uint64_t v, uint64_t* sh, uin
 
 // Groups are the (tensor, exponent) cells with changes, tensors in caller order, exponents
 // ascending (codec.py:146, :317-323): one CTA scans the cells.
-__global__ void __launch_bounds__(1024) k_groups(const uint64_t* __restrict__ GC, int64_t n_cells, int32_t* __restrict__ gidx,
+__global__ void __launch_bounds__(1024) k_groups(const uint64_t* __restrict__ GC, int64_t n_cells, uint64_t* __restrict__ gcell,
                                                  int32_t* __restrict__ g_tensor, int32_t* __restrict__ g_exp,
                                                  uint64_t* __restrict__ g_start, uint64_t* __restrict__ g_count,
                                                  unsigned long long* __restrict__ counters) {
@@ -267,13 +429,13 @@ __global__ void __launch_bounds__(1024) k_groups(const uint64_t* __restrict__ GC
         if (cell < n_cells) {
             if (f) {
                 const uint32_t g = gbase + exf;
-                gidx[cell] = int32_t(g);
+                gcell[cell] = cbase + exc;
                 g_tensor[g] = int32_t(cell >> 8);
                 g_exp[g] = int32_t(cell & 255);
                 g_start[g] = cbase + exc;
                 g_count[g] = cnt;
             } else {
-                gidx[cell] = -1;
+                gcell[cell] = ~0ull;
             }
         }
         gbase += nf;
@@ -286,28 +448,30 @@ __global__ void __launch_bounds__(1024) k_groups(const uint64_t* __restrict__ GC
     }
 }
 
-// records (any order) -> changes in group order
-__global__ void __launch_bounds__(256) k_place(const EncTensor* __restrict__ T, int nT, const uint64_t* __restrict__ rec_key,
-                                               const uint32_t* __restrict__ rec_val, uint64_t n_rec,
-                                               const uint32_t* __restrict__ HSP, const uint32_t* __restrict__ CSP,
-                                               const int32_t* __restrict__ gidx, const uint64_t* __restrict__ g_start,
-                                               uint32_t* __restrict__ local, uint32_t* __restrict__ vals,
-                                               uint64_t total, unsigned long long* __restrict__ counters) {
-    const uint64_t j = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+// records -> changes in group order.  Each sub-tile's records are sorted by (exponent, rank), so
+// consecutive lanes mostly write consecutive destinations.
+__global__ void __launch_bounds__(256) k_place(const uint64_t* __restrict__ rec_key, const uint32_t* __restrict__ rec_val,
+                                               uint64_t n_rec, const uint32_t* __restrict__ HSP,
+                                               const uint32_t* __restrict__ CSP, const uint64_t* __restrict__ gcell,
+                                               const int32_t* __restrict__ super_t, uint32_t* __restrict__ local,
+                                               uint32_t* __restrict__ vals, uint64_t total,
+                                               unsigned long long* __restrict__ counters) {
+    const uint64_t j = uint64_t(blockIdx.x) * 256 + threadIdx.x;
     if (j >= n_rec) return;
     const uint64_t key = rec_key[j];
     const uint32_t x = rec_val[j];
     const int64_t s = int64_t(key >> 36);
-    const uint32_t rankA = uint32_t(key >> 18) & 0x3FFFFu;
-    const uint32_t rankC = uint32_t(key) & 0x3FFFFu;
     const int e = exp_of(x & 0xFFFFu);
-    const int t = tensor_of_super(T, nT, s);
-    const int32_t g = gidx[int64_t(t) * 256 + e];
-    if (g < 0) { atomicOr(&counters[1], (unsigned long long)ERR_INTERNAL); return; }
-    const uint64_t dest = g_start[g] + CSP[s * 256 + e] + rankC;
-    if (dest >= total) { atomicOr(&counters[1], (unsigned long long)ERR_INTERNAL); return; }
-    local[dest] = HSP[s * 256 + e] + rankA;
-    vals[dest] = x;
+    const int t = super_t[s];
+    const uint32_t csp = CSP[s * 256 + e], hsp = HSP[s * 256 + e];
+    const uint64_t gs = gcell[int64_t(t) * 256 + e];
+    const uint64_t dest = gs == ~0ull ? total : gs + csp + (uint32_t(key) & 0x3FFFFu);
+    if (dest < total) {
+        local[dest] = hsp + (uint32_t(key >> 18) & 0x3FFFFu);
+        vals[dest] = x;
+    } else {
+        atomicOr(&counters[1], (unsigned long long)ERR_INTERNAL);
+    }
 }
 
 // floor(log2(max(mean gap, 1))) clamped to [0, 30], by exact integer comparison: the mean is
@@ -337,7 +501,10 @@ struct StatsSmem {
     int64_t g0;
 };
 
-// Rice candidate costs sum((gap >> c) + 1 + c) per group and (exponent, zigzag) counts
+// Rice candidate costs sum((gap >> c) + 1 + c) per group (codec.py:274) and (exponent, zigzag)
+// symbol counts (codec.py:355-367).  Lanes take consecutive changes; each lane keeps its sums and
+// a packed count of the symbols 0..7 in registers while its group stays the same, so atomics are
+// needed only at group boundaries and for larger symbols.
 __global__ void __launch_bounds__(256) k_stats(const uint64_t* __restrict__ g_start, const int32_t* __restrict__ g_exp,
                                                const uint32_t* __restrict__ g_cand, int64_t ng, uint64_t total,
                                                const uint32_t* __restrict__ local, const uint32_t* __restrict__ vals,
@@ -346,6 +513,7 @@ __global__ void __launch_bounds__(256) k_stats(const uint64_t* __restrict__ g_st
     __shared__ StatsSmem S;
     const uint64_t j0 = uint64_t(blockIdx.x) * STATS_PER_CTA;
     const uint64_t j1 = tmin<uint64_t>(j0 + STATS_PER_CTA, total);
+    const int lane = threadIdx.x & 31;
     if (threadIdx.x == 0) S.g0 = group_of(g_start, ng, j0);
     for (int k = threadIdx.x; k < STATS_LOCAL_GROUPS * DENSE_SYM; k += blockDim.x) (&S.hist[0][0])[k] = 0;
     for (int k = threadIdx.x; k < STATS_LOCAL_GROUPS * 3; k += blockDim.x) (&S.cost[0][0])[k] = 0;
@@ -353,48 +521,59 @@ __global__ void __launch_bounds__(256) k_stats(const uint64_t* __restrict__ g_st
     const int64_t g0 = S.g0;
     if (threadIdx.x < STATS_LOCAL_GROUPS && g0 + threadIdx.x < ng) S.gexp[threadIdx.x] = g_exp[g0 + threadIdx.x];
     __syncthreads();
-    constexpr int PER = STATS_PER_CTA / 256;
-    const uint64_t a = j0 + uint64_t(threadIdx.x) * PER;
-    const uint64_t b = tmin<uint64_t>(a + PER, j1);
-    if (a < b) {
-        int64_t g = group_of(g_start, ng, a);
-        uint64_t gs = g_start[g], ge = g_start[g + 1];
-        uint32_t cand = g_cand[g];
-        int e = g_exp[g];
-        uint64_t acc0 = 0, acc1 = 0, acc2 = 0;
-        auto flush = [&]() {
-            const int64_t lg = g - g0;
-            if (lg < STATS_LOCAL_GROUPS) {
-                atomicAdd(&S.cost[lg][0], (unsigned long long)acc0);
-                atomicAdd(&S.cost[lg][1], (unsigned long long)acc1);
-                atomicAdd(&S.cost[lg][2], (unsigned long long)acc2);
-            } else {
-                atomicAdd(&costs[3 * g + 0], (unsigned long long)acc0);
-                atomicAdd(&costs[3 * g + 1], (unsigned long long)acc1);
-                atomicAdd(&costs[3 * g + 2], (unsigned long long)acc2);
+
+    int64_t g = -1;                    // this lane's current group and its register accumulators
+    uint64_t ge = 0, gs = 0, acc0 = 0, acc1 = 0, acc2 = 0, small = 0;
+    uint32_t cand = 0;
+    int e = 0;
+    auto flush = [&]() {
+        if (g < 0) return;
+        const int64_t lg = g - g0;
+        if (lg < STATS_LOCAL_GROUPS) {
+            if (acc0) atomicAdd(&S.cost[lg][0], (unsigned long long)acc0);
+            if (acc1) atomicAdd(&S.cost[lg][1], (unsigned long long)acc1);
+            if (acc2) atomicAdd(&S.cost[lg][2], (unsigned long long)acc2);
+            for (int z = 0; z < 8; ++z) {
+                const uint32_t c = uint32_t(small >> (8 * z)) & 0xFFu;
+                if (c) atomicAdd(&S.hist[lg][z], c);
             }
-            acc0 = acc1 = acc2 = 0;
-        };
-        uint32_t prev_local = a > gs ? local[a - 1] : 0;
-        for (uint64_t j = a; j < b; ++j) {
-            while (j >= ge) {
+        } else {
+            if (acc0) atomicAdd(&costs[3 * g + 0], (unsigned long long)acc0);
+            if (acc1) atomicAdd(&costs[3 * g + 1], (unsigned long long)acc1);
+            if (acc2) atomicAdd(&costs[3 * g + 2], (unsigned long long)acc2);
+            for (int z = 0; z < 8; ++z) {
+                const uint64_t c = (small >> (8 * z)) & 0xFFu;
+                if (c) atomicAdd(&dense_hist[e * DENSE_SYM + z], (unsigned long long)c);
+            }
+        }
+        acc0 = acc1 = acc2 = small = 0;
+    };
+    for (uint64_t jb = j0 + (threadIdx.x & ~31u); jb < j1; jb += blockDim.x) {
+        const uint64_t j = jb + lane;
+        const bool valid = j < j1;
+        const uint32_t loc = valid ? local[j] : 0u;
+        const uint32_t prevw = __shfl_up_sync(FULL, loc, 1);
+        if (valid) {
+            if (j >= ge) {
                 flush();
-                ++g;
+                g = g < 0 ? group_of(g_start, ng, j) : g + 1;
+                while (g_start[g + 1] <= j) ++g;
                 gs = g_start[g];
                 ge = g_start[g + 1];
                 cand = g_cand[g];
                 e = g_exp[g];
             }
-            const uint32_t loc = local[j];
-            const uint64_t gap = j == gs ? loc : uint64_t(loc) - prev_local - 1;
-            prev_local = loc;
+            const uint32_t prev = lane ? prevw : (j > gs ? local[j - 1] : 0u);
+            const uint64_t gap = j == gs ? loc : uint64_t(loc) - prev - 1;
             const uint32_t c0 = cand & 255, c1 = (cand >> 8) & 255, c2 = (cand >> 16) & 255;
             acc0 += (gap >> c0) + 1 + c0;
             acc1 += (gap >> c1) + 1 + c1;
             acc2 += (gap >> c2) + 1 + c2;
             const uint32_t z = zigzag_of(vals[j]);
-            const int64_t lg = g - g0;
-            if (z < DENSE_SYM) {
+            if (z < 8) {
+                small += 1ull << (8 * z);
+            } else if (z < DENSE_SYM) {
+                const int64_t lg = g - g0;
                 if (lg < STATS_LOCAL_GROUPS) atomicAdd(&S.hist[lg][z], 1u);
                 else atomicAdd(&dense_hist[e * DENSE_SYM + z], 1ull);
             } else {
@@ -402,8 +581,8 @@ __global__ void __launch_bounds__(256) k_stats(const uint64_t* __restrict__ g_st
                 if (!rare_flag[e]) rare_flag[e] = 1;
             }
         }
-        flush();
     }
+    flush();
     __syncthreads();
     for (int k = threadIdx.x; k < STATS_LOCAL_GROUPS * DENSE_SYM; k += blockDim.x) {
         const int lg = k / DENSE_SYM;
@@ -603,9 +782,17 @@ struct HostTables {
 Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* const* cur, const int64_t* numel,
                    const uint8_t* const* names, const int64_t* name_len, const uint64_t* cache_chk,
                    const uint8_t* has_cache, cudaStream_t st, Encoded* out, std::string* err) {
-    out->bytes.clear();
+    if (C.live) {           // an earlier result still reads the output buffers: give it its own copy
+        const cudaError_t de = C.live->detach();
+        C.live = nullptr;
+        if (de != cudaSuccess) { *err = std::string("detaching the previous update: ") + cudaGetErrorString(de); return kCudaError; }
+    }
+    out->ctx = &C;
+    out->head.clear();
+    out->len_varint.assign(1, 0);
     out->checksums.assign(size_t(nT), 0);
     out->present.assign(size_t(nT), 0);
+    trace_phase(C, "encode: start");
     // ---- tensor descriptors
     std::vector<EncTensor> T;
     std::vector<int> tmap;  // index into caller arrays
@@ -625,9 +812,9 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
         tmap.push_back(t);
     }
     const int nt = int(T.size());
-    auto empty_update = [&]() {
-        static const uint8_t kEmpty[8] = {'C', 'R', 'X', 'S', 2, 0, 0, 0};
-        out->bytes.assign(kEmpty, kEmpty + 8);
+    auto empty_update = [&]() {   // "CRXS" 2, no tables, no tensors, payload_len 0
+        static const uint8_t kEmpty[7] = {'C', 'R', 'X', 'S', 2, 0, 0};
+        out->head.assign(kEmpty, kEmpty + 7);
         return kOk;
     };
     if (nt == 0) return empty_update();
@@ -652,7 +839,8 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     CRX_CUDA(ensure_dev(C.b[S_TOTALS_C], sizeof(uint64_t) * cells, st));
     CRX_CUDA(ensure_dev(C.b[S_COUNTERS], sizeof(uint64_t) * 16, st));
     CRX_CUDA(ensure_dev(C.b[S_CHK], sizeof(uint64_t) * 2 * size_t(nt), st));
-    CRX_CUDA(ensure_dev(C.b[S_GIDX], sizeof(int32_t) * cells, st));
+    CRX_CUDA(ensure_dev(C.b[S_GIDX], sizeof(uint64_t) * cells, st));
+    CRX_CUDA(ensure_dev(C.b[S_SUPER_T], sizeof(int32_t) * size_t(n_super), st));
     // groups: tensor, exp (i32), start (cells+1), count, cand (u32), costs (3 u64), rice (u8), block start
     CRX_CUDA(ensure_dev(C.b[S_GROUPS], (4 + 4 + 8 + 8 + 4 + 24 + 1 + 8) * (cells + 1) + 64, st));
     int64_t total_el = 0;
@@ -663,7 +851,8 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     CRX_CUDA(ensure_dev(C.b[S_REC_VAL], sizeof(uint32_t) * want_cap, st));
     rec_cap = want_cap;
 
-    const size_t meta_bytes = sizeof(EncTensor) * size_t(nt) + sizeof(int64_t) * 2 * (size_t(nt) + 1);
+    const size_t meta_bytes = sizeof(EncTensor) * size_t(nt) + sizeof(int64_t) * 2 * (size_t(nt) + 1) +
+                              sizeof(int32_t) * size_t(n_super);
     CRX_CUDA(ensure_host(C, std::max<size_t>(meta_bytes, 1 << 20), st));
     {
         uint8_t* h = static_cast<uint8_t*>(C.host);
@@ -673,6 +862,10 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
         std::memcpy(rb, row_begin.data(), sizeof(int64_t) * (size_t(nt) + 1));
         std::memcpy(rb + nt + 1, chunk_begin.data(), sizeof(int64_t) * (size_t(nt) + 1));
         CRX_CUDA(cudaMemcpyAsync(C.b[S_CHUNK_ROWS].p, rb, sizeof(int64_t) * 2 * (size_t(nt) + 1), cudaMemcpyHostToDevice, st));
+        int32_t* stt = reinterpret_cast<int32_t*>(rb + 2 * (nt + 1));
+        for (int t = 0; t < nt; ++t)
+            for (int64_t s = row_begin[size_t(t)]; s < row_begin[size_t(t) + 1]; ++s) stt[s] = t;
+        CRX_CUDA(cudaMemcpyAsync(C.b[S_SUPER_T].p, stt, sizeof(int32_t) * size_t(n_super), cudaMemcpyHostToDevice, st));
     }
     const int64_t* d_row_begin = dev<int64_t>(C, S_CHUNK_ROWS);
     const int64_t* d_chunk_begin = d_row_begin + nt + 1;
@@ -687,7 +880,7 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
         CRX_CUDA(cudaMemsetAsync(counters, 0, sizeof(uint64_t) * 16, st));
         CRX_CUDA(cudaMemsetAsync(chk_delta, 0, sizeof(uint64_t) * 2 * size_t(nt), st));
         { KernelScope ks_(C, "k_enc_rank", st);
-        k_enc_rank<<<unsigned(n_super), RANK_THREADS, rank_smem, st>>>(
+        k_enc_rank<<<unsigned(n_super), ER_THREADS, rank_smem, st>>>(
             dev<EncTensor>(C, S_TENS), nt, dev<uint64_t>(C, S_REC_KEY), dev<uint32_t>(C, S_REC_VAL), rec_cap, counters,
             dev<uint32_t>(C, S_HS), dev<uint32_t>(C, S_CS), chk_delta, chk_full);
         }
@@ -701,6 +894,7 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
         rec_cap = need;
     }
     const uint64_t n_rec = hostc[0];
+    trace_phase(C, "encode: ranked (sync 1)");
     if (n_rec == 0) return empty_update();
 
     // ---- per tensor column scans and the group table
@@ -719,13 +913,14 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     auto* g_cand = reinterpret_cast<uint32_t*>(gb + 56 * gcap);
     auto* g_rice = reinterpret_cast<uint8_t*>(gb + 60 * gcap);
     { KernelScope ks_(C, "k_groups", st);
-    k_groups<<<1, 1024, 0, st>>>(dev<uint64_t>(C, S_TOTALS_C), int64_t(cells), dev<int32_t>(C, S_GIDX), g_tensor, g_exp,
+    k_groups<<<1, 1024, 0, st>>>(dev<uint64_t>(C, S_TOTALS_C), int64_t(cells), dev<uint64_t>(C, S_GIDX), g_tensor, g_exp,
                                 g_start, g_count, counters);
     }
     CRX_CUDA(cudaGetLastError());
     CRX_CUDA(cudaMemcpyAsync(hostc, counters, sizeof(uint64_t) * 4, cudaMemcpyDeviceToHost, st));
     CRX_CUDA(cudaStreamSynchronize(st));
     const int64_t ng = int64_t(hostc[2]);
+    trace_phase(C, "encode: groups (sync 2)");
     const uint64_t total = hostc[3];
     if (total != n_rec || (hostc[1] & ERR_INTERNAL)) { *err = "internal: change count mismatch"; return kCudaError; }
 
@@ -734,10 +929,9 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     auto* local = dev<uint32_t>(C, S_LOCAL);
     auto* vals = dev<uint32_t>(C, S_VALS);
     { KernelScope ks_(C, "k_place", st);
-    k_place<<<unsigned((n_rec + 255) / 256), 256, 0, st>>>(dev<EncTensor>(C, S_TENS), nt, dev<uint64_t>(C, S_REC_KEY),
-                                                           dev<uint32_t>(C, S_REC_VAL), n_rec, dev<uint32_t>(C, S_HS),
-                                                           dev<uint32_t>(C, S_CS), dev<int32_t>(C, S_GIDX), g_start, local,
-                                                           vals, total, counters);
+    k_place<<<unsigned((n_rec + 255) / 256), 256, 0, st>>>(dev<uint64_t>(C, S_REC_KEY), dev<uint32_t>(C, S_REC_VAL), n_rec,
+                                                           dev<uint32_t>(C, S_HS), dev<uint32_t>(C, S_CS), dev<uint64_t>(C, S_GIDX),
+                                                           dev<int32_t>(C, S_SUPER_T), local, vals, total, counters);
     }
     CRX_CUDA(cudaGetLastError());
     { KernelScope ks_(C, "k_r0", st);
@@ -793,6 +987,7 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     CRX_CUDA(cudaStreamSynchronize(st));
     std::vector<uint32_t> hcand(static_cast<size_t>(ng));
     std::memcpy(hcand.data(), h + off_cand, 4 * size_t(ng));
+    trace_phase(C, "encode: stats down (sync 3)");
     std::vector<int32_t> hg_tensor(static_cast<size_t>(ng)), hg_exp(static_cast<size_t>(ng));
     std::vector<uint64_t> hg_count(static_cast<size_t>(ng)), hcost(3 * static_cast<size_t>(ng)), hdense(256 * DENSE_SYM), hrb(256), hchk(2 * static_cast<size_t>(nt));
     std::vector<uint32_t> hrc(256);
@@ -849,6 +1044,7 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
         canonical_codes(tabs.len[e].data(), int64_t(ns), tabs.code[e].data());
     }
 
+    trace_phase(C, "encode: huffman (host)");
     // ---- upload rice, block starts, code tables
     std::vector<uint32_t> dense_code(256 * DENSE_SYM, 0);
     std::vector<uint64_t> rare_codes;
@@ -909,6 +1105,7 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     CRX_CUDA(cudaMemcpyAsync(hostc + 1, counters + 1, 8, cudaMemcpyDeviceToHost, st));
     CRX_CUDA(cudaStreamSynchronize(st));
     const uint64_t total_bits = hostc[0];
+    trace_phase(C, "encode: block bits (sync 4)");
     if (hostc[1] & ERR_BLOCK_TOO_LONG) {
         *err = "a block exceeds 2^32 bits; the update cannot be represented";
         return kValueError;
@@ -924,9 +1121,9 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     }
     CRX_CUDA(cudaGetLastError());
 
-    // ---- header (wire.py:64-89), block table and payload
-    std::vector<uint8_t>& ob = out->bytes;
-    ob.reserve(size_t(64 + 4 * n_blocks + payload_len) + 1024);
+    // ---- header (wire.py:64-89); block table and payload go to pinned memory in one pass each
+    std::vector<uint8_t>& ob = out->head;
+    ob.reserve(4096);
     const uint8_t magic[5] = {'C', 'R', 'X', 'S', 2};
     ob.insert(ob.end(), magic, magic + 5);
     int n_tables = 0;
@@ -968,20 +1165,22 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
             ob.push_back(rice[size_t(g)]);
         }
     }
-    const size_t bt_at = ob.size();
-    ob.resize(bt_at + 4 * size_t(n_blocks));
-    put_varint(ob, payload_len);
-    const size_t pl_at = ob.size();
-    ob.resize(pl_at + payload_len);
+    out->len_varint.clear();
+    put_varint(out->len_varint, payload_len);
+    out->n_blocks = n_blocks;
+    out->payload_len = payload_len;
     const size_t down2 = 4 * size_t(n_blocks) + payload_len;
-    CRX_CUDA(ensure_host(C, down2 + 16, st));
-    h = static_cast<uint8_t*>(C.host);
-    CRX_CUDA(cudaMemcpyAsync(h, C.b[S_BB32].p, 4 * size_t(n_blocks), cudaMemcpyDeviceToHost, st));
-    if (payload_len)
-        CRX_CUDA(cudaMemcpyAsync(h + 4 * size_t(n_blocks), C.b[S_PAYLOAD].p, payload_len, cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(ensure_pinned(C.out_host, down2 + 16, st));
+    uint8_t* oh = static_cast<uint8_t*>(C.out_host.p);
+    CRX_CUDA(cudaMemcpyAsync(oh, C.b[S_BB32].p, 4 * size_t(n_blocks), cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaMemcpyAsync(hostc + 2, counters + 1, 8, cudaMemcpyDeviceToHost, st));
     CRX_CUDA(cudaStreamSynchronize(st));
-    std::memcpy(ob.data() + bt_at, h, 4 * size_t(n_blocks));
-    std::memcpy(ob.data() + pl_at, h + 4 * size_t(n_blocks), payload_len);
+    trace_phase(C, "encode: packed (sync 5)");
+    if (hostc[2] & ERR_INTERNAL) { *err = "internal: encoder consistency check failed"; return kCudaError; }
+    out->stream = st;
+    out->table = oh;
+    out->dpay = static_cast<const uint8_t*>(C.b[S_PAYLOAD].p);
+    C.live = out;
     out->changes = total;
     return kOk;
 }

@@ -162,10 +162,29 @@ class ParsedUpdate:
             raise RuntimeError(f"crukx_sync_b200: parse failed ({st}): {err.value.decode(errors='replace')}")
         self._tensors = None
         self._tables = None
+        self._table = None
 
     @property
     def handle(self):
         return self._h
+
+    def tensor_table(self) -> list[tuple[str, int, int]]:
+        """(name, numel, checksum) of every tensor, in update order, in one call."""
+        if self._table is None:
+            L = _ext.load()
+            n = int(L.crx_update_n_tensors(self._h))
+            names = (ctypes.c_void_p * max(n, 1))()
+            lens = (ctypes.c_int64 * max(n, 1))()
+            numels = (ctypes.c_int64 * max(n, 1))()
+            chks = (ctypes.c_uint64 * max(n, 1))()
+            L.crx_update_tensor_table(self._h, names, lens, numels, chks)
+            self._table = [(ctypes.string_at(names[i], lens[i]).decode("utf-8"), int(numels[i]), int(chks[i]))
+                           for i in range(n)]
+        return self._table
+
+    @property
+    def n_tensors(self) -> int:
+        return int(_ext.load().crx_update_n_tensors(self._h))
 
     @property
     def tensors(self) -> list[TensorHeader]:

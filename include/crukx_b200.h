@@ -84,6 +84,9 @@ int64_t crx_update_changes(const crx_update* u);
 int crx_update_tensor(const crx_update* u, int64_t i, const uint8_t** name, int64_t* name_len, int64_t* numel,
                       uint64_t* checksum, int32_t* n_groups);
 int crx_update_group(const crx_update* u, int64_t i, int32_t k, int32_t* exponent, int64_t* count, int32_t* rice);
+/* All tensor headers at once (arrays of crx_update_n_tensors entries; any may be NULL). */
+int crx_update_tensor_table(const crx_update* u, const uint8_t** names, int64_t* name_lens, int64_t* numels,
+                            uint64_t* checksums);
 int32_t crx_update_n_tables(const crx_update* u);
 int crx_update_table(const crx_update* u, int32_t k, int32_t* exponent, int64_t* n_symbols);
 int crx_update_table_entries(const crx_update* u, int32_t k, uint32_t* symbols, uint8_t* lengths);

@@ -140,3 +140,16 @@ def test_empty_update_needs_no_device():
     from crukx_sync_b200 import apply_update
     st = apply_update({}, b"CRXS\x02\x00\x00\x00")
     assert (st.tensors, st.changed, st.bytes) == (0, 0, 8)
+
+
+@pytest.mark.timeout(60)
+def test_first_context_call_does_not_deadlock(lib, monkeypatch):
+    """context() before any load(): must return or raise, never block on its own lock."""
+    from crukx_sync_b200 import _ext
+    monkeypatch.setattr(_ext, "_lib", None)
+    monkeypatch.setattr(_ext, "_ctx", {})
+    if torch.cuda.is_available():
+        assert _ext.context(0)
+    else:
+        with pytest.raises(RuntimeError):
+            _ext.context(0)
