@@ -82,6 +82,9 @@ CONFIGS = {
                  name="qwen2.5-1.5b-shape"),
     "toy": dict(shapes=lambda: qwen_shapes(4, 1024, 16, 16, 64, 2816, 32768, tied=True, bias=False), lr=1e-6,
                 name="toy-4l-d1024"),
+    # two decoder layers of the 7B shape (0.47B params): the small case for ncu captures
+    "7b-2l": dict(shapes=lambda: qwen_shapes(2, 3584, 28, 4, 128, 18944, 152064, tied=True, bias=True) | {},
+                  lr=2e-6, name="qwen2.5-7b-shape-2-layers", drop_embed=True),
     "32b-tp8": dict(shapes=lambda: tp8_shard(qwen_shapes(64, 5120, 40, 8, 128, 27648, 152064, tied=False)), lr=1e-6,
                     name="qwen2.5-32b-shape-tp8-shard"),
 }
@@ -240,6 +243,8 @@ def run_ours(args, rank, world, dist):
     torch.cuda.set_device(dev)
     cfg = CONFIGS[args.config]
     shapes_all = cfg["shapes"]()
+    if cfg.get("drop_embed"):
+        shapes_all = {k: v for k, v in shapes_all.items() if "embed" not in k}
     owner = lpt_partition(shapes_all, world)
     shapes = {k: v for k, v in shapes_all.items() if owner[k] == rank}
     total_params = sum(int(torch.tensor(s).prod()) for s in shapes_all.values())
