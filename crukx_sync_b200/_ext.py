@@ -21,7 +21,7 @@ EXPORTS = [
     "crx_encoded_changes", "crx_encoded_checksums", "crx_encoded_free", "crx_parse", "crx_update_n_tensors",
     "crx_update_changes", "crx_update_tensor", "crx_update_group", "crx_update_tensor_table", "crx_update_n_tables", "crx_update_table",
     "crx_update_table_entries", "crx_update_n_blocks", "crx_update_block_bits", "crx_update_payload",
-    "crx_update_free", "crx_apply", "crx_huffman_lengths", "crx_checksum",
+    "crx_update_free", "crx_apply", "crx_huffman_lengths", "crx_checksum", "crx_checksum_noalloc",
 ]
 
 _lib = None
@@ -71,6 +71,7 @@ def load():
             "crx_apply": ([P, P, P, P, P, P, P, CP, SZ], ctypes.c_int),
             "crx_huffman_lengths": ([P, I64, P], ctypes.c_int),
             "crx_checksum": ([P, P, I64, P, P, CP, SZ], ctypes.c_int),
+            "crx_checksum_noalloc": ([P, I64, P, P, CP, SZ], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

@@ -113,6 +113,23 @@ int crx_huffman_lengths(const uint64_t* counts, int64_t n, uint8_t* lengths);
 /* Full checksum of n int16 elements on the device (src/crukx_sync/codec.py:61-68). */
 int crx_checksum(crx_ctx* ctx, const int16_t* data, int64_t n, void* stream, uint64_t* out, char* err, size_t errlen);
 
+/* The same checksum for callers that must not allocate device memory; no counterpart in the
+ * reference.  Examples: a serving process whose HBM is reserved up front for weights and
+ * KV-cache (a cudaMalloc in steady state fails or breaks the budget), code inside an allocator
+ * callback or out-of-memory handler (re-entering the allocator can deadlock), or a loop that must
+ * not stall other streams (cudaFree synchronizes the device).  It needs no crx_ctx, allocates
+ * nothing and does not synchronize: data (n int16 elements) and out (8 bytes, 8-byte aligned)
+ * are device memory on the current device, and the result is in *out once the work on `stream`
+ * is done.
+ *
+ * Limit: n <= CRX_CHECKSUM_NOALLOC_MAX (2^30 elements); larger n returns CRX_VALUE_ERROR — use
+ * crx_checksum.  Its scratch is one fixed 128 KiB device array per device: the first call on a
+ * device (with it current) looks the array up, which loads this library on that device, so make
+ * one call before capturing a stream.  Nothing has to start at zero.  Calls that overlap on one
+ * device (two streams or unordered host threads) race on the scratch; order them. */
+#define CRX_CHECKSUM_NOALLOC_MAX (INT64_C(1) << 30)
+int crx_checksum_noalloc(const int16_t* data, int64_t n, void* stream, uint64_t* out, char* err, size_t errlen);
+
 #ifdef __cplusplus
 }
 #endif
