@@ -90,18 +90,6 @@ CONFIGS = {
 }
 
 
-def lpt_partition(shapes, n):
-    """Deterministic longest-processing-time assignment of tensors to n ranks."""
-    order = sorted(shapes, key=lambda k: (-int(torch.tensor(shapes[k]).prod()), k))
-    load = [0] * n
-    owner = {}
-    for k in order:
-        r = min(range(n), key=lambda i: (load[i], i))
-        owner[k] = r
-        load[r] += int(torch.tensor(shapes[k]).prod())
-    return owner
-
-
 def make_states(shapes, lr, device, seed=0):
     """(prev, cur) bf16 dicts on `device` for one Adam-like step of the fp32 master weights."""
     g = torch.Generator(device=device).manual_seed(seed)
@@ -238,6 +226,7 @@ def log(*a):
 def run_ours(args, rank, world, dist):
     import crukx_sync_b200 as crx
     from crukx_sync_b200 import _ext
+    from crukx_sync_b200 import dist as cdist
 
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
     torch.cuda.set_device(dev)
@@ -245,7 +234,7 @@ def run_ours(args, rank, world, dist):
     shapes_all = cfg["shapes"]()
     if cfg.get("drop_embed"):
         shapes_all = {k: v for k, v in shapes_all.items() if "embed" not in k}
-    owner = lpt_partition(shapes_all, world)
+    owner = cdist.partition({k: int(torch.tensor(v).prod()) for k, v in shapes_all.items()}, world)
     shapes = {k: v for k, v in shapes_all.items() if owner[k] == rank}
     total_params = sum(int(torch.tensor(s).prod()) for s in shapes_all.values())
     my_params = sum(int(torch.tensor(s).prod()) for s in shapes.values())
@@ -265,19 +254,8 @@ def run_ours(args, rank, world, dist):
         torch.cuda.synchronize(dev)
 
     def exchange(upd: bytes):
-        """All-gather of the compressed payloads (NCCL); returns this rank's update from the gather."""
-        if dist is None:
-            return upd
-        n = torch.tensor([len(upd)], dtype=torch.int64, device=dev)
-        sizes = [torch.zeros_like(n) for _ in range(world)]
-        dist.all_gather(sizes, n)
-        mx = int(max(s.item() for s in sizes))
-        buf = torch.zeros(mx, dtype=torch.uint8, device=dev)
-        buf[: len(upd)].copy_(torch.frombuffer(bytearray(upd), dtype=torch.uint8))
-        out = torch.empty(world * mx, dtype=torch.uint8, device=dev)
-        dist.all_gather_into_tensor(out, buf)
-        mine = int(sizes[rank].item())
-        return out[rank * mx: rank * mx + mine].cpu().numpy().tobytes()
+        """All-gather of the compressed updates (NCCL); returns this rank's update from the gather."""
+        return cdist.allgather_updates(upd, ranks=[rank])[0]
 
     state = {"src": A, "dst": B}
 
