@@ -34,13 +34,35 @@ def _trace(what: str, t0: float) -> None:
         print(f"[crx-py] {what:<28} {1e3 * (time.perf_counter() - t0):9.3f} ms", file=sys.stderr, flush=True)
 
 
-def bits16(name: str, t) -> torch.Tensor:
-    """Flat int16 view of a bf16 (or int16 bit-pattern) tensor."""
-    if not isinstance(t, torch.Tensor) or t.dtype not in (torch.bfloat16, torch.int16):
+_BITS16 = (torch.bfloat16, torch.int16)
+
+
+def check16(name: str, t) -> None:
+    """The bits16 rules without building a view: bf16 or int16, contiguous."""
+    if not isinstance(t, torch.Tensor) or t.dtype not in _BITS16:
         raise ValueError(f"{name}: expected a bfloat16 or int16 torch tensor, got {getattr(t, 'dtype', type(t))}")
     if not t.is_contiguous():
         raise ValueError(f"{name}: tensor must be contiguous")
+
+
+def bits16(name: str, t) -> torch.Tensor:
+    """Flat int16 view of a bf16 (or int16 bit-pattern) tensor."""
+    check16(name, t)
     return t.view(torch.int16).view(-1)
+
+
+def _name_table(names):
+    """UTF-8 names as one buffer: (keep-alive, pointer array, length array)."""
+    raw = [n.encode("utf-8") for n in names]
+    blob = b"".join(raw) + b"\0"
+    base = ctypes.cast(ctypes.c_char_p(blob), ctypes.c_void_p).value
+    ptrs, lens, off = [], [], 0
+    for r in raw:
+        ptrs.append(base + off)
+        lens.append(len(r))
+        off += len(r)
+    k = max(len(raw), 1)
+    return blob, (ctypes.c_void_p * k)(*ptrs), (ctypes.c_int64 * k)(*lens)
 
 
 def _cuda_device(dev: torch.device) -> torch.device:
@@ -65,43 +87,46 @@ def _raise(status: int, err) -> None:
 def encode(old: Mapping[str, torch.Tensor], new: Mapping[str, torch.Tensor],
            checksums: dict | None = None) -> EncodedUpdate:
     """The encoded update (not yet bytes); ``.checksums`` holds what the sender cache commits."""
-    pairs = []
-    for name in old:
-        a, b = bits16(name, old[name]), bits16(name, new[name])
-        if a.shape != b.shape:
+    names = list(old)
+    olds = [old[n] for n in names]
+    news = [new[n] for n in names]
+    for name, a, b in zip(names, olds, news):     # the reference's order of checks
+        check16(name, a)
+        check16(name, b)
+        if a.numel() != b.numel():
             raise ValueError(f"{name}: old and new differ in shape")
-        pairs.append((name, a, b))
-    if not pairs:
-        return _encode_on(torch.device("cpu"), [], None)
-    devs = {t.device for _, a, b in pairs for t in (a, b)}
+    if not names:
+        return _encode_on(torch.device("cpu"), [], [], [], None)
+    devs = {t.device for t in olds} | {t.device for t in news}
     if len(devs) != 1:
         raise ValueError("all tensors must be on one device")
-    return _encode_on(next(iter(devs)), pairs, checksums)
+    return _encode_on(next(iter(devs)), names, olds, news, checksums)
 
 
-def _encode_on(dev, pairs, checksums) -> EncodedUpdate:
+def _encode_on(dev, names, olds, news, checksums) -> EncodedUpdate:
     cdev = _cuda_device(dev)
     if dev.type != "cuda":
-        pairs = [(n, a.to(cdev), b.to(cdev)) for n, a, b in pairs]
+        olds = [a.to(cdev) for a in olds]
+        news = [b.to(cdev) for b in news]
     L = _ext.load()
-    names = [n for n, _, _ in pairs]
-    raw = [n.encode("utf-8") for n in names]
-    k = len(pairs)
-    prev = _ext.ptr_array([a.data_ptr() for _, a, _ in pairs])
-    cur = _ext.ptr_array([b.data_ptr() for _, _, b in pairs])
-    numel = (ctypes.c_int64 * max(k, 1))(*[a.numel() for _, a, _ in pairs])
-    name_bufs = [ctypes.create_string_buffer(r, len(r) or 1) for r in raw]
-    name_ptrs = _ext.ptr_array([ctypes.addressof(b) for b in name_bufs])
-    name_len = (ctypes.c_int64 * max(k, 1))(*[len(r) for r in raw])
-    cache = (ctypes.c_uint64 * max(k, 1))(*[int(checksums[n]) & (2**64 - 1) if checksums is not None and n in checksums
-                                            else 0 for n in names])
-    has = (ctypes.c_uint8 * max(k, 1))(*[1 if checksums is not None and n in checksums else 0 for n in names])
+    k = len(names)
+    prev = _ext.ptr_array([a.data_ptr() for a in olds])
+    cur = _ext.ptr_array([b.data_ptr() for b in news])
+    numel = (ctypes.c_int64 * max(k, 1))(*[a.numel() for a in olds])
+    keep, name_ptrs, name_len = _name_table(names)
+    if checksums:
+        hits = [checksums.get(n) for n in names]
+        cache = (ctypes.c_uint64 * max(k, 1))(*[int(c) & (2**64 - 1) if c is not None else 0 for c in hits])
+        has = (ctypes.c_uint8 * max(k, 1))(*[c is not None for c in hits])
+    else:
+        cache, has = None, None
     h = ctypes.c_void_p()
     err = ctypes.create_string_buffer(1024)
     with torch.cuda.device(cdev):
         stream = torch.cuda.current_stream(cdev).cuda_stream
         st = L.crx_encode(_ext.context(cdev.index), k, prev, cur, numel, name_ptrs, name_len, cache, has,
                           ctypes.c_void_p(stream), ctypes.byref(h), err, 1024)
+    del keep
     if st != _ext.CRX_OK:
         _raise(st, err)
     return EncodedUpdate(h, names)
@@ -122,7 +147,8 @@ def apply(weights: Mapping[str, torch.Tensor], u: ParsedUpdate, checksums: dict 
     for name, numel, _ in headers:
         if name not in weights:
             raise ValueError(f"update has tensor {name!r} that the receiver does not have")
-        a = bits16(name, weights[name])
+        a = weights[name]
+        check16(name, a)
         if a.numel() != numel:
             raise ValueError(f"{name}: update is for {numel} elements, receiver has {a.numel()}")
         targets.append(a)
@@ -132,9 +158,12 @@ def apply(weights: Mapping[str, torch.Tensor], u: ParsedUpdate, checksums: dict 
     cdev = _cuda_device(dev)
     work = targets if dev.type == "cuda" else [a.to(cdev) for a in targets]
     k = len(headers)
-    cached = [_cache_get(checksums, name, weights[name]) for name, _, _ in headers]
-    cache = (ctypes.c_uint64 * k)(*[c if c is not None else 0 for c in cached])
-    has = (ctypes.c_uint8 * k)(*[1 if c is not None else 0 for c in cached])
+    if checksums:
+        cached = [_cache_get(checksums, name, a) for (name, _, _), a in zip(headers, targets)]
+        cache = (ctypes.c_uint64 * k)(*[c if c is not None else 0 for c in cached])
+        has = (ctypes.c_uint8 * k)(*[c is not None for c in cached])
+    else:
+        cache, has = None, None
     ptrs = _ext.ptr_array([a.data_ptr() for a in work])
     changed = ctypes.c_int64()
     err = ctypes.create_string_buffer(1024)
@@ -145,14 +174,13 @@ def apply(weights: Mapping[str, torch.Tensor], u: ParsedUpdate, checksums: dict 
                          ctypes.byref(changed), err, 1024)
     if st != _ext.CRX_OK:
         _raise(st, err)
-    if dev.type == "cuda":
-        for name, _, _ in headers:   # the commit wrote through raw pointers: move the version like a[idx] = v
-            torch.autograd.graph.increment_version(weights[name])
+    if dev.type == "cuda":   # the commit wrote through raw pointers: move the version like a[idx] = v
+        torch.autograd.graph.increment_version(targets)
     else:
         for a, wk in zip(targets, work):
             a.copy_(wk)     # in-place copy back: bumps the version and reaches every view
     if checksums is not None:   # record the version after our own write
-        checksums.update({name: (chk, weights[name]._version) for name, _, chk in headers})
+        checksums.update({name: (chk, a._version) for (name, _, chk), a in zip(headers, targets)})
     return int(changed.value)
 
 

@@ -361,6 +361,8 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
     for (int64_t base = e_begin; base < e_end; base += MP_SUB) {
         const int n = int(tmin<int64_t>(MP_SUB, e_end - base));
         const int16_t* p = tt.w + base;
+        if (tid == 0 && base + MP_SUB < e_end)     // the next sub-tile streams into L2 meanwhile
+            prefetch_l2(p + MP_SUB, size_t(tmin<int64_t>(MP_SUB, e_end - base - MP_SUB)) * 2);
         uint32_t mx = 0;
         if (n == MP_SUB && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
             const uint4* v = reinterpret_cast<const uint4*>(p);
@@ -386,8 +388,16 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
         }
         mx = __reduce_max_sync(FULL, mx);
         if (lane == 0) atomicMax(&S.emax, int(mx));
-        for (int k = tid; k < MP_WARPS * MWIN * 34 / 2; k += MP_THREADS) reinterpret_cast<uint32_t*>(&S.cnt[0][0][0])[k] = 0;
-        for (int k = tid; k < MP_WARPS * 256; k += MP_THREADS) (&S.ocnt[0][0])[k] = 0;
+        {   // counters to zero, 16 bytes per store
+            static_assert(sizeof(S.cnt) % 16 == 0 && offsetof(MapSmem, cnt) % 16 == 0, "uint4 zeroing");
+            static_assert(sizeof(S.ocnt) % 16 == 0 && offsetof(MapSmem, ocnt) % 16 == 0, "uint4 zeroing");
+            uint4* c4 = reinterpret_cast<uint4*>(&S.cnt[0][0][0]);
+#pragma unroll
+            for (int k = tid; k < int(sizeof(S.cnt) / 16); k += MP_THREADS) c4[k] = make_uint4(0, 0, 0, 0);
+            uint4* o4 = reinterpret_cast<uint4*>(&S.ocnt[0][0]);
+#pragma unroll
+            for (int k = tid; k < int(sizeof(S.ocnt) / 16); k += MP_THREADS) o4[k] = make_uint4(0, 0, 0, 0);
+        }
         S.mark[tid] = 0;
         if (tid < MP_WARPS) S.oow[tid] = 0;
         __syncthreads();
@@ -396,19 +406,34 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
         const int r0 = lane * MP_RUN;
         const int vn = tmax(0, tmin(MP_RUN, span_n - r0));
         const int pb = mpidx(span0 + r0);
-        // ---- lane walk: own ranks with private counters
+        // ---- lane walk: own ranks with private counters, four elements at a time (counters loaded
+        //      together, ranks corrected for equal exponents inside the group, stored in order)
         {
             uint16_t* myc = &S.cnt[w][0][lane];
             bool any_oow = false;
-            for (int k = 0; k < vn; ++k) {
-                const uint32_t x = S.tile[pb + k];
-                const int d = int((x >> 7) & 0xFFu) - ebase;
-                if (unsigned(d) < unsigned(MWIN)) {
-                    const uint32_t c = myc[d * 34];
-                    S.tile[pb + k] = x | (c << 16);
-                    myc[d * 34] = uint16_t(c + 1);
-                } else {
-                    any_oow = true;
+            for (int k = 0; k < vn; k += 4) {
+                uint32_t x[4], inc[4], c[4];
+                int d[4];
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    const bool valid = k + h < vn;
+                    x[h] = valid ? S.tile[pb + k + h] : 0u;
+                    const int dd = int((x[h] >> 7) & 0xFFu) - ebase;
+                    const bool in = valid && unsigned(dd) < unsigned(MWIN);
+                    any_oow |= valid && !in;
+                    d[h] = in ? dd : 0;
+                    inc[h] = in ? 1u : 0u;
+                }
+#pragma unroll
+                for (int h = 0; h < 4; ++h) c[h] = myc[d[h] * 34];
+#pragma unroll
+                for (int h = 1; h < 4; ++h)
+#pragma unroll
+                    for (int g = 0; g < h; ++g) c[h] += d[h] == d[g] ? inc[g] : 0u;
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    myc[d[h] * 34] = uint16_t(c[h] + inc[h]);
+                    if (inc[h]) S.tile[pb + k + h] = x[h] | (c[h] << 16);
                 }
             }
             if (any_oow) atomicOr(&S.oow[w], 1u << lane);
@@ -426,6 +451,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
         }
         if (lane < MWIN) {
             uint32_t run = 0;
+#pragma unroll
             for (int col = 0; col < 32; ++col) {
                 const uint32_t v = S.cnt[w][lane][col];
                 S.cnt[w][lane][col] = uint16_t(run);
@@ -470,6 +496,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
         }
         __syncthreads();
         // ---- second lane walk: every element to its sorted slot
+#pragma unroll 4
         for (int k = 0; k < vn; ++k) {
             const uint32_t x = S.tile[pb + k];
             const uint32_t e = (x >> 7) & 0xFFu;
@@ -487,16 +514,16 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             if (S.nextloc[k] - lo >= tot) continue;
             const uint64_t ge = S.gend[k];
             uint64_t cur = S.cursor[k];
+            uint32_t next = 0xFFFFFFFFu;
             for (;;) {
                 const uint64_t j = cur + lane;
-                uint32_t lc = 0;
-                bool valid = j < ge;
-                if (valid) { lc = local[j]; valid = lc >= lo && lc - lo < tot; }
+                uint32_t lc = 0xFFFFFFFFu, z = 0;
+                if (j < ge) { lc = local[j]; z = zz[j]; }   // one round trip: both loads issued together
+                const bool valid = lc != 0xFFFFFFFFu && lc >= lo && lc - lo < tot;
                 if (valid) {
                     const uint32_t i = S.order[S.estart[e] + (lc - lo)];
                     const int pi = mpidx(int(i));
                     const uint32_t old = S.tile[pi] & 0xFFFFu;
-                    const uint32_t z = zz[j];
                     const int32_t res = int32_t(z >> 1) ^ -int32_t(z & 1);
                     const uint32_t nv = uint32_t(int32_t(old) + res) & 0xFFFFu;
                     S.tile[pi] = old | (nv << 16);
@@ -506,11 +533,19 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                 const uint32_t m = __ballot_sync(FULL, valid);
                 const int taken = __popc(~m) ? __ffs(~m) - 1 : 32;   // consumed changes are a prefix
                 cur += uint64_t(taken);
-                if (taken < 32) break;
+                if (taken < 32) {
+                    next = __shfl_sync(FULL, lc, taken);   // local[cur], or ~0 past the group's end
+                    break;
+                }
             }
             if (lane == 0) {
                 S.cursor[k] = cur;
-                S.nextloc[k] = cur < ge ? local[cur] : 0xFFFFFFFFu;
+                S.nextloc[k] = next;
+                if (cur < ge) {   // the group's next changes, for a later sub-tile
+                    const size_t nb = size_t(tmin<uint64_t>(ge - cur, 128));
+                    prefetch_l2(local + cur, 4 * nb);
+                    prefetch_l2(zz + cur, 4 * nb);
+                }
             }
         }
         __syncthreads();

@@ -55,6 +55,15 @@ __device__ __forceinline__ uint32_t lanemask_lt() {
 
 __device__ __forceinline__ uint32_t bswap32(uint32_t x) { return __byte_perm(x, 0, 0x0123); }
 
+// Start moving [p, p + bytes) from HBM into L2 (one bulk prefetch, no data returned).  Only the
+// 16-byte-aligned interior is requested, so the range never reaches past the caller's buffer.
+__device__ __forceinline__ void prefetch_l2(const void* p, size_t bytes) {
+    const uintptr_t lo = (reinterpret_cast<uintptr_t>(p) + 15) & ~uintptr_t(15);
+    const uintptr_t hi = (reinterpret_cast<uintptr_t>(p) + bytes) & ~uintptr_t(15);
+    if (hi > lo)
+        asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(lo), "r"(uint32_t(hi - lo)) : "memory");
+}
+
 // Stable rank of this lane's key (0..255) among the same-key lanes of this chunk and of every
 // earlier chunk this warp ranked with the same counters.  The lowest lane of each peer group adds
 // the group's size to the warp's counter with one shared-memory atomic and broadcasts the old

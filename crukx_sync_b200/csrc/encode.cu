@@ -194,34 +194,64 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
         }
         mx = __reduce_max_sync(FULL, mx);
         if (lane == 0) atomicMax(&S.emax, int(mx));
-        for (int k = tid; k < ER_WARPS * WIN * 33; k += ER_THREADS) (&S.cnt[0][0][0])[k] = 0;
-        for (int k = tid; k < ER_WARPS * 256; k += ER_THREADS) (&S.ocnt[0][0])[k] = 0;
+        {   // counters to zero, 16 bytes per store
+            static_assert(sizeof(S.cnt) % 16 == 0 && offsetof(RankSmem, cnt) % 16 == 0, "uint4 zeroing");
+            static_assert(sizeof(S.ocnt) % 16 == 0 && offsetof(RankSmem, ocnt) % 16 == 0, "uint4 zeroing");
+            uint4* c4 = reinterpret_cast<uint4*>(&S.cnt[0][0][0]);
+#pragma unroll
+            for (int k = tid; k < int(sizeof(S.cnt) / 16); k += ER_THREADS) c4[k] = make_uint4(0, 0, 0, 0);
+            uint4* o4 = reinterpret_cast<uint4*>(&S.ocnt[0][0]);
+#pragma unroll
+            for (int k = tid; k < int(sizeof(S.ocnt) / 16); k += ER_THREADS) o4[k] = make_uint4(0, 0, 0, 0);
+        }
         if (tid < ER_WARPS) { S.nrec[tid] = 0; S.norec[tid] = 0; S.oow[tid] = 0; }
         __syncthreads();
         const int ebase = tmax(S.emax - (WIN - 1), 0);
         const int span_n = tmax(0, tmin(ER_SPAN, n - span0));
 
-        // ---- lane walk: private counters, in-window change records
+        // ---- lane walk: private counters, in-window change records.  Four elements at a time: their
+        //      counters are loaded together, ranks corrected for equal exponents inside the group,
+        //      and stored in order (the last store of a counter carries all four increments).
         {
             const int r0 = lane * ER_RUN;
             const int vn = tmax(0, tmin(ER_RUN, span_n - r0));
             const int pb = pidx(span0 + r0);
             uint32_t* myc = &S.cnt[w][0][lane];
             bool any_oow = false;
-            for (int k = 0; k < vn; ++k) {
-                const uint32_t x = S.tile[pb + k];
-                const int d = int((x >> 7) & 0xFFu) - ebase;
-                const bool ch = changed_bits(x);
-                if (unsigned(d) < unsigned(WIN)) {
-                    const uint32_t c = myc[d * 33];
-                    if (ch) {
-                        const uint32_t slot = atomicAdd(&S.nrec[w], 1u);
-                        if (slot < WREC)
-                            S.rec[w][slot] = (uint32_t(r0 + k) << 16) | (uint32_t(d) << 12) | ((c & 0xFFFFu) << 6) | (c >> 16);
+            for (int k = 0; k < vn; k += 4) {
+                uint32_t x[4], inc[4], c[4];
+                int d[4];
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    const bool valid = k + h < vn;
+                    x[h] = valid ? S.tile[pb + k + h] : 0u;
+                    const int dd = int((x[h] >> 7) & 0xFFu) - ebase;
+                    const bool in = valid && unsigned(dd) < unsigned(WIN);
+                    any_oow |= valid && !in;
+                    d[h] = in ? dd : 0;
+                    inc[h] = in ? (changed_bits(x[h]) ? 0x10001u : 1u) : 0u;
+                }
+#pragma unroll
+                for (int h = 0; h < 4; ++h) c[h] = myc[d[h] * 33];
+#pragma unroll
+                for (int h = 1; h < 4; ++h)
+#pragma unroll
+                    for (int g = 0; g < h; ++g) c[h] += d[h] == d[g] ? inc[g] : 0u;
+#pragma unroll
+                for (int h = 0; h < 4; ++h) myc[d[h] * 33] = c[h] + inc[h];
+                // records of the in-window changes: one shared-memory atomic per lane and group
+                const uint32_t nb = (inc[0] >> 16) + (inc[1] >> 16) + (inc[2] >> 16) + (inc[3] >> 16);
+                if (nb) {
+                    uint32_t slot = atomicAdd(&S.nrec[w], nb);
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                        if (inc[h] >> 16) {
+                            if (slot < WREC)
+                                S.rec[w][slot] = (uint32_t(r0 + k + h) << 16) | (uint32_t(d[h]) << 12) |
+                                                 ((c[h] & 0xFFFFu) << 6) | (c[h] >> 16);
+                            ++slot;
+                        }
                     }
-                    myc[d * 33] = c + (ch ? 0x10001u : 1u);
-                } else {
-                    any_oow = true;
                 }
             }
             if (any_oow) atomicOr(&S.oow[w], 1u << lane);
@@ -247,6 +277,7 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
         // ---- lane prefixes: lane d scans window row d (rows are padded to 33 words)
         if (lane < WIN) {
             uint32_t run = 0;
+#pragma unroll
             for (int col = 0; col < 32; ++col) {
                 const uint32_t v = S.cnt[w][lane][col];
                 S.cnt[w][lane][col] = run;
