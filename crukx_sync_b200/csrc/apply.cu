@@ -153,106 +153,170 @@ __global__ void __launch_bounds__(HIST_THREADS) k_app_hist(const AppTensor* __re
 }
 
 // ------------------------------------------------------------------ block decoder
+//
+// One thread per 256-change block.  Each thread reads its block through a private 64-bit bit
+// buffer (bits [pos, pos + avail) MSB-aligned, zeros below), refilled 32 big-endian bits at a time
+// from 16-byte payload loads made ahead of use; no shared memory, so occupancy is set by
+// registers.  Steps whose unary run, remainder and longest code do not fit in the buffer (long
+// unary runs, large Rice parameters) take the generic reader at absolute positions.
 
-constexpr int DEC_WARPS = 4;                 // warps per CTA; a warp decodes 32 consecutive blocks
-constexpr int DEC_WORDS = 1536;              // payload words a warp stages in shared memory (12 KB)
+constexpr int DEC_THREADS = 256;
 
-// 64 payload bits starting at bit `pos` from words staged in shared memory (w0 = first word)
-__device__ __forceinline__ uint64_t read64s(const uint64_t* W, uint64_t w0, uint64_t pos) {
-    const uint64_t w = (pos >> 6) - w0;
-    const int s = int(pos & 63);
-    const uint64_t hi = W[w];
-    if (!s) return hi;
-    return (hi << s) | (W[w + 1] >> (64 - s));
+// canonical code at the top of `peek` (17 bits): length and symbol-table index; false if none
+__device__ __forceinline__ bool find_code(const DecTable* __restrict__ tab, uint32_t peek, int& L, uint32_t& idx) {
+    const uint32_t lv = tab->lut[peek >> (kMaxCodeLen - LUT_BITS)];
+    if (lv) {
+        L = int(lv >> 24);
+        idx = lv & 0xFFFFFFu;
+        return true;
+    }
+    L = LUT_BITS + 1;   // no code of <= LUT_BITS bits starts with these bits
+    while (L <= kMaxCodeLen && peek >= tab->limit[L]) ++L;
+    if (L > kMaxCodeLen) return false;
+    idx = tab->base[L] + (peek >> (kMaxCodeLen - L)) - tab->first[L];
+    return true;
 }
 
-template <bool kShared>
-__device__ __forceinline__ bool decode_block(const uint64_t* Wsrc, uint64_t w0, uint64_t cur, const uint64_t end, int cnt,
-                                             uint64_t ebase, uint64_t qmax, int rice, const DecTable* __restrict__ tab,
-                                             const uint32_t* __restrict__ SYMS, uint32_t* __restrict__ gaps,
-                                             uint32_t* __restrict__ zz, uint64_t* sum_out) {
-    auto rd = [&](uint64_t p) { return kShared ? read64s(Wsrc, w0, p) : read64(Wsrc, p); };
-    uint64_t sum = 0;
-    for (int step = 0; step < cnt; ++step) {
-        if (cur >= end) return false;
-        uint64_t y = ~rd(cur);
-        uint64_t q;
-        if (y) {
-            q = uint64_t(__clzll(y));
-        } else {
-            // a run of more than 64 ones: follow it window by window, never past this block's end
-            // or past q_max, so hostile updates cost at most their own bits
-            q = 64;
-            while (q <= qmax && cur + q < end) {
-                y = ~rd(cur + q);
-                if (y) { q += uint64_t(__clzll(y)); break; }
-                q += 64;
-            }
-        }
-        if (q > qmax || cur + q >= end) return false;
-        const uint64_t c = cur + q + 1;
-        const uint64_t x = rd(c);
-        const uint64_t rem = rice ? (x >> (64 - rice)) : 0;
-        const uint32_t peek = uint32_t((x << rice) >> (64 - kMaxCodeLen));
-        const uint32_t lv = tab->lut[peek >> (kMaxCodeLen - LUT_BITS)];
-        int L;
-        uint32_t idx;
-        if (lv) {
-            L = int(lv >> 24);
-            idx = lv & 0xFFFFFFu;
-        } else {
-            L = 1;
-            while (L <= kMaxCodeLen && peek >= tab->limit[L]) ++L;
-            if (L > kMaxCodeLen) return false;
-            idx = tab->base[L] + (peek >> (kMaxCodeLen - L)) - tab->first[L];
-        }
-        const uint32_t sym = SYMS[tab->sym_off + tmin(idx, tab->nsym - 1)];
-        const uint64_t gap = (q << rice) | rem;
-        gaps[ebase + step] = gap > 0xFFFFFFFFull ? 0xFFFFFFFFu : uint32_t(gap);
-        zz[ebase + step] = sym;
-        sum += gap + 1;
-        cur = c + uint64_t(rice) + uint64_t(L);
+// Payload words for one lane: 32-bit big-endian words read through a window of two 16-byte
+// quads held in registers; moving past the first quad loads the one after the second, so each
+// load is issued about 128 bits before its words are needed.
+struct QuadReader {
+    const uint4* __restrict__ W4;
+    uint64_t n4;   // 16-byte quads in the buffer
+    uint64_t qa;   // index of quad a
+    uint4 a, b;
+    __device__ __forceinline__ uint4 load(uint64_t i) const { return __ldg(W4 + tmin(i, n4 - 1)); }
+    __device__ __forceinline__ void seek(uint64_t word) {   // window starts at the quad holding `word`
+        qa = word >> 2;
+        a = load(qa);
+        b = load(qa + 1);
     }
-    *sum_out = sum;
-    return cur == end;
-}
+    __device__ __forceinline__ uint32_t word(uint64_t i) {   // i >= 4 * qa; advances the window as needed
+        while (i >= 4 * qa + 4) {
+            a = b;
+            ++qa;
+            b = load(qa + 1);
+        }
+        const uint32_t k = uint32_t(i & 3);
+        const uint32_t v = k == 0 ? a.x : k == 1 ? a.y : k == 2 ? a.z : a.w;
+        return bswap32(v);
+    }
+};
 
-__global__ void __launch_bounds__(DEC_WARPS * 32) k_decode(const uint64_t* __restrict__ W, const uint32_t* __restrict__ bb,
-                                                           const uint64_t* __restrict__ boff, int64_t n_blocks,
-                                                           const AppGroup* __restrict__ G, const uint64_t* __restrict__ gblock,
-                                                           int64_t ng, const DecTable* __restrict__ TB,
-                                                           const uint32_t* __restrict__ SYMS, const uint64_t* __restrict__ GS,
-                                                           uint32_t* __restrict__ gaps, uint32_t* __restrict__ zz,
-                                                           uint64_t* __restrict__ bsum, unsigned long long* __restrict__ counters) {
-    __shared__ uint64_t stage[DEC_WARPS][DEC_WORDS];
-    const int lane = threadIdx.x & 31, wi = threadIdx.x >> 5;
-    const int64_t b0 = (int64_t(blockIdx.x) * DEC_WARPS + wi) * 32;
-    if (b0 >= n_blocks) return;
-    const int64_t b_last = tmin<int64_t>(b0 + 31, n_blocks - 1);
-    const int64_t b = b0 + lane;
-    // this warp's blocks are consecutive in the payload: stage their words when they fit
-    const uint64_t w0 = boff[b0] >> 6;
-    const uint64_t w1 = ((boff[b_last] + bb[b_last]) >> 6) + 2;   // + the window a read can reach
-    const bool staged = w1 - w0 <= DEC_WORDS;
-    if (staged) {
-        for (uint64_t k = lane; k < w1 - w0; k += 32) stage[wi][k] = bswap64(__ldg(W + w0 + k));
-        __syncwarp();
-    }
-    if (b > b_last) return;
+__global__ void __launch_bounds__(DEC_THREADS) k_decode(const uint64_t* __restrict__ W, uint64_t n32,
+                                                        const uint32_t* __restrict__ bb, const uint64_t* __restrict__ boff,
+                                                        int64_t n_blocks, const AppGroup* __restrict__ G,
+                                                        const uint64_t* __restrict__ gblock, int64_t ng,
+                                                        const DecTable* __restrict__ TB, const uint32_t* __restrict__ SYMS,
+                                                        const uint64_t* __restrict__ GS, uint32_t* __restrict__ gaps,
+                                                        uint32_t* __restrict__ zz, uint64_t* __restrict__ bsum,
+                                                        unsigned long long* __restrict__ counters) {
+    const int64_t b = int64_t(blockIdx.x) * DEC_THREADS + threadIdx.x;
+    if (b >= n_blocks) return;
     const int64_t g = last_le(gblock, ng, uint64_t(b));
     const AppGroup grp = G[g];
-    const uint64_t k = uint64_t(b) - gblock[g];
-    const int cnt = int(tmin<uint64_t>(kBlock, grp.count - k * kBlock));
-    const uint64_t ebase = grp.start + k * kBlock;
-    const uint64_t cur = boff[b];
-    const uint64_t end = cur + bb[b];
-    const uint64_t size = GS[int64_t(grp.tensor) * 256 + grp.exp];
+    const uint64_t kb = uint64_t(b) - gblock[g];
+    const int cnt = int(tmin<uint64_t>(kBlock, grp.count - kb * kBlock));
+    const uint64_t ebase = grp.start + kb * kBlock;
+    uint64_t pos = boff[b];
+    const uint64_t end = pos + bb[b];
+    const uint64_t qmax = GS[int64_t(grp.tensor) * 256 + grp.exp] >> grp.rice;
     const int rice = grp.rice;
-    const uint64_t qmax = size >> rice;
     const DecTable* tab = TB + grp.table;
+    const uint32_t* SY = SYMS + tab->sym_off;
+    const uint32_t nsym1 = tab->nsym - 1;
+    QuadReader R{reinterpret_cast<const uint4*>(W), n32 / 4, 0, {}, {}};
+
+    uint64_t wi, buf;   // wi: the payload word that follows the buffered bits
+    int avail;
+    auto fill = [&]() {   // buffer := 64 - (pos & 31) bits from pos
+        wi = pos >> 5;
+        R.seek(wi);
+        buf = ((uint64_t(R.word(wi)) << 32) | R.word(wi + 1)) << (pos & 31);
+        avail = 64 - int(pos & 31);
+        wi += 2;
+    };
+    fill();
     uint64_t sum = 0;
-    const bool ok = staged ? decode_block<true>(stage[wi], w0, cur, end, cnt, ebase, qmax, rice, tab, SYMS, gaps, zz, &sum)
-                           : decode_block<false>(W, 0, cur, end, cnt, ebase, qmax, rice, tab, SYMS, gaps, zz, &sum);
+    bool ok = true;
+    // outputs go out four at a time as 16-byte stores at indices that are multiples of 4 (the
+    // buffers are 256-byte aligned); the unaligned head and tail of the block are stored singly
+    uint4 gq = make_uint4(0, 0, 0, 0), zq = make_uint4(0, 0, 0, 0);
+    int step = 0;
+    for (; step < cnt; ++step) {
+        if (pos >= end) { ok = false; break; }
+        const int q = __clzll(~buf);   // ones ahead; bits past `avail` are zeros, so q < avail when it fits
+        uint64_t gap;
+        uint32_t sym;
+        if (q + 1 + rice + kMaxCodeLen <= avail) {
+            if (uint64_t(q) > qmax || pos + uint64_t(q) >= end) { ok = false; break; }
+            uint64_t t = buf << (q + 1);
+            const uint64_t rem = rice ? (t >> (64 - rice)) : 0;
+            t <<= rice;
+            int L;
+            uint32_t idx;
+            if (!find_code(tab, uint32_t(t >> (64 - kMaxCodeLen)), L, idx)) { ok = false; break; }
+            sym = SY[tmin(idx, nsym1)];
+            gap = (uint64_t(q) << rice) | rem;
+            const int used = q + 1 + rice + L;
+            buf = t << L;
+            avail -= used;
+            pos += uint64_t(used);
+            while (avail <= 32) {
+                buf |= uint64_t(R.word(wi++)) << (32 - avail);
+                avail += 32;
+            }
+        } else {
+            // generic step: a unary run of more than 64 ones is followed window by window, never
+            // past this block's end or past q_max, so hostile updates cost at most their own bits
+            uint64_t y = ~read64(W, pos);
+            uint64_t qq;
+            if (y) {
+                qq = uint64_t(__clzll(y));
+            } else {
+                qq = 64;
+                while (qq <= qmax && pos + qq < end) {
+                    y = ~read64(W, pos + qq);
+                    if (y) { qq += uint64_t(__clzll(y)); break; }
+                    qq += 64;
+                }
+            }
+            if (qq > qmax || pos + qq >= end) { ok = false; break; }
+            const uint64_t c = pos + qq + 1;
+            const uint64_t x = read64(W, c);
+            const uint64_t rem = rice ? (x >> (64 - rice)) : 0;
+            int L;
+            uint32_t idx;
+            if (!find_code(tab, uint32_t((x << rice) >> (64 - kMaxCodeLen)), L, idx)) { ok = false; break; }
+            sym = SY[tmin(idx, nsym1)];
+            gap = (qq << rice) | rem;
+            pos = c + uint64_t(rice) + uint64_t(L);
+            fill();
+        }
+        gq = make_uint4(gq.y, gq.z, gq.w, gap > 0xFFFFFFFFull ? 0xFFFFFFFFu : uint32_t(gap));
+        zq = make_uint4(zq.y, zq.z, zq.w, sym);
+        const uint64_t i = ebase + uint64_t(step);
+        if ((i & 3) == 3) {
+            if (step >= 3) {
+                *reinterpret_cast<uint4*>(gaps + i - 3) = gq;
+                *reinterpret_cast<uint4*>(zz + i - 3) = zq;
+            } else {   // head: steps 0..step
+                if (step >= 2) { gaps[i - 2] = gq.y; zz[i - 2] = zq.y; }
+                if (step >= 1) { gaps[i - 1] = gq.z; zz[i - 1] = zq.z; }
+                gaps[i] = gq.w;
+                zz[i] = zq.w;
+            }
+        }
+        sum += gap + 1;
+    }
+    if (ok) {   // tail: the last (ebase + cnt) % 4 outputs, unless already in the head
+        const uint64_t e = ebase + uint64_t(cnt);
+        const int r = tmin(int(e & 3), cnt);
+        if (r >= 3) { gaps[e - 3] = gq.y; zz[e - 3] = zq.y; }
+        if (r >= 2) { gaps[e - 2] = gq.z; zz[e - 2] = zq.z; }
+        if (r >= 1) { gaps[e - 1] = gq.w; zz[e - 1] = zq.w; }
+    }
+    ok = ok && pos == end;
     bsum[b] = ok ? sum : 0;
     if (!ok) atomicOr(&counters[1], (unsigned long long)ERR_DECODE);
 }
@@ -758,8 +822,8 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     }
     launch_exclusive_scan_u64(C, boff, n_blocks, scan_tmp, d_total, st);
     { KernelScope ks_(C, "k_decode", st);
-    k_decode<<<unsigned((n_blocks + DEC_WARPS * 32 - 1) / (DEC_WARPS * 32)), DEC_WARPS * 32, 0, st>>>(
-        dev<uint64_t>(C, S_A_PAYLOAD), dev<uint32_t>(C, S_A_BB), boff, n_blocks, dG, dgblock, ng, dev<DecTable>(C, S_A_TABLES),
+    k_decode<<<unsigned((n_blocks + DEC_THREADS - 1) / DEC_THREADS), DEC_THREADS, 0, st>>>(
+        dev<uint64_t>(C, S_A_PAYLOAD), uint64_t(payload_alloc / 4), dev<uint32_t>(C, S_A_BB), boff, n_blocks, dG, dgblock, ng, dev<DecTable>(C, S_A_TABLES),
         dev<uint32_t>(C, S_A_SYMS), dev<uint64_t>(C, S_A_TOT), dev<uint32_t>(C, S_A_GAPS), dev<uint32_t>(C, S_A_ZZ),
         dev<uint64_t>(C, S_A_BSUM), counters);
     }
