@@ -385,6 +385,7 @@ struct MapSmem {
     uint8_t gexp[256];
     uint32_t oow[MP_WARPS], wcnt[MP_WARPS], wbase[MP_WARPS];
     unsigned long long stage_base;
+    uint32_t nstage;
     int emax;
     uint64_t red[MP_WARPS];
 };
@@ -626,15 +627,24 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
         if (tid == 0) {
             uint32_t r = 0;
             for (int ww = 0; ww < MP_WARPS; ++ww) { S.wbase[ww] = r; r += S.wcnt[ww]; }
+            S.nstage = r;
             S.stage_base = r ? atomicAdd(staged, (unsigned long long)r) : 0ull;
         }
         __syncthreads();
-        uint64_t at = S.stage_base + S.wbase[w] + incl - __popc(bits);
-        for (uint32_t b = bits; b; b &= b - 1, ++at) {
-            const int i = span0 + lane * 32 + (__ffs(b) - 1);
-            if (at < stage_cap) {
-                caddr[at] = (unsigned long long)(reinterpret_cast<uintptr_t>(tt.w + base + i));
-                cval[at] = uint16_t(S.tile[mpidx(i)] >> 16);
+        // the sorted order is no longer needed: it now lists the changed positions, which all
+        // threads then write out contiguously
+        uint32_t at = S.wbase[w] + incl - __popc(bits);
+        for (uint32_t b = bits; b; b &= b - 1, ++at) S.order[at] = uint16_t(span0 + lane * 32 + (__ffs(b) - 1));
+        __syncthreads();
+        {
+            const uint64_t sb = S.stage_base;
+            const uint32_t ns = S.nstage;
+            for (uint32_t k = tid; k < ns; k += MP_THREADS) {
+                const int i = S.order[k];
+                if (sb + k < stage_cap) {
+                    caddr[sb + k] = (unsigned long long)(reinterpret_cast<uintptr_t>(tt.w + base + i));
+                    cval[sb + k] = uint16_t(S.tile[mpidx(i)] >> 16);
+                }
             }
         }
         __syncthreads();
@@ -848,7 +858,7 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     uint64_t* hc = C.small;
     const size_t nsmall = 16 + 2 * size_t(nt);
     std::vector<uint64_t> hv(nsmall);
-    if (nsmall <= 512) {
+    if (nsmall < size_t(kEncStatusWord)) {
         CRX_CUDA(cudaMemcpyAsync(hc, counters, 8 * nsmall, cudaMemcpyDeviceToHost, st));
         CRX_CUDA(cudaStreamSynchronize(st));
         std::memcpy(hv.data(), hc, 8 * nsmall);

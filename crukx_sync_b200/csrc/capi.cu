@@ -9,6 +9,7 @@
 
 #include "../../include/crukx_b200.h"
 #include "capi_internal.h"
+#include "common.cuh"
 
 struct crx_ctx {
     crx::Ctx c;
@@ -140,9 +141,7 @@ cudaError_t ensure_pinned(DevBuf& buf, size_t bytes, cudaStream_t s) {
     return cudaSuccess;
 }
 
-static constexpr size_t kCopyChunk = size_t(32) << 20;
-
-static cudaError_t chunk_events(Ctx& c, size_t n_chunks) {
+cudaError_t chunk_events(Ctx& c, size_t n_chunks) {
     while (c.copy_ev.size() < n_chunks) {
         cudaEvent_t e = nullptr;
         const cudaError_t r = cudaEventCreateWithFlags(&e, cudaEventDisableTiming);
@@ -162,53 +161,46 @@ cudaError_t upload_pipelined(Ctx& c, void* dev_dst, const void* host_src, uint8_
     return cudaSuccess;
 }
 
-cudaError_t download_pipelined(Ctx& c, void* host_dst, const void* dev_src, uint8_t* pinned, size_t n, cudaStream_t s) {
-    const size_t nc = (n + kCopyChunk - 1) / kCopyChunk;
-    cudaError_t e = chunk_events(c, nc);
-    if (e != cudaSuccess) return e;
-    for (size_t k = 0; k < nc; ++k) {
-        const size_t off = k * kCopyChunk, len = std::min(kCopyChunk, n - off);
-        e = cudaMemcpyAsync(pinned + off, static_cast<const uint8_t*>(dev_src) + off, len, cudaMemcpyDeviceToHost, s);
-        if (e == cudaSuccess) e = cudaEventRecord(c.copy_ev[k], s);
-        if (e != cudaSuccess) return e;
-    }
-    for (size_t k = 0; k < nc; ++k) {
-        const size_t off = k * kCopyChunk, len = std::min(kCopyChunk, n - off);
-        e = cudaEventSynchronize(c.copy_ev[k]);
-        if (e != cudaSuccess) return e;
-        parallel_copy(static_cast<uint8_t*>(host_dst) + off, pinned + off, len);
-    }
-    return cudaSuccess;
-}
-
 cudaError_t Encoded::write(uint8_t* dst) const {
+    if (pending) prefault(dst, size());   // the GPU is still packing and copying meanwhile
     std::memcpy(dst, head.data(), head.size());
     dst += head.size();
     const size_t bt = 4 * size_t(n_blocks);
+    if (pending) {
+        const cudaError_t e = cudaEventSynchronize(ctx->copy_ev[0]);
+        if (e != cudaSuccess) return e;
+        if (ctx->small[kEncStatusWord] & ERR_INTERNAL) return cudaErrorUnknown;
+    } else if (internal_error) {
+        return cudaErrorUnknown;
+    }
     if (bt) parallel_copy(dst, table, bt);
     dst += bt;
     std::memcpy(dst, len_varint.data(), len_varint.size());
     dst += len_varint.size();
-    if (!payload_len) return cudaSuccess;
-    if (!dpay) {
-        parallel_copy(dst, own.data() + bt, payload_len);
+    if (!pending) {
+        if (payload_len) parallel_copy(dst, table + bt, payload_len);
         return cudaSuccess;
     }
-    return download_pipelined(*ctx, dst, dpay, static_cast<uint8_t*>(ctx->out_host.p) + bt, payload_len, stream);
+    for (uint64_t off = 0, k = 0; off < payload_len; off += kCopyChunk, ++k) {
+        const size_t len = size_t(std::min<uint64_t>(kCopyChunk, payload_len - off));
+        const cudaError_t e = cudaEventSynchronize(ctx->copy_ev[1 + k]);
+        if (e != cudaSuccess) return e;
+        parallel_copy(dst + off, table + bt + off, len);
+    }
+    return cudaSuccess;
 }
 
 cudaError_t Encoded::detach() {
-    const size_t bt = 4 * size_t(n_blocks);
-    std::vector<uint8_t> tmp(bt + payload_len);
-    if (bt) std::memcpy(tmp.data(), table, bt);
-    if (dpay && payload_len) {
-        cudaError_t e = cudaMemcpyAsync(tmp.data() + bt, dpay, payload_len, cudaMemcpyDeviceToHost, stream);
-        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
-        if (e != cudaSuccess) return e;
-    }
+    if (!pending) return cudaSuccess;
+    const cudaError_t e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) return e;
+    internal_error = (ctx->small[kEncStatusWord] & ERR_INTERNAL) != 0;
+    const size_t n = 4 * size_t(n_blocks) + payload_len;
+    std::vector<uint8_t> tmp(n);
+    if (n) std::memcpy(tmp.data(), table, n);
     own.swap(tmp);
     table = own.data();
-    dpay = nullptr;
+    pending = false;
     return cudaSuccess;
 }
 
@@ -324,6 +316,11 @@ void crx_encoded_free(crx_encoded* enc) {
     if (!enc) return;
     if (enc->e.ctx) {
         std::lock_guard<std::mutex> lock(enc->e.ctx->mu);
+        // copies still landing in the context's pinned buffer must finish before it is reused
+        if (enc->e.pending) {
+            DeviceGuard g(enc->e.ctx->device);
+            cudaStreamSynchronize(enc->e.stream);
+        }
         if (enc->e.ctx->live == &enc->e) enc->e.ctx->live = nullptr;
     }
     delete enc;

@@ -22,8 +22,10 @@ struct Encoded {
     Ctx* ctx = nullptr;
     cudaStream_t stream = nullptr;
     std::vector<uint8_t> head;         // magic .. last group header
-    const uint8_t* table = nullptr;    // 4 * n_blocks block-table bytes (pinned, or own)
-    const uint8_t* dpay = nullptr;     // payload in device memory (context workspace) until detached
+    const uint8_t* table = nullptr;    // 4 * n_blocks block-table bytes, then the payload (pinned, or own)
+    bool pending = false;              // device -> host copies into `table` still in flight: ctx->copy_ev[0]
+                                       // covers the block table and the error flags, copy_ev[1 + k] payload chunk k
+    bool internal_error = false;       // the encoder's consistency check failed (seen once the copies landed)
     std::vector<uint8_t> own;          // block table + payload after detach()
     int64_t n_blocks = 0;
     uint64_t payload_len = 0;
@@ -33,8 +35,10 @@ struct Encoded {
     uint64_t changes = 0;
 
     size_t size() const { return head.size() + 4 * size_t(n_blocks) + len_varint.size() + payload_len; }
+    // Serialized bytes into dst (size() bytes): cudaSuccess, a CUDA error, or cudaErrorUnknown when
+    // the encoder's consistency check failed.  Pre-faults dst while the copies are in flight.
     cudaError_t write(uint8_t* dst) const;   // capi.cu
-    cudaError_t detach();                    // capi.cu
+    cudaError_t detach();                    // capi.cu: wait for the copies and keep a private copy
 };
 
 // Encode n tensors (device pointers).  cache_chk/has_cache may be null.

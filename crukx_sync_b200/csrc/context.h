@@ -27,11 +27,18 @@ cudaError_t ensure_host(Ctx& c, size_t bytes, cudaStream_t s);
 cudaError_t ensure_pinned(DevBuf& buf, size_t bytes, cudaStream_t s);
 // memcpy split over threads (large copies; also spreads first-touch page faults)
 void parallel_copy(void* dst, const void* src, size_t n);
+// Touch every page of [dst, dst + n) from the worker threads, so that a freshly allocated
+// destination takes its page faults in parallel (and ahead of the copy into it).
+void prefault(void* dst, size_t n);
 // host -> device through pinned staging, chunk by chunk: the host copy of chunk k+1 overlaps the
 // DMA of chunk k.  `pinned` holds at least n bytes.
 cudaError_t upload_pipelined(Ctx& c, void* dev_dst, const void* host_src, uint8_t* pinned, size_t n, cudaStream_t s);
-// device -> host the same way, into pageable memory
-cudaError_t download_pipelined(Ctx& c, void* host_dst, const void* dev_src, uint8_t* pinned, size_t n, cudaStream_t s);
+// pipelined copies move kCopyChunk bytes per cudaMemcpyAsync; chunk_events makes sure the context
+// holds at least n timing-free events (Ctx::copy_ev)
+constexpr size_t kCopyChunk = size_t(32) << 20;
+cudaError_t chunk_events(Ctx& c, size_t n);
+// word of Ctx::small that receives the error flags of an encode whose copies are still in flight
+constexpr int kEncStatusWord = 511;
 
 // Named slots of Ctx::b.
 enum Slot : int {

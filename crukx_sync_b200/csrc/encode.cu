@@ -1200,17 +1200,25 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     put_varint(out->len_varint, payload_len);
     out->n_blocks = n_blocks;
     out->payload_len = payload_len;
-    const size_t down2 = 4 * size_t(n_blocks) + payload_len;
-    CRX_CUDA(ensure_pinned(C.out_host, down2 + 16, st));
+    // block table, error flags and payload go to pinned memory behind k_pack; nothing waits for
+    // them here: the serializer pre-faults its destination meanwhile (Encoded::write)
+    const size_t bt = 4 * size_t(n_blocks);
+    CRX_CUDA(ensure_pinned(C.out_host, bt + payload_len + 16, st));
     uint8_t* oh = static_cast<uint8_t*>(C.out_host.p);
-    CRX_CUDA(cudaMemcpyAsync(oh, C.b[S_BB32].p, 4 * size_t(n_blocks), cudaMemcpyDeviceToHost, st));
-    CRX_CUDA(cudaMemcpyAsync(hostc + 2, counters + 1, 8, cudaMemcpyDeviceToHost, st));
-    CRX_CUDA(cudaStreamSynchronize(st));
-    trace_phase(C, "encode: packed (sync 5)");
-    if (hostc[2] & ERR_INTERNAL) { *err = "internal: encoder consistency check failed"; return kCudaError; }
+    CRX_CUDA(chunk_events(C, 1 + size_t((payload_len + kCopyChunk - 1) / kCopyChunk)));
+    CRX_CUDA(cudaMemcpyAsync(oh, C.b[S_BB32].p, bt, cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaMemcpyAsync(C.small + kEncStatusWord, counters + 1, 8, cudaMemcpyDeviceToHost, st));
+    CRX_CUDA(cudaEventRecord(C.copy_ev[0], st));
+    const uint8_t* dpay = static_cast<const uint8_t*>(C.b[S_PAYLOAD].p);
+    for (uint64_t off = 0, k = 0; off < payload_len; off += kCopyChunk, ++k) {
+        const size_t len = size_t(std::min<uint64_t>(kCopyChunk, payload_len - off));
+        CRX_CUDA(cudaMemcpyAsync(oh + bt + off, dpay + off, len, cudaMemcpyDeviceToHost, st));
+        CRX_CUDA(cudaEventRecord(C.copy_ev[1 + k], st));
+    }
+    trace_phase(C, "encode: copies queued");
     out->stream = st;
     out->table = oh;
-    out->dpay = static_cast<const uint8_t*>(C.b[S_PAYLOAD].p);
+    out->pending = true;
     C.live = out;
     out->changes = total;
     return kOk;

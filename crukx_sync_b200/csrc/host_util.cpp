@@ -114,4 +114,18 @@ void parallel_copy(void* dst, const void* src, size_t n) {
     });
 }
 
+void prefault(void* dst, size_t n) {
+    constexpr size_t kPiece = size_t(2) << 20;
+    if (n < 4 * kPiece) return;
+    const uintptr_t a = (reinterpret_cast<uintptr_t>(dst) + kPiece - 1) & ~uintptr_t(kPiece - 1);
+    const uintptr_t b = (reinterpret_cast<uintptr_t>(dst) + n) & ~uintptr_t(kPiece - 1);
+    if (b > a) madvise(reinterpret_cast<void*>(a), b - a, MADV_HUGEPAGE);
+    const size_t pieces = (n + kPiece - 1) / kPiece;
+    pool().run(pieces, [&](size_t k) {
+        volatile uint8_t* p = static_cast<uint8_t*>(dst) + k * kPiece;
+        const size_t len = std::min(kPiece, n - k * kPiece);
+        for (size_t off = 0; off < len; off += 4096) p[off] = 0;
+    });
+}
+
 }  // namespace crx
