@@ -821,8 +821,13 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     const size_t bt_bytes = 4 * size_t(n_blocks);
     CRX_CUDA(ensure_pinned(C.in_host, bt_bytes + size_t(u.payload_len) + 16, st));
     uint8_t* ih = static_cast<uint8_t*>(C.in_host.p);
-    CRX_CUDA(upload_pipelined(C, C.b[S_A_BB].p, u.block_table, ih, bt_bytes, st));
-    CRX_CUDA(upload_pipelined(C, C.b[S_A_PAYLOAD].p, u.payload, ih + bt_bytes, size_t(u.payload_len), st));
+    CRX_CUDA(ensure_copy_stream(C));
+    CRX_CUDA(cudaEventRecord(C.ev_main, st));
+    CRX_CUDA(cudaStreamWaitEvent(C.copy_stream, C.ev_main, 0));
+    CRX_CUDA(upload_pipelined(C, C.b[S_A_BB].p, u.block_table, ih, bt_bytes, C.copy_stream));
+    CRX_CUDA(upload_pipelined(C, C.b[S_A_PAYLOAD].p, u.payload, ih + bt_bytes, size_t(u.payload_len), C.copy_stream));
+    CRX_CUDA(cudaEventRecord(C.ev_copy, C.copy_stream));
+    CRX_CUDA(cudaStreamWaitEvent(st, C.ev_copy, 0));
     // ---- block offsets and decode
     uint64_t* boff = dev<uint64_t>(C, S_A_BOFF);
     uint64_t* scan_tmp = dev<uint64_t>(C, S_A_SCAN_TMP);

@@ -76,6 +76,9 @@ Ctx::~Ctx() {
     cudaDeviceSynchronize();
     for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
     for (cudaEvent_t e : copy_ev) cudaEventDestroy(e);
+    if (ev_main) cudaEventDestroy(ev_main);
+    if (ev_copy) cudaEventDestroy(ev_copy);
+    if (copy_stream) cudaStreamDestroy(copy_stream);
     for (auto& d : b)
         if (d.p) cudaFree(d.p);
     if (host) cudaFreeHost(host);
@@ -139,6 +142,14 @@ cudaError_t ensure_pinned(DevBuf& buf, size_t bytes, cudaStream_t s) {
     if (e != cudaSuccess) { buf.p = nullptr; return e; }
     buf.cap = cap;
     return cudaSuccess;
+}
+
+cudaError_t ensure_copy_stream(Ctx& c) {
+    if (c.copy_stream) return cudaSuccess;
+    cudaError_t e = cudaEventCreateWithFlags(&c.ev_main, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&c.ev_copy, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&c.copy_stream, cudaStreamNonBlocking);
+    return e;
 }
 
 cudaError_t chunk_events(Ctx& c, size_t n_chunks) {

@@ -37,6 +37,8 @@ cudaError_t upload_pipelined(Ctx& c, void* dev_dst, const void* host_src, uint8_
 // holds at least n timing-free events (Ctx::copy_ev)
 constexpr size_t kCopyChunk = size_t(32) << 20;
 cudaError_t chunk_events(Ctx& c, size_t n);
+// creates Ctx::copy_stream and its two events on first use (the context's device is current)
+cudaError_t ensure_copy_stream(Ctx& c);
 // word of Ctx::small that receives the error flags of an encode whose copies are still in flight
 constexpr int kEncStatusWord = 511;
 
@@ -78,6 +80,10 @@ struct Ctx {
     std::vector<ProfMark> marks;
     double phase_t = 0.0;
     std::vector<cudaEvent_t> copy_ev;   // chunk events of the pipelined host <-> device copies
+    // apply's uploads run on their own stream so that the DMA overlaps the histogram pass;
+    // ev_main orders them after the caller's stream, ev_copy the decode after them
+    cudaStream_t copy_stream = nullptr;
+    cudaEvent_t ev_main = nullptr, ev_copy = nullptr;
     ~Ctx();
 };
 

@@ -178,29 +178,52 @@ Status parse_update(const uint8_t* data, int64_t len, Update* u, std::string* er
     if (!r.varint(&pl) || !r.take(pl, &u->payload)) return bad("update is truncated");
     u->payload_len = pl;
     if (r.remaining() != 0) return bad("trailing bytes after the payload");
-    uint64_t total_bits = 0;
-    const uint8_t* bt = u->block_table;
-    for (int64_t b = 0; b < u->n_blocks; ++b) {
-        uint32_t w;
-        std::memcpy(&w, bt + 4 * b, 4);
-        total_bits += w;
+    // block table, one pass split over the worker threads: the bit total, and every change costs
+    // at least 2 + rice bits (wire.py:204-211)
+    struct Span { int64_t b0, count; int rice; };
+    std::vector<Span> spans;
+    int64_t changes = 0;
+    {
+        int64_t b = 0;
+        for (const TensorHeader& h : u->tensors)
+            for (const Group& g : h.groups) {
+                spans.push_back(Span{b, g.count, g.rice});
+                b += (g.count + kBlock - 1) / kBlock;
+                changes += g.count;
+            }
     }
+    const uint8_t* bt = u->block_table;
+    constexpr int64_t kPer = int64_t(1) << 16;   // blocks per task
+    const size_t n_tasks = size_t((u->n_blocks + kPer - 1) / kPer);
+    std::vector<uint64_t> part_bits(n_tasks, 0);
+    std::vector<uint8_t> part_bad(n_tasks, 0);
+    auto task = [&](size_t k) {
+        const int64_t lo = int64_t(k) * kPer, hi = std::min(u->n_blocks, lo + kPer);
+        // the span holding block lo, then walk forward
+        size_t sp = size_t(std::upper_bound(spans.begin(), spans.end(), lo,
+                                            [](int64_t v, const Span& x) { return v < x.b0; }) - spans.begin()) - 1;
+        uint64_t bits = 0;
+        bool bad_block = false;
+        for (int64_t b = lo; b < hi; ++b) {
+            while (sp + 1 < spans.size() && spans[sp + 1].b0 <= b) ++sp;
+            uint32_t w;
+            std::memcpy(&w, bt + 4 * b, 4);
+            bits += w;
+            const Span& x = spans[sp];
+            const int64_t m = std::min<int64_t>(kBlock, x.count - (b - x.b0) * kBlock);
+            bad_block |= uint64_t(w) < uint64_t(m) * uint64_t(2 + x.rice);
+        }
+        part_bits[k] = bits;
+        part_bad[k] = bad_block;
+    };
+    if (n_tasks > 1) parallel_for(n_tasks, task);
+    else if (n_tasks == 1) task(0);
+    uint64_t total_bits = 0;
+    bool short_block = false;
+    for (size_t k = 0; k < n_tasks; ++k) { total_bits += part_bits[k]; short_block |= part_bad[k] != 0; }
     if ((total_bits + 7) / 8 != uint64_t(pl)) return bad("payload length does not match its block table");
     if ((total_bits & 7) && (u->payload[pl - 1] & ((1u << (8 - (total_bits & 7))) - 1))) return bad("non-zero padding bits");
-    // every change costs at least 2 + rice bits (wire.py:204-211)
-    int64_t b = 0;
-    int64_t changes = 0;
-    for (const TensorHeader& h : u->tensors) {
-        for (const Group& g : h.groups) {
-            changes += g.count;
-            for (int64_t k = 0; k * kBlock < g.count; ++k, ++b) {
-                uint32_t w;
-                std::memcpy(&w, bt + 4 * b, 4);
-                const int64_t m = std::min<int64_t>(kBlock, g.count - k * kBlock);
-                if (uint64_t(w) < uint64_t(m) * uint64_t(2 + g.rice)) return bad("block shorter than its symbols could be");
-            }
-        }
-    }
+    if (short_block) return bad("block shorter than its symbols could be");
     u->total_bits = total_bits;
     u->total_changes = changes;
     return kOk;

@@ -12,10 +12,15 @@
 
 #include <cstddef>
 #include <cstdint>
+#include <functional>
 #include <string>
 #include <vector>
 
 namespace crx {
+
+// fn(0 .. n-1) on the calling thread and a pool of worker threads; returns when all are done
+// (host_util.cpp)
+void parallel_for(size_t n, const std::function<void(size_t)>& fn);
 
 constexpr int kMaxCodeLen = 17;
 constexpr uint32_t kMaxSymbol = 131070;

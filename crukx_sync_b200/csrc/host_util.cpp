@@ -13,6 +13,8 @@
 #include <thread>
 #include <vector>
 
+#include "host_codec.h"
+
 namespace crx {
 
 namespace {
@@ -113,6 +115,8 @@ void parallel_copy(void* dst, const void* src, size_t n) {
         std::memcpy(static_cast<uint8_t*>(dst) + lo, static_cast<const uint8_t*>(src) + lo, len);
     });
 }
+
+void parallel_for(size_t n, const std::function<void(size_t)>& fn) { pool().run(n, fn); }
 
 void prefault(void* dst, size_t n) {
     constexpr size_t kPiece = size_t(2) << 20;
