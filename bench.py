@@ -338,6 +338,40 @@ def run_ours(args, rank, world, dist):
     weight_bytes = 2.0 * total_params
     value = weight_bytes / (ms_step * 1e-3) / 1e9
 
+    # ---- the device-resident path (encode_update_device -> NCCL -> apply from device memory):
+    #      same steps, the update never crosses PCIe; reported beside the bytes-API headline
+    device_path = None
+    if not args.no_device_path:
+        def dstep(events):
+            src, dst = state["src"], state["dst"]
+            events[0].record(stream)
+            t = crx.encode_update_device(src, dst, sender)
+            events[1].record(stream)
+            mine = cdist.allgather_updates_device(t, ranks=[rank])[0]
+            events[2].record(stream)
+            crx.apply_update(recv, mine, receiver)
+            events[3].record(stream)
+            state["src"], state["dst"] = dst, src
+
+        for _ in range(2):
+            dstep([torch.cuda.Event(enable_timing=True) for _ in range(4)])
+        devs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+        barrier()
+        for k in range(args.steps):
+            dstep(devs[k])
+        barrier()
+        for k in recv:
+            assert torch.equal(recv[k], state["src"][k]), f"receiver differs after the device path: {k}"
+        dt = torch.tensor([sum(e[0].elapsed_time(e[3]) for e in devs) / args.steps,
+                           sum(e[0].elapsed_time(e[1]) for e in devs) / args.steps,
+                           sum(e[2].elapsed_time(e[3]) for e in devs) / args.steps], dtype=torch.float64, device=dev)
+        if dist is not None:
+            dist.all_reduce(dt, op=dist.ReduceOp.MAX)
+        d_step, d_enc, d_app = dt.tolist()
+        device_path = {"value": round(2.0 * total_params / (d_step * 1e-3) / 1e9, 2), "unit": "GB/s",
+                       "ms_per_step": round(d_step, 4), "encode_ms": round(d_enc, 4), "apply_ms": round(d_app, 4),
+                       "note": "encode_update_device + NCCL all-gather + apply_update from device memory"}
+
     # ---- per-kernel times on this stream (a separate profiled pass of 2 steps)
     L.crx_ctx_profile(ctx, 1)
     for _ in range(2):
@@ -402,7 +436,7 @@ def run_ours(args, rank, world, dist):
         "exchange_ms": round(ms_ex, 4), "encode_ms": round(ms_enc, 4), "apply_ms": round(ms_app, 4),
         "update_bytes": int(upd_bytes), "bytes_per_changed": round(upd_bytes / max(changed_all, 1), 4),
         "wall_s_timed": round(t_wall, 3),
-        "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e,
+        "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e, "device_path": device_path,
         "gpu_launches": launches, "clocks": clk.summary(),
     }
     return result
@@ -482,6 +516,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="7b", choices=sorted(CONFIGS))
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-device-path", action="store_true", help="skip the device-resident update measurement")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=1_000_000_000, help="elements in the CPU-baseline sample")

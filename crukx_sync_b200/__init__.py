@@ -23,9 +23,9 @@ from dataclasses import dataclass
 import torch
 
 from . import codec
-from .wire import CorruptUpdate, parse, serialize
+from .wire import CorruptUpdate, parse, parse_device, serialize
 
-__all__ = ["encode_update", "apply_update", "UpdateStats", "CorruptUpdate"]
+__all__ = ["encode_update", "apply_update", "encode_update_device", "UpdateStats", "CorruptUpdate"]
 
 
 @dataclass
@@ -52,14 +52,36 @@ def encode_update(old: Mapping[str, torch.Tensor], new: Mapping[str, torch.Tenso
     return data
 
 
-def apply_update(weights: Mapping[str, torch.Tensor], update: bytes,
+def encode_update_device(old: Mapping[str, torch.Tensor], new: Mapping[str, torch.Tensor],
+                         checksums: dict | None = None) -> torch.Tensor:
+    """encode_update whose result stays in device memory: a uint8 CUDA tensor holding exactly the
+    bytes encode_update returns, on the tensors' device (CPU tensors: the current CUDA device).
+    For transports that move updates between GPUs (NCCL, NVLink) without a host round trip.
+    The sender cache follows the same rule: it is updated only once the update exists."""
+    if old.keys() != new.keys():
+        raise ValueError(f"old and new differ in tensor names: {sorted(old.keys() ^ new.keys())[:5]}")
+    with torch.no_grad():
+        update = codec.encode(old, new, checksums, device_result=True)
+        dev = getattr(update, "device", None)
+        if dev is None or dev.type != "cuda":
+            dev = torch.device("cuda", torch.cuda.current_device())
+        data = update.to_device(dev)
+    update.close()
+    if checksums is not None:
+        checksums.update(update.checksums)
+    return data
+
+
+def apply_update(weights: Mapping[str, torch.Tensor], update,
                  checksums: dict | None = None) -> UpdateStats:
-    """Write the update into `weights` in place; on any error nothing is written."""
+    """Write the update into `weights` in place; on any error nothing is written.  `update` is the
+    bytes encode_update returned, or (no reference counterpart) the uint8 CUDA tensor that
+    encode_update_device returned, read where it lies."""
     t0 = time.perf_counter()
-    u = parse(update)
+    u = parse_device(update) if isinstance(update, torch.Tensor) else parse(update)
     codec._trace("parse", t0)
     t1 = time.perf_counter()
     with torch.no_grad():
         changed = codec.apply(weights, u, checksums)
     codec._trace("apply (C-ABI call)", t1)
-    return UpdateStats(u.n_tensors, changed, len(update))
+    return UpdateStats(u.n_tensors, changed, update.numel() if isinstance(update, torch.Tensor) else len(update))

@@ -13,7 +13,7 @@ import threading
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(_HERE, "libcrukx_b200.so")
 
-CRX_OK, CRX_VALUE_ERROR, CRX_CORRUPT, CRX_CUDA_ERROR, CRX_NO_MEMORY, CRX_BAD_ARGUMENT = range(6)
+CRX_OK, CRX_VALUE_ERROR, CRX_CORRUPT, CRX_CUDA_ERROR, CRX_NO_MEMORY, CRX_BAD_ARGUMENT, CRX_NEED_MORE = range(7)
 
 EXPORTS = [
     "crx_wire_version", "crx_ctx_create", "crx_ctx_destroy", "crx_ctx_launches", "crx_ctx_profile",
@@ -22,6 +22,7 @@ EXPORTS = [
     "crx_update_changes", "crx_update_tensor", "crx_update_group", "crx_update_tensor_table", "crx_update_n_tables", "crx_update_table",
     "crx_update_table_entries", "crx_update_n_blocks", "crx_update_block_bits", "crx_update_payload",
     "crx_update_free", "crx_apply", "crx_huffman_lengths", "crx_checksum", "crx_checksum_noalloc",
+    "crx_encode_device", "crx_encoded_copy_device", "crx_parse_head", "crx_parse_device",
 ]
 
 _lib = None
@@ -72,6 +73,11 @@ def load():
             "crx_huffman_lengths": ([P, I64, P], ctypes.c_int),
             "crx_checksum": ([P, P, I64, P, P, CP, SZ], ctypes.c_int),
             "crx_checksum_noalloc": ([P, I64, P, P, CP, SZ], ctypes.c_int),
+            "crx_encode_device": ([P, I32, P, P, P, P, P, P, P, P, ctypes.POINTER(P), CP, SZ], ctypes.c_int),
+            "crx_encoded_copy_device": ([P, P, I64, P], ctypes.c_int),
+            "crx_parse_head": ([P, I64, I64, ctypes.c_uint8, ctypes.POINTER(P), ctypes.POINTER(I64), CP, SZ],
+                               ctypes.c_int),
+            "crx_parse_device": ([P, I64, P, ctypes.POINTER(P), CP, SZ], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

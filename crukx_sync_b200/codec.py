@@ -85,7 +85,7 @@ def _raise(status: int, err) -> None:
 
 
 def encode(old: Mapping[str, torch.Tensor], new: Mapping[str, torch.Tensor],
-           checksums: dict | None = None) -> EncodedUpdate:
+           checksums: dict | None = None, device_result: bool = False) -> EncodedUpdate:
     """The encoded update (not yet bytes); ``.checksums`` holds what the sender cache commits."""
     names = list(old)
     olds = [old[n] for n in names]
@@ -96,14 +96,14 @@ def encode(old: Mapping[str, torch.Tensor], new: Mapping[str, torch.Tensor],
         if a.numel() != b.numel():
             raise ValueError(f"{name}: old and new differ in shape")
     if not names:
-        return _encode_on(torch.device("cpu"), [], [], [], None)
+        return _encode_on(torch.device("cpu"), [], [], [], None, device_result)
     devs = {t.device for t in olds} | {t.device for t in news}
     if len(devs) != 1:
         raise ValueError("all tensors must be on one device")
-    return _encode_on(next(iter(devs)), names, olds, news, checksums)
+    return _encode_on(next(iter(devs)), names, olds, news, checksums, device_result)
 
 
-def _encode_on(dev, names, olds, news, checksums) -> EncodedUpdate:
+def _encode_on(dev, names, olds, news, checksums, device_result=False) -> EncodedUpdate:
     cdev = _cuda_device(dev)
     if dev.type != "cuda":
         olds = [a.to(cdev) for a in olds]
@@ -124,12 +124,15 @@ def _encode_on(dev, names, olds, news, checksums) -> EncodedUpdate:
     err = ctypes.create_string_buffer(1024)
     with torch.cuda.device(cdev):
         stream = torch.cuda.current_stream(cdev).cuda_stream
-        st = L.crx_encode(_ext.context(cdev.index), k, prev, cur, numel, name_ptrs, name_len, cache, has,
-                          ctypes.c_void_p(stream), ctypes.byref(h), err, 1024)
+        fn = L.crx_encode_device if device_result else L.crx_encode
+        st = fn(_ext.context(cdev.index), k, prev, cur, numel, name_ptrs, name_len, cache, has,
+                ctypes.c_void_p(stream), ctypes.byref(h), err, 1024)
     del keep
     if st != _ext.CRX_OK:
         _raise(st, err)
-    return EncodedUpdate(h, names)
+    out = EncodedUpdate(h, names)
+    out.device = cdev
+    return out
 
 
 def _cache_get(checksums, name, t):

@@ -696,6 +696,10 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
                   cudaStream_t st, int64_t* changed, std::string* err) {
     *changed = 0;
     const int nt = int(u.tensors.size());
+    if (u.payload_len && !u.payload && !u.payload_device) {
+        *err = "the update was parsed from its head only; its payload is not at hand";
+        return kValueError;
+    }
     if (nt == 0) return kOk;
     trace_phase(C, "apply: start");
     // ---- host tables
@@ -825,7 +829,11 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     CRX_CUDA(cudaEventRecord(C.ev_main, st));
     CRX_CUDA(cudaStreamWaitEvent(C.copy_stream, C.ev_main, 0));
     CRX_CUDA(upload_pipelined(C, C.b[S_A_BB].p, u.block_table, ih, bt_bytes, C.copy_stream));
-    CRX_CUDA(upload_pipelined(C, C.b[S_A_PAYLOAD].p, u.payload, ih + bt_bytes, size_t(u.payload_len), C.copy_stream));
+    if (u.payload)
+        CRX_CUDA(upload_pipelined(C, C.b[S_A_PAYLOAD].p, u.payload, ih + bt_bytes, size_t(u.payload_len), C.copy_stream));
+    else if (u.payload_len)   // the update lives in device memory
+        CRX_CUDA(cudaMemcpyAsync(C.b[S_A_PAYLOAD].p, u.payload_device, size_t(u.payload_len), cudaMemcpyDeviceToDevice,
+                                 C.copy_stream));
     CRX_CUDA(cudaEventRecord(C.ev_copy, C.copy_stream));
     CRX_CUDA(cudaStreamWaitEvent(st, C.ev_copy, 0));
     // ---- block offsets and decode

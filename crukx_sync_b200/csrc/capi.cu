@@ -19,6 +19,7 @@ struct crx_encoded {
 };
 struct crx_update {
     crx::Update u;
+    std::vector<uint8_t> head;   // the update's head copied from device memory (crx_parse_device)
 };
 
 namespace crx {
@@ -173,6 +174,21 @@ cudaError_t upload_pipelined(Ctx& c, void* dev_dst, const void* host_src, uint8_
 }
 
 cudaError_t Encoded::write(uint8_t* dst) const {
+    if (device) {   // from the device workspace, synchronously
+        cudaError_t e = cudaEventSynchronize(ctx->copy_ev[0]);
+        if (e != cudaSuccess) return e;
+        if (ctx->small[kEncStatusWord] & ERR_INTERNAL) return cudaErrorUnknown;
+        std::memcpy(dst, head.data(), head.size());
+        dst += head.size();
+        const size_t bt = 4 * size_t(n_blocks);
+        if (bt) e = cudaMemcpyAsync(dst, dtable, bt, cudaMemcpyDeviceToHost, stream);
+        dst += bt;
+        std::memcpy(dst, len_varint.data(), len_varint.size());
+        dst += len_varint.size();
+        if (e == cudaSuccess && payload_len) e = cudaMemcpyAsync(dst, dpay, payload_len, cudaMemcpyDeviceToHost, stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+        return e;
+    }
     if (pending) prefault(dst, size());   // the GPU is still packing and copying meanwhile
     std::memcpy(dst, head.data(), head.size());
     dst += head.size();
@@ -201,7 +217,54 @@ cudaError_t Encoded::write(uint8_t* dst) const {
     return cudaSuccess;
 }
 
+cudaError_t Encoded::write_device(uint8_t* dst, cudaStream_t s) const {
+    const size_t bt = 4 * size_t(n_blocks);
+    cudaError_t e = cudaSuccess;
+    if (device) {
+        e = cudaEventSynchronize(ctx->copy_ev[0]);
+        if (e != cudaSuccess) return e;
+        if (ctx->small[kEncStatusWord] & ERR_INTERNAL) return cudaErrorUnknown;
+        // the header and the length varint are a few KB of host bytes; the rest moves on the device
+        e = cudaMemcpyAsync(dst, head.data(), head.size(), cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess && bt) e = cudaMemcpyAsync(dst + head.size(), dtable, bt, cudaMemcpyDeviceToDevice, s);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(dst + head.size() + bt, len_varint.data(), len_varint.size(), cudaMemcpyHostToDevice, s);
+        if (e == cudaSuccess && payload_len)
+            e = cudaMemcpyAsync(dst + head.size() + bt + len_varint.size(), dpay, payload_len, cudaMemcpyDeviceToDevice, s);
+        // pageable host sources: make sure they were read before head/len_varint can go away
+        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        return e;
+    }
+    if (pending) {
+        e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) return e;
+        if (ctx->small[kEncStatusWord] & ERR_INTERNAL) return cudaErrorUnknown;
+    } else if (internal_error) {
+        return cudaErrorUnknown;
+    }
+    std::vector<uint8_t> all(size());
+    e = write(all.data());
+    if (e == cudaSuccess) e = cudaMemcpyAsync(dst, all.data(), all.size(), cudaMemcpyHostToDevice, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    return e;
+}
+
 cudaError_t Encoded::detach() {
+    if (device) {   // keep a host copy: the next encode reuses the device workspace
+        const cudaError_t e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) return e;
+        internal_error = (ctx->small[kEncStatusWord] & ERR_INTERNAL) != 0;
+        const size_t bt = 4 * size_t(n_blocks);
+        std::vector<uint8_t> tmp(bt + payload_len);
+        cudaError_t r = cudaSuccess;
+        if (bt) r = cudaMemcpy(tmp.data(), dtable, bt, cudaMemcpyDeviceToHost);
+        if (r == cudaSuccess && payload_len) r = cudaMemcpy(tmp.data() + bt, dpay, payload_len, cudaMemcpyDeviceToHost);
+        if (r != cudaSuccess) return r;
+        own.swap(tmp);
+        table = own.data();
+        device = false;
+        return cudaSuccess;
+    }
     if (!pending) return cudaSuccess;
     const cudaError_t e = cudaStreamSynchronize(stream);
     if (e != cudaSuccess) return e;
@@ -298,6 +361,51 @@ int crx_encode(crx_ctx* ctx, int32_t n_tensors, const int16_t* const* prev, cons
     }
 }
 
+int crx_encode_device(crx_ctx* ctx, int32_t n_tensors, const int16_t* const* prev, const int16_t* const* cur,
+                      const int64_t* numel, const uint8_t* const* names, const int64_t* name_len,
+                      const uint64_t* cached_checksums, const uint8_t* has_cached, void* stream,
+                      crx_encoded** out, char* err, size_t errlen) {
+    if (!ctx || !out || n_tensors < 0 || (n_tensors && (!prev || !cur || !numel || !names || !name_len))) {
+        put_err(err, errlen, "crx_encode_device: bad argument");
+        return CRX_BAD_ARGUMENT;
+    }
+    *out = nullptr;
+    try {
+        std::lock_guard<std::mutex> lock(ctx->c.mu);
+        DeviceGuard g(ctx->c.device);
+        crx_encoded* e = new crx_encoded;
+        std::string msg;
+        const crx::Status s = crx::encode_impl(ctx->c, n_tensors, prev, cur, numel, names, name_len, cached_checksums,
+                                               has_cached, static_cast<cudaStream_t>(stream), &e->e, &msg, true);
+        if (s != crx::kOk) {
+            delete e;
+            put_err(err, errlen, msg);
+            return int(s);
+        }
+        *out = e;
+        return CRX_OK;
+    } catch (const std::bad_alloc&) {
+        put_err(err, errlen, "crx_encode_device: out of host memory");
+        return CRX_NO_MEMORY;
+    } catch (const std::exception& ex) {
+        put_err(err, errlen, std::string("crx_encode_device: ") + ex.what());
+        return CRX_CUDA_ERROR;
+    }
+}
+
+int crx_encoded_copy_device(const crx_encoded* enc, void* dst, int64_t cap, void* stream) {
+    if (!enc || !dst || cap < int64_t(enc->e.size())) return CRX_BAD_ARGUMENT;
+    cudaError_t e;
+    if (enc->e.ctx) {
+        std::lock_guard<std::mutex> lock(enc->e.ctx->mu);
+        DeviceGuard g(enc->e.ctx->device);
+        e = enc->e.write_device(static_cast<uint8_t*>(dst), static_cast<cudaStream_t>(stream));
+    } else {
+        e = enc->e.write_device(static_cast<uint8_t*>(dst), static_cast<cudaStream_t>(stream));
+    }
+    return e == cudaSuccess ? CRX_OK : CRX_CUDA_ERROR;
+}
+
 int64_t crx_encoded_size(const crx_encoded* enc) { return enc ? int64_t(enc->e.size()) : -1; }
 
 int crx_encoded_copy(const crx_encoded* enc, uint8_t* dst, int64_t cap) {
@@ -328,7 +436,7 @@ void crx_encoded_free(crx_encoded* enc) {
     if (enc->e.ctx) {
         std::lock_guard<std::mutex> lock(enc->e.ctx->mu);
         // copies still landing in the context's pinned buffer must finish before it is reused
-        if (enc->e.pending) {
+        if (enc->e.pending || enc->e.device) {
             DeviceGuard g(enc->e.ctx->device);
             cudaStreamSynchronize(enc->e.stream);
         }
@@ -353,6 +461,72 @@ int crx_parse(const uint8_t* data, int64_t len, crx_update** out, char* err, siz
         return CRX_OK;
     } catch (const std::bad_alloc&) {
         put_err(err, errlen, "crx_parse: out of host memory");
+        return CRX_NO_MEMORY;
+    }
+}
+
+int crx_parse_head(const uint8_t* head, int64_t head_len, int64_t len, uint8_t last, crx_update** out, int64_t* need,
+                   char* err, size_t errlen) {
+    if (!out || len < 0 || head_len < 0 || (head_len && !head)) return CRX_BAD_ARGUMENT;
+    *out = nullptr;
+    if (need) *need = 0;
+    try {
+        crx_update* u = new crx_update;
+        std::string msg;
+        int64_t nd = 0;
+        const crx::Status s = crx::parse_head(head, head_len, len, last, &u->u, &nd, &msg);
+        if (s != crx::kOk) {
+            delete u;
+            if (s == crx::kNeedMore) {
+                if (need) *need = nd;
+                return CRX_NEED_MORE;
+            }
+            put_err(err, errlen, msg);
+            return int(s);
+        }
+        *out = u;
+        return CRX_OK;
+    } catch (const std::bad_alloc&) {
+        put_err(err, errlen, "crx_parse_head: out of host memory");
+        return CRX_NO_MEMORY;
+    }
+}
+
+int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update** out, char* err, size_t errlen) {
+    if (!out || len < 0 || (len && !data)) return CRX_BAD_ARGUMENT;
+    *out = nullptr;
+    try {
+        const cudaStream_t st = static_cast<cudaStream_t>(stream);
+        uint8_t last = 0;
+        if (len && cudaMemcpyAsync(&last, data + len - 1, 1, cudaMemcpyDeviceToHost, st) != cudaSuccess) return CRX_CUDA_ERROR;
+        std::vector<uint8_t> head;
+        int64_t have = std::min<int64_t>(len, int64_t(1) << 16);
+        for (;;) {   // copy a head, parse it, copy more when the header or block table reaches past it
+            const int64_t old = int64_t(head.size());
+            head.resize(size_t(have));
+            if (have > old && cudaMemcpyAsync(head.data() + old, data + old, size_t(have - old), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                return CRX_CUDA_ERROR;
+            if (cudaStreamSynchronize(st) != cudaSuccess) return CRX_CUDA_ERROR;
+            crx_update* u = new crx_update;
+            std::string msg;
+            int64_t nd = 0;
+            const crx::Status s = crx::parse_head(head.data(), have, len, last, &u->u, &nd, &msg);
+            if (s == crx::kOk) {
+                u->u.payload_device = data + u->u.payload_offset;
+                u->u.payload = nullptr;
+                u->head.swap(head);   // the header's pointers stay valid: the vector's buffer moves with it
+                *out = u;
+                return CRX_OK;
+            }
+            delete u;
+            if (s != crx::kNeedMore) {
+                put_err(err, errlen, msg);
+                return int(s);
+            }
+            have = std::min(len, std::max(nd, 4 * have));
+        }
+    } catch (const std::bad_alloc&) {
+        put_err(err, errlen, "crx_parse_device: out of host memory");
         return CRX_NO_MEMORY;
     }
 }
@@ -423,7 +597,7 @@ int crx_update_block_bits(const crx_update* u, uint32_t* out) {
 int crx_update_payload(const crx_update* u, const uint8_t** data, int64_t* len) {
     if (!u) return CRX_BAD_ARGUMENT;
     if (data) *data = u->u.payload;
-    if (len) *len = u->u.payload_len;
+    if (len) *len = u->u.payload ? u->u.payload_len : 0;   // none at hand: head-only or device update
     return CRX_OK;
 }
 

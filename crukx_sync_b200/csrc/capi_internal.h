@@ -26,6 +26,9 @@ struct Encoded {
     bool pending = false;              // device -> host copies into `table` still in flight: ctx->copy_ev[0]
                                        // covers the block table and the error flags, copy_ev[1 + k] payload chunk k
     bool internal_error = false;       // the encoder's consistency check failed (seen once the copies landed)
+    bool device = false;               // block table and payload stay in the context's device workspace
+    const uint8_t* dtable = nullptr;   // (device) block table
+    const uint8_t* dpay = nullptr;     // (device) payload
     std::vector<uint8_t> own;          // block table + payload after detach()
     int64_t n_blocks = 0;
     uint64_t payload_len = 0;
@@ -38,13 +41,16 @@ struct Encoded {
     // Serialized bytes into dst (size() bytes): cudaSuccess, a CUDA error, or cudaErrorUnknown when
     // the encoder's consistency check failed.  Pre-faults dst while the copies are in flight.
     cudaError_t write(uint8_t* dst) const;   // capi.cu
+    // The same bytes into device memory on `s` (stream-ordered; nothing is read back).
+    cudaError_t write_device(uint8_t* dst, cudaStream_t s) const;   // capi.cu
     cudaError_t detach();                    // capi.cu: wait for the copies and keep a private copy
 };
 
 // Encode n tensors (device pointers).  cache_chk/has_cache may be null.
 Status encode_impl(Ctx& C, int n, const int16_t* const* prev, const int16_t* const* cur, const int64_t* numel,
                    const uint8_t* const* names, const int64_t* name_len, const uint64_t* cache_chk,
-                   const uint8_t* has_cache, cudaStream_t st, Encoded* out, std::string* err);
+                   const uint8_t* has_cache, cudaStream_t st, Encoded* out, std::string* err,
+                   bool device_result = false);
 
 // Verify `u` against `weights` (one device pointer per update tensor, same order) and commit on
 // success.  old_chk/has_chk: the receiver's trusted checksum of each tensor's current contents.

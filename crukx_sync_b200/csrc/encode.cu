@@ -812,7 +812,7 @@ struct HostTables {
 
 Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* const* cur, const int64_t* numel,
                    const uint8_t* const* names, const int64_t* name_len, const uint64_t* cache_chk,
-                   const uint8_t* has_cache, cudaStream_t st, Encoded* out, std::string* err) {
+                   const uint8_t* has_cache, cudaStream_t st, Encoded* out, std::string* err, bool device_result) {
     if (C.live) {           // an earlier result still reads the output buffers: give it its own copy
         const cudaError_t de = C.live->detach();
         C.live = nullptr;
@@ -1200,6 +1200,18 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     put_varint(out->len_varint, payload_len);
     out->n_blocks = n_blocks;
     out->payload_len = payload_len;
+    out->changes = total;
+    if (device_result) {   // block table and payload stay on the device; only the error flags come back
+        CRX_CUDA(chunk_events(C, 1));
+        CRX_CUDA(cudaMemcpyAsync(C.small + kEncStatusWord, counters + 1, 8, cudaMemcpyDeviceToHost, st));
+        CRX_CUDA(cudaEventRecord(C.copy_ev[0], st));
+        out->stream = st;
+        out->device = true;
+        out->dtable = static_cast<const uint8_t*>(C.b[S_BB32].p);
+        out->dpay = static_cast<const uint8_t*>(C.b[S_PAYLOAD].p);
+        C.live = out;
+        return kOk;
+    }
     // block table, error flags and payload go to pinned memory behind k_pack; nothing waits for
     // them here: the serializer pre-faults its destination meanwhile (Encoded::write)
     const size_t bt = 4 * size_t(n_blocks);

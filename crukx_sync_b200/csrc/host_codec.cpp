@@ -10,19 +10,36 @@ namespace crx {
 
 namespace {
 
-// Sequential reader: any overrun is a corrupt update (wire.py:92-123).
+// Sequential reader over an update of n bytes of which the first `avail` are at hand: reading
+// past n is a corrupt update (wire.py:92-123); reading past `avail` fails too but records in
+// `need` how many bytes the read wanted, so the caller can fetch more and parse again.
 struct Reader {
     const uint8_t* d;
     int64_t n;
+    int64_t avail;
     int64_t pos = 0;
-    bool take(int64_t k, const uint8_t** p) {
+    int64_t need = 0;
+    bool have(int64_t k) {
         if (k < 0 || k > n - pos) return false;
+        if (k > avail - pos) {
+            need = std::max(need, pos + k);
+            return false;
+        }
+        return true;
+    }
+    bool take(int64_t k, const uint8_t** p) {
+        if (!have(k)) return false;
         *p = d + pos;
         pos += k;
         return true;
     }
+    bool skip(int64_t k) {   // bytes the parser does not look at (the payload)
+        if (k < 0 || k > n - pos) return false;
+        pos += k;
+        return true;
+    }
     bool u8(int* v) {
-        if (pos >= n) return false;
+        if (!have(1)) return false;
         *v = d[pos++];
         return true;
     }
@@ -74,9 +91,21 @@ bool valid_utf8(const uint8_t* s, int64_t n) {
 
 }  // namespace
 
-Status parse_update(const uint8_t* data, int64_t len, Update* u, std::string* err) {
-    auto bad = [&](const char* m) { if (err) *err = m; return kCorrupt; };
-    Reader r{data, len};
+namespace {
+
+// The whole parse over the first `avail` of `len` bytes; `last` is the update's final byte (the
+// padding check needs it).  kNeedMore with *need set when the head does not fit in `avail`.
+Status parse_core(const uint8_t* data, int64_t avail, int64_t len, uint8_t last, Update* u, int64_t* need,
+                  std::string* err) {
+    Reader r{data, len, avail};
+    auto bad = [&](const char* m) {
+        if (r.need > 0) {   // ran out of the bytes at hand, not out of the update
+            if (need) *need = r.need;
+            return kNeedMore;
+        }
+        if (err) *err = m;
+        return kCorrupt;
+    };
     const uint8_t* p;
     int v;
     int64_t x;
@@ -175,7 +204,10 @@ Status parse_update(const uint8_t* data, int64_t len, Update* u, std::string* er
     u->n_blocks = int64_t(total_blocks);
     if (!r.take(4 * u->n_blocks, &u->block_table)) return bad("update is truncated");
     int64_t pl;
-    if (!r.varint(&pl) || !r.take(pl, &u->payload)) return bad("update is truncated");
+    if (!r.varint(&pl)) return bad("update is truncated");
+    u->payload_offset = r.pos;
+    if (!r.skip(pl)) return bad("update is truncated");
+    u->payload = r.pos <= avail ? data + u->payload_offset : nullptr;
     u->payload_len = pl;
     if (r.remaining() != 0) return bad("trailing bytes after the payload");
     // block table, one pass split over the worker threads: the bit total, and every change costs
@@ -222,11 +254,22 @@ Status parse_update(const uint8_t* data, int64_t len, Update* u, std::string* er
     bool short_block = false;
     for (size_t k = 0; k < n_tasks; ++k) { total_bits += part_bits[k]; short_block |= part_bad[k] != 0; }
     if ((total_bits + 7) / 8 != uint64_t(pl)) return bad("payload length does not match its block table");
-    if ((total_bits & 7) && (u->payload[pl - 1] & ((1u << (8 - (total_bits & 7))) - 1))) return bad("non-zero padding bits");
+    if ((total_bits & 7) && (last & ((1u << (8 - (total_bits & 7))) - 1))) return bad("non-zero padding bits");
     if (short_block) return bad("block shorter than its symbols could be");
     u->total_bits = total_bits;
     u->total_changes = changes;
     return kOk;
+}
+
+}  // namespace
+
+Status parse_update(const uint8_t* data, int64_t len, Update* u, std::string* err) {
+    return parse_core(data, len, len, len > 0 ? data[len - 1] : 0, u, nullptr, err);
+}
+
+Status parse_head(const uint8_t* head, int64_t head_len, int64_t len, uint8_t last, Update* u, int64_t* need,
+                  std::string* err) {
+    return parse_core(head, std::min(head_len, len), len, last, u, need, err);
 }
 
 // ---------------------------------------------------------------- Huffman

@@ -28,7 +28,7 @@ constexpr uint32_t kSymSpace = kMaxSymbol + 1;
 constexpr int kMaxRice = 30;
 constexpr int kBlock = 256;
 
-enum Status : int { kOk = 0, kValueError = 1, kCorrupt = 2, kCudaError = 3, kNoMemory = 4, kBadArgument = 5 };
+enum Status : int { kOk = 0, kValueError = 1, kCorrupt = 2, kCudaError = 3, kNoMemory = 4, kBadArgument = 5, kNeedMore = 6 };
 
 struct Table {
     int exponent = 0;
@@ -56,7 +56,9 @@ struct Update {
     std::vector<TensorHeader> tensors;
     const uint8_t* block_table = nullptr;  // n_blocks little-endian u32 words, borrowed
     int64_t n_blocks = 0;
-    const uint8_t* payload = nullptr;      // borrowed
+    const uint8_t* payload = nullptr;      // borrowed; null when only the head was parsed
+    int64_t payload_offset = 0;            // of the payload within the update
+    const uint8_t* payload_device = nullptr;  // the payload in device memory (update parsed from its head)
     int64_t payload_len = 0;
     uint64_t total_bits = 0;
     int64_t total_changes = 0;
@@ -65,6 +67,13 @@ struct Update {
 // Parse and validate `data` exactly as the reference's wire.parse does; the result borrows
 // `data`, which must outlive it.  Returns kOk or kCorrupt (message in *err).
 Status parse_update(const uint8_t* data, int64_t len, Update* out, std::string* err);
+
+// The same parse from the update's head only: `head` holds its first head_len of len bytes and
+// `last` is its final byte.  Every check is the same as parse_update's (the payload bytes are
+// never inspected except the last, for the padding bits).  Returns kNeedMore with *need = a length
+// the head must at least have when the header or block table reaches past head_len.
+Status parse_head(const uint8_t* head, int64_t head_len, int64_t len, uint8_t last, Update* out, int64_t* need,
+                  std::string* err);
 
 // Length-limited Huffman code lengths with the reference's tie order.
 void huffman_lengths(const uint64_t* counts, int64_t n, uint8_t* lengths);

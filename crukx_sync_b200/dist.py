@@ -12,6 +12,8 @@ N grows.
     upd = crukx_sync_b200.encode_update(prev_mine, cur_mine, send_chk)
     for u in allgather_updates(upd, ranks=holders):
         crukx_sync_b200.apply_update(weights, u, recv_chk)
+
+With encode_update_device and allgather_updates_device the updates stay in GPU memory end to end.
 """
 
 from __future__ import annotations
@@ -67,3 +69,26 @@ def allgather_updates(update: bytes, group=None, device: torch.device | None = N
     td.all_gather_into_tensor(out, buf, group=group)
     want = range(world) if ranks is None else ranks
     return [out[r * mx: r * mx + sizes[r]].cpu().numpy().tobytes() for r in want]
+
+
+def allgather_updates_device(update, group=None, ranks: Sequence[int] | None = None) -> list:
+    """allgather_updates for device-resident updates (uint8 CUDA tensors from
+    encode_update_device): the sizes, then the padded updates, gathered into one device buffer
+    over NCCL; returns device views of the requested ranks' updates, ready for apply_update."""
+    import torch.distributed as td
+
+    world = td.get_world_size(group) if td.is_initialized() else 1
+    if world == 1:
+        return [update]
+    device = update.device
+    n = torch.tensor([update.numel()], dtype=torch.int64, device=device)
+    sizes_t = torch.empty(world, dtype=torch.int64, device=device)
+    td.all_gather_into_tensor(sizes_t, n, group=group)
+    sizes = sizes_t.tolist()
+    mx = max(max(sizes), 1)
+    buf = torch.zeros(mx, dtype=torch.uint8, device=device)
+    buf[: update.numel()].copy_(update)
+    out = torch.empty(world * mx, dtype=torch.uint8, device=device)
+    td.all_gather_into_tensor(out, buf, group=group)
+    want = range(world) if ranks is None else ranks
+    return [out[r * mx: r * mx + sizes[r]] for r in want]

@@ -127,6 +127,19 @@ class EncodedUpdate:
             raise RuntimeError("crukx_sync_b200: encoded update copy failed")
         return out
 
+    def to_device(self, device, stream=None):
+        """The serialized update as a uint8 tensor on `device` (a CUDA device): the same bytes as
+        to_bytes(), written on the device without a host round trip of the payload."""
+        import torch
+
+        L = _ext.load()
+        n = int(L.crx_encoded_size(self._h))
+        out = torch.empty(n, dtype=torch.uint8, device=device)
+        st = stream if stream is not None else torch.cuda.current_stream(out.device).cuda_stream
+        if n and L.crx_encoded_copy_device(self._h, ctypes.c_void_p(out.data_ptr()), n, ctypes.c_void_p(st)) != _ext.CRX_OK:
+            raise RuntimeError("crukx_sync_b200: encoded update device copy failed")
+        return out
+
     def close(self):
         if self._h:
             _ext.load().crx_encoded_free(self._h)
@@ -149,7 +162,14 @@ def serialize(u) -> bytes:
 class ParsedUpdate:
     """A validated update (C handle).  Borrows ``data``; attribute views match wire.Update."""
 
-    def __init__(self, data: bytes):
+    def __init__(self, data: bytes | None = None, *, _handle=None, _keep=None):
+        self._tensors = None
+        self._tables = None
+        self._table = None
+        if _handle is not None:   # made by parse_device / parse_head
+            self._data = _keep
+            self._h = _handle
+            return
         L = _ext.load()
         self._data = data if isinstance(data, bytes) else bytes(data)
         self._h = ctypes.c_void_p()
@@ -160,9 +180,6 @@ class ParsedUpdate:
             raise CorruptUpdate(err.value.decode(errors="replace"))
         if st != _ext.CRX_OK:
             raise RuntimeError(f"crukx_sync_b200: parse failed ({st}): {err.value.decode(errors='replace')}")
-        self._tensors = None
-        self._tables = None
-        self._table = None
 
     @property
     def handle(self):
@@ -233,7 +250,7 @@ class ParsedUpdate:
     def payload(self) -> bytes:
         p, n = ctypes.c_void_p(), ctypes.c_int64()
         _ext.load().crx_update_payload(self._h, ctypes.byref(p), ctypes.byref(n))
-        return ctypes.string_at(p, n.value) if n.value else b""
+        return ctypes.string_at(p, n.value) if n.value and p.value else b""
 
     @property
     def changes(self) -> int:
@@ -257,3 +274,46 @@ class ParsedUpdate:
 def parse(data: bytes) -> ParsedUpdate:
     """Parse and structurally validate an update (every limit of the format); CorruptUpdate if not."""
     return ParsedUpdate(data)
+
+
+def parse_device(update, stream=None) -> ParsedUpdate:
+    """parse() for an update held in device memory (a contiguous uint8 CUDA tensor): the head is
+    copied to the host and validated there; the payload stays on the device for apply."""
+    import torch
+
+    if not (isinstance(update, torch.Tensor) and update.dtype == torch.uint8 and update.is_cuda
+            and update.dim() == 1 and update.is_contiguous()):
+        raise ValueError("a device update must be a contiguous 1-D uint8 CUDA tensor")
+    L = _ext.load()
+    h = ctypes.c_void_p()
+    err = ctypes.create_string_buffer(512)
+    st = stream if stream is not None else torch.cuda.current_stream(update.device).cuda_stream
+    with torch.cuda.device(update.device):
+        rc = L.crx_parse_device(ctypes.c_void_p(update.data_ptr() if update.numel() else 0), update.numel(),
+                                ctypes.c_void_p(st), ctypes.byref(h), err, 512)
+    if rc == _ext.CRX_CORRUPT:
+        raise CorruptUpdate(err.value.decode(errors="replace"))
+    if rc != _ext.CRX_OK:
+        raise RuntimeError(f"crukx_sync_b200: device parse failed ({rc}): {err.value.decode(errors='replace')}")
+    return ParsedUpdate(_handle=h, _keep=update)
+
+
+def parse_head(head: bytes, length: int, last: int):
+    """Validate an update from its first bytes: ``head`` = the first bytes of an update of
+    ``length`` bytes whose final byte is ``last``.  Returns a ParsedUpdate (header view only; it
+    cannot be applied), or, when ``head`` is too short, a length the head must at least have (grow
+    it geometrically); CorruptUpdate when the update is invalid (the same verdict as parse())."""
+    L = _ext.load()
+    head = bytes(head)
+    h = ctypes.c_void_p()
+    need = ctypes.c_int64()
+    err = ctypes.create_string_buffer(512)
+    buf = ctypes.cast(ctypes.c_char_p(head), ctypes.c_void_p)
+    rc = L.crx_parse_head(buf, len(head), int(length), int(last) & 0xFF, ctypes.byref(h), ctypes.byref(need), err, 512)
+    if rc == _ext.CRX_NEED_MORE:
+        return int(need.value)
+    if rc == _ext.CRX_CORRUPT:
+        raise CorruptUpdate(err.value.decode(errors="replace"))
+    if rc != _ext.CRX_OK:
+        raise RuntimeError(f"crukx_sync_b200: head parse failed ({rc}): {err.value.decode(errors='replace')}")
+    return ParsedUpdate(_handle=h, _keep=head)

@@ -34,6 +34,7 @@ extern "C" {
 #define CRX_CUDA_ERROR 3
 #define CRX_NO_MEMORY 4
 #define CRX_BAD_ARGUMENT 5
+#define CRX_NEED_MORE 6      /* crx_parse_head: the head given is too short; *need is a lower bound */
 
 typedef struct crx_ctx crx_ctx;
 typedef struct crx_encoded crx_encoded;
@@ -75,10 +76,37 @@ void crx_encoded_checksums(const crx_encoded* enc, uint64_t* checksums, uint8_t*
 void crx_encoded_free(crx_encoded* enc);
 
 /*
+ * Device-resident updates (no reference counterpart: the reference always returns host bytes).
+ * crx_encode_device runs the same encoder but leaves the block table and payload in the context's
+ * device workspace; crx_encoded_copy_device writes the complete update, byte-identical to
+ * crx_encoded_copy's, into device memory `dst` (cap >= crx_encoded_size) on `stream`, reading back
+ * only a status word.  Copy (or free) the result before the next encode on the same context, which
+ * otherwise first moves it to host memory.  crx_encoded_copy also works on such a result.
+ */
+int crx_encode_device(crx_ctx* ctx, int32_t n_tensors, const int16_t* const* prev, const int16_t* const* cur,
+                      const int64_t* numel, const uint8_t* const* names, const int64_t* name_len,
+                      const uint64_t* cached_checksums, const uint8_t* has_cached, void* stream,
+                      crx_encoded** out, char* err, size_t errlen);
+int crx_encoded_copy_device(const crx_encoded* enc, void* dst, int64_t cap, void* stream);
+
+/*
  * Parse and validate an update on the host: every limit of wire.parse
  * (src/crukx_sync/wire.py:126-212).  The handle borrows data[0..len), which must outlive it.
  */
 int crx_parse(const uint8_t* data, int64_t len, crx_update** out, char* err, size_t errlen);
+/* The same validation from the update's head alone (wire.py:126-212 reads the payload only for its
+ * length and final padding bits): head = the first head_len of the update's len bytes, last = its
+ * final byte.  CRX_NEED_MORE when the header or block table reaches past head_len, with *need = a
+ * length the head must at least have (grow it geometrically); otherwise the same verdict as
+ * crx_parse.  The handle borrows `head` and has
+ * no payload (crx_update_payload gives NULL), so it cannot be applied; it serves transports that
+ * validate an update before its payload has arrived. */
+int crx_parse_head(const uint8_t* head, int64_t head_len, int64_t len, uint8_t last, crx_update** out, int64_t* need,
+                   char* err, size_t errlen);
+/* Parse an update held in device memory (len bytes at `data`): its head is copied to the host on
+ * `stream` and validated as crx_parse does; the payload stays where it is and crx_apply reads it
+ * there (data must stay valid until crx_apply returns).  No reference counterpart. */
+int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update** out, char* err, size_t errlen);
 int64_t crx_update_n_tensors(const crx_update* u);
 int64_t crx_update_changes(const crx_update* u);
 int crx_update_tensor(const crx_update* u, int64_t i, const uint8_t** name, int64_t* name_len, int64_t* numel,
@@ -92,6 +120,7 @@ int crx_update_table(const crx_update* u, int32_t k, int32_t* exponent, int64_t*
 int crx_update_table_entries(const crx_update* u, int32_t k, uint32_t* symbols, uint8_t* lengths);
 int64_t crx_update_n_blocks(const crx_update* u);
 int crx_update_block_bits(const crx_update* u, uint32_t* out);
+/* The payload bytes at hand (NULL and 0 for an update parsed from its head or from device memory). */
 int crx_update_payload(const crx_update* u, const uint8_t** data, int64_t* len);
 void crx_update_free(crx_update* u);
 
