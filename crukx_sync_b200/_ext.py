@@ -23,7 +23,13 @@ EXPORTS = [
     "crx_update_table_entries", "crx_update_n_blocks", "crx_update_block_bits", "crx_update_payload",
     "crx_update_free", "crx_apply", "crx_huffman_lengths", "crx_checksum", "crx_checksum_noalloc",
     "crx_encode_device", "crx_encoded_copy_device", "crx_parse_head", "crx_parse_device",
+    "crx_encode_global", "crx_encoded_part", "crx_encoded_part_copy",
 ]
+
+# collective callbacks of crx_encode_global
+SUM_U64_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(ctypes.c_uint64), ctypes.c_int64)
+ALLGATHER_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
+                                ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(ctypes.c_int64))
 
 _lib = None
 _lock = threading.RLock()   # context() calls load() while holding it
@@ -78,6 +84,10 @@ def load():
             "crx_parse_head": ([P, I64, I64, ctypes.c_uint8, ctypes.POINTER(P), ctypes.POINTER(I64), CP, SZ],
                                ctypes.c_int),
             "crx_parse_device": ([P, I64, P, ctypes.POINTER(P), CP, SZ], ctypes.c_int),
+            "crx_encode_global": ([P, I32, P, P, P, P, P, P, P, P, I32, I32, SUM_U64_FN, ALLGATHER_FN, P,
+                                   ctypes.POINTER(P), CP, SZ], ctypes.c_int),
+            "crx_encoded_part": ([P, P, P, P, P, P, P], ctypes.c_int),
+            "crx_encoded_part_copy": ([P, P, P, P, P], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

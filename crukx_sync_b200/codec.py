@@ -135,6 +135,84 @@ def _encode_on(dev, names, olds, news, checksums, device_result=False) -> Encode
     return out
 
 
+def encode_global(old, new, checksums, rank: int, world: int, sum_u64, allgather, ctx=None) -> EncodedUpdate:
+    """This rank's part of one update encoded by `world` ranks (crx_encode_global).
+
+    sum_u64(values: numpy uint64 array) -> None sums in place over ranks; allgather(mine: bytes)
+    -> bytes returns every rank's bytes concatenated in rank order.  Both are called on every
+    rank in the same order.  The part's pieces come from EncodedUpdate.part()."""
+    import numpy as np
+
+    names = list(old)
+    olds = [old[n] for n in names]
+    news = [new[n] for n in names]
+    for name, a, b in zip(names, olds, news):
+        check16(name, a)
+        check16(name, b)
+        if a.numel() != b.numel():
+            raise ValueError(f"{name}: old and new differ in shape")
+    devs = {t.device for t in olds} | {t.device for t in news}
+    if len(devs) > 1:
+        raise ValueError("all tensors must be on one device")
+    dev = next(iter(devs)) if devs else torch.device("cuda", torch.cuda.current_device())
+    cdev = _cuda_device(dev)
+    if dev.type != "cuda":
+        olds = [a.to(cdev) for a in olds]
+        news = [b.to(cdev) for b in news]
+    L = _ext.load()
+    k = len(names)
+    prev = _ext.ptr_array([a.data_ptr() for a in olds])
+    cur = _ext.ptr_array([b.data_ptr() for b in news])
+    numel = (ctypes.c_int64 * max(k, 1))(*[a.numel() for a in olds])
+    keep, name_ptrs, name_len = _name_table(names)
+    if checksums:
+        hits = [checksums.get(n) for n in names]
+        cache = (ctypes.c_uint64 * max(k, 1))(*[int(c) & (2**64 - 1) if c is not None else 0 for c in hits])
+        has = (ctypes.c_uint8 * max(k, 1))(*[c is not None for c in hits])
+    else:
+        cache, has = None, None
+    held = []   # gathered buffers stay alive until the call returns
+
+    def _sum(user, data, n):
+        try:
+            arr = np.ctypeslib.as_array(data, shape=(n,)) if n else np.zeros(0, dtype=np.uint64)
+            sum_u64(arr)
+            return 0
+        except Exception as exc:   # the C side turns a non-zero status into an error
+            held.append(exc)
+            return 1
+
+    def _gather(user, mine, n, all_p, all_len):
+        try:
+            out = allgather(ctypes.string_at(mine, n) if n else b"")
+            buf = ctypes.create_string_buffer(out, max(len(out), 1))
+            held.append(buf)
+            all_p[0] = ctypes.addressof(buf)
+            all_len[0] = len(out)
+            return 0
+        except Exception as exc:
+            held.append(exc)
+            return 1
+
+    sum_cb, gather_cb = _ext.SUM_U64_FN(_sum), _ext.ALLGATHER_FN(_gather)
+    h = ctypes.c_void_p()
+    err = ctypes.create_string_buffer(1024)
+    with torch.cuda.device(cdev):
+        stream = torch.cuda.current_stream(cdev).cuda_stream
+        st = L.crx_encode_global(ctx if ctx is not None else _ext.context(cdev.index), k, prev, cur, numel, name_ptrs,
+                                 name_len, cache, has, ctypes.c_void_p(stream), int(rank), int(world), sum_cb, gather_cb,
+                                 None, ctypes.byref(h), err, 1024)
+    del keep
+    errors = [x for x in held if isinstance(x, Exception)]
+    if errors:
+        raise RuntimeError(f"crukx_sync_b200: a collective failed: {errors[0]!r}") from errors[0]
+    if st != _ext.CRX_OK:
+        _raise(st, err)
+    out = EncodedUpdate(h, names)
+    out.device = cdev
+    return out
+
+
 def _cache_get(checksums, name, t):
     """A cached checksum, trusted only if the tensor was not modified since it was recorded."""
     hit = checksums.get(name) if checksums is not None else None

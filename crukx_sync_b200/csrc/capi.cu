@@ -217,6 +217,22 @@ cudaError_t Encoded::write(uint8_t* dst) const {
     return cudaSuccess;
 }
 
+cudaError_t Encoded::write_part(uint8_t* prefix, uint8_t* tensors, uint8_t* tbl, uint8_t* pay) const {
+    const size_t bt = 4 * size_t(n_blocks);
+    if (pending) {
+        const cudaError_t e = cudaStreamSynchronize(stream);
+        if (e != cudaSuccess) return e;
+        if (ctx->small[kEncStatusWord] & ERR_INTERNAL) return cudaErrorUnknown;
+    } else if (internal_error) {
+        return cudaErrorUnknown;
+    }
+    if (prefix) std::memcpy(prefix, head.data(), head.size());
+    if (tensors && !part_tensors.empty()) std::memcpy(tensors, part_tensors.data(), part_tensors.size());
+    if (tbl && bt) std::memcpy(tbl, table, bt);
+    if (pay && payload_len) parallel_copy(pay, table + bt, payload_len);
+    return cudaSuccess;
+}
+
 cudaError_t Encoded::write_device(uint8_t* dst, cudaStream_t s) const {
     const size_t bt = 4 * size_t(n_blocks);
     cudaError_t e = cudaSuccess;
@@ -393,8 +409,89 @@ int crx_encode_device(crx_ctx* ctx, int32_t n_tensors, const int16_t* const* pre
     }
 }
 
+namespace {
+
+struct CallbackExchange {   // adapts the C callbacks to crx::GlobalExchange
+    crx_sum_u64_fn sum;
+    crx_allgather_fn gather;
+    void* user;
+};
+
+int cb_sum(void* u, uint64_t* d, int64_t n) {
+    auto* x = static_cast<CallbackExchange*>(u);
+    return x->sum(x->user, d, n);
+}
+
+int cb_gather(void* u, const uint8_t* mine, int64_t len, const uint8_t** all, int64_t* all_len) {
+    auto* x = static_cast<CallbackExchange*>(u);
+    return x->gather(x->user, mine, len, all, all_len);
+}
+
+}  // namespace
+
+int crx_encode_global(crx_ctx* ctx, int32_t n_tensors, const int16_t* const* prev, const int16_t* const* cur,
+                      const int64_t* numel, const uint8_t* const* names, const int64_t* name_len,
+                      const uint64_t* cached_checksums, const uint8_t* has_cached, void* stream, int32_t rank,
+                      int32_t world, crx_sum_u64_fn sum_u64, crx_allgather_fn allgather, void* user,
+                      crx_encoded** out, char* err, size_t errlen) {
+    if (!ctx || !out || n_tensors < 0 || (n_tensors && (!prev || !cur || !numel || !names || !name_len)) ||
+        world < 1 || rank < 0 || rank >= world || !sum_u64 || !allgather) {
+        put_err(err, errlen, "crx_encode_global: bad argument");
+        return CRX_BAD_ARGUMENT;
+    }
+    *out = nullptr;
+    try {
+        std::lock_guard<std::mutex> lock(ctx->c.mu);
+        DeviceGuard g(ctx->c.device);
+        CallbackExchange cx{sum_u64, allgather, user};
+        const crx::GlobalExchange gx{cb_sum, cb_gather, &cx, rank, world};
+        crx_encoded* e = new crx_encoded;
+        std::string msg;
+        const crx::Status s = crx::encode_impl(ctx->c, n_tensors, prev, cur, numel, names, name_len, cached_checksums,
+                                               has_cached, static_cast<cudaStream_t>(stream), &e->e, &msg, false, &gx);
+        if (s != crx::kOk) {
+            delete e;
+            put_err(err, errlen, msg);
+            return int(s);
+        }
+        *out = e;
+        return CRX_OK;
+    } catch (const std::bad_alloc&) {
+        put_err(err, errlen, "crx_encode_global: out of host memory");
+        return CRX_NO_MEMORY;
+    } catch (const std::exception& ex) {
+        put_err(err, errlen, std::string("crx_encode_global: ") + ex.what());
+        return CRX_CUDA_ERROR;
+    }
+}
+
+int crx_encoded_part(const crx_encoded* enc, int64_t* prefix_len, int64_t* tensors_len, int64_t* table_len,
+                     int64_t* payload_len, uint64_t* bit_offset, uint64_t* total_bits) {
+    if (!enc || !enc->e.part) return CRX_BAD_ARGUMENT;
+    if (prefix_len) *prefix_len = int64_t(enc->e.head.size());
+    if (tensors_len) *tensors_len = int64_t(enc->e.part_tensors.size());
+    if (table_len) *table_len = 4 * enc->e.n_blocks;
+    if (payload_len) *payload_len = int64_t(enc->e.payload_len);
+    if (bit_offset) *bit_offset = enc->e.bit_offset;
+    if (total_bits) *total_bits = enc->e.total_bits;
+    return CRX_OK;
+}
+
+int crx_encoded_part_copy(const crx_encoded* enc, uint8_t* prefix, uint8_t* tensors, uint8_t* table, uint8_t* payload) {
+    if (!enc || !enc->e.part) return CRX_BAD_ARGUMENT;
+    cudaError_t e;
+    if (enc->e.ctx) {
+        std::lock_guard<std::mutex> lock(enc->e.ctx->mu);
+        DeviceGuard g(enc->e.ctx->device);
+        e = enc->e.write_part(prefix, tensors, table, payload);
+    } else {
+        e = enc->e.write_part(prefix, tensors, table, payload);
+    }
+    return e == cudaSuccess ? CRX_OK : CRX_CUDA_ERROR;
+}
+
 int crx_encoded_copy_device(const crx_encoded* enc, void* dst, int64_t cap, void* stream) {
-    if (!enc || !dst || cap < int64_t(enc->e.size())) return CRX_BAD_ARGUMENT;
+    if (!enc || !dst || enc->e.part || cap < int64_t(enc->e.size())) return CRX_BAD_ARGUMENT;
     cudaError_t e;
     if (enc->e.ctx) {
         std::lock_guard<std::mutex> lock(enc->e.ctx->mu);
@@ -406,10 +503,10 @@ int crx_encoded_copy_device(const crx_encoded* enc, void* dst, int64_t cap, void
     return e == cudaSuccess ? CRX_OK : CRX_CUDA_ERROR;
 }
 
-int64_t crx_encoded_size(const crx_encoded* enc) { return enc ? int64_t(enc->e.size()) : -1; }
+int64_t crx_encoded_size(const crx_encoded* enc) { return enc && !enc->e.part ? int64_t(enc->e.size()) : -1; }
 
 int crx_encoded_copy(const crx_encoded* enc, uint8_t* dst, int64_t cap) {
-    if (!enc || !dst || cap < int64_t(enc->e.size())) return CRX_BAD_ARGUMENT;
+    if (!enc || !dst || enc->e.part || cap < int64_t(enc->e.size())) return CRX_BAD_ARGUMENT;
     cudaError_t e;
     if (enc->e.ctx) {   // the context lock keeps the next encode from reusing the buffers meanwhile
         std::lock_guard<std::mutex> lock(enc->e.ctx->mu);

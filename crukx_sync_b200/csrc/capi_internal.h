@@ -18,6 +18,16 @@ namespace crx {
 // the payload, still in device memory until write() streams it down chunk by chunk, overlapping
 // each chunk's DMA with the host copy of the previous one.  The next encode on the same context
 // first moves block table and payload into `own` (detach()).
+// Collectives of one update encoded by several ranks (crx_encode_global); each returns 0 on
+// success.  sum_u64: element-wise sum over ranks, in place.  allgather_bytes: every rank's bytes
+// concatenated in rank order, in a buffer the caller's side keeps alive until the next call.
+struct GlobalExchange {
+    int (*sum_u64)(void* user, uint64_t* data, int64_t n);
+    int (*allgather_bytes)(void* user, const uint8_t* mine, int64_t len, const uint8_t** all, int64_t* all_len);
+    void* user;
+    int rank, world;
+};
+
 struct Encoded {
     Ctx* ctx = nullptr;
     cudaStream_t stream = nullptr;
@@ -30,6 +40,12 @@ struct Encoded {
     const uint8_t* dtable = nullptr;   // (device) block table
     const uint8_t* dpay = nullptr;     // (device) payload
     std::vector<uint8_t> own;          // block table + payload after detach()
+    // a rank's share of a global update: `head` is then the update's prefix (magic .. tensor count),
+    // part_tensors this rank's tensor headers, and the payload starts bit_offset % 8 bits into its
+    // first byte; total_bits counts the whole update's payload
+    bool part = false;
+    std::vector<uint8_t> part_tensors;
+    uint64_t bit_offset = 0, total_bits = 0;
     int64_t n_blocks = 0;
     uint64_t payload_len = 0;
     std::vector<uint8_t> len_varint;   // payload_len as LEB128
@@ -41,6 +57,8 @@ struct Encoded {
     // Serialized bytes into dst (size() bytes): cudaSuccess, a CUDA error, or cudaErrorUnknown when
     // the encoder's consistency check failed.  Pre-faults dst while the copies are in flight.
     cudaError_t write(uint8_t* dst) const;   // capi.cu
+    // A part of a global update: its prefix, tensor headers, block table and payload (any may be null).
+    cudaError_t write_part(uint8_t* prefix, uint8_t* tensors, uint8_t* table, uint8_t* payload) const;   // capi.cu
     // The same bytes into device memory on `s` (stream-ordered; nothing is read back).
     cudaError_t write_device(uint8_t* dst, cudaStream_t s) const;   // capi.cu
     cudaError_t detach();                    // capi.cu: wait for the copies and keep a private copy
@@ -50,7 +68,7 @@ struct Encoded {
 Status encode_impl(Ctx& C, int n, const int16_t* const* prev, const int16_t* const* cur, const int64_t* numel,
                    const uint8_t* const* names, const int64_t* name_len, const uint64_t* cache_chk,
                    const uint8_t* has_cache, cudaStream_t st, Encoded* out, std::string* err,
-                   bool device_result = false);
+                   bool device_result = false, const GlobalExchange* gx = nullptr);
 
 // Verify `u` against `weights` (one device pointer per update tensor, same order) and commit on
 // success.  old_chk/has_chk: the receiver's trusted checksum of each tensor's current contents.

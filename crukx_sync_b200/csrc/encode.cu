@@ -745,7 +745,7 @@ __global__ void __launch_bounds__(256) k_pack(const uint64_t* __restrict__ g_sta
                                               int64_t ng, int64_t n_blocks, const uint32_t* __restrict__ local,
                                               const uint32_t* __restrict__ vals, const uint32_t* __restrict__ dense_code,
                                               const uint32_t* __restrict__ big_code, const uint64_t* __restrict__ block_off,
-                                              uint32_t* __restrict__ words) {
+                                              uint32_t* __restrict__ words, uint32_t bit0) {
     const int64_t b = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (b >= n_blocks) return;
@@ -755,7 +755,7 @@ __global__ void __launch_bounds__(256) k_pack(const uint64_t* __restrict__ g_sta
     const uint64_t j1 = tmin<uint64_t>(j0 + kBlock, ge);
     const int r = g_rice[g];
     const int e = g_exp[g];
-    uint64_t pos = block_off[b];
+    uint64_t pos = block_off[b] + bit0;   // bit0: where this part starts inside its first byte
     for (uint64_t jb = j0; jb < j1; jb += 32) {
         const uint64_t j = jb + lane;
         uint64_t L = 0, gap = 0;
@@ -808,11 +808,114 @@ struct HostTables {
     std::vector<uint32_t> code[256];
 };
 
+// Huffman tables from the symbol histogram: dense counts [256][DENSE_SYM] and the larger symbols
+// as (exponent << 17 | symbol, count) pairs sorted by key (codec.py:369-392).
+void build_tables(const std::vector<uint64_t>& dense, const std::vector<std::pair<uint64_t, uint64_t>>& rare,
+                  HostTables* tabs) {
+    size_t r = 0;
+    for (int e = 0; e < 256; ++e) {
+        for (int z = 0; z < DENSE_SYM; ++z) {
+            const uint64_t c = dense[size_t(e) * DENSE_SYM + size_t(z)];
+            if (c) { tabs->sym[e].push_back(uint32_t(z)); tabs->cnt[e].push_back(c); }
+        }
+        for (; r < rare.size() && (rare[r].first >> 17) == uint64_t(e); ++r) {
+            tabs->sym[e].push_back(uint32_t(rare[r].first & 0x1FFFFu));
+            tabs->cnt[e].push_back(rare[r].second);
+        }
+        const size_t ns = tabs->sym[e].size();
+        if (!ns) continue;
+        tabs->len[e].resize(ns);
+        tabs->code[e].resize(ns);
+        huffman_lengths(tabs->cnt[e].data(), int64_t(ns), tabs->len[e].data());
+        canonical_codes(tabs->len[e].data(), int64_t(ns), tabs->code[e].data());
+    }
+}
+
+// Global mode: the histogram summed over ranks (dense part by sum, rare pairs gathered and merged)
+Status exchange_histogram(const GlobalExchange& gx, std::vector<uint64_t>* dense,
+                          std::vector<std::pair<uint64_t, uint64_t>>* rare, std::string* err) {
+    if (gx.sum_u64(gx.user, dense->data(), int64_t(dense->size()))) { *err = "histogram sum failed"; return kCudaError; }
+    std::vector<uint64_t> mine;
+    for (const auto& p : *rare) { mine.push_back(p.first); mine.push_back(p.second); }
+    const uint8_t* all = nullptr;
+    int64_t all_len = 0;
+    if (gx.allgather_bytes(gx.user, reinterpret_cast<const uint8_t*>(mine.data()), int64_t(8 * mine.size()), &all, &all_len) ||
+        all_len % 16 || (all_len && !all)) {
+        *err = "rare-symbol gather failed";
+        return kCudaError;
+    }
+    std::vector<std::pair<uint64_t, uint64_t>> merged(size_t(all_len / 16));
+    for (size_t k = 0; k < merged.size(); ++k) {
+        std::memcpy(&merged[k].first, all + 16 * k, 8);
+        std::memcpy(&merged[k].second, all + 16 * k + 8, 8);
+    }
+    std::sort(merged.begin(), merged.end());
+    rare->clear();
+    for (const auto& p : merged) {
+        if (!rare->empty() && rare->back().first == p.first) rare->back().second += p.second;
+        else rare->push_back(p);
+    }
+    return kOk;
+}
+
+// Global mode: every rank's value gathered by a sum over a one-hot vector
+Status exchange_per_rank(const GlobalExchange& gx, uint64_t mine, std::vector<uint64_t>* all, std::string* err) {
+    all->assign(size_t(gx.world), 0);
+    (*all)[size_t(gx.rank)] = mine;
+    if (gx.sum_u64(gx.user, all->data(), int64_t(gx.world))) { *err = "per-rank exchange failed"; return kCudaError; }
+    return kOk;
+}
+
+// magic, version and tables of an update (wire.py:64-78); the tensor count follows
+void put_prefix(std::vector<uint8_t>& ob, const HostTables& tabs) {
+    const uint8_t magic[5] = {'C', 'R', 'X', 'S', 2};
+    ob.insert(ob.end(), magic, magic + 5);
+    int n_tables = 0;
+    for (int e = 0; e < 256; ++e) n_tables += !tabs.sym[e].empty();
+    put_varint(ob, uint64_t(n_tables));
+    for (int e = 0; e < 256; ++e) {
+        if (tabs.sym[e].empty()) continue;
+        ob.push_back(uint8_t(e));
+        put_varint(ob, tabs.sym[e].size());
+        for (size_t k = 0; k < tabs.sym[e].size(); ++k) {
+            put_varint(ob, tabs.sym[e][k]);
+            ob.push_back(tabs.len[e][k]);
+        }
+    }
+}
+
+// Global mode for a rank without changes: the same collectives with empty contributions
+Status global_empty_part(const GlobalExchange& gx, Encoded* out, std::string* err) {
+    std::vector<uint64_t> dense(size_t(256) * DENSE_SYM, 0);
+    std::vector<std::pair<uint64_t, uint64_t>> rare;
+    Status s = exchange_histogram(gx, &dense, &rare, err);
+    if (s != kOk) return s;
+    std::vector<uint64_t> np, bits;
+    if ((s = exchange_per_rank(gx, 0, &np, err)) != kOk) return s;
+    HostTables tabs;
+    build_tables(dense, rare, &tabs);
+    out->head.clear();
+    put_prefix(out->head, tabs);
+    uint64_t n_tensors = 0;
+    for (uint64_t v : np) n_tensors += v;
+    put_varint(out->head, n_tensors);
+    if ((s = exchange_per_rank(gx, 0, &bits, err)) != kOk) return s;
+    uint64_t before = 0, total = 0;
+    for (int r = 0; r < gx.world; ++r) { if (r < gx.rank) before += bits[size_t(r)]; total += bits[size_t(r)]; }
+    out->part = true;
+    out->bit_offset = before;
+    out->total_bits = total;
+    out->len_varint.clear();
+    put_varint(out->len_varint, (total + 7) / 8);
+    return kOk;
+}
+
 }  // namespace
 
 Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* const* cur, const int64_t* numel,
                    const uint8_t* const* names, const int64_t* name_len, const uint64_t* cache_chk,
-                   const uint8_t* has_cache, cudaStream_t st, Encoded* out, std::string* err, bool device_result) {
+                   const uint8_t* has_cache, cudaStream_t st, Encoded* out, std::string* err, bool device_result,
+                   const GlobalExchange* gx) {
     if (C.live) {           // an earlier result still reads the output buffers: give it its own copy
         const cudaError_t de = C.live->detach();
         C.live = nullptr;
@@ -848,7 +951,7 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
         out->head.assign(kEmpty, kEmpty + 7);
         return kOk;
     };
-    if (nt == 0) return empty_update();
+    if (nt == 0) return gx ? global_empty_part(*gx, out, err) : empty_update();
     if (n_super >= (int64_t(1) << 28)) { *err = "update too large for one call"; return kValueError; }
 
     // ---- buffers
@@ -926,7 +1029,7 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     }
     const uint64_t n_rec = hostc[0];
     trace_phase(C, "encode: ranked (sync 1)");
-    if (n_rec == 0) return empty_update();
+    if (n_rec == 0) return gx ? global_empty_part(*gx, out, err) : empty_update();
 
     // ---- per tensor column scans and the group table
     launch_column_scan(C, dev<uint32_t>(C, S_HS), n_super, d_row_begin, nt, d_chunk_begin, n_chunks,
@@ -1055,25 +1158,28 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     }
     const int64_t n_blocks = int64_t(gblock[size_t(ng)]);
 
-    // ---- one Huffman table per exponent over the whole update (codec.py:369-392)
-    HostTables tabs;
-    for (int e = 0; e < 256; ++e) {
-        for (int z = 0; z < DENSE_SYM; ++z) {
-            const uint64_t c = hdense[size_t(e) * DENSE_SYM + size_t(z)];
-            if (c) { tabs.sym[e].push_back(uint32_t(z)); tabs.cnt[e].push_back(c); }
-        }
+    // ---- one Huffman table per exponent over the whole update (codec.py:369-392); a global
+    //      update sums the histogram over its ranks first
+    std::vector<std::pair<uint64_t, uint64_t>> rare_pairs;
+    for (int e = 0; e < 256; ++e)
         for (uint32_t k = 0; k < hrc[size_t(e)]; ++k) {
             const uint64_t v = hrare[size_t(hrb[size_t(e)] + k)];
-            tabs.sym[e].push_back(uint32_t(v >> 32));
-            tabs.cnt[e].push_back(v & 0xFFFFFFFFull);
+            rare_pairs.emplace_back((uint64_t(e) << 17) | (v >> 32), v & 0xFFFFFFFFull);
         }
-        const size_t ns = tabs.sym[e].size();
-        if (!ns) continue;
-        tabs.len[e].resize(ns);
-        tabs.code[e].resize(ns);
-        huffman_lengths(tabs.cnt[e].data(), int64_t(ns), tabs.len[e].data());
-        canonical_codes(tabs.len[e].data(), int64_t(ns), tabs.code[e].data());
+    std::vector<uint64_t> np_all;
+    int n_present_local = 0;
+    {
+        std::vector<uint8_t> has(static_cast<size_t>(nt), 0);
+        for (int64_t g = 0; g < ng; ++g) has[size_t(hg_tensor[size_t(g)])] = 1;
+        for (uint8_t x : has) n_present_local += x;
     }
+    if (gx) {
+        Status xs = exchange_histogram(*gx, &hdense, &rare_pairs, err);
+        if (xs == kOk) xs = exchange_per_rank(*gx, uint64_t(n_present_local), &np_all, err);
+        if (xs != kOk) return xs;
+    }
+    HostTables tabs;
+    build_tables(hdense, rare_pairs, &tabs);
 
     trace_phase(C, "encode: huffman (host)");
     // ---- upload rice, block starts, code tables
@@ -1141,44 +1247,45 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
         *err = "a block exceeds 2^32 bits; the update cannot be represented";
         return kValueError;
     }
-    const uint64_t payload_len = (total_bits + 7) / 8;
-    const size_t n_words = size_t((total_bits + 31) / 32) + 4;
+    uint64_t bit_before = 0, bits_all = total_bits;   // global mode: this part's offset, the update's bits
+    if (gx) {
+        std::vector<uint64_t> bits;
+        const Status xs = exchange_per_rank(*gx, total_bits, &bits, err);
+        if (xs != kOk) return xs;
+        bits_all = 0;
+        for (int r = 0; r < gx->world; ++r) { if (r < gx->rank) bit_before += bits[size_t(r)]; bits_all += bits[size_t(r)]; }
+    }
+    const uint32_t bit0 = uint32_t(bit_before & 7);
+    const uint64_t payload_len = (bit0 + total_bits + 7) / 8;
+    const size_t n_words = size_t((bit0 + total_bits + 31) / 32) + 4;
     CRX_CUDA(ensure_dev(C.b[S_PAYLOAD], 4 * n_words, st));
     CRX_CUDA(cudaMemsetAsync(C.b[S_PAYLOAD].p, 0, 4 * n_words, st));
     { KernelScope ks_(C, "k_pack", st);
     k_pack<<<warps_grid, 256, 0, st>>>(g_start, g_exp, g_rice, g_block, ng, n_blocks, local, vals,
                                        dev<uint32_t>(C, S_DENSE_CODE), big_code, dev<uint64_t>(C, S_BLOCK_BITS),
-                                       dev<uint32_t>(C, S_PAYLOAD));
+                                       dev<uint32_t>(C, S_PAYLOAD), bit0);
     }
     CRX_CUDA(cudaGetLastError());
 
     // ---- header (wire.py:64-89); block table and payload go to pinned memory in one pass each
-    std::vector<uint8_t>& ob = out->head;
-    ob.reserve(4096);
-    const uint8_t magic[5] = {'C', 'R', 'X', 'S', 2};
-    ob.insert(ob.end(), magic, magic + 5);
-    int n_tables = 0;
-    for (int e = 0; e < 256; ++e) n_tables += !tabs.sym[e].empty();
-    put_varint(ob, uint64_t(n_tables));
-    for (int e = 0; e < 256; ++e) {
-        if (tabs.sym[e].empty()) continue;
-        ob.push_back(uint8_t(e));
-        put_varint(ob, tabs.sym[e].size());
-        for (size_t k = 0; k < tabs.sym[e].size(); ++k) {
-            put_varint(ob, tabs.sym[e][k]);
-            ob.push_back(tabs.len[e][k]);
-        }
-    }
-    // tensors present = those with groups, in caller order
+    out->head.clear();
+    out->head.reserve(4096);
+    put_prefix(out->head, tabs);
+    // tensors present = those with groups, in caller order; a part of a global update keeps its
+    // tensor headers apart and counts the whole update's tensors
+    std::vector<uint8_t>& ob = gx ? out->part_tensors : out->head;
     std::vector<int64_t> t_first(static_cast<size_t>(nt), -1), t_ng(static_cast<size_t>(nt), 0);
     for (int64_t g = 0; g < ng; ++g) {
         const int t = hg_tensor[size_t(g)];
         if (t_first[size_t(t)] < 0) t_first[size_t(t)] = g;
         t_ng[size_t(t)]++;
     }
-    int n_present = 0;
-    for (int t = 0; t < nt; ++t) n_present += t_ng[size_t(t)] > 0;
-    put_varint(ob, uint64_t(n_present));
+    uint64_t n_present = uint64_t(n_present_local);
+    if (gx) {
+        n_present = 0;
+        for (uint64_t v : np_all) n_present += v;
+    }
+    put_varint(out->head, n_present);
     for (int t = 0; t < nt; ++t) {
         if (!t_ng[size_t(t)]) continue;
         const int ct = tmap[size_t(t)];
@@ -1197,7 +1304,12 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
         }
     }
     out->len_varint.clear();
-    put_varint(out->len_varint, payload_len);
+    put_varint(out->len_varint, gx ? (bits_all + 7) / 8 : payload_len);
+    if (gx) {
+        out->part = true;
+        out->bit_offset = bit_before;
+        out->total_bits = bits_all;
+    }
     out->n_blocks = n_blocks;
     out->payload_len = payload_len;
     out->changes = total;

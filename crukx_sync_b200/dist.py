@@ -92,3 +92,83 @@ def allgather_updates_device(update, group=None, ranks: Sequence[int] | None = N
     td.all_gather_into_tensor(out, buf, group=group)
     want = range(world) if ranks is None else ranks
     return [out[r * mx: r * mx + sizes[r]] for r in want]
+
+
+def partition_contiguous(numels: Sequence[int], world: int) -> list[tuple[int, int]]:
+    """Split tensors 0..n-1 (update order) into `world` contiguous ranges of about equal elements;
+    range r = (first, end) for rank r (possibly empty)."""
+    if world < 1:
+        raise ValueError(f"world size must be >= 1, got {world}")
+    total = sum(int(x) for x in numels)
+    bounds, acc, r = [0], 0, 1
+    for i, x in enumerate(numels):
+        acc += int(x)
+        while r < world and acc * world >= r * total and i + 1 > bounds[-1]:
+            bounds.append(i + 1)
+            r += 1
+    while len(bounds) < world:
+        bounds.append(len(numels))
+    bounds.append(len(numels))
+    return [(bounds[k], bounds[k + 1]) for k in range(world)]
+
+
+_PART_KEYS = ("prefix", "tensors", "table", "payload")
+
+
+def _pack_part(p: dict) -> bytes:
+    import struct
+    head = struct.pack("<6Q", *[len(p[k]) for k in _PART_KEYS], p["bit_offset"], p["total_bits"])
+    return head + b"".join(p[k] for k in _PART_KEYS)
+
+
+def _unpack_part(b: bytes) -> dict:
+    import struct
+    lens = struct.unpack_from("<6Q", b, 0)
+    out, o = {}, 48
+    for k, n in zip(_PART_KEYS, lens[:4]):
+        out[k] = bytes(b[o: o + n])
+        o += n
+    out["bit_offset"], out["total_bits"] = lens[4], lens[5]
+    return out
+
+
+def encode_update_global(old, new, checksums: dict | None = None, group=None) -> bytes:
+    """One update for the whole model, encoded by every rank of the group together: the bytes are
+    identical to a single-GPU encode_update of all ranks' tensors in rank order.  `old`/`new` hold
+    this rank's tensors, which must be its contiguous range of the update's tensor order (see
+    partition_contiguous).  Every rank returns the whole update; the sender cache gets this rank's
+    tensors.  Collectives: a 128 KiB histogram sum, small gathers, and the parts' all-gather."""
+    import numpy as np
+    import torch.distributed as td
+
+    from . import codec
+    from .wire import assemble
+
+    if old.keys() != new.keys():
+        raise ValueError(f"old and new differ in tensor names: {sorted(old.keys() ^ new.keys())[:5]}")
+    world = td.get_world_size(group) if td.is_initialized() else 1
+    rank = td.get_rank(group) if td.is_initialized() else 0
+    nccl = td.is_initialized() and td.get_backend(group) == "nccl"
+    cdev = torch.device("cuda", torch.cuda.current_device()) if nccl else torch.device("cpu")
+
+    def sum_u64(arr):
+        if world == 1:
+            return
+        t = torch.from_numpy(arr.view(np.int64).copy()).to(cdev)
+        td.all_reduce(t, group=group)
+        arr[:] = t.cpu().numpy().view(np.uint64)
+
+    def allgather(mine: bytes) -> bytes:
+        return b"".join(allgather_updates(mine, group=group, device=cdev)) if world > 1 else mine
+
+    with torch.no_grad():
+        enc = codec.encode_global(old, new, checksums, rank, world, sum_u64, allgather)
+    part = enc.part()
+    enc_checksums = enc.checksums
+    enc.close()
+    blobs = allgather_updates(_pack_part(part), group=group, device=cdev) if world > 1 else [_pack_part(part)]
+    parts = [_unpack_part(b) for b in blobs]
+    data = assemble(parts)
+    if checksums is not None:
+        checksums.update(enc_checksums)
+    return data

@@ -140,6 +140,21 @@ class EncodedUpdate:
             raise RuntimeError("crukx_sync_b200: encoded update device copy failed")
         return out
 
+    def part(self) -> dict:
+        """A rank's part of a global update: prefix, tensors, table and payload bytes, with the
+        part's bit offset in the update's payload and the update's payload bits."""
+        L = _ext.load()
+        v = [ctypes.c_int64() for _ in range(4)] + [ctypes.c_uint64(), ctypes.c_uint64()]
+        if L.crx_encoded_part(self._h, *[ctypes.byref(x) for x in v]) != _ext.CRX_OK:
+            raise ValueError("not a part of a global update")
+        bufs = [ctypes.create_string_buffer(max(int(x.value), 1)) for x in v[:4]]
+        if L.crx_encoded_part_copy(self._h, *bufs) != _ext.CRX_OK:
+            raise RuntimeError("crukx_sync_b200: part copy failed")
+        keys = ("prefix", "tensors", "table", "payload")
+        out = {k: b.raw[: int(x.value)] for k, b, x in zip(keys, bufs, v[:4])}
+        out["bit_offset"], out["total_bits"] = int(v[4].value), int(v[5].value)
+        return out
+
     def close(self):
         if self._h:
             _ext.load().crx_encoded_free(self._h)
@@ -150,6 +165,29 @@ class EncodedUpdate:
             self.close()
         except Exception:
             pass
+
+
+def assemble(parts: list) -> bytes:
+    """The update of a global encode from every rank's part, in rank order (see
+    crx_encode_global): prefix + tensor headers + block tables + payload length + payloads, the
+    parts' boundary bytes OR-ed together."""
+    import numpy as np
+
+    total_bits = parts[0]["total_bits"]
+    pay = np.zeros((total_bits + 7) // 8, dtype=np.uint8)
+    for p in parts:
+        b = np.frombuffer(p["payload"], dtype=np.uint8)
+        lo = p["bit_offset"] // 8
+        if len(b):
+            pay[lo: lo + len(b)] |= b[: len(pay) - lo]
+    out = bytearray(parts[0]["prefix"])
+    for p in parts:
+        out += p["tensors"]
+    for p in parts:
+        out += p["table"]
+    write_varint(out, len(pay))
+    out += pay.tobytes()
+    return bytes(out)
 
 
 def serialize(u) -> bytes:

@@ -90,6 +90,35 @@ int crx_encode_device(crx_ctx* ctx, int32_t n_tensors, const int16_t* const* pre
 int crx_encoded_copy_device(const crx_encoded* enc, void* dst, int64_t cap, void* stream);
 
 /*
+ * One update encoded by several ranks (no reference counterpart; the single-GPU encode of the
+ * whole dict is the reference's encode_update, and the result is byte-identical to it).  Rank r
+ * passes its own tensors, which must be the r-th contiguous range of the update's tensor order.
+ * Inside, the library calls the two collectives below on every rank in the same order (each
+ * returns 0 on success; a rank that fails must still have taken every earlier call):
+ *   sum_u64(user, data, n): element-wise sum over ranks of n u64 values, in place (wrapping);
+ *   allgather(user, mine, len, &all, &all_len): every rank's bytes, concatenated in rank order, in
+ *     a buffer the caller's side keeps valid until the next callback or until crx_encode_global
+ *     returns.
+ * The symbol histogram is summed over ranks so the Huffman tables are the whole update's, and
+ * each rank packs its payload at its bit offset in the whole payload.  The result is a part:
+ * crx_encoded_part gives the sizes of its pieces, crx_encoded_part_copy copies them.  The update
+ * is prefix (rank-independent) + every rank's tensor headers + every rank's block table + LEB128
+ * of (total_bits + 7) / 8 + the payloads OR-ed together, rank r's starting at byte
+ * bit_offset / 8 (its first byte holds the previous rank's last bits when bit_offset % 8 != 0).
+ * crx_encoded_size/_copy/_copy_device refuse a part.
+ */
+typedef int (*crx_sum_u64_fn)(void* user, uint64_t* data, int64_t n);
+typedef int (*crx_allgather_fn)(void* user, const uint8_t* mine, int64_t len, const uint8_t** all, int64_t* all_len);
+int crx_encode_global(crx_ctx* ctx, int32_t n_tensors, const int16_t* const* prev, const int16_t* const* cur,
+                      const int64_t* numel, const uint8_t* const* names, const int64_t* name_len,
+                      const uint64_t* cached_checksums, const uint8_t* has_cached, void* stream, int32_t rank,
+                      int32_t world, crx_sum_u64_fn sum_u64, crx_allgather_fn allgather, void* user,
+                      crx_encoded** out, char* err, size_t errlen);
+int crx_encoded_part(const crx_encoded* enc, int64_t* prefix_len, int64_t* tensors_len, int64_t* table_len,
+                     int64_t* payload_len, uint64_t* bit_offset, uint64_t* total_bits);
+int crx_encoded_part_copy(const crx_encoded* enc, uint8_t* prefix, uint8_t* tensors, uint8_t* table, uint8_t* payload);
+
+/*
  * Parse and validate an update on the host: every limit of wire.parse
  * (src/crukx_sync/wire.py:126-212).  The handle borrows data[0..len), which must outlive it.
  */
