@@ -277,17 +277,19 @@ def run_ours(args, rank, world, dist):
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    def exchange(upd: bytes):
-        """All-gather of the compressed updates (NCCL); returns this rank's update from the gather."""
-        return cdist.allgather_updates(upd, ranks=[rank])[0]
+    def exchange(upd):
+        """All-gather of the device-resident updates over NCCL; this rank's update from the gather."""
+        return cdist.allgather_updates_device(upd, ranks=[rank])[0]
 
     state = {"src": A, "dst": B}
 
     def step(events=None):
+        """One sync step with the updates resident in HBM: encode_update_device (the reference's
+        bytes, in device memory), NCCL all-gather, apply_update of the device update."""
         src, dst = state["src"], state["dst"]
         if events:
             events[0].record(stream)
-        upd = crx.encode_update(src, dst, sender)
+        upd = crx.encode_update_device(src, dst, sender)
         if events:
             events[1].record(stream)
         mine = exchange(upd)
@@ -314,7 +316,7 @@ def run_ours(args, rank, world, dist):
         t_wall0 = time.perf_counter()
         for k in range(args.steps):
             upd, st = step(evs[k])
-            sizes.append(len(upd))
+            sizes.append(upd.numel())
         barrier()
         t_wall = time.perf_counter() - t_wall0
     launches = int(L.crx_ctx_launches(ctx) - launches0)
@@ -338,39 +340,38 @@ def run_ours(args, rank, world, dist):
     weight_bytes = 2.0 * total_params
     value = weight_bytes / (ms_step * 1e-3) / 1e9
 
-    # ---- the device-resident path (encode_update_device -> NCCL -> apply from device memory):
-    #      same steps, the update never crosses PCIe; reported beside the bytes-API headline
-    device_path = None
-    if not args.no_device_path:
-        def dstep(events):
+    # ---- the same steps through the host-bytes API (encode_update -> bytes -> apply_update), the
+    #      reference's own interface: the update crosses PCIe twice; each rank applies its own
+    #      update (no exchange of host bytes between processes)
+    bytes_api = None
+    if not args.no_bytes_api:
+        def bstep(events):
             src, dst = state["src"], state["dst"]
             events[0].record(stream)
-            t = crx.encode_update_device(src, dst, sender)
+            u = crx.encode_update(src, dst, sender)
             events[1].record(stream)
-            mine = cdist.allgather_updates_device(t, ranks=[rank])[0]
+            crx.apply_update(recv, u, receiver)
             events[2].record(stream)
-            crx.apply_update(recv, mine, receiver)
-            events[3].record(stream)
             state["src"], state["dst"] = dst, src
 
         for _ in range(2):
-            dstep([torch.cuda.Event(enable_timing=True) for _ in range(4)])
-        devs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
+            bstep([torch.cuda.Event(enable_timing=True) for _ in range(3)])
+        bevs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(args.steps)]
         barrier()
         for k in range(args.steps):
-            dstep(devs[k])
+            bstep(bevs[k])
         barrier()
         for k in recv:
-            assert torch.equal(recv[k], state["src"][k]), f"receiver differs after the device path: {k}"
-        dt = torch.tensor([sum(e[0].elapsed_time(e[3]) for e in devs) / args.steps,
-                           sum(e[0].elapsed_time(e[1]) for e in devs) / args.steps,
-                           sum(e[2].elapsed_time(e[3]) for e in devs) / args.steps], dtype=torch.float64, device=dev)
+            assert torch.equal(recv[k], state["src"][k]), f"receiver differs after the bytes API: {k}"
+        bt = torch.tensor([sum(e[0].elapsed_time(e[2]) for e in bevs) / args.steps,
+                           sum(e[0].elapsed_time(e[1]) for e in bevs) / args.steps,
+                           sum(e[1].elapsed_time(e[2]) for e in bevs) / args.steps], dtype=torch.float64, device=dev)
         if dist is not None:
-            dist.all_reduce(dt, op=dist.ReduceOp.MAX)
-        d_step, d_enc, d_app = dt.tolist()
-        device_path = {"value": round(2.0 * total_params / (d_step * 1e-3) / 1e9, 2), "unit": "GB/s",
-                       "ms_per_step": round(d_step, 4), "encode_ms": round(d_enc, 4), "apply_ms": round(d_app, 4),
-                       "note": "encode_update_device + NCCL all-gather + apply_update from device memory"}
+            dist.all_reduce(bt, op=dist.ReduceOp.MAX)
+        b_step, b_enc, b_app = bt.tolist()
+        bytes_api = {"value": round(2.0 * total_params / (b_step * 1e-3) / 1e9, 2), "unit": "GB/s",
+                     "ms_per_step": round(b_step, 4), "encode_ms": round(b_enc, 4), "apply_ms": round(b_app, 4),
+                     "note": "encode_update -> host bytes -> apply_update(bytes), weights resident in HBM"}
 
     # ---- per-kernel times on this stream (a separate profiled pass of 2 steps)
     L.crx_ctx_profile(ctx, 1)
@@ -428,15 +429,17 @@ def run_ours(args, rank, world, dist):
         "data": f"synthetic: random-init {cfg['name']} weights, one Adam-like step (lr {cfg['lr']}), seed 0",
         "config": {"workload": cfg["name"], "params": total_params, "tensors": len(shapes_all),
                    "lr": cfg["lr"], "changed_frac": round(changed_all / total_params, 5),
-                   "parallelism": f"tensor partition x{world} (LPT on numel), NCCL all-gather of payloads"
+                   "parallelism": f"tensor partition x{world} (LPT on numel), NCCL all-gather of the device-resident updates"
                    if world > 1 else "single GPU",
+                   "path": "encode_update_device -> (NCCL all-gather) -> apply_update of the device update; "
+                           "the reference's bytes, kept in HBM",
                    "l2": "inputs larger than L2 (each state 2 B x params; no flush needed)"},
         "encode_gbs": round(weight_bytes / (ms_enc * 1e-3) / 1e9, 2),
         "apply_gbs": round(weight_bytes / (ms_app * 1e-3) / 1e9, 2),
         "exchange_ms": round(ms_ex, 4), "encode_ms": round(ms_enc, 4), "apply_ms": round(ms_app, 4),
         "update_bytes": int(upd_bytes), "bytes_per_changed": round(upd_bytes / max(changed_all, 1), 4),
         "wall_s_timed": round(t_wall, 3),
-        "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e, "device_path": device_path,
+        "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e, "bytes_api": bytes_api,
         "gpu_launches": launches, "clocks": clk.summary(),
     }
     return result
@@ -458,10 +461,9 @@ def run_e2e(args, A, B, dev, weight_bytes, exchange, barrier, dist):
     nsteps = max(1, min(args.steps, args.e2e_steps))
     n_el = sum(v.numel() for v in A.values())
 
-    def one():
+    def one():   # each rank applies its own update (host bytes are not exchanged between processes)
         upd = crx.encode_update(st["src"], st["dst"], sender)
-        mine = exchange(upd)
-        crx.apply_update(Rh, mine, receiver)
+        crx.apply_update(Rh, upd, receiver)
         st["src"], st["dst"] = st["dst"], st["src"]
         return len(upd)
 
@@ -516,7 +518,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default="7b", choices=sorted(CONFIGS))
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--no-device-path", action="store_true", help="skip the device-resident update measurement")
+    ap.add_argument("--no-bytes-api", action="store_true", help="skip the host-bytes API measurement")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-sample", type=int, default=1_000_000_000, help="elements in the CPU-baseline sample")

@@ -4,6 +4,7 @@
 #include <sys/mman.h>
 
 #include <algorithm>
+#include <cstdlib>
 #include <atomic>
 #include <condition_variable>
 #include <cstdint>
@@ -25,7 +26,12 @@ namespace {
 class Pool {
 public:
     Pool() {
-        const unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+        // one process per GPU shares the host: split the cores between the local processes
+        unsigned hw = std::max(1u, std::thread::hardware_concurrency());
+        if (const char* lw = std::getenv("LOCAL_WORLD_SIZE")) {
+            const long k = std::strtol(lw, nullptr, 10);
+            if (k > 1) hw = std::max(2u, hw / unsigned(k));
+        }
         const unsigned n = std::min(hw, 32u) - 1;
         for (unsigned k = 0; k < n; ++k) workers_.emplace_back([this] { loop(); });
     }
