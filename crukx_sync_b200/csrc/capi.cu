@@ -589,21 +589,48 @@ int crx_parse_head(const uint8_t* head, int64_t head_len, int64_t len, uint8_t l
     }
 }
 
+namespace {
+
+// pinned staging for the heads crx_parse_device copies back (one buffer for the process, grown on
+// demand; device -> pageable copies run at a fraction of the link's bandwidth)
+std::mutex g_head_mu;
+uint8_t* g_head_pinned = nullptr;
+size_t g_head_cap = 0;
+
+}  // namespace
+
 int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update** out, char* err, size_t errlen) {
     if (!out || len < 0 || (len && !data)) return CRX_BAD_ARGUMENT;
     *out = nullptr;
     try {
         const cudaStream_t st = static_cast<cudaStream_t>(stream);
-        uint8_t last = 0;
-        if (len && cudaMemcpyAsync(&last, data + len - 1, 1, cudaMemcpyDeviceToHost, st) != cudaSuccess) return CRX_CUDA_ERROR;
+        std::lock_guard<std::mutex> lock(g_head_mu);
         std::vector<uint8_t> head;
+        uint8_t last = 0;
         int64_t have = std::min<int64_t>(len, int64_t(1) << 16);
+        int64_t got = 0;   // bytes of the head already in `head`
         for (;;) {   // copy a head, parse it, copy more when the header or block table reaches past it
-            const int64_t old = int64_t(head.size());
-            head.resize(size_t(have));
-            if (have > old && cudaMemcpyAsync(head.data() + old, data + old, size_t(have - old), cudaMemcpyDeviceToHost, st) != cudaSuccess)
-                return CRX_CUDA_ERROR;
-            if (cudaStreamSynchronize(st) != cudaSuccess) return CRX_CUDA_ERROR;
+            if (have > got) {
+                const size_t need = size_t(have - got) + 1;
+                if (need > g_head_cap) {
+                    if (g_head_pinned) cudaFreeHost(g_head_pinned);
+                    g_head_pinned = nullptr;
+                    g_head_cap = 0;
+                    const size_t cap = std::max(need, size_t(1) << 20);
+                    if (cudaMallocHost(reinterpret_cast<void**>(&g_head_pinned), cap) != cudaSuccess) return CRX_CUDA_ERROR;
+                    g_head_cap = cap;
+                }
+                if (cudaMemcpyAsync(g_head_pinned, data + got, size_t(have - got), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                    return CRX_CUDA_ERROR;
+                if (got == 0 && len &&
+                    cudaMemcpyAsync(g_head_pinned + (have - got), data + len - 1, 1, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                    return CRX_CUDA_ERROR;
+                if (cudaStreamSynchronize(st) != cudaSuccess) return CRX_CUDA_ERROR;
+                if (got == 0 && len) last = g_head_pinned[have];
+                head.resize(size_t(have));
+                crx::parallel_copy(head.data() + got, g_head_pinned, size_t(have - got));
+                got = have;
+            }
             crx_update* u = new crx_update;
             std::string msg;
             int64_t nd = 0;
@@ -620,7 +647,8 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
                 put_err(err, errlen, msg);
                 return int(s);
             }
-            have = std::min(len, std::max(nd, 4 * have));
+            // past a block table comes at most a 10-byte length varint: ask for it in the same copy
+            have = std::min(len, std::max(nd + 16, 4 * have));
         }
     } catch (const std::bad_alloc&) {
         put_err(err, errlen, "crx_parse_device: out of host memory");
