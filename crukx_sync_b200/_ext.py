@@ -23,7 +23,8 @@ EXPORTS = [
     "crx_update_table_entries", "crx_update_n_blocks", "crx_update_block_bits", "crx_update_payload",
     "crx_update_free", "crx_apply", "crx_huffman_lengths", "crx_checksum", "crx_checksum_noalloc",
     "crx_encode_device", "crx_encoded_copy_device", "crx_parse_head", "crx_parse_device",
-    "crx_encode_global", "crx_encoded_part", "crx_encoded_part_copy",
+    "crx_encode_global", "crx_encoded_part", "crx_encoded_part_copy", "crx_apply_versioned",
+    "crx_ctx_hist_cache_hits",
 ]
 
 # collective callbacks of crx_encode_global
@@ -88,6 +89,8 @@ def load():
                                    ctypes.POINTER(P), CP, SZ], ctypes.c_int),
             "crx_encoded_part": ([P, P, P, P, P, P, P], ctypes.c_int),
             "crx_encoded_part_copy": ([P, P, P, P, P], ctypes.c_int),
+            "crx_apply_versioned": ([P, P, P, P, P, P, P, P, P, CP, SZ], ctypes.c_int),
+            "crx_ctx_hist_cache_hits": ([P], U64),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

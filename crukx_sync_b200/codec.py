@@ -251,8 +251,16 @@ def apply(weights: Mapping[str, torch.Tensor], u: ParsedUpdate, checksums: dict 
     L = _ext.load()
     with torch.cuda.device(cdev):
         stream = torch.cuda.current_stream(cdev).cuda_stream
-        st = L.crx_apply(_ext.context(cdev.index), u.handle, ptrs, cache, has, ctypes.c_void_p(stream),
-                         ctypes.byref(changed), err, 1024)
+        if dev.type == "cuda" and checksums is not None:
+            # tensors written in place on the device: the library may keep their exponent
+            # histograms for the next apply, tagged with the version they will have after it
+            vers = (ctypes.c_uint64 * k)(*[a._version for a in targets])
+            tag = (ctypes.c_uint8 * k)(*([1] * k))
+            st = L.crx_apply_versioned(_ext.context(cdev.index), u.handle, ptrs, cache, has, vers, tag,
+                                       ctypes.c_void_p(stream), ctypes.byref(changed), err, 1024)
+        else:
+            st = L.crx_apply(_ext.context(cdev.index), u.handle, ptrs, cache, has, ctypes.c_void_p(stream),
+                             ctypes.byref(changed), err, 1024)
     if st != _ext.CRX_OK:
         _raise(st, err)
     if dev.type == "cuda":   # the commit wrote through raw pointers: move the version like a[idx] = v

@@ -38,6 +38,7 @@ struct AppTensor {
     int32_t g_begin;
     int32_t g_end;
     int32_t pad;
+    const uint32_t* hcache;   // the tensor's cached histogram rows (null: compute them)
 };
 
 struct AppGroup {
@@ -103,6 +104,10 @@ __global__ void __launch_bounds__(HIST_THREADS) k_app_hist(const AppTensor* __re
     const int64_t s = blockIdx.x;
     const int t = tensor_of_super(T, nT, s);
     const AppTensor tt = T[t];
+    if (tt.hcache) {   // histogram cached by the previous apply: no pass over the weights
+        for (int k = threadIdx.x; k < 256; k += HIST_THREADS) HS[s * 256 + k] = tt.hcache[(s - tt.super_begin) * 256 + k];
+        return;
+    }
     const int64_t e0 = (s - tt.super_begin) * SUPER_N;
     const int64_t e1 = min(tt.numel, e0 + SUPER_N);
     const int w = threadIdx.x >> 5;
@@ -394,7 +399,7 @@ __global__ void __launch_bounds__(MP_THREADS, 3)
 k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, const uint32_t* __restrict__ PS,
       const uint32_t* __restrict__ local, const uint32_t* __restrict__ zz, unsigned long long* __restrict__ caddr,
       uint16_t* __restrict__ cval, uint64_t stage_cap, unsigned long long* __restrict__ chk_delta,
-      unsigned long long* __restrict__ staged) {
+      unsigned long long* __restrict__ staged, const uint64_t* __restrict__ GS, uint32_t* __restrict__ HNEW) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     MapSmem& S = *reinterpret_cast<MapSmem*>(smem_raw);
     const int64_t s = blockIdx.x;
@@ -407,6 +412,11 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
     const int ngt = tt.g_end - tt.g_begin;
     const int span0 = w * MP_SPAN;
     S.pcur[tid] = PS[s * 256 + tid];
+    if (HNEW) {   // the weights' histogram after this update: the old one here, exponent moves added below
+        const bool last = e_end >= tt.numel;
+        const uint32_t nxt = last ? uint32_t(GS[int64_t(t) * 256 + tid]) : PS[(s + 1) * 256 + tid];
+        HNEW[s * 256 + tid] = nxt - S.pcur[tid];
+    }
     if (tid == 0) S.emax = 0;
     __syncthreads();
     if (tid < ngt) {
@@ -615,7 +625,10 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
         }
         __syncthreads();
         // ---- stage the sub-tile's new values in position order (one atomic per sub-tile): lane l
-        //      owns mark word l of its warp's span
+        //      owns mark word l of its warp's span.  With HNEW, the exponent moves of the sub-tile's
+        //      changes are counted in the out-of-window counters (free since the second walk).
+        int32_t* hdelta = reinterpret_cast<int32_t*>(&S.ocnt[0][0]);
+        if (HNEW) hdelta[tid] = 0;
         const uint32_t bits = S.mark[(span0 >> 5) + lane];
         uint32_t incl = __popc(bits);
         for (int o = 1; o < 32; o <<= 1) {
@@ -641,13 +654,22 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             const uint32_t ns = S.nstage;
             for (uint32_t k = tid; k < ns; k += MP_THREADS) {
                 const int i = S.order[k];
+                const uint32_t x = S.tile[mpidx(i)];
                 if (sb + k < stage_cap) {
                     caddr[sb + k] = (unsigned long long)(reinterpret_cast<uintptr_t>(tt.w + base + i));
-                    cval[sb + k] = uint16_t(S.tile[mpidx(i)] >> 16);
+                    cval[sb + k] = uint16_t(x >> 16);
+                }
+                if (HNEW) {
+                    const uint32_t eo = (x >> 7) & 0xFFu, en = (x >> 23) & 0xFFu;
+                    if (eo != en) {
+                        atomicSub(&hdelta[eo], 1);
+                        atomicAdd(&hdelta[en], 1);
+                    }
                 }
             }
         }
         __syncthreads();
+        if (HNEW && hdelta[tid]) atomicAdd(&HNEW[s * 256 + tid], uint32_t(hdelta[tid]));
         S.pcur[tid] += S.tot[tid];
         if (tid == 0) S.emax = 0;
         __syncthreads();
@@ -692,8 +714,18 @@ void build_lut(const DecodeTable& d, uint32_t* lut) {
 
 }  // namespace
 
+__global__ void k_hist_store(const uint32_t* __restrict__ src, uint32_t* const* __restrict__ dst,
+                             const int64_t* __restrict__ row0, const int64_t* __restrict__ rows, int n) {
+    const int t = blockIdx.y;
+    if (t >= n) return;
+    const int64_t cells = rows[t] * 256;
+    for (int64_t k = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; k < cells; k += int64_t(gridDim.x) * blockDim.x)
+        dst[t][k] = src[row0[t] * 256 + k];
+}
+
 Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64_t* old_chk, const uint8_t* has_chk,
-                  cudaStream_t st, int64_t* changed, std::string* err) {
+                  cudaStream_t st, int64_t* changed, std::string* err, const uint64_t* versions,
+                  const uint8_t* has_version) {
     *changed = 0;
     const int nt = int(u.tensors.size());
     if (u.payload_len && !u.payload && !u.payload_device) {
@@ -717,6 +749,15 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
         d.numel = h.numel;
         d.super_begin = n_super;
         d.want_full = has_chk && has_chk[t] ? 0 : 1;
+        d.hcache = nullptr;
+        if (versions && has_version && has_version[t] && !d.want_full) {   // histogram from the last apply?
+            const auto it = C.hist_cache.find(reinterpret_cast<uintptr_t>(weights[t]));
+            if (it != C.hist_cache.end() && it->second.numel == h.numel && it->second.tag == versions[t] &&
+                it->second.checksum == old_chk[t]) {
+                d.hcache = static_cast<const uint32_t*>(it->second.rows.p);
+                ++C.hist_hits;
+            }
+        }
         d.g_begin = int32_t(G.size());
         for (const Group& g : h.groups) {
             AppGroup ag{};
@@ -777,6 +818,10 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     CRX_CUDA(ensure_dev(C.b[S_A_CADDR], sizeof(uint64_t) * total, st));
     CRX_CUDA(ensure_dev(C.b[S_A_CVAL], sizeof(uint16_t) * total, st));
     CRX_CUDA(ensure_dev(C.b[S_A_HS], sizeof(uint32_t) * 256 * size_t(n_super), st));
+    bool keep_hist = false;   // some tensor asks for its histogram to be cached
+    for (int t = 0; t < nt && versions && has_version; ++t) keep_hist |= has_version[t] != 0;
+    if (keep_hist) CRX_CUDA(ensure_dev(C.b[S_A_HNEW], sizeof(uint32_t) * 256 * size_t(n_super), st));
+    uint32_t* hnew = keep_hist ? dev<uint32_t>(C, S_A_HNEW) : nullptr;
     CRX_CUDA(ensure_dev(C.b[S_A_TOT], sizeof(uint64_t) * cells, st));
     CRX_CUDA(ensure_dev(C.b[S_A_CHUNK_ROWS], sizeof(int64_t) * 2 * (size_t(nt) + 1), st));
     CRX_CUDA(ensure_dev(C.b[S_A_CHUNK_SUMS], sizeof(uint32_t) * 256 * size_t(n_chunks), st));
@@ -864,7 +909,8 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     { KernelScope ks_(C, "k_map", st);
     k_map<<<unsigned(n_super), MP_THREADS, map_smem, st>>>(dT, nt, dG, dev<uint32_t>(C, S_A_HS), dev<uint32_t>(C, S_A_LOCAL),
                                                             dev<uint32_t>(C, S_A_ZZ), dev<unsigned long long>(C, S_A_CADDR),
-                                                            dev<uint16_t>(C, S_A_CVAL), total, chk_delta, counters + 2);
+                                                            dev<uint16_t>(C, S_A_CVAL), total, chk_delta, counters + 2,
+                                                            dev<uint64_t>(C, S_A_TOT), hnew);
     }
     CRX_CUDA(cudaGetLastError());
     // ---- verdict (one synchronisation for the whole update)
@@ -911,6 +957,61 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
                                                            total);
     }
     CRX_CUDA(cudaGetLastError());
+    // ---- the new weights' histograms for the next apply (tagged version + 1: the caller bumps it)
+    for (int t = 0; t < nt; ++t) {
+        const auto key = reinterpret_cast<uintptr_t>(weights[t]);
+        if (!(keep_hist && has_version[t])) {   // written without a tag: forget what was cached
+            const auto it = C.hist_cache.find(key);
+            if (it != C.hist_cache.end()) {
+                if (it->second.rows.p) cudaFree(it->second.rows.p);
+                C.hist_cache.erase(it);
+            }
+        }
+    }
+    if (keep_hist) {
+        size_t cached_bytes = 0;
+        for (auto& kv : C.hist_cache) cached_bytes += kv.second.rows.cap;
+        if (cached_bytes > (size_t(4) << 30)) {   // bound the cache: start over
+            for (auto& kv : C.hist_cache)
+                if (kv.second.rows.p) cudaFree(kv.second.rows.p);
+            C.hist_cache.clear();
+        }
+        std::vector<uint32_t*> dst;
+        std::vector<int64_t> row0, rows;
+        for (int t = 0; t < nt; ++t) {
+            if (!has_version[t]) continue;
+            auto& ent = C.hist_cache[reinterpret_cast<uintptr_t>(weights[t])];
+            const int64_t nr = (T[size_t(t)].numel + SUPER_N - 1) / SUPER_N;
+            CRX_CUDA(ensure_dev(ent.rows, sizeof(uint32_t) * 256 * size_t(nr), st));
+            ent.numel = T[size_t(t)].numel;
+            ent.tag = versions[t] + 1;
+            ent.checksum = u.tensors[size_t(t)].checksum;
+            dst.push_back(static_cast<uint32_t*>(ent.rows.p));
+            row0.push_back(T[size_t(t)].super_begin);
+            rows.push_back(nr);
+        }
+        const int ne = int(dst.size());
+        if (ne) {
+            const size_t tb = 8 * size_t(ne) * 3;
+            CRX_CUDA(ensure_dev(C.b[S_A_HSTORE], tb, st));
+            if (!C.hstore_ev) CRX_CUDA(cudaEventCreateWithFlags(&C.hstore_ev, cudaEventDisableTiming));
+            CRX_CUDA(cudaEventSynchronize(C.hstore_ev));   // the previous store's copy has read the table
+            CRX_CUDA(ensure_pinned(C.hstore_table, tb, st));
+            uint8_t* hh = static_cast<uint8_t*>(C.hstore_table.p);
+            std::memcpy(hh, dst.data(), 8 * size_t(ne));
+            std::memcpy(hh + 8 * ne, row0.data(), 8 * size_t(ne));
+            std::memcpy(hh + 16 * ne, rows.data(), 8 * size_t(ne));
+            uint8_t* dd = static_cast<uint8_t*>(C.b[S_A_HSTORE].p);
+            CRX_CUDA(cudaMemcpyAsync(dd, hh, tb, cudaMemcpyHostToDevice, st));
+            { KernelScope ks_(C, "k_hist_store", st);
+            k_hist_store<<<dim3(64, unsigned(ne)), 256, 0, st>>>(hnew, reinterpret_cast<uint32_t* const*>(dd),
+                                                                reinterpret_cast<const int64_t*>(dd + 8 * ne),
+                                                                reinterpret_cast<const int64_t*>(dd + 16 * ne), ne);
+            }
+            CRX_CUDA(cudaGetLastError());
+            CRX_CUDA(cudaEventRecord(C.hstore_ev, st));
+        }
+    }
     *changed = int64_t(total);
     return kOk;
 }

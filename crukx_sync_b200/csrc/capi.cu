@@ -78,10 +78,14 @@ Ctx::~Ctx() {
     for (cudaEvent_t e : ev_pool) cudaEventDestroy(e);
     for (cudaEvent_t e : copy_ev) cudaEventDestroy(e);
     if (ev_main) cudaEventDestroy(ev_main);
+    if (hstore_ev) cudaEventDestroy(hstore_ev);
+    if (hstore_table.p) cudaFreeHost(hstore_table.p);
     if (ev_copy) cudaEventDestroy(ev_copy);
     if (copy_stream) cudaStreamDestroy(copy_stream);
     for (auto& d : b)
         if (d.p) cudaFree(d.p);
+    for (auto& kv : hist_cache)
+        if (kv.second.rows.p) cudaFree(kv.second.rows.p);
     if (host) cudaFreeHost(host);
     if (out_host.p) cudaFreeHost(out_host.p);
     if (in_host.p) cudaFreeHost(in_host.p);
@@ -757,6 +761,39 @@ int crx_apply(crx_ctx* ctx, const crx_update* u, int16_t* const* weights, const 
         return CRX_CUDA_ERROR;
     }
 }
+
+int crx_apply_versioned(crx_ctx* ctx, const crx_update* u, int16_t* const* weights, const uint64_t* cached_checksums,
+                        const uint8_t* has_cached, const uint64_t* versions, const uint8_t* has_version, void* stream,
+                        int64_t* changed, char* err, size_t errlen) {
+    if (!ctx || !u || !changed || (!u->u.tensors.empty() && !weights) || (has_version && !versions)) {
+        put_err(err, errlen, "crx_apply_versioned: bad argument");
+        return CRX_BAD_ARGUMENT;
+    }
+    if (has_cached && !cached_checksums) {
+        put_err(err, errlen, "crx_apply_versioned: has_cached without cached_checksums");
+        return CRX_BAD_ARGUMENT;
+    }
+    try {
+        std::lock_guard<std::mutex> lock(ctx->c.mu);
+        DeviceGuard g(ctx->c.device);
+        std::string msg;
+        const crx::Status s = crx::apply_impl(ctx->c, u->u, weights, cached_checksums, has_cached,
+                                              static_cast<cudaStream_t>(stream), changed, &msg, versions, has_version);
+        if (s != crx::kOk) {
+            put_err(err, errlen, msg);
+            return int(s);
+        }
+        return CRX_OK;
+    } catch (const std::bad_alloc&) {
+        put_err(err, errlen, "crx_apply_versioned: out of host memory");
+        return CRX_NO_MEMORY;
+    } catch (const std::exception& ex) {
+        put_err(err, errlen, std::string("crx_apply_versioned: ") + ex.what());
+        return CRX_CUDA_ERROR;
+    }
+}
+
+uint64_t crx_ctx_hist_cache_hits(crx_ctx* ctx) { return ctx ? ctx->c.hist_hits : 0; }
 
 int crx_huffman_lengths(const uint64_t* counts, int64_t n, uint8_t* lengths) {
     if (n <= 0 || !counts || !lengths) return CRX_BAD_ARGUMENT;

@@ -73,7 +73,8 @@ Status encode_impl(Ctx& C, int n, const int16_t* const* prev, const int16_t* con
 // Verify `u` against `weights` (one device pointer per update tensor, same order) and commit on
 // success.  old_chk/has_chk: the receiver's trusted checksum of each tensor's current contents.
 Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64_t* old_chk, const uint8_t* has_chk,
-                  cudaStream_t st, int64_t* changed, std::string* err);
+                  cudaStream_t st, int64_t* changed, std::string* err, const uint64_t* versions = nullptr,
+                  const uint8_t* has_version = nullptr);
 
 // Full checksum of one device tensor (reference codec.checksum).
 Status checksum_impl(Ctx& C, const int16_t* data, int64_t n, cudaStream_t st, uint64_t* out, std::string* err);

@@ -7,6 +7,7 @@
 #include <cstdint>
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 #include <string>
 #include <vector>
 
@@ -50,7 +51,7 @@ enum Slot : int {
     // apply
     S_A_TENS, S_A_GROUPS, S_A_TABLES, S_A_SYMS, S_A_PAYLOAD, S_A_BB, S_A_BOFF, S_A_GAPS, S_A_ZZ, S_A_BSUM,
     S_A_LOCAL, S_A_CADDR, S_A_CVAL, S_A_HS, S_A_TOT, S_A_CHUNK_ROWS, S_A_CHUNK_SUMS, S_A_COUNTERS, S_A_SCAN_TMP,
-    S_CHK, S_REC_POS, S_SUPER_T,
+    S_CHK, S_REC_POS, S_SUPER_T, S_A_HNEW, S_A_HSTORE,
     S_NSLOTS
 };
 
@@ -84,6 +85,18 @@ struct Ctx {
     // ev_main orders them after the caller's stream, ev_copy the decode after them
     cudaStream_t copy_stream = nullptr;
     cudaEvent_t ev_main = nullptr, ev_copy = nullptr;
+    // receiver: exponent histograms per super-tile of weights this context last wrote, keyed by the
+    // weights' address, valid while the caller's version tag matches (crx_apply_versioned)
+    struct HistEntry {
+        int64_t numel = 0;
+        uint64_t tag = 0;
+        uint64_t checksum = 0;   // of the weights the rows describe: a hit also needs the caller's checksum to match
+        DevBuf rows;   // [super-tiles of the tensor][256] u32
+    };
+    std::unordered_map<uintptr_t, HistEntry> hist_cache;
+    uint64_t hist_hits = 0;   // tensors whose histogram pass was skipped
+    DevBuf hstore_table;      // pinned: the table of the last histogram store, read by an async copy
+    cudaEvent_t hstore_ev = nullptr;   // recorded after that copy
     ~Ctx();
 };
 

@@ -164,6 +164,23 @@ void crx_update_free(crx_update* u);
 int crx_apply(crx_ctx* ctx, const crx_update* u, int16_t* const* weights, const uint64_t* cached_checksums,
               const uint8_t* has_cached, void* stream, int64_t* changed, char* err, size_t errlen);
 
+/*
+ * crx_apply with the context's exponent-histogram cache (the caching of per-super-tile exponent
+ * tables across steps; no reference counterpart).  versions[i]/has_version[i] tag update tensor
+ * i's weights with the caller's version counter (torch: tensor._version).  A tagged tensor whose
+ * weights address, size and tag match what this context stored after its last apply, and whose
+ * cached checksum (cached_checksums[i], required) equals the checksum that apply established,
+ * skips the pass that histograms its exponents.  After a successful apply every tagged tensor's
+ * histogram is stored with tag versions[i] + 1: the caller bumps its version counter by one for
+ * the in-place write.  Untagged tensors that the update writes drop their entry.  A stale entry can
+ * only make the update fail verification (CorruptUpdate, nothing written), never write wrong values.
+ */
+int crx_apply_versioned(crx_ctx* ctx, const crx_update* u, int16_t* const* weights, const uint64_t* cached_checksums,
+                        const uint8_t* has_cached, const uint64_t* versions, const uint8_t* has_version, void* stream,
+                        int64_t* changed, char* err, size_t errlen);
+/* Tensors whose histogram pass was skipped by the cache so far (instrumentation). */
+uint64_t crx_ctx_hist_cache_hits(crx_ctx* ctx);
+
 /* Length-limited canonical Huffman code lengths for n symbol counts, with the reference's tie
  * order (src/crukx_sync/codec.py:71-98).  Host only; the encoder uses the same routine. */
 int crx_huffman_lengths(const uint64_t* counts, int64_t n, uint8_t* lengths);
