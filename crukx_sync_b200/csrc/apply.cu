@@ -362,9 +362,13 @@ __global__ void __launch_bounds__(256) k_locals(const uint64_t* __restrict__ bsc
 
 // ------------------------------------------------------------------ (exponent, rank) -> position
 //
-// Per sub-tile a stable counting sort of the old exponents built the same way as the encoder's
-// ranks (lane runs with private counters over a 16-exponent window, warp matching below it), then
-// every change is placed by (exponent, group-local rank) and its new value staged in position order.
+// Per sub-tile every lane counts the old exponents of its own run of 32 elements (private counters
+// over a 16-exponent window ending at the sub-tile's largest exponent, one extra row for the
+// elements below it).  A change with exponent e and rank r among the sub-tile's elements of
+// exponent e is then found by selection: the warp whose exclusive base is the last <= r, the lane
+// likewise, and the remaining rank among the equal exponent bytes of that lane's run.  Exponents
+// below the window (zeros, tiny weights) are few: their positions are listed in (exponent, index)
+// order by warp matching.  New values are staged in position order.
 
 constexpr int MP_THREADS = 256;
 constexpr int MP_WARPS = MP_THREADS / 32;
@@ -374,26 +378,31 @@ constexpr int MP_RUN = MP_SPAN / 32;         // 32
 constexpr int MWIN = 16;
 static_assert(MP_SUB * 32 == SUPER_N, "32 sub-tiles per super-tile");
 
-__device__ __forceinline__ int mpidx(int i) { return i + (i >> 5); }
-
 struct MapSmem {
-    uint32_t tile[MP_SUB + MP_SUB / 32];  // old bits | (own rank, later the new bits) << 16, padded
-    uint16_t order[MP_SUB];               // sub-tile index of the k-th element in (exponent, index) order
-    uint32_t mark[MP_SUB / 32];           // changed positions (unpadded index)
-    uint16_t cnt[MP_WARPS][MWIN][34];     // per-lane counts, then exclusive prefixes over lanes
-    uint32_t ocnt[MP_WARPS][256];         // out-of-window per-warp counts, then warp bases
+    uint32_t texp[MP_SUB / 32 * 9];       // old exponent bytes: run r (32 elements) in words 9r..9r+7
+    uint16_t order[MP_SUB];               // below-window positions in (exponent, index) order, then the changed positions
+    uint16_t nval[MP_SUB];                // new bits of every changed position
+    uint32_t mark[MP_SUB / 32];           // changed positions
+    uint16_t cnt[MP_WARPS][MWIN + 1][32]; // per-lane counts (row MWIN: below the window), then exclusive prefixes over lanes
+    uint32_t ocnt[MP_WARPS][256];         // below-window per-warp counts, then warp bases
     uint32_t wwin[MP_WARPS][MWIN];        // per-warp window totals, then warp bases
     uint16_t tot[256], estart[256];
     uint32_t pcur[256];
     uint64_t cursor[256], gend[256];
     uint32_t nextloc[256];                // group-local index of each group's next change (~0: none)
+    int32_t hdelta[256];                  // exponent moves of this super-tile's changes
     uint8_t gexp[256];
-    uint32_t oow[MP_WARPS], wcnt[MP_WARPS], wbase[MP_WARPS];
+    uint32_t wcnt[MP_WARPS], wbase[MP_WARPS];
     unsigned long long stage_base;
     uint32_t nstage;
     int emax;
     uint64_t red[MP_WARPS];
 };
+
+// 0x80 in every byte of x that is zero, nothing elsewhere
+__device__ __forceinline__ uint32_t zero_bytes(uint32_t x) {
+    return ~(((x & 0x7F7F7F7Fu) + 0x7F7F7F7Fu) | x) & 0x80808080u;
+}
 
 __global__ void __launch_bounds__(MP_THREADS, 3)
 k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, const uint32_t* __restrict__ PS,
@@ -412,11 +421,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
     const int ngt = tt.g_end - tt.g_begin;
     const int span0 = w * MP_SPAN;
     S.pcur[tid] = PS[s * 256 + tid];
-    if (HNEW) {   // the weights' histogram after this update: the old one here, exponent moves added below
-        const bool last = e_end >= tt.numel;
-        const uint32_t nxt = last ? uint32_t(GS[int64_t(t) * 256 + tid]) : PS[(s + 1) * 256 + tid];
-        HNEW[s * 256 + tid] = nxt - S.pcur[tid];
-    }
+    S.hdelta[tid] = 0;
     if (tid == 0) S.emax = 0;
     __syncthreads();
     if (tid < ngt) {
@@ -438,27 +443,27 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
         const int16_t* p = tt.w + base;
         if (tid == 0 && base + MP_SUB < e_end)     // the next sub-tile streams into L2 meanwhile
             prefetch_l2(p + MP_SUB, size_t(tmin<int64_t>(MP_SUB, e_end - base - MP_SUB)) * 2);
+        // ---- stage the old exponent bytes and find the largest
         uint32_t mx = 0;
         if (n == MP_SUB && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
             const uint4* v = reinterpret_cast<const uint4*>(p);
 #pragma unroll
             for (int k = 0; k < MP_SUB / 8 / MP_THREADS; ++k) {
-                const int vi = tid + k * MP_THREADS;
-                const uint4 q = __ldcs(v + vi);
-                const uint32_t wd[4] = {q.x, q.y, q.z, q.w};
-                const int pi = mpidx(8 * vi);
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    S.tile[pi + 2 * h] = wd[h] & 0xFFFFu;
-                    S.tile[pi + 2 * h + 1] = wd[h] >> 16;
-                    mx = tmax(mx, tmax((wd[h] >> 7) & 0xFFu, (wd[h] >> 23) & 0xFFu));
-                }
+                const int vi = tid + k * MP_THREADS;     // elements 8vi .. 8vi+7: run vi/4, quarter vi%4
+                const uint4 q = v[vi];
+                const uint32_t w0 = __byte_perm((q.x >> 7) & 0x00FF00FFu, (q.y >> 7) & 0x00FF00FFu, 0x6420);
+                const uint32_t w1 = __byte_perm((q.z >> 7) & 0x00FF00FFu, (q.w >> 7) & 0x00FF00FFu, 0x6420);
+                S.texp[(vi >> 2) * 9 + 2 * (vi & 3)] = w0;
+                S.texp[(vi >> 2) * 9 + 2 * (vi & 3) + 1] = w1;
+                mx = __vmaxu4(mx, __vmaxu4(w0, w1));
             }
+            mx = tmax(tmax(mx & 0xFFu, (mx >> 8) & 0xFFu), tmax((mx >> 16) & 0xFFu, mx >> 24));
         } else {
+            uint8_t* tb = reinterpret_cast<uint8_t*>(S.texp);
             for (int i = tid; i < n; i += MP_THREADS) {
-                const uint32_t x = uint16_t(p[i]);
-                S.tile[mpidx(i)] = x;
-                mx = tmax(mx, (x >> 7) & 0xFFu);
+                const uint32_t e = (uint32_t(uint16_t(p[i])) >> 7) & 0xFFu;
+                tb[(i >> 5) * 36 + (i & 31)] = uint8_t(e);
+                mx = tmax(mx, e);
             }
         }
         mx = __reduce_max_sync(FULL, mx);
@@ -474,68 +479,62 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             for (int k = tid; k < int(sizeof(S.ocnt) / 16); k += MP_THREADS) o4[k] = make_uint4(0, 0, 0, 0);
         }
         S.mark[tid] = 0;
-        if (tid < MP_WARPS) S.oow[tid] = 0;
         __syncthreads();
-        const int ebase = tmax(S.emax - (MWIN - 1), 0);
+        const uint32_t ebase = uint32_t(tmax(S.emax - (MWIN - 1), 0));
         const int span_n = tmax(0, tmin(MP_SPAN, n - span0));
-        const int r0 = lane * MP_RUN;
-        const int vn = tmax(0, tmin(MP_RUN, span_n - r0));
-        const int pb = mpidx(span0 + r0);
-        // ---- lane walk: own ranks with private counters, four elements at a time (counters loaded
-        //      together, ranks corrected for equal exponents inside the group, stored in order)
+        const int vn = tmax(0, tmin(MP_RUN, span_n - lane * MP_RUN));
+        auto exp_at = [&](int i) { return (S.texp[(i >> 5) * 9 + ((i & 31) >> 2)] >> (8 * (i & 3))) & 0xFFu; };
+        // ---- lane walk: counts per window row; an exponent below the window wraps past MWIN
         {
+            const uint32_t* ew = &S.texp[(w * 32 + lane) * 9];
             uint16_t* myc = &S.cnt[w][0][lane];
-            bool any_oow = false;
-            for (int k = 0; k < vn; k += 4) {
-                uint32_t x[4], inc[4], c[4];
-                int d[4];
+            if (vn == MP_RUN) {
 #pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    const bool valid = k + h < vn;
-                    x[h] = valid ? S.tile[pb + k + h] : 0u;
-                    const int dd = int((x[h] >> 7) & 0xFFu) - ebase;
-                    const bool in = valid && unsigned(dd) < unsigned(MWIN);
-                    any_oow |= valid && !in;
-                    d[h] = in ? dd : 0;
-                    inc[h] = in ? 1u : 0u;
+                for (int g = 0; g < MP_RUN / 4; ++g) {
+                    const uint32_t eb = ew[g];
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) {
+                        const uint32_t d = tmin(((eb >> (8 * h)) & 0xFFu) - ebase, uint32_t(MWIN));
+                        myc[d * 32] += 1;
+                    }
                 }
-#pragma unroll
-                for (int h = 0; h < 4; ++h) c[h] = myc[d[h] * 34];
-#pragma unroll
-                for (int h = 1; h < 4; ++h)
-#pragma unroll
-                    for (int g = 0; g < h; ++g) c[h] += d[h] == d[g] ? inc[g] : 0u;
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    myc[d[h] * 34] = uint16_t(c[h] + inc[h]);
-                    if (inc[h]) S.tile[pb + k + h] = x[h] | (c[h] << 16);
+            } else {
+                for (int k = 0; k < vn; ++k) {
+                    const uint32_t d = tmin(((ew[k >> 2] >> (8 * (k & 3))) & 0xFFu) - ebase, uint32_t(MWIN));
+                    myc[d * 32] += 1;
                 }
             }
-            if (any_oow) atomicOr(&S.oow[w], 1u << lane);
         }
         __syncwarp();
-        for (uint32_t m = S.oow[w]; m; m &= m - 1) {      // below the window: match, in index order
-            const int run = __ffs(m) - 1;
-            const int ii = run * MP_RUN + lane;
-            const bool valid = ii < span_n;
-            const uint32_t x = valid ? S.tile[mpidx(span0 + ii)] : 0u;
-            const uint32_t e = (x >> 7) & 0xFFu;
-            const bool oow = valid && int(e) < ebase;
-            const uint32_t r = warp_rank(S.ocnt[w], e, oow, lt, lane);
-            if (oow) S.tile[mpidx(span0 + ii)] = x | (r << 16);
+        const uint32_t oowm = __ballot_sync(FULL, S.cnt[w][MWIN][lane] != 0);   // runs with below-window elements
+        // ---- below the window, first pass: per-warp counts by matching, run by run in index order
+        for (uint32_t m = oowm; m; m &= m - 1) {
+            const int ii = (__ffs(m) - 1) * MP_RUN + lane;
+            const uint32_t e = ii < span_n ? exp_at(span0 + ii) : 0u;
+            warp_rank(S.ocnt[w], e, ii < span_n && e < ebase, lt, lane);
         }
-        if (lane < MWIN) {
-            uint32_t run = 0;
+        // ---- lane prefixes of the window rows: each half-warp scans one row, two counts per word
+        {
+            const int m = lane & 15;
 #pragma unroll
-            for (int col = 0; col < 32; ++col) {
-                const uint32_t v = S.cnt[w][lane][col];
-                S.cnt[w][lane][col] = uint16_t(run);
-                run += v;
+            for (int j = 0; j < MWIN / 2; ++j) {
+                const int d = 2 * j + (lane >> 4);
+                uint32_t* row = reinterpret_cast<uint32_t*>(&S.cnt[w][d][0]);
+                const uint32_t wd = row[m];
+                const uint32_t sum = (wd & 0xFFFFu) + (wd >> 16);
+                uint32_t incl = sum;
+#pragma unroll
+                for (int o = 1; o < 16; o <<= 1) {
+                    const uint32_t y = __shfl_up_sync(FULL, incl, o, 16);
+                    if (m >= o) incl += y;
+                }
+                const uint32_t ex = incl - sum;
+                row[m] = ex | ((ex + (wd & 0xFFFFu)) << 16);
+                if (m == 15) S.wwin[w][d] = incl;
             }
-            S.wwin[w][lane] = run;
         }
         __syncthreads();
-        {
+        {   // warp bases per exponent and the sub-tile's totals
             const int e = tid;
             uint32_t o = 0;
             for (int ww = 0; ww < MP_WARPS; ++ww) {
@@ -543,8 +542,8 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                 S.ocnt[ww][e] = o;
                 o += v;
             }
-            const int d = e - ebase;
-            if (unsigned(d) < unsigned(MWIN)) {
+            const uint32_t d = uint32_t(e) - ebase;
+            if (d < uint32_t(MWIN)) {
                 uint32_t a = 0;
                 for (int ww = 0; ww < MP_WARPS; ++ww) {
                     const uint32_t v = S.wwin[ww][d];
@@ -570,23 +569,24 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             for (int k = 0; k < 8; ++k) { S.estart[lane * 8 + k] = uint16_t(run); run += v[k]; }
         }
         __syncthreads();
-        // ---- second lane walk: every element to its sorted slot
-#pragma unroll 4
-        for (int k = 0; k < vn; ++k) {
-            const uint32_t x = S.tile[pb + k];
-            const uint32_t e = (x >> 7) & 0xFFu;
-            const int d = int(e) - ebase;
-            const uint32_t sp = S.estart[e] + (x >> 16) +
-                                (unsigned(d) < unsigned(MWIN) ? S.wwin[w][d] + S.cnt[w][d][lane] : S.ocnt[w][e]);
-            S.order[sp] = uint16_t(span0 + r0 + k);
+        // ---- below the window, second pass: the counters now hold warp bases, so matching again
+        //      in the same order yields every such element's slot in (exponent, index) order
+        for (uint32_t m = oowm; m; m &= m - 1) {
+            const int ii = (__ffs(m) - 1) * MP_RUN + lane;
+            const uint32_t e = ii < span_n ? exp_at(span0 + ii) : 0u;
+            const bool below = ii < span_n && e < ebase;
+            const uint32_t r = warp_rank(S.ocnt[w], e, below, lt, lane);
+            if (below) S.order[S.estart[e] + r] = uint16_t(span0 + ii);
         }
         __syncthreads();
-        // ---- place this sub-tile's changes group by group; new bits go to the tile's upper half.
-        //      Groups whose next change lies beyond this sub-tile are skipped from shared memory.
+        // ---- place this sub-tile's changes group by group.  Groups whose next change lies beyond
+        //      this sub-tile are skipped from shared memory.
         for (int k = w; k < ngt; k += MP_WARPS) {
-            const int e = S.gexp[k];
+            const uint32_t e = S.gexp[k];
             const uint32_t lo = S.pcur[e], tot = S.tot[e];
             if (S.nextloc[k] - lo >= tot) continue;
+            const uint32_t d = e - ebase;            // window row (>= MWIN: below the window)
+            const uint32_t e4 = e * 0x01010101u;
             const uint64_t ge = S.gend[k];
             uint64_t cur = S.cursor[k];
             uint32_t next = 0xFFFFFFFFu;
@@ -596,14 +596,55 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                 if (j < ge) { lc = local[j]; z = zz[j]; }   // one round trip: both loads issued together
                 const bool valid = lc != 0xFFFFFFFFu && lc >= lo && lc - lo < tot;
                 if (valid) {
-                    const uint32_t i = S.order[S.estart[e] + (lc - lo)];
-                    const int pi = mpidx(int(i));
-                    const uint32_t old = S.tile[pi] & 0xFFFFu;
-                    const int32_t res = int32_t(z >> 1) ^ -int32_t(z & 1);
-                    const uint32_t nv = uint32_t(int32_t(old) + res) & 0xFFFFu;
-                    S.tile[pi] = old | (nv << 16);
-                    atomicOr(&S.mark[i >> 5], 1u << (i & 31));
-                    delta += (uint64_t(nv) - uint64_t(old)) * splitmix_weight(uint64_t(base + i));
+                    uint32_t r = lc - lo;
+                    int i;
+                    if (d < uint32_t(MWIN)) {
+                        int ww = 0;                  // last warp whose base is <= r
+#pragma unroll
+                        for (int q = 1; q < MP_WARPS; ++q) ww += S.wwin[q][d] <= r;
+                        r -= S.wwin[ww][d];
+                        const uint16_t* pre = &S.cnt[ww][d][0];
+                        int l = 0;                   // last lane whose prefix is <= r
+#pragma unroll
+                        for (int st = 16; st; st >>= 1) l += pre[l + st] <= r ? st : 0;
+                        r -= pre[l];
+                        // the r-th byte equal to e in the run of (ww, l)
+                        const uint32_t* ew = &S.texp[(ww * 32 + l) * 9];
+                        uint32_t zsel = 0, qsel = 0;
+                        bool done = false;
+#pragma unroll
+                        for (int q = 0; q < MP_RUN / 4; ++q) {
+                            const uint32_t zb = zero_bytes(ew[q] ^ e4);
+                            const uint32_t c = __popc(zb);
+                            const bool hit = !done && r < c;
+                            zsel = hit ? zb : zsel;
+                            qsel = hit ? uint32_t(q) : qsel;
+                            r = (done || hit) ? r : r - c;
+                            done |= hit;
+                        }
+#pragma unroll
+                        for (int q = 0; q < 3; ++q) zsel = uint32_t(q) < r ? zsel & (zsel - 1) : zsel;
+                        // (a selection that found nothing leaves the change unplaced: the host
+                        // then reports that not every change was placed)
+                        i = done ? ww * MP_SPAN + l * MP_RUN + int(qsel) * 4 + ((__ffs(zsel) - 1) >> 3) : -1;
+                    } else {
+                        i = S.order[S.estart[e] + r];
+                    }
+                    if (unsigned(i) < unsigned(n)) {
+                        const uint32_t old = uint16_t(p[i]);
+                        const int32_t res = int32_t(z >> 1) ^ -int32_t(z & 1);
+                        const uint32_t nv = uint32_t(int32_t(old) + res) & 0xFFFFu;
+                        S.nval[i] = uint16_t(nv);
+                        atomicOr(&S.mark[i >> 5], 1u << (i & 31));
+                        delta += (uint64_t(nv) - uint64_t(old)) * splitmix_weight(uint64_t(base + i));
+                        if (HNEW) {
+                            const uint32_t eo = (old >> 7) & 0xFFu, en = (nv >> 7) & 0xFFu;
+                            if (eo != en) {
+                                atomicSub(&S.hdelta[eo], 1);
+                                atomicAdd(&S.hdelta[en], 1);
+                            }
+                        }
+                    }
                 }
                 const uint32_t m = __ballot_sync(FULL, valid);
                 const int taken = __popc(~m) ? __ffs(~m) - 1 : 32;   // consumed changes are a prefix
@@ -625,10 +666,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
         }
         __syncthreads();
         // ---- stage the sub-tile's new values in position order (one atomic per sub-tile): lane l
-        //      owns mark word l of its warp's span.  With HNEW, the exponent moves of the sub-tile's
-        //      changes are counted in the out-of-window counters (free since the second walk).
-        int32_t* hdelta = reinterpret_cast<int32_t*>(&S.ocnt[0][0]);
-        if (HNEW) hdelta[tid] = 0;
+        //      owns mark word l of its warp's span
         const uint32_t bits = S.mark[(span0 >> 5) + lane];
         uint32_t incl = __popc(bits);
         for (int o = 1; o < 32; o <<= 1) {
@@ -644,8 +682,8 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             S.stage_base = r ? atomicAdd(staged, (unsigned long long)r) : 0ull;
         }
         __syncthreads();
-        // the sorted order is no longer needed: it now lists the changed positions, which all
-        // threads then write out contiguously
+        // the below-window order is no longer needed: it now lists the changed positions, which
+        // all threads then write out contiguously
         uint32_t at = S.wbase[w] + incl - __popc(bits);
         for (uint32_t b = bits; b; b &= b - 1, ++at) S.order[at] = uint16_t(span0 + lane * 32 + (__ffs(b) - 1));
         __syncthreads();
@@ -654,25 +692,20 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             const uint32_t ns = S.nstage;
             for (uint32_t k = tid; k < ns; k += MP_THREADS) {
                 const int i = S.order[k];
-                const uint32_t x = S.tile[mpidx(i)];
                 if (sb + k < stage_cap) {
                     caddr[sb + k] = (unsigned long long)(reinterpret_cast<uintptr_t>(tt.w + base + i));
-                    cval[sb + k] = uint16_t(x >> 16);
-                }
-                if (HNEW) {
-                    const uint32_t eo = (x >> 7) & 0xFFu, en = (x >> 23) & 0xFFu;
-                    if (eo != en) {
-                        atomicSub(&hdelta[eo], 1);
-                        atomicAdd(&hdelta[en], 1);
-                    }
+                    cval[sb + k] = S.nval[i];
                 }
             }
         }
-        __syncthreads();
-        if (HNEW && hdelta[tid]) atomicAdd(&HNEW[s * 256 + tid], uint32_t(hdelta[tid]));
         S.pcur[tid] += S.tot[tid];
         if (tid == 0) S.emax = 0;
         __syncthreads();
+    }
+    if (HNEW) {   // the weights' histogram after this update: the old one plus the exponent moves
+        const bool last = e_end >= tt.numel;
+        const uint32_t nxt = last ? uint32_t(GS[int64_t(t) * 256 + tid]) : PS[(s + 1) * 256 + tid];
+        HNEW[s * 256 + tid] = nxt - PS[s * 256 + tid] + uint32_t(S.hdelta[tid]);
     }
     block_add_u64<MP_THREADS>(delta, &chk_delta[t], S.red);
 }

@@ -78,10 +78,9 @@ constexpr int WREC = 128;                    // in-window change records per war
 constexpr int OREC = 32;                     // out-of-window change records per warp
 static_assert(ER_SUB * 32 == SUPER_N, "32 sub-tiles per super-tile");
 
-__device__ __forceinline__ int pidx(int i) { return i + (i >> 5); }   // one pad word per 32: no bank conflicts
-
 struct RankSmem {
-    uint32_t tile[ER_SUB + ER_SUB / 32];  // prev | cur << 16, padded layout
+    uint32_t texp[ER_SUB / 32 * 9];       // old exponent bytes; run r (32 elements) in words 9r..9r+7
+    uint32_t chm[ER_SUB / 32];            // changed bit of every element, one word per run
     uint32_t cnt[ER_WARPS][WIN][33];      // per-lane counts A | C << 16, then exclusive prefixes over lanes
     uint32_t ocnt[ER_WARPS][256];         // per-warp counts A | C << 16 of out-of-window elements, then warp bases
     uint32_t wwin[ER_WARPS][WIN];         // per-warp window totals, then exclusive bases over warps
@@ -137,7 +136,7 @@ __device__ __forceinline__ void scan_change_starts(const uint32_t* tot, uint32_t
     for (int k = 0; k < 8; ++k) { cstart[lane * 8 + k] = run; run += v[k]; }
 }
 
-__global__ void __launch_bounds__(ER_THREADS, 3)
+__global__ void __launch_bounds__(ER_THREADS, 4)
 k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_key, uint32_t* __restrict__ rec_val,
            uint64_t rec_cap, unsigned long long* __restrict__ counters, uint32_t* __restrict__ HS,
            uint32_t* __restrict__ CS, unsigned long long* __restrict__ chk_delta, unsigned long long* __restrict__ chk_full) {
@@ -162,33 +161,53 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
         const int n = int(tmin<int64_t>(ER_SUB, e_end - base));
         const int16_t* pp = tt.prev + base;
         const int16_t* cp = tt.cur + base;
-        // ---- stage prev|cur (padded) and find the largest old exponent
+        // the (prev, cur) bits of sub-tile element i; only changed elements are read back
+        auto bits_of = [&](int i) { return uint32_t(uint16_t(pp[i])) | (uint32_t(uint16_t(cp[i])) << 16); };
+        // ---- stage old exponents (bytes) and changed bits; largest old exponent
         uint32_t mx = 0;
         if (n == ER_SUB && ((reinterpret_cast<uintptr_t>(pp) | reinterpret_cast<uintptr_t>(cp)) & 15) == 0) {
             const uint4* pv = reinterpret_cast<const uint4*>(pp);
             const uint4* cv = reinterpret_cast<const uint4*>(cp);
 #pragma unroll
             for (int k = 0; k < ER_SUB / 8 / ER_THREADS; ++k) {
-                const int v = tid + k * ER_THREADS;
-                const uint4 a = __ldcs(pv + v);
-                const uint4 b = __ldcs(cv + v);
-                const uint32_t wd[8] = {__byte_perm(a.x, b.x, 0x5410), __byte_perm(a.x, b.x, 0x7632),
-                                        __byte_perm(a.y, b.y, 0x5410), __byte_perm(a.y, b.y, 0x7632),
-                                        __byte_perm(a.z, b.z, 0x5410), __byte_perm(a.z, b.z, 0x7632),
-                                        __byte_perm(a.w, b.w, 0x5410), __byte_perm(a.w, b.w, 0x7632)};
-                const int p = pidx(8 * v);
+                const int v = tid + k * ER_THREADS;     // elements 8v .. 8v+7: run v/4, quarter v%4
+                const uint4 a = pv[v];
+                const uint4 b = cv[v];
+                const uint32_t w0 = __byte_perm((a.x >> 7) & 0x00FF00FFu, (a.y >> 7) & 0x00FF00FFu, 0x6420);
+                const uint32_t w1 = __byte_perm((a.z >> 7) & 0x00FF00FFu, (a.w >> 7) & 0x00FF00FFu, 0x6420);
+                const int r = v >> 2, q = v & 3;
+                S.texp[r * 9 + 2 * q] = w0;
+                S.texp[r * 9 + 2 * q + 1] = w1;
+                mx = __vmaxu4(mx, __vmaxu4(w0, w1));
+                // changed bits of the 8 elements (low half of a word first), then the run's 32
+                const uint32_t c0 = __vcmpne2(a.x, b.x), c1 = __vcmpne2(a.y, b.y);
+                const uint32_t c2 = __vcmpne2(a.z, b.z), c3 = __vcmpne2(a.w, b.w);
+                uint32_t cb = (c0 & 1u) | ((c0 >> 15) & 2u) | ((c1 & 1u) << 2) | ((c1 >> 13) & 8u) |
+                              ((c2 & 1u) << 4) | ((c2 >> 11) & 32u) | ((c3 & 1u) << 6) | ((c3 >> 9) & 128u);
+                cb <<= 8 * q;
+                cb |= __shfl_xor_sync(FULL, cb, 1);
+                cb |= __shfl_xor_sync(FULL, cb, 2);
+                if (q == 0) S.chm[r] = cb;
+                if (tt.want_full) {
+                    const uint32_t cw[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-                for (int h = 0; h < 8; ++h) {
-                    S.tile[p + h] = wd[h];
-                    mx = tmax(mx, (wd[h] >> 7) & 0xFFu);
-                    if (tt.want_full) full += uint64_t(wd[h] >> 16) * splitmix_weight(uint64_t(base + 8 * v + h));
+                    for (int h = 0; h < 4; ++h) {
+                        full += uint64_t(cw[h] & 0xFFFFu) * splitmix_weight(uint64_t(base + 8 * v + 2 * h));
+                        full += uint64_t(cw[h] >> 16) * splitmix_weight(uint64_t(base + 8 * v + 2 * h + 1));
+                    }
                 }
             }
+            mx = tmax(tmax(mx & 0xFFu, (mx >> 8) & 0xFFu), tmax((mx >> 16) & 0xFFu, mx >> 24));
         } else {
+            uint8_t* tb = reinterpret_cast<uint8_t*>(S.texp);
+            S.chm[tid] = 0;
+            __syncthreads();
             for (int i = tid; i < n; i += ER_THREADS) {
-                const uint32_t x = uint32_t(uint16_t(pp[i])) | (uint32_t(uint16_t(cp[i])) << 16);
-                S.tile[pidx(i)] = x;
-                mx = tmax(mx, (x >> 7) & 0xFFu);
+                const uint32_t x = bits_of(i);
+                const uint32_t e = (x >> 7) & 0xFFu;
+                tb[(i >> 5) * 36 + (i & 31)] = uint8_t(e);
+                if (changed_bits(x)) atomicOr(&S.chm[i >> 5], 1u << (i & 31));
+                mx = tmax(mx, e);
                 if (tt.want_full) full += uint64_t(x >> 16) * splitmix_weight(uint64_t(base + i));
             }
         }
@@ -208,28 +227,32 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
         __syncthreads();
         const int ebase = tmax(S.emax - (WIN - 1), 0);
         const int span_n = tmax(0, tmin(ER_SPAN, n - span0));
+        // exponent byte and changed bit of sub-tile element i
+        auto exp_of_i = [&](int i) { return (S.texp[(i >> 5) * 9 + ((i & 31) >> 2)] >> (8 * (i & 3))) & 0xFFu; };
+        auto changed_i = [&](int i) { return ((S.chm[i >> 5] >> (i & 31)) & 1u) != 0; };
 
-        // ---- lane walk: private counters, in-window change records.  Four elements at a time: their
-        //      counters are loaded together, ranks corrected for equal exponents inside the group,
-        //      and stored in order (the last store of a counter carries all four increments).
+        // ---- lane walk: private counters, in-window change records.  Four elements at a time (one
+        //      exponent word): their counters are loaded together, ranks corrected for equal
+        //      exponents inside the group, and stored in order (the last store carries all four).
         {
             const int r0 = lane * ER_RUN;
             const int vn = tmax(0, tmin(ER_RUN, span_n - r0));
-            const int pb = pidx(span0 + r0);
+            const uint32_t* ew = &S.texp[(w * 32 + lane) * 9];
+            const uint32_t cm = S.chm[w * 32 + lane];
             uint32_t* myc = &S.cnt[w][0][lane];
             bool any_oow = false;
             for (int k = 0; k < vn; k += 4) {
-                uint32_t x[4], inc[4], c[4];
+                const uint32_t eb = ew[k >> 2];
+                uint32_t inc[4], c[4];
                 int d[4];
 #pragma unroll
                 for (int h = 0; h < 4; ++h) {
                     const bool valid = k + h < vn;
-                    x[h] = valid ? S.tile[pb + k + h] : 0u;
-                    const int dd = int((x[h] >> 7) & 0xFFu) - ebase;
+                    const int dd = int((eb >> (8 * h)) & 0xFFu) - ebase;
                     const bool in = valid && unsigned(dd) < unsigned(WIN);
                     any_oow |= valid && !in;
                     d[h] = in ? dd : 0;
-                    inc[h] = in ? (changed_bits(x[h]) ? 0x10001u : 1u) : 0u;
+                    inc[h] = in ? (((cm >> (k + h)) & 1u) ? 0x10001u : 1u) : 0u;
                 }
 #pragma unroll
                 for (int h = 0; h < 4; ++h) c[h] = myc[d[h] * 33];
@@ -262,10 +285,9 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
             const int run = __ffs(m) - 1;
             const int ii = run * ER_RUN + lane;
             const bool valid = ii < span_n;
-            const uint32_t x = valid ? S.tile[pidx(span0 + ii)] : 0u;
-            const uint32_t e = (x >> 7) & 0xFFu;
+            const uint32_t e = valid ? exp_of_i(span0 + ii) : 0u;
             const bool oow = valid && int(e) < ebase;
-            const bool ch = oow && changed_bits(x);
+            const bool ch = oow && changed_i(span0 + ii);
             const uint32_t rA = warp_rank_packed(S.ocnt[w], e, oow, 0, lt, lane);
             const uint32_t rC = warp_rank_packed(S.ocnt[w], e, ch, 16, lt, lane);
             if (ch) {
@@ -331,7 +353,7 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
                 const int ii = int(r >> 16), d = int((r >> 12) & 15u);
                 const uint32_t e = uint32_t(ebase + d);
                 const uint32_t lp = S.cnt[w][d][ii >> 5], wb = S.wwin[w][d];
-                const uint32_t x = S.tile[pidx(span0 + ii)];
+                const uint32_t x = bits_of(span0 + ii);
                 const uint32_t rc = (wb >> 16) + (lp >> 16) + (r & 63u);   // rank among the sub-tile's changes
                 put_record(rec_key, rec_val, rec_cap, rb + S.cstart[e] + rc, s,
                            S.runA[e] + (wb & 0xFFFFu) + (lp & 0xFFFFu) + ((r >> 6) & 63u), S.runC[e] + rc, x);
@@ -343,7 +365,7 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
                 const int ii = int(q & 1023u);
                 const uint32_t e = uint32_t(q >> 10) & 0xFFu;
                 const uint32_t wb = S.ocnt[w][e];
-                const uint32_t x = S.tile[pidx(span0 + ii)];
+                const uint32_t x = bits_of(span0 + ii);
                 const uint32_t rc = (wb >> 16) + (uint32_t(q >> 29) & 2047u);
                 put_record(rec_key, rec_val, rec_cap, rb + S.cstart[e] + rc, s,
                            S.runA[e] + (wb & 0xFFFFu) + (uint32_t(q >> 18) & 2047u), S.runC[e] + rc, x);
@@ -356,10 +378,9 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
             for (int c = 0; c * 32 < span_n; ++c) {
                 const int ii = c * 32 + lane;
                 const bool valid = ii < span_n;
-                const uint32_t x = valid ? S.tile[pidx(span0 + ii)] : 0u;
-                const uint32_t e = (x >> 7) & 0xFFu;
+                const uint32_t e = valid ? exp_of_i(span0 + ii) : 0u;
                 warp_rank_packed(S.ocnt[w], e, valid, 0, lt, lane);
-                warp_rank_packed(S.ocnt[w], e, valid && changed_bits(x), 16, lt, lane);
+                warp_rank_packed(S.ocnt[w], e, valid && changed_i(span0 + ii), 16, lt, lane);
             }
             __syncthreads();
             {
@@ -378,12 +399,12 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
             for (int c = 0; c * 32 < span_n; ++c) {
                 const int ii = c * 32 + lane;
                 const bool valid = ii < span_n;
-                const uint32_t x = valid ? S.tile[pidx(span0 + ii)] : 0u;
-                const uint32_t e = (x >> 7) & 0xFFu;
-                const bool ch = valid && changed_bits(x);
+                const uint32_t e = valid ? exp_of_i(span0 + ii) : 0u;
+                const bool ch = valid && changed_i(span0 + ii);
                 const uint32_t rA = warp_rank_packed(S.ocnt[w], e, valid, 0, lt, lane);
                 const uint32_t rC = warp_rank_packed(S.ocnt[w], e, ch, 16, lt, lane);
                 if (ch) {
+                    const uint32_t x = bits_of(span0 + ii);
                     put_record(rec_key, rec_val, rec_cap, rb + S.cstart[e] + rC, s, S.runA[e] + rA, S.runC[e] + rC, x);
                     delta += change_delta(x, base + span0 + ii);
                 }
