@@ -362,12 +362,13 @@ __global__ void __launch_bounds__(256) k_locals(const uint64_t* __restrict__ bsc
 
 // ------------------------------------------------------------------ (exponent, rank) -> position
 //
-// Per sub-tile every lane counts the old exponents of its own run of 32 elements (private counters
-// over a 16-exponent window ending at the sub-tile's largest exponent, one extra row for the
-// elements below it).  A change with exponent e and rank r among the sub-tile's elements of
-// exponent e is then found by selection: the warp whose exclusive base is the last <= r, the lane
-// likewise, and the remaining rank among the equal exponent bytes of that lane's run.  Exponents
-// below the window (zeros, tiny weights) are few: their positions are listed in (exponent, index)
+// Every super-tile picks the 16 consecutive old exponents that hold most of its elements (its
+// histogram is known from the column scans).  Per sub-tile every lane marks, for its own run of 32
+// elements, which elements carry each window exponent (one 32-bit mask per window row; one more
+// row for the elements outside the window).  A change with exponent e and rank r among the
+// sub-tile's elements of exponent e is then found by selection: the warp whose exclusive base is
+// the last <= r, the lane likewise, and the r-th set bit of that lane's mask.  Elements outside the
+// window (zeros, tiny or huge weights) are few: their positions are listed in (exponent, index)
 // order by warp matching.  New values are staged in position order.
 
 constexpr int MP_THREADS = 256;
@@ -379,29 +380,41 @@ constexpr int MWIN = 16;
 static_assert(MP_SUB * 32 == SUPER_N, "32 sub-tiles per super-tile");
 
 struct MapSmem {
-    uint32_t texp[MP_SUB / 32 * 9];       // old exponent bytes: run r (32 elements) in words 9r..9r+7
-    uint16_t order[MP_SUB];               // below-window positions in (exponent, index) order, then the changed positions
-    uint16_t nval[MP_SUB];                // new bits of every changed position
-    uint32_t mark[MP_SUB / 32];           // changed positions
-    uint16_t cnt[MP_WARPS][MWIN + 1][32]; // per-lane counts (row MWIN: below the window), then exclusive prefixes over lanes
-    uint32_t ocnt[MP_WARPS][256];         // below-window per-warp counts, then warp bases
-    uint32_t wwin[MP_WARPS][MWIN];        // per-warp window totals, then warp bases
+    uint32_t msk[MP_WARPS][MWIN + 1][32];  // per lane and window row: its run's elements of that exponent (row MWIN: outside)
+    uint16_t pre[MP_WARPS][MWIN][32];      // exclusive prefixes over the lanes of the masks' counts
+    uint16_t order[MP_SUB];                // outside-window positions in (exponent, index) order, then the changed positions
+    union {
+        uint32_t ocnt[MP_WARPS][256];      // outside-window per-warp counts, then warp bases
+        uint16_t nval[MP_SUB];             // new bits of every changed position (placement onwards)
+    } u;
+    uint32_t mark[MP_SUB / 32];            // changed positions
+    uint32_t wwin[MP_WARPS][MWIN];         // per-warp window totals, then warp bases
     uint16_t tot[256], estart[256];
     uint32_t pcur[256];
     uint64_t cursor[256], gend[256];
-    uint32_t nextloc[256];                // group-local index of each group's next change (~0: none)
-    int32_t hdelta[256];                  // exponent moves of this super-tile's changes
+    uint32_t nextloc[256];                 // group-local index of each group's next change (~0: none)
+    int32_t hdelta[256];                   // this super-tile's histogram, then plus its exponent moves
     uint8_t gexp[256];
     uint32_t wcnt[MP_WARPS], wbase[MP_WARPS];
     unsigned long long stage_base;
+    unsigned long long wkey[MP_WARPS];
     uint32_t nstage;
-    int emax;
+    uint32_t ebase;
     uint64_t red[MP_WARPS];
 };
 
-// 0x80 in every byte of x that is zero, nothing elsewhere
-__device__ __forceinline__ uint32_t zero_bytes(uint32_t x) {
-    return ~(((x & 0x7F7F7F7Fu) + 0x7F7F7F7Fu) | x) & 0x80808080u;
+// position of the r-th (0-based) set bit of m; m has more than r set bits
+__device__ __forceinline__ uint32_t nth_set_bit(uint32_t m, uint32_t r) {
+    uint32_t pos = 0;
+#pragma unroll
+    for (int s = 16; s; s >>= 1) {
+        const uint32_t c = __popc(m & ((1u << s) - 1u));
+        const bool up = r >= c;
+        r = up ? r - c : r;
+        m = up ? m >> s : m;
+        pos = up ? pos + uint32_t(s) : pos;
+    }
+    return pos;
 }
 
 __global__ void __launch_bounds__(MP_THREADS, 3)
@@ -421,9 +434,23 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
     const int ngt = tt.g_end - tt.g_begin;
     const int span0 = w * MP_SPAN;
     S.pcur[tid] = PS[s * 256 + tid];
-    S.hdelta[tid] = 0;
-    if (tid == 0) S.emax = 0;
+    {   // this super-tile's histogram: the next row's prefix (or the tensor's total) minus this one's
+        const bool last = e_end >= tt.numel;
+        const uint32_t nxt = last ? uint32_t(GS[int64_t(t) * 256 + tid]) : PS[(s + 1) * 256 + tid];
+        S.hdelta[tid] = int32_t(nxt - S.pcur[tid]);
+    }
     __syncthreads();
+    {   // the window: 16 consecutive exponents holding the most elements (ties: the lowest start)
+        uint64_t key = 0;
+        if (tid <= 256 - MWIN) {
+            uint32_t sum = 0;
+#pragma unroll
+            for (int k = 0; k < MWIN; ++k) sum += uint32_t(S.hdelta[tid + k]);
+            key = (uint64_t(sum) << 8) | uint64_t(255 - tid);
+        }
+        for (int o = 16; o; o >>= 1) key = tmax(key, (uint64_t)__shfl_xor_sync(FULL, key, o));
+        if (lane == 0) S.wkey[w] = key;
+    }
     if (tid < ngt) {
         const AppGroup grp = G[tt.g_begin + tid];
         const uint32_t p0 = S.pcur[grp.exp];
@@ -437,100 +464,87 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
         S.gexp[tid] = uint8_t(grp.exp);
         S.nextloc[tid] = lo < grp.start + grp.count ? local[lo] : 0xFFFFFFFFu;
     }
+    __syncthreads();
+    if (tid == 0) {
+        unsigned long long k = 0;
+        for (int ww = 0; ww < MP_WARPS; ++ww) k = tmax(k, S.wkey[ww]);
+        S.ebase = 255u - uint32_t(k & 0xFFu);
+    }
+    __syncthreads();
+    const uint32_t ebase = S.ebase;
+    auto row_of = [&](uint32_t e) { return tmin(e - ebase, uint32_t(MWIN)); };   // outside: wraps to MWIN
     uint64_t delta = 0;
     for (int64_t base = e_begin; base < e_end; base += MP_SUB) {
         const int n = int(tmin<int64_t>(MP_SUB, e_end - base));
         const int16_t* p = tt.w + base;
         if (tid == 0 && base + MP_SUB < e_end)     // the next sub-tile streams into L2 meanwhile
             prefetch_l2(p + MP_SUB, size_t(tmin<int64_t>(MP_SUB, e_end - base - MP_SUB)) * 2);
-        // ---- stage the old exponent bytes and find the largest
-        uint32_t mx = 0;
-        if (n == MP_SUB && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
-            const uint4* v = reinterpret_cast<const uint4*>(p);
-#pragma unroll
-            for (int k = 0; k < MP_SUB / 8 / MP_THREADS; ++k) {
-                const int vi = tid + k * MP_THREADS;     // elements 8vi .. 8vi+7: run vi/4, quarter vi%4
-                const uint4 q = v[vi];
-                const uint32_t w0 = __byte_perm((q.x >> 7) & 0x00FF00FFu, (q.y >> 7) & 0x00FF00FFu, 0x6420);
-                const uint32_t w1 = __byte_perm((q.z >> 7) & 0x00FF00FFu, (q.w >> 7) & 0x00FF00FFu, 0x6420);
-                S.texp[(vi >> 2) * 9 + 2 * (vi & 3)] = w0;
-                S.texp[(vi >> 2) * 9 + 2 * (vi & 3) + 1] = w1;
-                mx = __vmaxu4(mx, __vmaxu4(w0, w1));
-            }
-            mx = tmax(tmax(mx & 0xFFu, (mx >> 8) & 0xFFu), tmax((mx >> 16) & 0xFFu, mx >> 24));
-        } else {
-            uint8_t* tb = reinterpret_cast<uint8_t*>(S.texp);
-            for (int i = tid; i < n; i += MP_THREADS) {
-                const uint32_t e = (uint32_t(uint16_t(p[i])) >> 7) & 0xFFu;
-                tb[(i >> 5) * 36 + (i & 31)] = uint8_t(e);
-                mx = tmax(mx, e);
-            }
-        }
-        mx = __reduce_max_sync(FULL, mx);
-        if (lane == 0) atomicMax(&S.emax, int(mx));
-        {   // counters to zero, 16 bytes per store
-            static_assert(sizeof(S.cnt) % 16 == 0 && offsetof(MapSmem, cnt) % 16 == 0, "uint4 zeroing");
-            static_assert(sizeof(S.ocnt) % 16 == 0 && offsetof(MapSmem, ocnt) % 16 == 0, "uint4 zeroing");
-            uint4* c4 = reinterpret_cast<uint4*>(&S.cnt[0][0][0]);
-#pragma unroll
-            for (int k = tid; k < int(sizeof(S.cnt) / 16); k += MP_THREADS) c4[k] = make_uint4(0, 0, 0, 0);
-            uint4* o4 = reinterpret_cast<uint4*>(&S.ocnt[0][0]);
-#pragma unroll
-            for (int k = tid; k < int(sizeof(S.ocnt) / 16); k += MP_THREADS) o4[k] = make_uint4(0, 0, 0, 0);
-        }
-        S.mark[tid] = 0;
-        __syncthreads();
-        const uint32_t ebase = uint32_t(tmax(S.emax - (MWIN - 1), 0));
         const int span_n = tmax(0, tmin(MP_SPAN, n - span0));
-        const int vn = tmax(0, tmin(MP_RUN, span_n - lane * MP_RUN));
-        auto exp_at = [&](int i) { return (S.texp[(i >> 5) * 9 + ((i & 31) >> 2)] >> (8 * (i & 3))) & 0xFFu; };
-        // ---- lane walk: counts per window row; an exponent below the window wraps past MWIN
+        const int r0 = lane * MP_RUN;
+        const int vn = tmax(0, tmin(MP_RUN, span_n - r0));
+        // ---- this warp's masks to zero, then each lane marks its run
         {
-            const uint32_t* ew = &S.texp[(w * 32 + lane) * 9];
-            uint16_t* myc = &S.cnt[w][0][lane];
-            if (vn == MP_RUN) {
+            uint4* m4 = reinterpret_cast<uint4*>(&S.msk[w][0][0]);
+            static_assert(sizeof(S.msk[0]) % 16 == 0 && offsetof(MapSmem, msk) % 16 == 0, "uint4 zeroing");
 #pragma unroll
-                for (int g = 0; g < MP_RUN / 4; ++g) {
-                    const uint32_t eb = ew[g];
+            for (int k = lane; k < int(sizeof(S.msk[0]) / 16); k += 32) m4[k] = make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+        {
+            uint32_t* mine = &S.msk[w][0][lane];
+            const int16_t* run = p + span0 + r0;
+            if (vn == MP_RUN && (reinterpret_cast<uintptr_t>(run) & 15) == 0) {
+                const uint4* rv = reinterpret_cast<const uint4*>(run);
+                uint4 q[4];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) q[c] = rv[c];
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const uint32_t wd[4] = {q[c].x, q[c].y, q[c].z, q[c].w};
 #pragma unroll
                     for (int h = 0; h < 4; ++h) {
-                        const uint32_t d = tmin(((eb >> (8 * h)) & 0xFFu) - ebase, uint32_t(MWIN));
-                        myc[d * 32] += 1;
+                        const int k = c * 8 + h * 2;
+                        uint32_t* a = mine + row_of((wd[h] >> 7) & 0xFFu) * 32;
+                        *a |= 1u << k;
+                        uint32_t* b = mine + row_of((wd[h] >> 23) & 0xFFu) * 32;
+                        *b |= 2u << k;
                     }
                 }
             } else {
-                for (int k = 0; k < vn; ++k) {
-                    const uint32_t d = tmin(((ew[k >> 2] >> (8 * (k & 3))) & 0xFFu) - ebase, uint32_t(MWIN));
-                    myc[d * 32] += 1;
-                }
+                for (int k = 0; k < vn; ++k) mine[row_of((uint32_t(uint16_t(run[k])) >> 7) & 0xFFu) * 32] |= 1u << k;
             }
         }
+        {   // outside-window counters to zero (the union's first 8 KB)
+            uint4* o4 = reinterpret_cast<uint4*>(&S.u.ocnt[w][0]);
+            o4[lane * 2] = make_uint4(0, 0, 0, 0);
+            o4[lane * 2 + 1] = make_uint4(0, 0, 0, 0);
+        }
+        S.mark[tid] = 0;
         __syncwarp();
-        const uint32_t oowm = __ballot_sync(FULL, S.cnt[w][MWIN][lane] != 0);   // runs with below-window elements
-        // ---- below the window, first pass: per-warp counts by matching, run by run in index order
+        const uint32_t oowm = __ballot_sync(FULL, S.msk[w][MWIN][lane] != 0);   // runs with outside elements
+        auto exp_at = [&](int i) { return (uint32_t(uint16_t(p[i])) >> 7) & 0xFFu; };
+        // ---- outside the window, first pass: per-warp counts by matching, run by run in index order
         for (uint32_t m = oowm; m; m &= m - 1) {
             const int ii = (__ffs(m) - 1) * MP_RUN + lane;
             const uint32_t e = ii < span_n ? exp_at(span0 + ii) : 0u;
-            warp_rank(S.ocnt[w], e, ii < span_n && e < ebase, lt, lane);
+            warp_rank(S.u.ocnt[w], e, ii < span_n && row_of(e) == uint32_t(MWIN), lt, lane);
         }
-        // ---- lane prefixes of the window rows: each half-warp scans one row, two counts per word
-        {
-            const int m = lane & 15;
+        // ---- lane prefixes of the window rows, two rows per scan (16-bit halves)
 #pragma unroll
-            for (int j = 0; j < MWIN / 2; ++j) {
-                const int d = 2 * j + (lane >> 4);
-                uint32_t* row = reinterpret_cast<uint32_t*>(&S.cnt[w][d][0]);
-                const uint32_t wd = row[m];
-                const uint32_t sum = (wd & 0xFFFFu) + (wd >> 16);
-                uint32_t incl = sum;
+        for (int j = 0; j < MWIN / 2; ++j) {
+            const uint32_t v = uint32_t(__popc(S.msk[w][2 * j][lane])) | (uint32_t(__popc(S.msk[w][2 * j + 1][lane])) << 16);
+            uint32_t incl = v;
 #pragma unroll
-                for (int o = 1; o < 16; o <<= 1) {
-                    const uint32_t y = __shfl_up_sync(FULL, incl, o, 16);
-                    if (m >= o) incl += y;
-                }
-                const uint32_t ex = incl - sum;
-                row[m] = ex | ((ex + (wd & 0xFFFFu)) << 16);
-                if (m == 15) S.wwin[w][d] = incl;
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(FULL, incl, o);
+                if (lane >= o) incl += y;
+            }
+            const uint32_t ex = incl - v;
+            S.pre[w][2 * j][lane] = uint16_t(ex & 0xFFFFu);
+            S.pre[w][2 * j + 1][lane] = uint16_t(ex >> 16);
+            if (lane == 31) {
+                S.wwin[w][2 * j] = incl & 0xFFFFu;
+                S.wwin[w][2 * j + 1] = incl >> 16;
             }
         }
         __syncthreads();
@@ -538,8 +552,8 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             const int e = tid;
             uint32_t o = 0;
             for (int ww = 0; ww < MP_WARPS; ++ww) {
-                const uint32_t v = S.ocnt[ww][e];
-                S.ocnt[ww][e] = o;
+                const uint32_t v = S.u.ocnt[ww][e];
+                S.u.ocnt[ww][e] = o;
                 o += v;
             }
             const uint32_t d = uint32_t(e) - ebase;
@@ -569,14 +583,14 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             for (int k = 0; k < 8; ++k) { S.estart[lane * 8 + k] = uint16_t(run); run += v[k]; }
         }
         __syncthreads();
-        // ---- below the window, second pass: the counters now hold warp bases, so matching again
+        // ---- outside the window, second pass: the counters now hold warp bases, so matching again
         //      in the same order yields every such element's slot in (exponent, index) order
         for (uint32_t m = oowm; m; m &= m - 1) {
             const int ii = (__ffs(m) - 1) * MP_RUN + lane;
             const uint32_t e = ii < span_n ? exp_at(span0 + ii) : 0u;
-            const bool below = ii < span_n && e < ebase;
-            const uint32_t r = warp_rank(S.ocnt[w], e, below, lt, lane);
-            if (below) S.order[S.estart[e] + r] = uint16_t(span0 + ii);
+            const bool outside = ii < span_n && row_of(e) == uint32_t(MWIN);
+            const uint32_t r = warp_rank(S.u.ocnt[w], e, outside, lt, lane);
+            if (outside) S.order[S.estart[e] + r] = uint16_t(span0 + ii);
         }
         __syncthreads();
         // ---- place this sub-tile's changes group by group.  Groups whose next change lies beyond
@@ -585,8 +599,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             const uint32_t e = S.gexp[k];
             const uint32_t lo = S.pcur[e], tot = S.tot[e];
             if (S.nextloc[k] - lo >= tot) continue;
-            const uint32_t d = e - ebase;            // window row (>= MWIN: below the window)
-            const uint32_t e4 = e * 0x01010101u;
+            const uint32_t d = row_of(e);
             const uint64_t ge = S.gend[k];
             uint64_t cur = S.cursor[k];
             uint32_t next = 0xFFFFFFFFu;
@@ -601,32 +614,17 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                     if (d < uint32_t(MWIN)) {
                         int ww = 0;                  // last warp whose base is <= r
 #pragma unroll
-                        for (int q = 1; q < MP_WARPS; ++q) ww += S.wwin[q][d] <= r;
+                        for (int st = MP_WARPS / 2; st; st >>= 1) ww += S.wwin[ww + st][d] <= r ? st : 0;
                         r -= S.wwin[ww][d];
-                        const uint16_t* pre = &S.cnt[ww][d][0];
+                        const uint16_t* pr = &S.pre[ww][d][0];
                         int l = 0;                   // last lane whose prefix is <= r
 #pragma unroll
-                        for (int st = 16; st; st >>= 1) l += pre[l + st] <= r ? st : 0;
-                        r -= pre[l];
-                        // the r-th byte equal to e in the run of (ww, l)
-                        const uint32_t* ew = &S.texp[(ww * 32 + l) * 9];
-                        uint32_t zsel = 0, qsel = 0;
-                        bool done = false;
-#pragma unroll
-                        for (int q = 0; q < MP_RUN / 4; ++q) {
-                            const uint32_t zb = zero_bytes(ew[q] ^ e4);
-                            const uint32_t c = __popc(zb);
-                            const bool hit = !done && r < c;
-                            zsel = hit ? zb : zsel;
-                            qsel = hit ? uint32_t(q) : qsel;
-                            r = (done || hit) ? r : r - c;
-                            done |= hit;
-                        }
-#pragma unroll
-                        for (int q = 0; q < 3; ++q) zsel = uint32_t(q) < r ? zsel & (zsel - 1) : zsel;
-                        // (a selection that found nothing leaves the change unplaced: the host
-                        // then reports that not every change was placed)
-                        i = done ? ww * MP_SPAN + l * MP_RUN + int(qsel) * 4 + ((__ffs(zsel) - 1) >> 3) : -1;
+                        for (int st = 16; st; st >>= 1) l += pr[l + st] <= r ? st : 0;
+                        r -= pr[l];
+                        const uint32_t m = S.msk[ww][d][l];
+                        // a selection past the mask's bits leaves the change unplaced: the host then
+                        // reports that not every change was placed
+                        i = r < uint32_t(__popc(m)) ? ww * MP_SPAN + l * MP_RUN + int(nth_set_bit(m, r)) : -1;
                     } else {
                         i = S.order[S.estart[e] + r];
                     }
@@ -634,7 +632,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                         const uint32_t old = uint16_t(p[i]);
                         const int32_t res = int32_t(z >> 1) ^ -int32_t(z & 1);
                         const uint32_t nv = uint32_t(int32_t(old) + res) & 0xFFFFu;
-                        S.nval[i] = uint16_t(nv);
+                        S.u.nval[i] = uint16_t(nv);
                         atomicOr(&S.mark[i >> 5], 1u << (i & 31));
                         delta += (uint64_t(nv) - uint64_t(old)) * splitmix_weight(uint64_t(base + i));
                         if (HNEW) {
@@ -682,7 +680,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             S.stage_base = r ? atomicAdd(staged, (unsigned long long)r) : 0ull;
         }
         __syncthreads();
-        // the below-window order is no longer needed: it now lists the changed positions, which
+        // the outside-window order is no longer needed: it now lists the changed positions, which
         // all threads then write out contiguously
         uint32_t at = S.wbase[w] + incl - __popc(bits);
         for (uint32_t b = bits; b; b &= b - 1, ++at) S.order[at] = uint16_t(span0 + lane * 32 + (__ffs(b) - 1));
@@ -694,19 +692,14 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                 const int i = S.order[k];
                 if (sb + k < stage_cap) {
                     caddr[sb + k] = (unsigned long long)(reinterpret_cast<uintptr_t>(tt.w + base + i));
-                    cval[sb + k] = S.nval[i];
+                    cval[sb + k] = S.u.nval[i];
                 }
             }
         }
         S.pcur[tid] += S.tot[tid];
-        if (tid == 0) S.emax = 0;
         __syncthreads();
     }
-    if (HNEW) {   // the weights' histogram after this update: the old one plus the exponent moves
-        const bool last = e_end >= tt.numel;
-        const uint32_t nxt = last ? uint32_t(GS[int64_t(t) * 256 + tid]) : PS[(s + 1) * 256 + tid];
-        HNEW[s * 256 + tid] = nxt - PS[s * 256 + tid] + uint32_t(S.hdelta[tid]);
-    }
+    if (HNEW) HNEW[s * 256 + tid] = uint32_t(S.hdelta[tid]);   // the weights' histogram after this update
     block_add_u64<MP_THREADS>(delta, &chk_delta[t], S.red);
 }
 
