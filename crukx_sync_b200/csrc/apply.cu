@@ -369,7 +369,9 @@ __global__ void __launch_bounds__(256) k_locals(const uint64_t* __restrict__ bsc
 // sub-tile's elements of exponent e is then found by selection: the warp whose exclusive base is
 // the last <= r, the lane likewise, and the r-th set bit of that lane's mask.  Elements outside the
 // window (zeros, tiny or huge weights) are few: their positions are listed in (exponent, index)
-// order by warp matching.  New values are staged in position order.
+// order by warp matching, into the super-tile's slot of a global scratch list.  New values are
+// staged in position order (per warp span), which keeps the commit's scattered writes of one
+// region together.
 
 constexpr int MP_THREADS = 256;
 constexpr int MP_WARPS = MP_THREADS / 32;
@@ -382,23 +384,18 @@ static_assert(MP_SUB * 32 == SUPER_N, "32 sub-tiles per super-tile");
 struct MapSmem {
     uint32_t msk[MP_WARPS][MWIN + 1][32];  // per lane and window row: its run's elements of that exponent (row MWIN: outside)
     uint16_t pre[MP_WARPS][MWIN][32];      // exclusive prefixes over the lanes of the masks' counts
-    uint16_t order[MP_SUB];                // outside-window positions in (exponent, index) order, then the changed positions
-    union {
-        uint32_t ocnt[MP_WARPS][256];      // outside-window per-warp counts, then warp bases
-        uint16_t nval[MP_SUB];             // new bits of every changed position (placement onwards)
-    } u;
+    uint16_t nval[MP_SUB];                 // new bits of every changed position
     uint32_t mark[MP_SUB / 32];            // changed positions
+    uint32_t ocnt[256];                    // outside-window counts per exponent (index order over the sub-tile)
     uint32_t wwin[MP_WARPS][MWIN];         // per-warp window totals, then warp bases
     uint16_t tot[256], estart[256];
     uint32_t pcur[256];
-    uint64_t cursor[256], gend[256];
+    uint64_t cursor[256];
     uint32_t nextloc[256];                 // group-local index of each group's next change (~0: none)
     int32_t hdelta[256];                   // this super-tile's histogram, then plus its exponent moves
     uint8_t gexp[256];
-    uint32_t wcnt[MP_WARPS], wbase[MP_WARPS];
-    unsigned long long stage_base;
+    uint32_t oowm[MP_WARPS];               // per warp: its runs that hold outside-window elements
     unsigned long long wkey[MP_WARPS];
-    uint32_t nstage;
     uint32_t ebase;
     uint64_t red[MP_WARPS];
 };
@@ -417,11 +414,12 @@ __device__ __forceinline__ uint32_t nth_set_bit(uint32_t m, uint32_t r) {
     return pos;
 }
 
-__global__ void __launch_bounds__(MP_THREADS, 3)
+__global__ void __launch_bounds__(MP_THREADS, 4)
 k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, const uint32_t* __restrict__ PS,
       const uint32_t* __restrict__ local, const uint32_t* __restrict__ zz, unsigned long long* __restrict__ caddr,
       uint16_t* __restrict__ cval, uint64_t stage_cap, unsigned long long* __restrict__ chk_delta,
-      unsigned long long* __restrict__ staged, const uint64_t* __restrict__ GS, uint32_t* __restrict__ HNEW) {
+      unsigned long long* __restrict__ staged, const uint64_t* __restrict__ GS, uint32_t* __restrict__ HNEW,
+      uint16_t* __restrict__ order_scratch) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     MapSmem& S = *reinterpret_cast<MapSmem*>(smem_raw);
     const int64_t s = blockIdx.x;
@@ -433,6 +431,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
     const uint32_t lt = lanemask_lt();
     const int ngt = tt.g_end - tt.g_begin;
     const int span0 = w * MP_SPAN;
+    uint16_t* const order = order_scratch + s * MP_SUB;   // outside-window positions in (exponent, index) order
     S.pcur[tid] = PS[s * 256 + tid];
     {   // this super-tile's histogram: the next row's prefix (or the tensor's total) minus this one's
         const bool last = e_end >= tt.numel;
@@ -460,7 +459,6 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             if (local[mid] < p0) lo = mid + 1; else hi = mid;
         }
         S.cursor[tid] = lo;
-        S.gend[tid] = grp.start + grp.count;
         S.gexp[tid] = uint8_t(grp.exp);
         S.nextloc[tid] = lo < grp.start + grp.count ? local[lo] : 0xFFFFFFFFu;
     }
@@ -514,21 +512,10 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                 for (int k = 0; k < vn; ++k) mine[row_of((uint32_t(uint16_t(run[k])) >> 7) & 0xFFu) * 32] |= 1u << k;
             }
         }
-        {   // outside-window counters to zero (the union's first 8 KB)
-            uint4* o4 = reinterpret_cast<uint4*>(&S.u.ocnt[w][0]);
-            o4[lane * 2] = make_uint4(0, 0, 0, 0);
-            o4[lane * 2 + 1] = make_uint4(0, 0, 0, 0);
-        }
-        S.mark[tid] = 0;
+        S.mark[(span0 >> 5) + lane] = 0;   // this warp's span (its staging below read the last ones)
         __syncwarp();
         const uint32_t oowm = __ballot_sync(FULL, S.msk[w][MWIN][lane] != 0);   // runs with outside elements
-        auto exp_at = [&](int i) { return (uint32_t(uint16_t(p[i])) >> 7) & 0xFFu; };
-        // ---- outside the window, first pass: per-warp counts by matching, run by run in index order
-        for (uint32_t m = oowm; m; m &= m - 1) {
-            const int ii = (__ffs(m) - 1) * MP_RUN + lane;
-            const uint32_t e = ii < span_n ? exp_at(span0 + ii) : 0u;
-            warp_rank(S.u.ocnt[w], e, ii < span_n && row_of(e) == uint32_t(MWIN), lt, lane);
-        }
+        if (lane == 0) S.oowm[w] = oowm;
         // ---- lane prefixes of the window rows, two rows per scan (16-bit halves)
 #pragma unroll
         for (int j = 0; j < MWIN / 2; ++j) {
@@ -547,15 +534,31 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                 S.wwin[w][2 * j + 1] = incl >> 16;
             }
         }
-        __syncthreads();
-        {   // warp bases per exponent and the sub-tile's totals
-            const int e = tid;
-            uint32_t o = 0;
+        const bool any_out = __syncthreads_or(oowm != 0);
+        auto exp_at = [&](int i) { return (uint32_t(uint16_t(p[i])) >> 7) & 0xFFu; };
+        // outside-window elements of the whole sub-tile in index order, by one warp (they are rare):
+        // slots from warp matching over the counters
+        auto rank_outside = [&](bool list) {
+            for (int k = lane; k < 256; k += 32) S.ocnt[k] = 0;
+            __syncwarp();
             for (int ww = 0; ww < MP_WARPS; ++ww) {
-                const uint32_t v = S.u.ocnt[ww][e];
-                S.u.ocnt[ww][e] = o;
-                o += v;
+                const int sn = tmax(0, tmin(MP_SPAN, n - ww * MP_SPAN));
+                for (uint32_t m = S.oowm[ww]; m; m &= m - 1) {
+                    const int ii = (__ffs(m) - 1) * MP_RUN + lane;
+                    const uint32_t e = ii < sn ? exp_at(ww * MP_SPAN + ii) : 0u;
+                    const bool outside = ii < sn && row_of(e) == uint32_t(MWIN);
+                    const uint32_t r = warp_rank(S.ocnt, e, outside, lt, lane);
+                    if (list && outside) order[S.estart[e] + r] = uint16_t(ww * MP_SPAN + ii);
+                }
             }
+        };
+        if (any_out) {   // first pass: the counts
+            if (w == 0) rank_outside(false);
+            __syncthreads();
+        }
+        {   // warp bases of the window rows and the sub-tile's totals
+            const int e = tid;
+            uint32_t o = any_out ? S.ocnt[e] : 0u;
             const uint32_t d = uint32_t(e) - ebase;
             if (d < uint32_t(MWIN)) {
                 uint32_t a = 0;
@@ -569,30 +572,24 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             S.tot[e] = uint16_t(o);
         }
         __syncthreads();
-        if (w == 0) {                       // exclusive scan of the 256 totals -> bucket starts
-            uint32_t v[8], sum = 0;
+        if (any_out) {   // second pass: bucket starts, then every outside element's slot
+            if (w == 0) {
+                uint32_t v[8], sum = 0;
 #pragma unroll
-            for (int k = 0; k < 8; ++k) { v[k] = S.tot[lane * 8 + k]; sum += v[k]; }
-            uint32_t incl = sum;
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t y = __shfl_up_sync(FULL, incl, o);
-                if (lane >= o) incl += y;
+                for (int k = 0; k < 8; ++k) { v[k] = S.tot[lane * 8 + k]; sum += v[k]; }
+                uint32_t incl = sum;
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t y = __shfl_up_sync(FULL, incl, o);
+                    if (lane >= o) incl += y;
+                }
+                uint32_t run = incl - sum;
+#pragma unroll
+                for (int k = 0; k < 8; ++k) { S.estart[lane * 8 + k] = uint16_t(run); run += v[k]; }
+                __syncwarp();
+                rank_outside(true);
             }
-            uint32_t run = incl - sum;
-#pragma unroll
-            for (int k = 0; k < 8; ++k) { S.estart[lane * 8 + k] = uint16_t(run); run += v[k]; }
+            __syncthreads();
         }
-        __syncthreads();
-        // ---- outside the window, second pass: the counters now hold warp bases, so matching again
-        //      in the same order yields every such element's slot in (exponent, index) order
-        for (uint32_t m = oowm; m; m &= m - 1) {
-            const int ii = (__ffs(m) - 1) * MP_RUN + lane;
-            const uint32_t e = ii < span_n ? exp_at(span0 + ii) : 0u;
-            const bool outside = ii < span_n && row_of(e) == uint32_t(MWIN);
-            const uint32_t r = warp_rank(S.u.ocnt[w], e, outside, lt, lane);
-            if (outside) S.order[S.estart[e] + r] = uint16_t(span0 + ii);
-        }
-        __syncthreads();
         // ---- place this sub-tile's changes group by group.  Groups whose next change lies beyond
         //      this sub-tile are skipped from shared memory.
         for (int k = w; k < ngt; k += MP_WARPS) {
@@ -600,7 +597,8 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             const uint32_t lo = S.pcur[e], tot = S.tot[e];
             if (S.nextloc[k] - lo >= tot) continue;
             const uint32_t d = row_of(e);
-            const uint64_t ge = S.gend[k];
+            const AppGroup grp = G[tt.g_begin + k];
+            const uint64_t ge = grp.start + grp.count;
             uint64_t cur = S.cursor[k];
             uint32_t next = 0xFFFFFFFFu;
             for (;;) {
@@ -626,13 +624,13 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                         // reports that not every change was placed
                         i = r < uint32_t(__popc(m)) ? ww * MP_SPAN + l * MP_RUN + int(nth_set_bit(m, r)) : -1;
                     } else {
-                        i = S.order[S.estart[e] + r];
+                        i = order[S.estart[e] + r];
                     }
                     if (unsigned(i) < unsigned(n)) {
                         const uint32_t old = uint16_t(p[i]);
                         const int32_t res = int32_t(z >> 1) ^ -int32_t(z & 1);
                         const uint32_t nv = uint32_t(int32_t(old) + res) & 0xFFFFu;
-                        S.u.nval[i] = uint16_t(nv);
+                        S.nval[i] = uint16_t(nv);
                         atomicOr(&S.mark[i >> 5], 1u << (i & 31));
                         delta += (uint64_t(nv) - uint64_t(old)) * splitmix_weight(uint64_t(base + i));
                         if (HNEW) {
@@ -663,41 +661,29 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             }
         }
         __syncthreads();
-        // ---- stage the sub-tile's new values in position order (one atomic per sub-tile): lane l
-        //      owns mark word l of its warp's span
-        const uint32_t bits = S.mark[(span0 >> 5) + lane];
-        uint32_t incl = __popc(bits);
-        for (int o = 1; o < 32; o <<= 1) {
-            const uint32_t y = __shfl_up_sync(FULL, incl, o);
-            if (lane >= o) incl += y;
-        }
-        if (lane == 31) S.wcnt[w] = incl;
-        __syncthreads();
-        if (tid == 0) {
-            uint32_t r = 0;
-            for (int ww = 0; ww < MP_WARPS; ++ww) { S.wbase[ww] = r; r += S.wcnt[ww]; }
-            S.nstage = r;
-            S.stage_base = r ? atomicAdd(staged, (unsigned long long)r) : 0ull;
-        }
-        __syncthreads();
-        // the outside-window order is no longer needed: it now lists the changed positions, which
-        // all threads then write out contiguously
-        uint32_t at = S.wbase[w] + incl - __popc(bits);
-        for (uint32_t b = bits; b; b &= b - 1, ++at) S.order[at] = uint16_t(span0 + lane * 32 + (__ffs(b) - 1));
-        __syncthreads();
+        // ---- stage this warp span's new values in position order: one atomic per warp, lane l
+        //      takes mark word l
         {
-            const uint64_t sb = S.stage_base;
-            const uint32_t ns = S.nstage;
-            for (uint32_t k = tid; k < ns; k += MP_THREADS) {
-                const int i = S.order[k];
-                if (sb + k < stage_cap) {
-                    caddr[sb + k] = (unsigned long long)(reinterpret_cast<uintptr_t>(tt.w + base + i));
-                    cval[sb + k] = S.u.nval[i];
+            const uint32_t bits = S.mark[(span0 >> 5) + lane];
+            const uint32_t c = __popc(bits);
+            uint32_t incl = c;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(FULL, incl, o);
+                if (lane >= o) incl += y;
+            }
+            unsigned long long sb = 0;
+            if (lane == 31 && incl) sb = atomicAdd(staged, (unsigned long long)incl);
+            sb = __shfl_sync(FULL, sb, 31) + (incl - c);
+            for (uint32_t b = bits; b; b &= b - 1, ++sb) {
+                const int i = span0 + lane * 32 + (__ffs(b) - 1);
+                if (sb < stage_cap) {
+                    caddr[sb] = (unsigned long long)(reinterpret_cast<uintptr_t>(p + i));
+                    cval[sb] = S.nval[i];
                 }
             }
         }
         S.pcur[tid] += S.tot[tid];
-        __syncthreads();
     }
     if (HNEW) HNEW[s * 256 + tid] = uint32_t(S.hdelta[tid]);   // the weights' histogram after this update
     block_add_u64<MP_THREADS>(delta, &chk_delta[t], S.red);
@@ -848,6 +834,7 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     for (int t = 0; t < nt && versions && has_version; ++t) keep_hist |= has_version[t] != 0;
     if (keep_hist) CRX_CUDA(ensure_dev(C.b[S_A_HNEW], sizeof(uint32_t) * 256 * size_t(n_super), st));
     uint32_t* hnew = keep_hist ? dev<uint32_t>(C, S_A_HNEW) : nullptr;
+    CRX_CUDA(ensure_dev(C.b[S_A_ORDER], sizeof(uint16_t) * MP_SUB * size_t(n_super), st));
     CRX_CUDA(ensure_dev(C.b[S_A_TOT], sizeof(uint64_t) * cells, st));
     CRX_CUDA(ensure_dev(C.b[S_A_CHUNK_ROWS], sizeof(int64_t) * 2 * (size_t(nt) + 1), st));
     CRX_CUDA(ensure_dev(C.b[S_A_CHUNK_SUMS], sizeof(uint32_t) * 256 * size_t(n_chunks), st));
@@ -936,7 +923,7 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     k_map<<<unsigned(n_super), MP_THREADS, map_smem, st>>>(dT, nt, dG, dev<uint32_t>(C, S_A_HS), dev<uint32_t>(C, S_A_LOCAL),
                                                             dev<uint32_t>(C, S_A_ZZ), dev<unsigned long long>(C, S_A_CADDR),
                                                             dev<uint16_t>(C, S_A_CVAL), total, chk_delta, counters + 2,
-                                                            dev<uint64_t>(C, S_A_TOT), hnew);
+                                                            dev<uint64_t>(C, S_A_TOT), hnew, dev<uint16_t>(C, S_A_ORDER));
     }
     CRX_CUDA(cudaGetLastError());
     // ---- verdict (one synchronisation for the whole update)
