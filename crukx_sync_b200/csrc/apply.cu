@@ -390,11 +390,12 @@ struct MapSmem {
     uint32_t wwin[MP_WARPS][MWIN];         // per-warp window totals, then warp bases
     uint16_t tot[256], estart[256];
     uint32_t pcur[256];
-    uint64_t cursor[256];
+    uint64_t cursor[256], gend[256];
     uint32_t nextloc[256];                 // group-local index of each group's next change (~0: none)
     int32_t hdelta[256];                   // this super-tile's histogram, then plus its exponent moves
     uint8_t gexp[256];
     uint32_t oowm[MP_WARPS];               // per warp: its runs that hold outside-window elements
+    uint32_t qnext;                        // next group to place (taken from the largest exponent down)
     unsigned long long wkey[MP_WARPS];
     uint32_t ebase;
     uint64_t red[MP_WARPS];
@@ -459,6 +460,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             if (local[mid] < p0) lo = mid + 1; else hi = mid;
         }
         S.cursor[tid] = lo;
+        S.gend[tid] = grp.start + grp.count;
         S.gexp[tid] = uint8_t(grp.exp);
         S.nextloc[tid] = lo < grp.start + grp.count ? local[lo] : 0xFFFFFFFFu;
     }
@@ -570,6 +572,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                 o += a;
             }
             S.tot[e] = uint16_t(o);
+            if (tid == 0) S.qnext = 0;
         }
         __syncthreads();
         if (any_out) {   // second pass: bucket starts, then every outside element's slot
@@ -590,21 +593,28 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             }
             __syncthreads();
         }
-        // ---- place this sub-tile's changes group by group.  Groups whose next change lies beyond
-        //      this sub-tile are skipped from shared memory.
-        for (int k = w; k < ngt; k += MP_WARPS) {
+        // ---- place this sub-tile's changes: warps take groups from a queue, largest exponents (the
+        //      most changes) first; groups whose next change lies beyond this sub-tile are skipped
+        //      from shared memory.  A change leaves its residual and its mark; the old value is read
+        //      when the span is staged.  The next chunk of a group is loaded while this one is placed.
+        for (;;) {
+            int q = 0;
+            if (lane == 0) q = int(atomicAdd(&S.qnext, 1u));
+            q = __shfl_sync(FULL, q, 0);
+            if (q >= ngt) break;
+            const int k = ngt - 1 - q;
             const uint32_t e = S.gexp[k];
             const uint32_t lo = S.pcur[e], tot = S.tot[e];
             if (S.nextloc[k] - lo >= tot) continue;
             const uint32_t d = row_of(e);
-            const AppGroup grp = G[tt.g_begin + k];
-            const uint64_t ge = grp.start + grp.count;
+            const uint64_t ge = S.gend[k];
             uint64_t cur = S.cursor[k];
-            uint32_t next = 0xFFFFFFFFu;
+            uint32_t lc = 0xFFFFFFFFu, z = 0, next;
+            if (cur + lane < ge) { lc = local[cur + lane]; z = zz[cur + lane]; }
             for (;;) {
-                const uint64_t j = cur + lane;
-                uint32_t lc = 0xFFFFFFFFu, z = 0;
-                if (j < ge) { lc = local[j]; z = zz[j]; }   // one round trip: both loads issued together
+                const uint64_t jn = cur + 32 + lane;
+                uint32_t lcn = 0xFFFFFFFFu, zn = 0;
+                if (jn < ge) { lcn = local[jn]; zn = zz[jn]; }
                 const bool valid = lc != 0xFFFFFFFFu && lc >= lo && lc - lo < tot;
                 if (valid) {
                     uint32_t r = lc - lo;
@@ -627,28 +637,20 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                         i = order[S.estart[e] + r];
                     }
                     if (unsigned(i) < unsigned(n)) {
-                        const uint32_t old = uint16_t(p[i]);
-                        const int32_t res = int32_t(z >> 1) ^ -int32_t(z & 1);
-                        const uint32_t nv = uint32_t(int32_t(old) + res) & 0xFFFFu;
-                        S.nval[i] = uint16_t(nv);
+                        S.nval[i] = uint16_t(int32_t(z >> 1) ^ -int32_t(z & 1));   // residual, mod 2^16
                         atomicOr(&S.mark[i >> 5], 1u << (i & 31));
-                        delta += (uint64_t(nv) - uint64_t(old)) * splitmix_weight(uint64_t(base + i));
-                        if (HNEW) {
-                            const uint32_t eo = (old >> 7) & 0xFFu, en = (nv >> 7) & 0xFFu;
-                            if (eo != en) {
-                                atomicSub(&S.hdelta[eo], 1);
-                                atomicAdd(&S.hdelta[en], 1);
-                            }
-                        }
                     }
                 }
                 const uint32_t m = __ballot_sync(FULL, valid);
                 const int taken = __popc(~m) ? __ffs(~m) - 1 : 32;   // consumed changes are a prefix
-                cur += uint64_t(taken);
                 if (taken < 32) {
+                    cur += uint64_t(taken);
                     next = __shfl_sync(FULL, lc, taken);   // local[cur], or ~0 past the group's end
                     break;
                 }
+                cur += 32;
+                lc = lcn;
+                z = zn;
             }
             if (lane == 0) {
                 S.cursor[k] = cur;
@@ -675,17 +677,43 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             unsigned long long sb = 0;
             if (lane == 31 && incl) sb = atomicAdd(staged, (unsigned long long)incl);
             sb = __shfl_sync(FULL, sb, 31) + (incl - c);
-            for (uint32_t b = bits; b; b &= b - 1, ++sb) {
-                const int i = span0 + lane * 32 + (__ffs(b) - 1);
-                if (sb < stage_cap) {
-                    caddr[sb] = (unsigned long long)(reinterpret_cast<uintptr_t>(p + i));
-                    cval[sb] = S.nval[i];
+            for (uint32_t b = bits; b;) {   // four positions at a time: their old values load together
+                int ip[4];
+                uint32_t ov[4];
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    ip[h] = b ? span0 + lane * 32 + (__ffs(b) - 1) : -1;
+                    b &= b - 1;
+                }
+#pragma unroll
+                for (int h = 0; h < 4; ++h) ov[h] = ip[h] >= 0 ? uint32_t(uint16_t(p[ip[h]])) : 0u;
+#pragma unroll
+                for (int h = 0; h < 4; ++h) {
+                    if (ip[h] < 0) break;
+                    const int i = ip[h];
+                    const uint32_t old = ov[h], nv = (old + S.nval[i]) & 0xFFFFu;
+                    if (sb < stage_cap) {
+                        caddr[sb] = (unsigned long long)(reinterpret_cast<uintptr_t>(p + i));
+                        cval[sb] = uint16_t(nv);
+                    }
+                    ++sb;
+                    delta += (uint64_t(nv) - uint64_t(old)) * splitmix_weight(uint64_t(base + i));
+                    if (HNEW) {
+                        const uint32_t eo = (old >> 7) & 0xFFu, en = (nv >> 7) & 0xFFu;
+                        if (eo != en) {
+                            atomicSub(&S.hdelta[eo], 1);
+                            atomicAdd(&S.hdelta[en], 1);
+                        }
+                    }
                 }
             }
         }
         S.pcur[tid] += S.tot[tid];
     }
-    if (HNEW) HNEW[s * 256 + tid] = uint32_t(S.hdelta[tid]);   // the weights' histogram after this update
+    if (HNEW) {   // the weights' histogram after this update (the last span's moves are in)
+        __syncthreads();
+        HNEW[s * 256 + tid] = uint32_t(S.hdelta[tid]);
+    }
     block_add_u64<MP_THREADS>(delta, &chk_delta[t], S.red);
 }
 
