@@ -61,37 +61,37 @@ __device__ __forceinline__ int64_t group_of(const uint64_t* __restrict__ start, 
 
 // ------------------------------------------------------------------ k_enc_rank
 //
-// Stable rank by old exponent without a sort and without per-element warp matching: every lane
-// walks its own contiguous run of 32 elements with private counters (one per exponent of a
-// 16-exponent window ending at the sub-tile's largest exponent), so an element's rank is
-//   running total of earlier sub-tiles + earlier warps + earlier lanes of its warp + its own count.
-// Elements below the window (zeros, tiny weights) take a side path with warp matching, in index
-// order; a sub-tile with too many changes for the record buffers is re-ranked by matching.
+// Stable rank by old exponent without a sort: every lane takes a run of 32 elements and marks, per
+// exponent of a 16-exponent window ending at the sub-tile's largest old exponent, which of its
+// elements carry it (one 32-bit mask per window row).  An element's rank among the equal exponents
+// is then the running total of earlier sub-tiles + earlier warps + earlier lanes (prefixes of the
+// masks' population counts) + the set bits of its own mask below it; the rank among the changed
+// ones likewise with the run's changed-bit mask.  Elements below the window (zeros, tiny weights)
+// are ranked by warp matching, in index order.
 
 constexpr int ER_THREADS = 256;
 constexpr int ER_WARPS = ER_THREADS / 32;
 constexpr int ER_SUB = 8192;                 // elements per sub-tile
 constexpr int ER_SPAN = ER_SUB / ER_WARPS;   // 1024 per warp
 constexpr int ER_RUN = ER_SPAN / 32;         // 32 per lane
-constexpr int WIN = 16;                      // exponents counted in registers-of-shared-memory per lane
-constexpr int WREC = 128;                    // in-window change records per warp (12.5% of its span)
-constexpr int OREC = 32;                     // out-of-window change records per warp
+constexpr int WIN = 16;                      // window rows
+constexpr int WLIST = 128;                   // in-window changes of a span listed for cooperative record writes
 static_assert(ER_SUB * 32 == SUPER_N, "32 sub-tiles per super-tile");
 
 struct RankSmem {
     uint32_t texp[ER_SUB / 32 * 9];       // old exponent bytes; run r (32 elements) in words 9r..9r+7
     uint32_t chm[ER_SUB / 32];            // changed bit of every element, one word per run
-    uint32_t cnt[ER_WARPS][WIN][33];      // per-lane counts A | C << 16, then exclusive prefixes over lanes
-    uint32_t ocnt[ER_WARPS][256];         // per-warp counts A | C << 16 of out-of-window elements, then warp bases
-    uint32_t wwin[ER_WARPS][WIN];         // per-warp window totals, then exclusive bases over warps
-    uint32_t rec[ER_WARPS][WREC];         // span index << 16 | window row << 12 | own count A << 6 | own count C
-    uint64_t orec[ER_WARPS][OREC];        // span index | exponent << 10 | warp rank A << 18 | warp rank C << 29
+    uint32_t msk[ER_WARPS][WIN + 1][32];  // per lane and window row: its run's elements of that exponent (row WIN: below)
+    uint32_t pre[ER_WARPS][WIN][32];      // exclusive lane prefixes of the rows' counts, all | changed << 16
+    uint32_t wwin[ER_WARPS][WIN];         // per-warp row totals, then warp bases (all | changed << 16)
+    uint32_t ocnt[256];                   // below-window counts per exponent, all | changed << 16
     uint32_t runA[256], runC[256];        // super-tile running totals
-    uint32_t tot[256];                    // this sub-tile's totals A | C << 16
+    uint32_t tot[256];                    // this sub-tile's totals, all | changed << 16
     uint32_t cstart[256];                 // exclusive scan of the changed totals: records sorted by exponent
-    uint32_t nrec[ER_WARPS], norec[ER_WARPS], oow[ER_WARPS], wbase[ER_WARPS];
+    uint16_t wl[ER_WARPS][WLIST];         // a warp's in-window changes (span indices)
+    uint32_t oowm[ER_WARPS];              // per warp: its runs holding below-window elements
     unsigned long long rec_base;
-    int emax, dense;
+    int emax[2];                          // largest old exponent, alternating between sub-tiles
     uint64_t red[ER_WARPS];
 };
 
@@ -154,10 +154,11 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
 
     S.runA[tid] = 0;
     S.runC[tid] = 0;
-    if (tid == 0) { S.emax = 0; S.dense = 0; }
+    if (tid == 0) { S.emax[0] = 0; S.emax[1] = 0; }
     __syncthreads();
 
-    for (int64_t base = e_begin; base < e_end; base += ER_SUB) {
+    int it = 0;
+    for (int64_t base = e_begin; base < e_end; base += ER_SUB, ++it) {
         const int n = int(tmin<int64_t>(ER_SUB, e_end - base));
         const int16_t* pp = tt.prev + base;
         const int16_t* cp = tt.cur + base;
@@ -212,114 +213,93 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
             }
         }
         mx = __reduce_max_sync(FULL, mx);
-        if (lane == 0) atomicMax(&S.emax, int(mx));
-        {   // counters to zero, 16 bytes per store
-            static_assert(sizeof(S.cnt) % 16 == 0 && offsetof(RankSmem, cnt) % 16 == 0, "uint4 zeroing");
-            static_assert(sizeof(S.ocnt) % 16 == 0 && offsetof(RankSmem, ocnt) % 16 == 0, "uint4 zeroing");
-            uint4* c4 = reinterpret_cast<uint4*>(&S.cnt[0][0][0]);
+        if (lane == 0) atomicMax(&S.emax[it & 1], int(mx));
+        {   // this warp's masks to zero
+            static_assert(sizeof(S.msk[0]) % 16 == 0 && offsetof(RankSmem, msk) % 16 == 0, "uint4 zeroing");
+            uint4* m4 = reinterpret_cast<uint4*>(&S.msk[w][0][0]);
 #pragma unroll
-            for (int k = tid; k < int(sizeof(S.cnt) / 16); k += ER_THREADS) c4[k] = make_uint4(0, 0, 0, 0);
-            uint4* o4 = reinterpret_cast<uint4*>(&S.ocnt[0][0]);
-#pragma unroll
-            for (int k = tid; k < int(sizeof(S.ocnt) / 16); k += ER_THREADS) o4[k] = make_uint4(0, 0, 0, 0);
+            for (int k = lane; k < int(sizeof(S.msk[0]) / 16); k += 32) m4[k] = make_uint4(0, 0, 0, 0);
         }
-        if (tid < ER_WARPS) { S.nrec[tid] = 0; S.norec[tid] = 0; S.oow[tid] = 0; }
         __syncthreads();
-        const int ebase = tmax(S.emax - (WIN - 1), 0);
+        if (tid == 0) S.emax[(it + 1) & 1] = 0;   // the next sub-tile's (its atomics come after later barriers)
+        const uint32_t ebase = uint32_t(tmax(S.emax[it & 1] - (WIN - 1), 0));
+        auto row_of = [&](uint32_t e) { return tmin(e - ebase, uint32_t(WIN)); };   // below: wraps to WIN
+        auto exp_at = [&](int i) { return (S.texp[(i >> 5) * 9 + ((i & 31) >> 2)] >> (8 * (i & 3))) & 0xFFu; };
         const int span_n = tmax(0, tmin(ER_SPAN, n - span0));
-        // exponent byte and changed bit of sub-tile element i
-        auto exp_of_i = [&](int i) { return (S.texp[(i >> 5) * 9 + ((i & 31) >> 2)] >> (8 * (i & 3))) & 0xFFu; };
-        auto changed_i = [&](int i) { return ((S.chm[i >> 5] >> (i & 31)) & 1u) != 0; };
-
-        // ---- lane walk: private counters, in-window change records.  Four elements at a time (one
-        //      exponent word): their counters are loaded together, ranks corrected for equal
-        //      exponents inside the group, and stored in order (the last store carries all four).
+        const int vn = tmax(0, tmin(ER_RUN, span_n - lane * ER_RUN));
+        // ---- lane walk: for every window row, which elements of the lane's run carry it
         {
-            const int r0 = lane * ER_RUN;
-            const int vn = tmax(0, tmin(ER_RUN, span_n - r0));
             const uint32_t* ew = &S.texp[(w * 32 + lane) * 9];
-            const uint32_t cm = S.chm[w * 32 + lane];
-            uint32_t* myc = &S.cnt[w][0][lane];
-            bool any_oow = false;
-            for (int k = 0; k < vn; k += 4) {
-                const uint32_t eb = ew[k >> 2];
-                uint32_t inc[4], c[4];
-                int d[4];
+            uint32_t* mine = &S.msk[w][0][lane];
+            if (vn == ER_RUN) {
 #pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    const bool valid = k + h < vn;
-                    const int dd = int((eb >> (8 * h)) & 0xFFu) - ebase;
-                    const bool in = valid && unsigned(dd) < unsigned(WIN);
-                    any_oow |= valid && !in;
-                    d[h] = in ? dd : 0;
-                    inc[h] = in ? (((cm >> (k + h)) & 1u) ? 0x10001u : 1u) : 0u;
+                for (int g = 0; g < ER_RUN / 4; ++g) {
+                    const uint32_t eb = ew[g];
+#pragma unroll
+                    for (int h = 0; h < 4; ++h) mine[row_of((eb >> (8 * h)) & 0xFFu) * 32] |= 1u << (4 * g + h);
                 }
+            } else {
+                for (int k = 0; k < vn; ++k) mine[row_of((ew[k >> 2] >> (8 * (k & 3))) & 0xFFu) * 32] |= 1u << k;
+            }
+        }
+        __syncwarp();
+        const uint32_t outm = S.msk[w][WIN][lane];              // the run's elements below the window
+        const uint32_t oowm = __ballot_sync(FULL, outm != 0);
+        if (lane == 0) S.oowm[w] = oowm;
+        const uint32_t cm = S.chm[w * 32 + lane];
+        // ---- lane prefixes per window row of (all, changed) counts; empty rows skipped
 #pragma unroll
-                for (int h = 0; h < 4; ++h) c[h] = myc[d[h] * 33];
+        for (int d = 0; d < WIN; ++d) {
+            const uint32_t m = S.msk[w][d][lane];
+            if (!__any_sync(FULL, m != 0)) {
+                if (lane == 0) S.wwin[w][d] = 0;
+                continue;
+            }
+            const uint32_t v = uint32_t(__popc(m)) | (uint32_t(__popc(m & cm)) << 16);
+            uint32_t incl = v;
 #pragma unroll
-                for (int h = 1; h < 4; ++h)
-#pragma unroll
-                    for (int g = 0; g < h; ++g) c[h] += d[h] == d[g] ? inc[g] : 0u;
-#pragma unroll
-                for (int h = 0; h < 4; ++h) myc[d[h] * 33] = c[h] + inc[h];
-                // records of the in-window changes: one shared-memory atomic per lane and group
-                const uint32_t nb = (inc[0] >> 16) + (inc[1] >> 16) + (inc[2] >> 16) + (inc[3] >> 16);
-                if (nb) {
-                    uint32_t slot = atomicAdd(&S.nrec[w], nb);
-#pragma unroll
-                    for (int h = 0; h < 4; ++h) {
-                        if (inc[h] >> 16) {
-                            if (slot < WREC)
-                                S.rec[w][slot] = (uint32_t(r0 + k + h) << 16) | (uint32_t(d[h]) << 12) |
-                                                 ((c[h] & 0xFFFFu) << 6) | (c[h] >> 16);
-                            ++slot;
-                        }
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(FULL, incl, o);
+                if (lane >= o) incl += y;
+            }
+            S.pre[w][d][lane] = incl - v;
+            if (lane == 31) S.wwin[w][d] = incl;
+        }
+        const bool any_out = __syncthreads_or(oowm != 0);
+        // elements below the window, whole sub-tile in index order, by one warp (they are rare):
+        // ranks (all, changed) by warp matching; the second pass writes the changes' records
+        auto rank_outside = [&](bool write) {
+            for (int k = lane; k < 256; k += 32) S.ocnt[k] = 0;
+            __syncwarp();
+            const uint64_t rb = S.rec_base;
+            for (int ww = 0; ww < ER_WARPS; ++ww) {
+                const int sn = tmax(0, tmin(ER_SPAN, n - ww * ER_SPAN));
+                for (uint32_t m = S.oowm[ww]; m; m &= m - 1) {
+                    const int run = __ffs(m) - 1;
+                    const int ii = run * ER_RUN + lane;
+                    const int i = ww * ER_SPAN + ii;
+                    const bool outside = ii < sn && row_of(exp_at(i)) == uint32_t(WIN);
+                    const uint32_t e = outside ? exp_at(i) : 0u;
+                    const bool ch = outside && ((S.chm[i >> 5] >> (i & 31)) & 1u);
+                    const uint32_t rA = warp_rank_packed(S.ocnt, e, outside, 0, lt, lane);
+                    const uint32_t rC = warp_rank_packed(S.ocnt, e, ch, 16, lt, lane);
+                    if (write && ch) {
+                        const uint32_t x = bits_of(i);
+                        put_record(rec_key, rec_val, rec_cap, rb + S.cstart[e] + rC, s, S.runA[e] + rA, S.runC[e] + rC, x);
+                        delta += change_delta(x, base + i);
                     }
                 }
             }
-            if (any_oow) atomicOr(&S.oow[w], 1u << lane);
+        };
+        if (any_out) {   // first pass: the counts
+            if (w == 0) rank_outside(false);
+            __syncthreads();
         }
-        __syncwarp();
-        // ---- out-of-window elements, run by run in index order (rare)
-        for (uint32_t m = S.oow[w]; m; m &= m - 1) {
-            const int run = __ffs(m) - 1;
-            const int ii = run * ER_RUN + lane;
-            const bool valid = ii < span_n;
-            const uint32_t e = valid ? exp_of_i(span0 + ii) : 0u;
-            const bool oow = valid && int(e) < ebase;
-            const bool ch = oow && changed_i(span0 + ii);
-            const uint32_t rA = warp_rank_packed(S.ocnt[w], e, oow, 0, lt, lane);
-            const uint32_t rC = warp_rank_packed(S.ocnt[w], e, ch, 16, lt, lane);
-            if (ch) {
-                const uint32_t slot = atomicAdd(&S.norec[w], 1u);
-                if (slot < OREC)
-                    S.orec[w][slot] = uint64_t(ii) | (uint64_t(e) << 10) | (uint64_t(rA) << 18) | (uint64_t(rC) << 29);
-            }
-        }
-        // ---- lane prefixes: lane d scans window row d (rows are padded to 33 words)
-        if (lane < WIN) {
-            uint32_t run = 0;
-#pragma unroll
-            for (int col = 0; col < 32; ++col) {
-                const uint32_t v = S.cnt[w][lane][col];
-                S.cnt[w][lane][col] = run;
-                run += v;
-            }
-            S.wwin[w][lane] = run;
-        }
-        __syncthreads();
-
-        // ---- warp bases per exponent, sub-tile totals, record slots
-        {
+        {   // warp bases of the window rows and the sub-tile's totals (all | changed << 16)
             const int e = tid;
-            uint32_t o = 0;
-            for (int ww = 0; ww < ER_WARPS; ++ww) {
-                const uint32_t v = S.ocnt[ww][e];
-                S.ocnt[ww][e] = o;
-                o += v;
-            }
-            const int d = e - ebase;
-            if (unsigned(d) < unsigned(WIN)) {
+            uint32_t o = any_out ? S.ocnt[e] : 0u;
+            const uint32_t d = uint32_t(e) - ebase;
+            if (d < uint32_t(WIN)) {
                 uint32_t a = 0;
                 for (int ww = 0; ww < ER_WARPS; ++ww) {
                     const uint32_t v = S.wwin[ww][d];
@@ -329,92 +309,56 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
                 o += a;
             }
             S.tot[e] = o;
-            if (tid == 0) {
-                uint32_t r = 0;
-                int dense = 0;
-                for (int ww = 0; ww < ER_WARPS; ++ww) {
-                    S.wbase[ww] = r;
-                    r += S.nrec[ww] + S.norec[ww];
-                    dense |= S.nrec[ww] > WREC || S.norec[ww] > OREC;
-                }
-                S.dense = dense;
+        }
+        __syncthreads();
+        if (w == 0) {   // record slots: the sub-tile's changes sorted by exponent, one atomic
+            scan_change_starts(S.tot, S.cstart, lane);
+            __syncwarp();
+            if (lane == 31) {
+                const uint32_t r = S.cstart[255] + (S.tot[255] >> 16);
                 S.rec_base = r ? atomicAdd(&counters[0], (unsigned long long)r) : 0ull;
             }
         }
         __syncthreads();
-        if (w == 0) scan_change_starts(S.tot, S.cstart, lane);
-        __syncthreads();
-
-        if (!S.dense) {
+        if (any_out && w == 0) rank_outside(true);
+        // ---- records of the in-window changes of this warp's span: listed, then taken 32 at a time
+        {
             const uint64_t rb = S.rec_base;
-            const uint32_t nr = S.nrec[w];
-            for (uint32_t k = lane; k < nr; k += 32) {
-                const uint32_t r = S.rec[w][k];
-                const int ii = int(r >> 16), d = int((r >> 12) & 15u);
-                const uint32_t e = uint32_t(ebase + d);
-                const uint32_t lp = S.cnt[w][d][ii >> 5], wb = S.wwin[w][d];
+            auto record = [&](int ii) {   // ii: index in this warp's span
+                const int l = ii >> 5, k = ii & 31;
+                const uint32_t e = exp_at(span0 + ii);
+                const uint32_t d = e - ebase;
+                const uint32_t below = (1u << k) - 1u;
+                const uint32_t m = S.msk[w][d][l];
+                const uint32_t c = S.chm[w * 32 + l];
+                const uint32_t pr = S.pre[w][d][l], wb = S.wwin[w][d];
+                const uint32_t rA = (wb & 0xFFFFu) + (pr & 0xFFFFu) + uint32_t(__popc(m & below));
+                const uint32_t rC = (wb >> 16) + (pr >> 16) + uint32_t(__popc(m & c & below));
                 const uint32_t x = bits_of(span0 + ii);
-                const uint32_t rc = (wb >> 16) + (lp >> 16) + (r & 63u);   // rank among the sub-tile's changes
-                put_record(rec_key, rec_val, rec_cap, rb + S.cstart[e] + rc, s,
-                           S.runA[e] + (wb & 0xFFFFu) + (lp & 0xFFFFu) + ((r >> 6) & 63u), S.runC[e] + rc, x);
+                put_record(rec_key, rec_val, rec_cap, rb + S.cstart[e] + rC, s, S.runA[e] + rA, S.runC[e] + rC, x);
                 delta += change_delta(x, base + span0 + ii);
+            };
+            const uint32_t mine = cm & ~outm;
+            const uint32_t cnt = __popc(mine);
+            uint32_t incl = cnt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(FULL, incl, o);
+                if (lane >= o) incl += y;
             }
-            const uint32_t no = S.norec[w];
-            for (uint32_t k = lane; k < no; k += 32) {
-                const uint64_t q = S.orec[w][k];
-                const int ii = int(q & 1023u);
-                const uint32_t e = uint32_t(q >> 10) & 0xFFu;
-                const uint32_t wb = S.ocnt[w][e];
-                const uint32_t x = bits_of(span0 + ii);
-                const uint32_t rc = (wb >> 16) + (uint32_t(q >> 29) & 2047u);
-                put_record(rec_key, rec_val, rec_cap, rb + S.cstart[e] + rc, s,
-                           S.runA[e] + (wb & 0xFFFFu) + (uint32_t(q >> 18) & 2047u), S.runC[e] + rc, x);
-                delta += change_delta(x, base + span0 + ii);
-            }
-        } else {
-            // ---- too many changes for the buffers: count per warp and exponent, then rank again
-            for (int k = tid; k < ER_WARPS * 256; k += ER_THREADS) (&S.ocnt[0][0])[k] = 0;
-            __syncthreads();
-            for (int c = 0; c * 32 < span_n; ++c) {
-                const int ii = c * 32 + lane;
-                const bool valid = ii < span_n;
-                const uint32_t e = valid ? exp_of_i(span0 + ii) : 0u;
-                warp_rank_packed(S.ocnt[w], e, valid, 0, lt, lane);
-                warp_rank_packed(S.ocnt[w], e, valid && changed_i(span0 + ii), 16, lt, lane);
-            }
-            __syncthreads();
-            {
-                uint32_t o = 0;
-                for (int ww = 0; ww < ER_WARPS; ++ww) {
-                    const uint32_t v = S.ocnt[ww][tid];
-                    S.ocnt[ww][tid] = o;
-                    o += v;
-                }
-                S.tot[tid] = o;
-            }
-            __syncthreads();
-            if (w == 0) scan_change_starts(S.tot, S.cstart, lane);
-            __syncthreads();
-            const uint64_t rb = S.rec_base;
-            for (int c = 0; c * 32 < span_n; ++c) {
-                const int ii = c * 32 + lane;
-                const bool valid = ii < span_n;
-                const uint32_t e = valid ? exp_of_i(span0 + ii) : 0u;
-                const bool ch = valid && changed_i(span0 + ii);
-                const uint32_t rA = warp_rank_packed(S.ocnt[w], e, valid, 0, lt, lane);
-                const uint32_t rC = warp_rank_packed(S.ocnt[w], e, ch, 16, lt, lane);
-                if (ch) {
-                    const uint32_t x = bits_of(span0 + ii);
-                    put_record(rec_key, rec_val, rec_cap, rb + S.cstart[e] + rC, s, S.runA[e] + rA, S.runC[e] + rC, x);
-                    delta += change_delta(x, base + span0 + ii);
-                }
+            const uint32_t total = __shfl_sync(FULL, incl, 31);
+            if (total <= uint32_t(WLIST)) {
+                uint32_t at = incl - cnt;
+                for (uint32_t b = mine; b; b &= b - 1, ++at) S.wl[w][at] = uint16_t(lane * 32 + (__ffs(b) - 1));
+                __syncwarp();
+                for (uint32_t k = lane; k < total; k += 32) record(S.wl[w][k]);
+            } else {
+                for (uint32_t b = mine; b; b &= b - 1) record(lane * 32 + (__ffs(b) - 1));
             }
         }
         __syncthreads();
         S.runA[tid] += S.tot[tid] & 0xFFFFu;
         S.runC[tid] += S.tot[tid] >> 16;
-        if (tid == 0) { S.emax = 0; S.dense = 0; }
-        __syncthreads();
     }
     HS[s * 256 + tid] = S.runA[tid];
     CS[s * 256 + tid] = S.runC[tid];
