@@ -663,9 +663,10 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             }
         }
         __syncthreads();
-        // ---- stage this warp span's new values in position order: one atomic per warp, lane l
-        //      takes mark word l
+        // ---- stage this warp span's new values in position order, one atomic per warp: the
+        //      span's changed positions are listed (in the warp's spent masks), then taken 32 at a time
         {
+            static_assert(sizeof(S.msk[0]) >= MP_SPAN * sizeof(uint16_t), "a span's list fits in its masks");
             const uint32_t bits = S.mark[(span0 >> 5) + lane];
             const uint32_t c = __popc(bits);
             uint32_t incl = c;
@@ -674,36 +675,27 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                 const uint32_t y = __shfl_up_sync(FULL, incl, o);
                 if (lane >= o) incl += y;
             }
+            const uint32_t total = __shfl_sync(FULL, incl, 31);
             unsigned long long sb = 0;
-            if (lane == 31 && incl) sb = atomicAdd(staged, (unsigned long long)incl);
-            sb = __shfl_sync(FULL, sb, 31) + (incl - c);
-            for (uint32_t b = bits; b;) {   // four positions at a time: their old values load together
-                int ip[4];
-                uint32_t ov[4];
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    ip[h] = b ? span0 + lane * 32 + (__ffs(b) - 1) : -1;
-                    b &= b - 1;
+            if (lane == 31 && total) sb = atomicAdd(staged, (unsigned long long)total);
+            sb = __shfl_sync(FULL, sb, 31);
+            uint16_t* lst = reinterpret_cast<uint16_t*>(&S.msk[w][0][0]);
+            uint32_t at = incl - c;
+            for (uint32_t b = bits; b; b &= b - 1, ++at) lst[at] = uint16_t(lane * 32 + (__ffs(b) - 1));
+            __syncwarp();
+            for (uint32_t k = lane; k < total; k += 32) {
+                const int i = span0 + lst[k];
+                const uint32_t old = uint16_t(p[i]), nv = (old + S.nval[i]) & 0xFFFFu;
+                if (sb + k < stage_cap) {
+                    caddr[sb + k] = (unsigned long long)(reinterpret_cast<uintptr_t>(p + i));
+                    cval[sb + k] = uint16_t(nv);
                 }
-#pragma unroll
-                for (int h = 0; h < 4; ++h) ov[h] = ip[h] >= 0 ? uint32_t(uint16_t(p[ip[h]])) : 0u;
-#pragma unroll
-                for (int h = 0; h < 4; ++h) {
-                    if (ip[h] < 0) break;
-                    const int i = ip[h];
-                    const uint32_t old = ov[h], nv = (old + S.nval[i]) & 0xFFFFu;
-                    if (sb < stage_cap) {
-                        caddr[sb] = (unsigned long long)(reinterpret_cast<uintptr_t>(p + i));
-                        cval[sb] = uint16_t(nv);
-                    }
-                    ++sb;
-                    delta += (uint64_t(nv) - uint64_t(old)) * splitmix_weight(uint64_t(base + i));
-                    if (HNEW) {
-                        const uint32_t eo = (old >> 7) & 0xFFu, en = (nv >> 7) & 0xFFu;
-                        if (eo != en) {
-                            atomicSub(&S.hdelta[eo], 1);
-                            atomicAdd(&S.hdelta[en], 1);
-                        }
+                delta += (uint64_t(nv) - uint64_t(old)) * splitmix_weight(uint64_t(base + i));
+                if (HNEW) {
+                    const uint32_t eo = (old >> 7) & 0xFFu, en = (nv >> 7) & 0xFFu;
+                    if (eo != en) {
+                        atomicSub(&S.hdelta[eo], 1);
+                        atomicAdd(&S.hdelta[en], 1);
                     }
                 }
             }
