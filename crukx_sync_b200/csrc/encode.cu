@@ -75,7 +75,7 @@ constexpr int ER_SUB = 8192;                 // elements per sub-tile
 constexpr int ER_SPAN = ER_SUB / ER_WARPS;   // 1024 per warp
 constexpr int ER_RUN = ER_SPAN / 32;         // 32 per lane
 constexpr int WIN = 16;                      // window rows
-constexpr int WLIST = 128;                   // in-window changes of a span listed for cooperative record writes
+constexpr int WLIST = 256;                   // in-window changes of a span listed for the CTA's record writes
 static_assert(ER_SUB * 32 == SUPER_N, "32 sub-tiles per super-tile");
 
 struct RankSmem {
@@ -88,7 +88,9 @@ struct RankSmem {
     uint32_t runA[256], runC[256];        // super-tile running totals
     uint32_t tot[256];                    // this sub-tile's totals, all | changed << 16
     uint32_t cstart[256];                 // exclusive scan of the changed totals: records sorted by exponent
-    uint16_t wl[ER_WARPS][WLIST];         // a warp's in-window changes (span indices)
+    uint16_t wl[ER_WARPS][WLIST];         // a warp's in-window changes (sub-tile indices)
+    uint32_t wcnt[ER_WARPS];              // listed changes per warp, then (lbase) their exclusive prefix
+    uint32_t lbase[ER_WARPS + 1];
     uint32_t oowm[ER_WARPS];              // per warp: its runs holding below-window elements
     unsigned long long rec_base;
     int emax[2];                          // largest old exponent, alternating between sub-tiles
@@ -164,6 +166,10 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
         const int16_t* cp = tt.cur + base;
         // the (prev, cur) bits of sub-tile element i; only changed elements are read back
         auto bits_of = [&](int i) { return uint32_t(uint16_t(pp[i])) | (uint32_t(uint16_t(cp[i])) << 16); };
+        if (base + ER_SUB < e_end && (tid & 31) == 0 && w < 2) {   // the next sub-tile streams into L2 meanwhile
+            const size_t nb = size_t(tmin<int64_t>(ER_SUB, e_end - base - ER_SUB)) * 2;
+            prefetch_l2((w ? cp : pp) + ER_SUB, nb);
+        }
         // ---- stage old exponents (bytes) and changed bits; largest old exponent
         uint32_t mx = 0;
         if (n == ER_SUB && ((reinterpret_cast<uintptr_t>(pp) | reinterpret_cast<uintptr_t>(cp)) & 15) == 0) {
@@ -247,6 +253,23 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
         const uint32_t oowm = __ballot_sync(FULL, outm != 0);
         if (lane == 0) S.oowm[w] = oowm;
         const uint32_t cm = S.chm[w * 32 + lane];
+        // this span's in-window changes, listed in index order for the CTA's record writes (a lane
+        // keeps what does not fit)
+        const uint32_t mine = cm & ~outm;
+        uint32_t lpos = __popc(mine);
+        {
+            uint32_t incl = lpos;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(FULL, incl, o);
+                if (lane >= o) incl += y;
+            }
+            lpos = incl - lpos;
+            uint32_t at = lpos;
+            for (uint32_t b = mine; b && at < uint32_t(WLIST); b &= b - 1, ++at)
+                S.wl[w][at] = uint16_t(span0 + lane * 32 + (__ffs(b) - 1));
+            if (lane == 31) S.wcnt[w] = tmin(incl, uint32_t(WLIST));
+        }
         // ---- lane prefixes per window row of (all, changed) counts; empty rows skipped
 #pragma unroll
         for (int d = 0; d < WIN; ++d) {
@@ -309,6 +332,11 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
                 o += a;
             }
             S.tot[e] = o;
+            if (tid == 0) {
+                uint32_t r = 0;
+                for (int ww = 0; ww < ER_WARPS; ++ww) { S.lbase[ww] = r; r += S.wcnt[ww]; }
+                S.lbase[ER_WARPS] = r;
+            }
         }
         __syncthreads();
         if (w == 0) {   // record slots: the sub-tile's changes sorted by exponent, one atomic
@@ -321,39 +349,44 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
         }
         __syncthreads();
         if (any_out && w == 0) rank_outside(true);
-        // ---- records of the in-window changes of this warp's span: listed, then taken 32 at a time
+        // ---- records of the in-window changes: the listed ones by all threads, two at a time (their
+        //      bits load together); a lane then writes those of its run that did not fit the list
         {
             const uint64_t rb = S.rec_base;
-            auto record = [&](int ii) {   // ii: index in this warp's span
-                const int l = ii >> 5, k = ii & 31;
-                const uint32_t e = exp_at(span0 + ii);
+            auto record = [&](int i, uint32_t x) {   // i: index in the sub-tile
+                const int ww = i >> 10, l = (i >> 5) & 31, k = i & 31;
+                const uint32_t e = exp_at(i);
                 const uint32_t d = e - ebase;
                 const uint32_t below = (1u << k) - 1u;
-                const uint32_t m = S.msk[w][d][l];
-                const uint32_t c = S.chm[w * 32 + l];
-                const uint32_t pr = S.pre[w][d][l], wb = S.wwin[w][d];
+                const uint32_t m = S.msk[ww][d][l];
+                const uint32_t c = S.chm[i >> 5];
+                const uint32_t pr = S.pre[ww][d][l], wb = S.wwin[ww][d];
                 const uint32_t rA = (wb & 0xFFFFu) + (pr & 0xFFFFu) + uint32_t(__popc(m & below));
                 const uint32_t rC = (wb >> 16) + (pr >> 16) + uint32_t(__popc(m & c & below));
-                const uint32_t x = bits_of(span0 + ii);
                 put_record(rec_key, rec_val, rec_cap, rb + S.cstart[e] + rC, s, S.runA[e] + rA, S.runC[e] + rC, x);
-                delta += change_delta(x, base + span0 + ii);
+                delta += change_delta(x, base + i);
             };
-            const uint32_t mine = cm & ~outm;
-            const uint32_t cnt = __popc(mine);
-            uint32_t incl = cnt;
+            auto entry = [&](uint32_t g) {
+                int ww = 0;
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t y = __shfl_up_sync(FULL, incl, o);
-                if (lane >= o) incl += y;
+                for (int q = 1; q < ER_WARPS; ++q) ww += S.lbase[q] <= g;
+                return int(S.wl[ww][g - S.lbase[ww]]);
+            };
+            const uint32_t nl = S.lbase[ER_WARPS];
+            for (uint32_t g = tid; g < nl; g += 2 * ER_THREADS) {
+                const uint32_t g2 = g + ER_THREADS;
+                const int i0 = entry(g), i1 = g2 < nl ? entry(g2) : -1;
+                const uint32_t x0 = bits_of(i0), x1 = i1 >= 0 ? bits_of(i1) : 0u;
+                record(i0, x0);
+                if (i1 >= 0) record(i1, x1);
             }
-            const uint32_t total = __shfl_sync(FULL, incl, 31);
-            if (total <= uint32_t(WLIST)) {
-                uint32_t at = incl - cnt;
-                for (uint32_t b = mine; b; b &= b - 1, ++at) S.wl[w][at] = uint16_t(lane * 32 + (__ffs(b) - 1));
-                __syncwarp();
-                for (uint32_t k = lane; k < total; k += 32) record(S.wl[w][k]);
-            } else {
-                for (uint32_t b = mine; b; b &= b - 1) record(lane * 32 + (__ffs(b) - 1));
+            if (lpos + __popc(mine) > uint32_t(WLIST)) {
+                uint32_t at = lpos;
+                for (uint32_t b = mine; b; b &= b - 1, ++at) {
+                    if (at < uint32_t(WLIST)) continue;
+                    const int i = span0 + lane * 32 + (__ffs(b) - 1);
+                    record(i, bits_of(i));
+                }
             }
         }
         __syncthreads();
