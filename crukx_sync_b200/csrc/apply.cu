@@ -342,13 +342,31 @@ __global__ void __launch_bounds__(256) k_locals(const uint64_t* __restrict__ bsc
     const uint64_t size = GS[int64_t(grp.tensor) * 256 + grp.exp];
     uint64_t base = bscan[b] - bscan[gblock[g]];
     bool bad = false;
-    for (uint64_t i0 = 0; i0 < cnt; i0 += 32) {
-        const uint64_t i = i0 + lane;
-        const uint64_t gp = i < cnt ? gaps[ebase + i] : 0;
-        uint64_t incl = i < cnt ? gp + 1 : 0;
-        for (int o = 1; o < 32; o <<= 1) {
-            const uint64_t y = __shfl_up_sync(FULL, incl, o);
-            if (lane >= o) incl += y;
+    static_assert(kBlock == 256, "eight chunks of 32 per block");
+    uint32_t gv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) gv[u] = uint64_t(32 * u + lane) < cnt ? gaps[ebase + 32 * u + lane] : 0u;   // loads together
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        if (uint64_t(32 * u) >= cnt) break;
+        const uint64_t i = uint64_t(32 * u + lane);
+        const uint64_t gp = gv[u];
+        // 32-bit running sums while every gap of the chunk is below 2^26 (the usual case)
+        uint64_t incl;
+        if (__all_sync(FULL, gp < (1u << 26))) {
+            uint32_t in32 = i < cnt ? uint32_t(gp) + 1u : 0u;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(FULL, in32, o);
+                if (lane >= o) in32 += y;
+            }
+            incl = in32;
+        } else {
+            incl = i < cnt ? gp + 1 : 0;
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint64_t y = __shfl_up_sync(FULL, incl, o);
+                if (lane >= o) incl += y;
+            }
         }
         if (i < cnt) {
             const uint64_t loc = base + incl - 1;

@@ -577,37 +577,52 @@ __global__ void __launch_bounds__(256) k_stats(const uint64_t* __restrict__ g_st
         }
         acc0 = acc1 = acc2 = small = 0;
     };
-    for (uint64_t jb = j0 + (threadIdx.x & ~31u); jb < j1; jb += blockDim.x) {
-        const uint64_t j = jb + lane;
-        const bool valid = j < j1;
-        const uint32_t loc = valid ? local[j] : 0u;
-        const uint32_t prevw = __shfl_up_sync(FULL, loc, 1);
-        if (valid) {
-            if (j >= ge) {
-                flush();
-                g = g < 0 ? group_of(g_start, ng, j) : g + 1;
-                while (g_start[g + 1] <= j) ++g;
-                gs = g_start[g];
-                ge = g_start[g + 1];
-                cand = g_cand[g];
-                e = g_exp[g];
-            }
-            const uint32_t prev = lane ? prevw : (j > gs ? local[j - 1] : 0u);
-            const uint64_t gap = j == gs ? loc : uint64_t(loc) - prev - 1;
-            const uint32_t c0 = cand & 255, c1 = (cand >> 8) & 255, c2 = (cand >> 16) & 255;
-            acc0 += (gap >> c0) + 1 + c0;
-            acc1 += (gap >> c1) + 1 + c1;
-            acc2 += (gap >> c2) + 1 + c2;
-            const uint32_t z = zigzag_of(vals[j]);
-            if (z < 8) {
-                small += 1ull << (8 * z);
-            } else if (z < DENSE_SYM) {
-                const int64_t lg = g - g0;
-                if (lg < STATS_LOCAL_GROUPS) atomicAdd(&S.hist[lg][z], 1u);
-                else atomicAdd(&dense_hist[e * DENSE_SYM + z], 1ull);
-            } else {
-                atomicAdd(&rare_hist[int64_t(e) * kSymSpace + z], 1u);
-                if (!rare_flag[e]) rare_flag[e] = 1;
+    // each warp takes a contiguous quarter of the CTA's changes, four chunks of 32 loaded at once
+    const uint64_t wb = j0 + uint64_t(threadIdx.x >> 5) * (STATS_PER_CTA / 8);
+    const uint64_t we = tmin<uint64_t>(wb + STATS_PER_CTA / 8, j1);
+    for (uint64_t jb = wb; jb < we; jb += 128) {
+        uint32_t locs[4], vs[4], pl[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const uint64_t j = jb + 32 * u + lane;
+            const bool v = j < we;
+            locs[u] = v ? local[j] : 0u;
+            vs[u] = v ? vals[j] : 0u;
+            pl[u] = (lane == 0 && v && j > 0) ? local[j - 1] : 0u;
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const uint64_t j = jb + 32 * u + lane;
+            const bool valid = j < we;
+            const uint32_t loc = locs[u];
+            const uint32_t prevw = __shfl_up_sync(FULL, loc, 1);
+            if (valid) {
+                if (j >= ge) {
+                    flush();
+                    g = g < 0 ? group_of(g_start, ng, j) : g + 1;
+                    while (g_start[g + 1] <= j) ++g;
+                    gs = g_start[g];
+                    ge = g_start[g + 1];
+                    cand = g_cand[g];
+                    e = g_exp[g];
+                }
+                const uint32_t prev = lane ? prevw : (j > gs ? pl[u] : 0u);
+                const uint64_t gap = j == gs ? loc : uint64_t(loc) - prev - 1;
+                const uint32_t c0 = cand & 255, c1 = (cand >> 8) & 255, c2 = (cand >> 16) & 255;
+                acc0 += (gap >> c0) + 1 + c0;
+                acc1 += (gap >> c1) + 1 + c1;
+                acc2 += (gap >> c2) + 1 + c2;
+                const uint32_t z = zigzag_of(vs[u]);
+                if (z < 8) {
+                    small += 1ull << (8 * z);
+                } else if (z < DENSE_SYM) {
+                    const int64_t lg = g - g0;
+                    if (lg < STATS_LOCAL_GROUPS) atomicAdd(&S.hist[lg][z], 1u);
+                    else atomicAdd(&dense_hist[e * DENSE_SYM + z], 1ull);
+                } else {
+                    atomicAdd(&rare_hist[int64_t(e) * kSymSpace + z], 1u);
+                    if (!rare_flag[e]) rare_flag[e] = 1;
+                }
             }
         }
     }
@@ -737,13 +752,37 @@ __device__ void put_ones(uint32_t* words, uint64_t pos, uint64_t q) {
     }
 }
 
-// one warp per block: Rice gap then canonical Huffman code per change, MSB first
+// `len` (<= 64) low bits of v at bit `rel` of a warp's shared-memory words (MSB-first stream)
+__device__ __forceinline__ void stage_bits(uint32_t* sw, uint32_t rel, uint64_t v, int len) {
+    if (len == 0) return;
+    const int o = int(rel & 31);
+    uint32_t* w = sw + (rel >> 5);
+    if (o + len <= 64) {
+        const uint64_t x = v << (64 - o - len);
+        if (uint32_t(x >> 32)) atomicOr(w, uint32_t(x >> 32));
+        if (o + len > 32 && uint32_t(x)) atomicOr(w + 1, uint32_t(x));
+    } else {   // 65..95 bits of window: three words
+        const int sh = 96 - o - len;   // 1..31
+        if (uint32_t(v >> (64 - sh))) atomicOr(w, uint32_t(v >> (64 - sh)));
+        if (uint32_t((v << sh) >> 32)) atomicOr(w + 1, uint32_t((v << sh) >> 32));
+        if (uint32_t(v << sh)) atomicOr(w + 2, uint32_t(v << sh));
+    }
+}
+
+constexpr int PACK_WORDS = 512;   // a warp assembles blocks of up to 16 Kbit in shared memory
+
+// one warp per block: Rice gap then canonical Huffman code per change, MSB first.  A block that
+// fits is assembled in shared memory, then its words are stored (the two edge words, which it may
+// share with its neighbours, by atomic OR into the zeroed payload); a longer block writes its bits
+// straight to the payload by atomic OR.
 __global__ void __launch_bounds__(256) k_pack(const uint64_t* __restrict__ g_start, const int32_t* __restrict__ g_exp,
                                               const uint8_t* __restrict__ g_rice, const uint64_t* __restrict__ g_block,
                                               int64_t ng, int64_t n_blocks, const uint32_t* __restrict__ local,
                                               const uint32_t* __restrict__ vals, const uint32_t* __restrict__ dense_code,
                                               const uint32_t* __restrict__ big_code, const uint64_t* __restrict__ block_off,
-                                              uint32_t* __restrict__ words, uint32_t bit0) {
+                                              const uint32_t* __restrict__ block_bits, uint32_t* __restrict__ words,
+                                              uint32_t bit0) {
+    __shared__ uint32_t stage[256 / 32][PACK_WORDS];
     const int64_t b = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (b >= n_blocks) return;
@@ -754,6 +793,67 @@ __global__ void __launch_bounds__(256) k_pack(const uint64_t* __restrict__ g_sta
     const int r = g_rice[g];
     const int e = g_exp[g];
     uint64_t pos = block_off[b] + bit0;   // bit0: where this part starts inside its first byte
+    const uint32_t o0 = uint32_t(pos & 31);
+    const uint32_t nw = uint32_t((uint64_t(o0) + block_bits[b] + 31) >> 5);   // words the block touches
+    if (nw <= uint32_t(PACK_WORDS)) {
+        uint32_t* sw = stage[threadIdx.x >> 5];
+        for (uint32_t k = lane; k < nw; k += 32) sw[k] = 0;
+        __syncwarp();
+        uint32_t rel = o0;
+        static_assert(kBlock == 256, "eight chunks of 32 per block");
+        uint32_t locs[8], vs[8];   // the block's loads issued together; previous indices by shuffle
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const uint64_t j = j0 + 32 * u + lane;
+            locs[u] = j < j1 ? local[j] : 0u;
+            vs[u] = j < j1 ? vals[j] : 0u;
+        }
+        uint32_t carry = lane == 0 && j0 > gs ? local[j0 - 1] : 0u;
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const uint64_t j = j0 + 32 * u + lane;
+            const uint32_t up = __shfl_up_sync(FULL, locs[u], 1);
+            const uint32_t prev = lane ? up : carry;
+            carry = __shfl_sync(FULL, locs[u], 31);
+            uint32_t L = 0, cl = 0;
+            uint64_t gap = 0;
+            if (j < j1) {
+                gap = j == gs ? locs[u] : uint64_t(locs[u]) - prev - 1;
+                cl = code_of(dense_code, big_code, e, zigzag_of(vs[u]));
+                L = uint32_t(gap >> r) + 1u + uint32_t(r) + (cl >> 24);   // < 2^14: the block fits
+            }
+            uint32_t incl = L;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint32_t y = __shfl_up_sync(FULL, incl, o);
+                if (lane >= o) incl += y;
+            }
+            if (j < j1) {
+                uint32_t at = rel + incl - L;
+                uint32_t q = uint32_t(gap >> r);
+                const int hl = int(cl >> 24);
+                const uint64_t rem = r ? (gap & ((1ull << r) - 1)) : 0;
+                const int tail_len = 1 + r + hl;                          // the 0, r remainder bits, code
+                const uint64_t tail = (rem << hl) | (cl & 0xFFFFFFu);     // leading 0 is implicit
+                while (q + uint32_t(tail_len) > 64u) {   // long unary runs: ones 32 at a time
+                    const uint32_t c = tmin(q, 32u);
+                    stage_bits(sw, at, (1ull << c) - 1, int(c));
+                    q -= c;
+                    at += c;
+                }
+                stage_bits(sw, at, q ? ((((1ull << q) - 1) << tail_len) | tail) : tail, int(q) + tail_len);
+            }
+            rel += __shfl_sync(FULL, incl, 31);
+        }
+        __syncwarp();
+        const uint64_t w0 = pos >> 5;
+        for (uint32_t k = lane; k < nw; k += 32) {
+            const uint32_t v = sw[k];
+            if (k == 0 || k + 1 == nw) or_word(words, w0 + k, v);
+            else words[w0 + k] = bswap32(v);
+        }
+        return;
+    }
     for (uint64_t jb = j0; jb < j1; jb += 32) {
         const uint64_t j = jb + lane;
         uint64_t L = 0, gap = 0;
@@ -1261,7 +1361,7 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     { KernelScope ks_(C, "k_pack", st);
     k_pack<<<warps_grid, 256, 0, st>>>(g_start, g_exp, g_rice, g_block, ng, n_blocks, local, vals,
                                        dev<uint32_t>(C, S_DENSE_CODE), big_code, dev<uint64_t>(C, S_BLOCK_BITS),
-                                       dev<uint32_t>(C, S_PAYLOAD), bit0);
+                                       dev<uint32_t>(C, S_BB32), dev<uint32_t>(C, S_PAYLOAD), bit0);
     }
     CRX_CUDA(cudaGetLastError());
 
