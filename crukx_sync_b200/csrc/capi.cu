@@ -20,6 +20,7 @@ struct crx_encoded {
 struct crx_update {
     crx::Update u;
     std::vector<uint8_t> head;   // the update's head copied from device memory (crx_parse_device)
+    ~crx_update();
 };
 
 namespace crx {
@@ -600,8 +601,18 @@ namespace {
 std::mutex g_head_mu;
 uint8_t* g_head_pinned = nullptr;
 size_t g_head_cap = 0;
+// host buffers of freed device-update heads, reused: a fresh multi-megabyte vector costs its
+// zero fill and page faults on every parse
+std::vector<std::vector<uint8_t>> g_head_pool;
+constexpr size_t kHeadPoolMax = 8;
 
 }  // namespace
+
+crx_update::~crx_update() {
+    if (head.capacity() == 0) return;
+    std::lock_guard<std::mutex> lock(g_head_mu);
+    if (g_head_pool.size() < kHeadPoolMax) g_head_pool.push_back(std::move(head));
+}
 
 int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update** out, char* err, size_t errlen) {
     if (!out || len < 0 || (len && !data)) return CRX_BAD_ARGUMENT;
@@ -610,6 +621,11 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
         const cudaStream_t st = static_cast<cudaStream_t>(stream);
         std::lock_guard<std::mutex> lock(g_head_mu);
         std::vector<uint8_t> head;
+        if (!g_head_pool.empty()) {
+            head.swap(g_head_pool.back());
+            g_head_pool.pop_back();
+        }
+        auto keep = [&]() { if (g_head_pool.size() < kHeadPoolMax) g_head_pool.push_back(std::move(head)); };
         uint8_t last = 0;
         int64_t have = std::min<int64_t>(len, int64_t(1) << 16);
         int64_t got = 0;   // bytes of the head already in `head`
@@ -631,7 +647,7 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
                     return CRX_CUDA_ERROR;
                 if (cudaStreamSynchronize(st) != cudaSuccess) return CRX_CUDA_ERROR;
                 if (got == 0 && len) last = g_head_pinned[have];
-                head.resize(size_t(have));
+                if (head.size() < size_t(have)) head.resize(size_t(have));   // a reused buffer keeps its size
                 crx::parallel_copy(head.data() + got, g_head_pinned, size_t(have - got));
                 got = have;
             }
@@ -648,6 +664,7 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
             }
             delete u;
             if (s != crx::kNeedMore) {
+                keep();
                 put_err(err, errlen, msg);
                 return int(s);
             }

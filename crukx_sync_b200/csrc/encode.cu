@@ -270,12 +270,14 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
                 S.wl[w][at] = uint16_t(span0 + lane * 32 + (__ffs(b) - 1));
             if (lane == 31) S.wcnt[w] = tmin(incl, uint32_t(WLIST));
         }
-        // ---- lane prefixes per window row of (all, changed) counts; empty rows skipped
+        // ---- lane prefixes per window row of (all, changed) counts.  Records read a row's prefixes
+        //      only where the span has changes in it; other rows need just the warp's total.
 #pragma unroll
         for (int d = 0; d < WIN; ++d) {
             const uint32_t m = S.msk[w][d][lane];
-            if (!__any_sync(FULL, m != 0)) {
-                if (lane == 0) S.wwin[w][d] = 0;
+            if (!__any_sync(FULL, (m & cm) != 0)) {
+                const uint32_t a = __reduce_add_sync(FULL, uint32_t(__popc(m)));
+                if (lane == 0) S.wwin[w][d] = a;
                 continue;
             }
             const uint32_t v = uint32_t(__popc(m)) | (uint32_t(__popc(m & cm)) << 16);
@@ -920,13 +922,20 @@ void build_tables(const std::vector<uint64_t>& dense, const std::vector<std::pai
             tabs->sym[e].push_back(uint32_t(rare[r].first & 0x1FFFFu));
             tabs->cnt[e].push_back(rare[r].second);
         }
+    }
+    // the exponents' tables are independent: built on the host pool, the largest first
+    std::vector<int> todo;
+    for (int e = 0; e < 256; ++e)
+        if (!tabs->sym[e].empty()) todo.push_back(e);
+    std::sort(todo.begin(), todo.end(), [&](int a, int b) { return tabs->sym[a].size() > tabs->sym[b].size(); });
+    parallel_for(todo.size(), [&](size_t k) {
+        const int e = todo[k];
         const size_t ns = tabs->sym[e].size();
-        if (!ns) continue;
         tabs->len[e].resize(ns);
         tabs->code[e].resize(ns);
         huffman_lengths(tabs->cnt[e].data(), int64_t(ns), tabs->len[e].data());
         canonical_codes(tabs->len[e].data(), int64_t(ns), tabs->code[e].data());
-    }
+    });
 }
 
 // Global mode: the histogram summed over ranks (dense part by sum, rare pairs gathered and merged)
@@ -1243,6 +1252,7 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
         CRX_CUDA(cudaStreamSynchronize(st));
         std::memcpy(hrare.data(), C.host, 8 * rare_total);
     }
+    trace_phase(C, "encode: rare symbols down");
 
     // ---- Rice per group: first cheapest of the three candidates (codec.py:273-275)
     std::vector<uint8_t> rice(static_cast<size_t>(ng));
@@ -1276,6 +1286,7 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
         if (xs == kOk) xs = exchange_per_rank(*gx, uint64_t(n_present_local), &np_all, err);
         if (xs != kOk) return xs;
     }
+    trace_phase(C, "encode: rice, rare pairs");
     HostTables tabs;
     build_tables(hdense, rare_pairs, &tabs);
 
