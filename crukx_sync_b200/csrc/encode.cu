@@ -180,17 +180,19 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
                 const int v = tid + k * ER_THREADS;     // elements 8v .. 8v+7: run v/4, quarter v%4
                 const uint4 a = pv[v];
                 const uint4 b = cv[v];
-                const uint32_t w0 = __byte_perm((a.x >> 7) & 0x00FF00FFu, (a.y >> 7) & 0x00FF00FFu, 0x6420);
-                const uint32_t w1 = __byte_perm((a.z >> 7) & 0x00FF00FFu, (a.w >> 7) & 0x00FF00FFu, 0x6420);
+                const uint32_t x0 = (a.x >> 7) & 0x00FF00FFu, x1 = (a.y >> 7) & 0x00FF00FFu;
+                const uint32_t x2 = (a.z >> 7) & 0x00FF00FFu, x3 = (a.w >> 7) & 0x00FF00FFu;
                 const int r = v >> 2, q = v & 3;
-                S.texp[r * 9 + 2 * q] = w0;
-                S.texp[r * 9 + 2 * q + 1] = w1;
-                mx = __vmaxu4(mx, __vmaxu4(w0, w1));
-                // changed bits of the 8 elements (low half of a word first), then the run's 32
-                const uint32_t c0 = __vcmpne2(a.x, b.x), c1 = __vcmpne2(a.y, b.y);
-                const uint32_t c2 = __vcmpne2(a.z, b.z), c3 = __vcmpne2(a.w, b.w);
-                uint32_t cb = (c0 & 1u) | ((c0 >> 15) & 2u) | ((c1 & 1u) << 2) | ((c1 >> 13) & 8u) |
-                              ((c2 & 1u) << 4) | ((c2 >> 11) & 32u) | ((c3 & 1u) << 6) | ((c3 >> 9) & 128u);
+                S.texp[r * 9 + 2 * q] = __byte_perm(x0, x1, 0x6420);
+                S.texp[r * 9 + 2 * q + 1] = __byte_perm(x2, x3, 0x6420);
+                mx = __vimax3_u16x2(mx, __vimax3_u16x2(x0, x1, x2), x3);   // exponents in 16-bit halves
+                // changed bits of the 8 elements (low half of a word first), then the run's 32.
+                // nzh: bit 15 / bit 31 set where the low / high 16-bit half is nonzero (the masked
+                // halves plus 0x7FFF carry into bit 15 exactly when nonzero, never into bit 16)
+                auto nzh = [](uint32_t x) { return (((x & 0x7FFF7FFFu) + 0x7FFF7FFFu) | x) & 0x80008000u; };
+                const uint32_t c0 = nzh(a.x ^ b.x), c1 = nzh(a.y ^ b.y), c2 = nzh(a.z ^ b.z), c3 = nzh(a.w ^ b.w);
+                uint32_t cb = ((c0 >> 15) & 1u) | ((c0 >> 30) & 2u) | ((c1 >> 13) & 4u) | ((c1 >> 28) & 8u) |
+                              ((c2 >> 11) & 16u) | ((c2 >> 26) & 32u) | ((c3 >> 9) & 64u) | ((c3 >> 24) & 128u);
                 cb <<= 8 * q;
                 cb |= __shfl_xor_sync(FULL, cb, 1);
                 cb |= __shfl_xor_sync(FULL, cb, 2);
@@ -204,7 +206,7 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
                     }
                 }
             }
-            mx = tmax(tmax(mx & 0xFFu, (mx >> 8) & 0xFFu), tmax((mx >> 16) & 0xFFu, mx >> 24));
+            mx = tmax(mx & 0xFFFFu, mx >> 16);
         } else {
             uint8_t* tb = reinterpret_cast<uint8_t*>(S.texp);
             S.chm[tid] = 0;
