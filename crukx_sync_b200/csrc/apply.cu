@@ -924,7 +924,10 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     CRX_CUDA(ensure_copy_stream(C));
     CRX_CUDA(cudaEventRecord(C.ev_main, st));
     CRX_CUDA(cudaStreamWaitEvent(C.copy_stream, C.ev_main, 0));
-    CRX_CUDA(upload_pipelined(C, C.b[S_A_BB].p, u.block_table, ih, bt_bytes, C.copy_stream));
+    if (u.block_table)
+        CRX_CUDA(upload_pipelined(C, C.b[S_A_BB].p, u.block_table, ih, bt_bytes, C.copy_stream));
+    else if (bt_bytes)   // the update lives in device memory (its table at any byte offset)
+        CRX_CUDA(cudaMemcpyAsync(C.b[S_A_BB].p, u.block_table_device, bt_bytes, cudaMemcpyDeviceToDevice, C.copy_stream));
     if (u.payload)
         CRX_CUDA(upload_pipelined(C, C.b[S_A_PAYLOAD].p, u.payload, ih + bt_bytes, size_t(u.payload_len), C.copy_stream));
     else if (u.payload_len)   // the update lives in device memory

@@ -614,6 +614,104 @@ crx_update::~crx_update() {
     if (g_head_pool.size() < kHeadPoolMax) g_head_pool.push_back(std::move(head));
 }
 
+namespace {
+
+// The block table of a device update, checked where it lies: its bit total and whether some block
+// is shorter than its symbols could be (every change costs at least 2 + rice bits).  The table
+// starts at any byte offset, so its words are read bytewise.
+__device__ unsigned long long g_bt_total;
+__device__ unsigned int g_bt_short;
+
+__global__ void __launch_bounds__(256) k_check_block_table(const uint8_t* __restrict__ table, int64_t n_blocks,
+                                                           const uint64_t* __restrict__ first_block,
+                                                           const uint64_t* __restrict__ count_rice, int64_t ns) {
+    uint64_t bits = 0;
+    bool bad = false;
+    for (int64_t b = int64_t(blockIdx.x) * blockDim.x + threadIdx.x; b < n_blocks; b += int64_t(gridDim.x) * blockDim.x) {
+        const uint8_t* p = table + 4 * b;
+        const uint32_t w = uint32_t(p[0]) | (uint32_t(p[1]) << 8) | (uint32_t(p[2]) << 16) | (uint32_t(p[3]) << 24);
+        int64_t lo = 0, hi = ns - 1;   // the group of block b: the last one starting at or before it
+        while (lo < hi) {
+            const int64_t mid = (lo + hi + 1) >> 1;
+            if (first_block[mid] <= uint64_t(b)) lo = mid; else hi = mid - 1;
+        }
+        const uint64_t cr = count_rice[lo];
+        const uint64_t m = crx::tmin<uint64_t>(crx::kBlock, (cr >> 8) - (uint64_t(b) - first_block[lo]) * crx::kBlock);
+        bad |= uint64_t(w) < m * (2 + (cr & 0xFF));
+        bits += w;
+    }
+    for (int o = 16; o; o >>= 1) bits += __shfl_xor_sync(0xffffffffu, bits, o);
+    const bool any_bad = __any_sync(0xffffffffu, bad);
+    if ((threadIdx.x & 31) == 0) {
+        if (bits) atomicAdd(&g_bt_total, (unsigned long long)bits);
+        if (any_bad) atomicOr(&g_bt_short, 1u);
+    }
+}
+
+// per device: the group spans of the last checked table (grown on demand, kept for the process)
+struct SpanBuf {
+    void* p = nullptr;
+    size_t cap = 0;
+};
+std::unordered_map<int, SpanBuf> g_span_bufs;
+
+// sums and checks u's block table at `table` in device memory (stream-ordered, one synchronisation)
+int check_device_block_table(crx::Update* u, const uint8_t* table, uint8_t last, cudaStream_t st, std::string* msg) {
+    uint64_t total = 0;
+    bool short_block = false;
+    if (u->n_blocks > 0) {
+        std::vector<uint64_t> fb, cr;
+        crx::block_spans(*u, &fb, &cr);
+        const int64_t ns = int64_t(fb.size());
+        const size_t span_bytes = 16 * size_t(ns);
+        if (span_bytes + 16 > g_head_cap) {
+            if (g_head_pinned) cudaFreeHost(g_head_pinned);
+            g_head_pinned = nullptr;
+            g_head_cap = 0;
+            if (cudaMallocHost(reinterpret_cast<void**>(&g_head_pinned), span_bytes + 16) != cudaSuccess) return CRX_CUDA_ERROR;
+            g_head_cap = span_bytes + 16;
+        }
+        std::memcpy(g_head_pinned, fb.data(), 8 * size_t(ns));
+        std::memcpy(g_head_pinned + 8 * size_t(ns), cr.data(), 8 * size_t(ns));
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) return CRX_CUDA_ERROR;
+        SpanBuf& sb = g_span_bufs[dev];
+        if (sb.cap < span_bytes) {
+            if (sb.p && cudaFree(sb.p) != cudaSuccess) return CRX_CUDA_ERROR;
+            sb.p = nullptr;
+            sb.cap = 0;
+            const size_t cap = std::max(span_bytes, size_t(1) << 20);
+            if (cudaMalloc(&sb.p, cap) != cudaSuccess) return CRX_CUDA_ERROR;
+            sb.cap = cap;
+        }
+        void* dspan = sb.p;
+        void* dtot = nullptr;
+        void* dshort = nullptr;
+        const uint64_t* dfb = static_cast<const uint64_t*>(dspan);
+        const uint64_t* dcr = dfb + ns;
+        bool ok = cudaMemcpyAsync(dspan, g_head_pinned, span_bytes, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+                  cudaGetSymbolAddress(&dtot, g_bt_total) == cudaSuccess &&
+                  cudaGetSymbolAddress(&dshort, g_bt_short) == cudaSuccess &&
+                  cudaMemsetAsync(dtot, 0, 8, st) == cudaSuccess && cudaMemsetAsync(dshort, 0, 4, st) == cudaSuccess;
+        if (ok) {
+            const int64_t grid = crx::tmin<int64_t>((u->n_blocks + 255) / 256, 148 * 8);
+            k_check_block_table<<<unsigned(grid), 256, 0, st>>>(table, u->n_blocks, dfb, dcr, ns);
+            ok = cudaGetLastError() == cudaSuccess &&
+                 cudaMemcpyAsync(g_head_pinned, dtot, 8, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+                 cudaMemcpyAsync(g_head_pinned + 8, dshort, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess;
+        }
+        ok = cudaStreamSynchronize(st) == cudaSuccess && ok;
+        if (!ok) return CRX_CUDA_ERROR;
+        std::memcpy(&total, g_head_pinned, 8);
+        uint32_t sh = 0;
+        std::memcpy(&sh, g_head_pinned + 8, 4);
+        short_block = sh != 0;
+    }
+    return int(crx::finish_block_table_checks(u, total, short_block, last, msg));
+}
+
+}  // namespace
+
 int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update** out, char* err, size_t errlen) {
     if (!out || len < 0 || (len && !data)) return CRX_BAD_ARGUMENT;
     *out = nullptr;
@@ -626,20 +724,23 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
             g_head_pool.pop_back();
         }
         auto keep = [&]() { if (g_head_pool.size() < kHeadPoolMax) g_head_pool.push_back(std::move(head)); };
+        auto stage = [&](size_t bytes) {   // pinned staging of at least `bytes`
+            if (bytes <= g_head_cap) return true;
+            if (g_head_pinned) cudaFreeHost(g_head_pinned);
+            g_head_pinned = nullptr;
+            g_head_cap = 0;
+            const size_t cap = std::max(bytes, size_t(1) << 20);
+            if (cudaMallocHost(reinterpret_cast<void**>(&g_head_pinned), cap) != cudaSuccess) return false;
+            g_head_cap = cap;
+            return true;
+        };
         uint8_t last = 0;
         int64_t have = std::min<int64_t>(len, int64_t(1) << 16);
-        int64_t got = 0;   // bytes of the head already in `head`
-        for (;;) {   // copy a head, parse it, copy more when the header or block table reaches past it
+        int64_t got = 0;      // bytes [0, got) of the update are in `head`
+        int64_t avail = 0;    // what the parser may read: [0, got), and past the block table a window after it
+        for (;;) {   // copy a head, parse it, copy more when the header reaches past it
             if (have > got) {
-                const size_t need = size_t(have - got) + 1;
-                if (need > g_head_cap) {
-                    if (g_head_pinned) cudaFreeHost(g_head_pinned);
-                    g_head_pinned = nullptr;
-                    g_head_cap = 0;
-                    const size_t cap = std::max(need, size_t(1) << 20);
-                    if (cudaMallocHost(reinterpret_cast<void**>(&g_head_pinned), cap) != cudaSuccess) return CRX_CUDA_ERROR;
-                    g_head_cap = cap;
-                }
+                if (!stage(size_t(have - got) + 1)) return CRX_CUDA_ERROR;
                 if (cudaMemcpyAsync(g_head_pinned, data + got, size_t(have - got), cudaMemcpyDeviceToHost, st) != cudaSuccess)
                     return CRX_CUDA_ERROR;
                 if (got == 0 && len &&
@@ -650,25 +751,50 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
                 if (head.size() < size_t(have)) head.resize(size_t(have));   // a reused buffer keeps its size
                 crx::parallel_copy(head.data() + got, g_head_pinned, size_t(have - got));
                 got = have;
+                avail = std::max(avail, got);
             }
             crx_update* u = new crx_update;
             std::string msg;
             int64_t nd = 0;
-            const crx::Status s = crx::parse_head(head.data(), have, len, last, &u->u, &nd, &msg);
+            const crx::Status s = crx::parse_head_device_table(head.data(), avail, len, last, &u->u, &nd, &msg);
             if (s == crx::kOk) {
+                const int64_t t0 = u->u.block_table_offset;
+                const int rc = check_device_block_table(&u->u, data + t0, last, st, &msg);
+                if (rc != CRX_OK) {
+                    delete u;
+                    keep();
+                    if (rc == int(crx::kCorrupt)) put_err(err, errlen, msg);
+                    return rc;
+                }
+                u->u.block_table_device = data + t0;
                 u->u.payload_device = data + u->u.payload_offset;
                 u->u.payload = nullptr;
                 u->head.swap(head);   // the header's pointers stay valid: the vector's buffer moves with it
                 *out = u;
                 return CRX_OK;
             }
+            const int64_t t0 = u->u.block_table_offset;
+            const int64_t t1 = t0 >= 0 ? t0 + 4 * u->u.n_blocks : -1;
             delete u;
             if (s != crx::kNeedMore) {
                 keep();
                 put_err(err, errlen, msg);
                 return int(s);
             }
-            // past a block table comes at most a 10-byte length varint: ask for it in the same copy
+            if (t0 >= 0 && nd > t0 && got >= t0) {
+                // the header is here; past the table comes at most a 10-byte length varint: copy
+                // that window only (the table itself is checked on the device)
+                const int64_t w1 = std::min(len, t1 + 16);
+                if (w1 <= avail) return CRX_CUDA_ERROR;   // no progress: cannot happen
+                if (!stage(size_t(w1 - t1))) return CRX_CUDA_ERROR;
+                if (cudaMemcpyAsync(g_head_pinned, data + t1, size_t(w1 - t1), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+                    cudaStreamSynchronize(st) != cudaSuccess)
+                    return CRX_CUDA_ERROR;
+                if (head.size() < size_t(w1)) head.resize(size_t(w1));
+                std::memcpy(head.data() + t1, g_head_pinned, size_t(w1 - t1));
+                avail = w1;
+                continue;
+            }
             have = std::min(len, std::max(nd + 16, 4 * have));
         }
     } catch (const std::bad_alloc&) {
@@ -736,7 +862,13 @@ int64_t crx_update_n_blocks(const crx_update* u) { return u ? u->u.n_blocks : -1
 
 int crx_update_block_bits(const crx_update* u, uint32_t* out) {
     if (!u || !out) return CRX_BAD_ARGUMENT;
-    std::memcpy(out, u->u.block_table, 4 * size_t(u->u.n_blocks));
+    if (u->u.block_table) {
+        std::memcpy(out, u->u.block_table, 4 * size_t(u->u.n_blocks));
+    } else if (u->u.n_blocks) {   // the table stayed in device memory
+        if (!u->u.block_table_device ||
+            cudaMemcpy(out, u->u.block_table_device, 4 * size_t(u->u.n_blocks), cudaMemcpyDeviceToHost) != cudaSuccess)
+            return CRX_CUDA_ERROR;
+    }
     return CRX_OK;
 }
 

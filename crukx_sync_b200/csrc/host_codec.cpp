@@ -96,7 +96,7 @@ namespace {
 // The whole parse over the first `avail` of `len` bytes; `last` is the update's final byte (the
 // padding check needs it).  kNeedMore with *need set when the head does not fit in `avail`.
 Status parse_core(const uint8_t* data, int64_t avail, int64_t len, uint8_t last, Update* u, int64_t* need,
-                  std::string* err) {
+                  std::string* err, bool table_elsewhere = false) {
     Reader r{data, len, avail};
     auto bad = [&](const char* m) {
         if (r.need > 0) {   // ran out of the bytes at hand, not out of the update
@@ -202,7 +202,13 @@ Status parse_core(const uint8_t* data, int64_t avail, int64_t len, uint8_t last,
         if ((unsigned __int128)tb.symbols.size() > per_exp[tb.exponent]) return bad("table unused or larger than its changes");
     if (total_blocks * 4 > (unsigned __int128)r.remaining()) return bad("block table longer than the update");
     u->n_blocks = int64_t(total_blocks);
-    if (!r.take(4 * u->n_blocks, &u->block_table)) return bad("update is truncated");
+    if (table_elsewhere) {   // the table's bytes are not here: only its place and length
+        u->block_table_offset = r.pos;
+        u->block_table = nullptr;
+        if (!r.skip(4 * u->n_blocks)) return bad("update is truncated");
+    } else if (!r.take(4 * u->n_blocks, &u->block_table)) {
+        return bad("update is truncated");
+    }
     int64_t pl;
     if (!r.varint(&pl)) return bad("update is truncated");
     u->payload_offset = r.pos;
@@ -210,6 +216,14 @@ Status parse_core(const uint8_t* data, int64_t avail, int64_t len, uint8_t last,
     u->payload = r.pos <= avail ? data + u->payload_offset : nullptr;
     u->payload_len = pl;
     if (r.remaining() != 0) return bad("trailing bytes after the payload");
+    if (table_elsewhere) {
+        int64_t changes = 0;
+        for (const TensorHeader& h : u->tensors)
+            for (const Group& g : h.groups) changes += g.count;
+        u->total_changes = changes;
+        u->total_bits = 0;
+        return kOk;
+    }
     // block table, one pass split over the worker threads: the bit total, and every change costs
     // at least 2 + rice bits (wire.py:204-211)
     struct Span { int64_t b0, count; int rice; };
@@ -253,12 +267,8 @@ Status parse_core(const uint8_t* data, int64_t avail, int64_t len, uint8_t last,
     uint64_t total_bits = 0;
     bool short_block = false;
     for (size_t k = 0; k < n_tasks; ++k) { total_bits += part_bits[k]; short_block |= part_bad[k] != 0; }
-    if ((total_bits + 7) / 8 != uint64_t(pl)) return bad("payload length does not match its block table");
-    if ((total_bits & 7) && (last & ((1u << (8 - (total_bits & 7))) - 1))) return bad("non-zero padding bits");
-    if (short_block) return bad("block shorter than its symbols could be");
-    u->total_bits = total_bits;
     u->total_changes = changes;
-    return kOk;
+    return finish_block_table_checks(u, total_bits, short_block, last, err);
 }
 
 }  // namespace
@@ -270,6 +280,35 @@ Status parse_update(const uint8_t* data, int64_t len, Update* u, std::string* er
 Status parse_head(const uint8_t* head, int64_t head_len, int64_t len, uint8_t last, Update* u, int64_t* need,
                   std::string* err) {
     return parse_core(head, std::min(head_len, len), len, last, u, need, err);
+}
+
+Status parse_head_device_table(const uint8_t* head, int64_t head_len, int64_t len, uint8_t last, Update* u,
+                               int64_t* need, std::string* err) {
+    return parse_core(head, std::min(head_len, len), len, last, u, need, err, true);
+}
+
+Status finish_block_table_checks(Update* u, uint64_t total_bits, bool short_block, uint8_t last, std::string* err) {
+    auto bad = [&](const char* m) {
+        if (err) *err = m;
+        return kCorrupt;
+    };
+    if ((total_bits + 7) / 8 != uint64_t(u->payload_len)) return bad("payload length does not match its block table");
+    if ((total_bits & 7) && (last & ((1u << (8 - (total_bits & 7))) - 1))) return bad("non-zero padding bits");
+    if (short_block) return bad("block shorter than its symbols could be");
+    u->total_bits = total_bits;
+    return kOk;
+}
+
+void block_spans(const Update& u, std::vector<uint64_t>* first_block, std::vector<uint64_t>* count_rice) {
+    first_block->clear();
+    count_rice->clear();
+    uint64_t b = 0;
+    for (const TensorHeader& h : u.tensors)
+        for (const Group& g : h.groups) {
+            first_block->push_back(b);
+            count_rice->push_back((uint64_t(g.count) << 8) | uint64_t(g.rice & 0xFF));
+            b += (uint64_t(g.count) + kBlock - 1) / kBlock;
+        }
 }
 
 // ---------------------------------------------------------------- Huffman

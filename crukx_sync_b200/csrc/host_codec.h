@@ -55,6 +55,8 @@ struct Update {
     int table_of_exp[256];
     std::vector<TensorHeader> tensors;
     const uint8_t* block_table = nullptr;  // n_blocks little-endian u32 words, borrowed
+    int64_t block_table_offset = -1;       // of the block table within the update (parse_head_device_table)
+    const uint8_t* block_table_device = nullptr;  // the block table in device memory (not 4-byte aligned)
     int64_t n_blocks = 0;
     const uint8_t* payload = nullptr;      // borrowed; null when only the head was parsed
     int64_t payload_offset = 0;            // of the payload within the update
@@ -74,6 +76,19 @@ Status parse_update(const uint8_t* data, int64_t len, Update* out, std::string* 
 // the head must at least have when the header or block table reaches past head_len.
 Status parse_head(const uint8_t* head, int64_t head_len, int64_t len, uint8_t last, Update* out, int64_t* need,
                   std::string* err);
+
+// parse_head for an update whose block table stays where it is (device memory): the table's bytes
+// are neither needed in `head` nor read; u->block_table_offset is set once the parse reaches it,
+// and a kNeedMore past that offset asks only for the bytes after the table.  On kOk every check
+// but the block table's is done: the caller sums the table and finishes with
+// finish_block_table_checks.
+Status parse_head_device_table(const uint8_t* head, int64_t head_len, int64_t len, uint8_t last, Update* out,
+                               int64_t* need, std::string* err);
+// The block table's checks from its bit total and whether some block is shorter than its symbols
+// could be (same messages and order as parse_update's); sets u->total_bits on kOk.
+Status finish_block_table_checks(Update* u, uint64_t total_bits, bool short_block, uint8_t last, std::string* err);
+// Per group in update order: its first block, and its change count << 8 | rice (the short-block check)
+void block_spans(const Update& u, std::vector<uint64_t>* first_block, std::vector<uint64_t>* count_rice);
 
 // Length-limited Huffman code lengths with the reference's tie order.
 void huffman_lengths(const uint64_t* counts, int64_t n, uint8_t* lengths);

@@ -315,8 +315,9 @@ def parse(data: bytes) -> ParsedUpdate:
 
 
 def parse_device(update, stream=None) -> ParsedUpdate:
-    """parse() for an update held in device memory (a contiguous uint8 CUDA tensor): the head is
-    copied to the host and validated there; the payload stays on the device for apply."""
+    """parse() for an update held in device memory (a contiguous uint8 CUDA tensor): the header is
+    copied to the host and validated there, the block table is checked on the device (same
+    verdicts as parse()); the block table and payload stay on the device for apply."""
     import torch
 
     if not (isinstance(update, torch.Tensor) and update.dtype == torch.uint8 and update.is_cuda

@@ -132,9 +132,11 @@ int crx_parse(const uint8_t* data, int64_t len, crx_update** out, char* err, siz
  * validate an update before its payload has arrived. */
 int crx_parse_head(const uint8_t* head, int64_t head_len, int64_t len, uint8_t last, crx_update** out, int64_t* need,
                    char* err, size_t errlen);
-/* Parse an update held in device memory (len bytes at `data`): its head is copied to the host on
- * `stream` and validated as crx_parse does; the payload stays where it is and crx_apply reads it
- * there (data must stay valid until crx_apply returns).  No reference counterpart. */
+/* Parse an update held in device memory (len bytes at `data`): its header is copied to the host on
+ * `stream`, its block table is summed and checked on the device where it lies, and every check of
+ * crx_parse is made with the same verdicts; the block table and payload stay where they are and
+ * crx_apply reads them there (data must stay valid until crx_apply returns).  No reference
+ * counterpart. */
 int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update** out, char* err, size_t errlen);
 int64_t crx_update_n_tensors(const crx_update* u);
 int64_t crx_update_changes(const crx_update* u);
