@@ -51,8 +51,15 @@ def bits16(name: str, t) -> torch.Tensor:
     return t.view(torch.int16).view(-1)
 
 
+_NAME_TABLES: dict = {}   # the last few name lists (a model syncs the same names every step)
+
+
 def _name_table(names):
     """UTF-8 names as one buffer: (keep-alive, pointer array, length array)."""
+    key = tuple(names)
+    hit = _NAME_TABLES.get(key)
+    if hit is not None:
+        return hit
     raw = [n.encode("utf-8") for n in names]
     blob = b"".join(raw) + b"\0"
     base = ctypes.cast(ctypes.c_char_p(blob), ctypes.c_void_p).value
@@ -61,8 +68,11 @@ def _name_table(names):
         ptrs.append(base + off)
         lens.append(len(r))
         off += len(r)
-    k = max(len(raw), 1)
-    return blob, (ctypes.c_void_p * k)(*ptrs), (ctypes.c_int64 * k)(*lens)
+    out = (blob, _ext.CBuf("Q", ptrs), _ext.CBuf("q", lens))
+    if len(_NAME_TABLES) >= 8:
+        _NAME_TABLES.clear()
+    _NAME_TABLES[key] = out
+    return out
 
 
 def _cuda_device(dev: torch.device) -> torch.device:
@@ -112,12 +122,12 @@ def _encode_on(dev, names, olds, news, checksums, device_result=False) -> Encode
     k = len(names)
     prev = _ext.ptr_array([a.data_ptr() for a in olds])
     cur = _ext.ptr_array([b.data_ptr() for b in news])
-    numel = (ctypes.c_int64 * max(k, 1))(*[a.numel() for a in olds])
+    numel = _ext.CBuf("q", [a.numel() for a in olds])
     keep, name_ptrs, name_len = _name_table(names)
     if checksums:
         hits = [checksums.get(n) for n in names]
-        cache = (ctypes.c_uint64 * max(k, 1))(*[int(c) & (2**64 - 1) if c is not None else 0 for c in hits])
-        has = (ctypes.c_uint8 * max(k, 1))(*[c is not None for c in hits])
+        cache = _ext.CBuf("Q", [int(c) & (2**64 - 1) if c is not None else 0 for c in hits])
+        has = _ext.CBuf("B", [c is not None for c in hits])
     else:
         cache, has = None, None
     h = ctypes.c_void_p()
@@ -163,12 +173,12 @@ def encode_global(old, new, checksums, rank: int, world: int, sum_u64, allgather
     k = len(names)
     prev = _ext.ptr_array([a.data_ptr() for a in olds])
     cur = _ext.ptr_array([b.data_ptr() for b in news])
-    numel = (ctypes.c_int64 * max(k, 1))(*[a.numel() for a in olds])
+    numel = _ext.CBuf("q", [a.numel() for a in olds])
     keep, name_ptrs, name_len = _name_table(names)
     if checksums:
         hits = [checksums.get(n) for n in names]
-        cache = (ctypes.c_uint64 * max(k, 1))(*[int(c) & (2**64 - 1) if c is not None else 0 for c in hits])
-        has = (ctypes.c_uint8 * max(k, 1))(*[c is not None for c in hits])
+        cache = _ext.CBuf("Q", [int(c) & (2**64 - 1) if c is not None else 0 for c in hits])
+        has = _ext.CBuf("B", [c is not None for c in hits])
     else:
         cache, has = None, None
     held = []   # gathered buffers stay alive until the call returns
@@ -241,8 +251,8 @@ def apply(weights: Mapping[str, torch.Tensor], u: ParsedUpdate, checksums: dict 
     k = len(headers)
     if checksums:
         cached = [_cache_get(checksums, name, a) for (name, _, _), a in zip(headers, targets)]
-        cache = (ctypes.c_uint64 * k)(*[c if c is not None else 0 for c in cached])
-        has = (ctypes.c_uint8 * k)(*[c is not None for c in cached])
+        cache = _ext.CBuf("Q", [c if c is not None else 0 for c in cached])
+        has = _ext.CBuf("B", [c is not None for c in cached])
     else:
         cache, has = None, None
     ptrs = _ext.ptr_array([a.data_ptr() for a in work])
@@ -254,8 +264,8 @@ def apply(weights: Mapping[str, torch.Tensor], u: ParsedUpdate, checksums: dict 
         if dev.type == "cuda" and checksums is not None:
             # tensors written in place on the device: the library may keep their exponent
             # histograms for the next apply, tagged with the version they will have after it
-            vers = (ctypes.c_uint64 * k)(*[a._version for a in targets])
-            tag = (ctypes.c_uint8 * k)(*([1] * k))
+            vers = _ext.CBuf("Q", [a._version for a in targets])
+            tag = _ext.CBuf("B", bytes([1]) * k)
             st = L.crx_apply_versioned(_ext.context(cdev.index), u.handle, ptrs, cache, has, vers, tag,
                                        ctypes.c_void_p(stream), ctypes.byref(changed), err, 1024)
         else:
