@@ -835,18 +835,23 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     if (int64_t(gblock.back()) != n_blocks) { *err = "internal: block count mismatch"; return kCudaError; }
     std::vector<DecTable> TB(u.tables.size());
     std::vector<uint32_t> syms;
-    for (size_t k = 0; k < u.tables.size(); ++k) {
-        DecodeTable d;
-        const size_t off = syms.size();
-        syms.resize(off + u.tables[k].symbols.size());
-        build_decode_table(u.tables[k], &d, syms.data() + off);
-        DecTable& x = TB[k];
-        std::memcpy(x.first, d.first, sizeof(x.first));
-        std::memcpy(x.base, d.base, sizeof(x.base));
-        std::memcpy(x.limit, d.limit, sizeof(x.limit));
-        x.sym_off = uint32_t(off);
-        x.nsym = uint32_t(u.tables[k].symbols.size());
-        build_lut(d, x.lut);
+    {   // decode tables and their lookup tables, independent per exponent: built on the host pool
+        std::vector<size_t> offs(u.tables.size() + 1, 0);
+        for (size_t k = 0; k < u.tables.size(); ++k) offs[k + 1] = offs[k] + u.tables[k].symbols.size();
+        syms.resize(offs.back());
+        auto one = [&](size_t k) {
+            DecodeTable d;
+            build_decode_table(u.tables[k], &d, syms.data() + offs[k]);
+            DecTable& x = TB[k];
+            std::memcpy(x.first, d.first, sizeof(x.first));
+            std::memcpy(x.base, d.base, sizeof(x.base));
+            std::memcpy(x.limit, d.limit, sizeof(x.limit));
+            x.sym_off = uint32_t(offs[k]);
+            x.nsym = uint32_t(u.tables[k].symbols.size());
+            build_lut(d, x.lut);
+        };
+        if (u.tables.size() > 4) parallel_for(u.tables.size(), one);
+        else for (size_t k = 0; k < u.tables.size(); ++k) one(k);
     }
 
     trace_phase(C, "apply: host tables");

@@ -650,33 +650,47 @@ __global__ void __launch_bounds__(1024) k_rare_compact(uint32_t* __restrict__ ra
                                                        uint64_t* __restrict__ out, uint64_t out_cap,
                                                        unsigned long long* __restrict__ rare_total,
                                                        uint64_t* __restrict__ rare_base, uint32_t* __restrict__ rare_cnt) {
-    __shared__ uint32_t sh[32];
+    constexpr uint32_t SLICE = (kSymSpace + 32 * 32 - 1) / (32 * 32) * 32;   // each of the 32 warps takes one slice, in order
+    __shared__ uint32_t wbase[32];
     __shared__ uint64_t base_sh;
     const int e = blockIdx.x;
+    const int w = int(threadIdx.x >> 5), lane = int(threadIdx.x & 31);
     if (!rare_flag[e]) { if (threadIdx.x == 0) rare_cnt[e] = 0; return; }
     uint32_t* row = rare_hist + int64_t(e) * kSymSpace;
+    const uint32_t s0 = uint32_t(w) * SLICE;
     uint32_t nz = 0;
-    for (uint32_t i = threadIdx.x; i < kSymSpace; i += 1024) nz += row[i] != 0;
-    uint32_t tot;
-    block_scan_u32(nz, sh, &tot);
-    if (threadIdx.x == 0) {
-        base_sh = atomicAdd(rare_total, (unsigned long long)tot);
-        rare_base[e] = base_sh;
-        rare_cnt[e] = tot;
-        rare_flag[e] = 0;
+    for (uint32_t i = s0 + lane; i < s0 + SLICE && i < kSymSpace; i += 32) nz += row[i] != 0;
+    nz = __reduce_add_sync(FULL, nz);
+    if (lane == 0) wbase[w] = nz;
+    __syncthreads();
+    if (w == 0) {   // warp bases, the exponent's total and its place in the list
+        const uint32_t v = wbase[lane];
+        uint32_t incl = v;
+        for (int o = 1; o < 32; o <<= 1) {
+            const uint32_t y = __shfl_up_sync(FULL, incl, o);
+            if (lane >= o) incl += y;
+        }
+        wbase[lane] = incl - v;
+        if (lane == 31) {
+            base_sh = atomicAdd(rare_total, (unsigned long long)incl);
+            rare_base[e] = base_sh;
+            rare_cnt[e] = incl;
+            rare_flag[e] = 0;
+        }
     }
     __syncthreads();
-    uint64_t pos = base_sh;
-    for (uint32_t b = 0; b < kSymSpace; b += 1024) {
-        const uint32_t i = b + threadIdx.x;
-        const uint32_t v = i < kSymSpace ? row[i] : 0;
-        uint32_t t2;
-        const uint32_t ex = block_scan_u32(v ? 1u : 0u, sh, &t2);
+    uint64_t pos = base_sh + wbase[w];
+    const uint32_t lt = lanemask_lt();
+    for (uint32_t b = s0; b < s0 + SLICE; b += 32) {
+        const uint32_t i = b + uint32_t(lane);
+        const uint32_t v = i < kSymSpace ? row[i] : 0u;
+        const uint32_t m = __ballot_sync(FULL, v != 0);
         if (v) {
-            if (pos + ex < out_cap) out[pos + ex] = (uint64_t(i) << 32) | v;
+            const uint64_t at = pos + uint64_t(__popc(m & lt));
+            if (at < out_cap) out[at] = (uint64_t(i) << 32) | v;
             row[i] = 0;
         }
-        pos += t2;
+        pos += uint64_t(__popc(m));
     }
 }
 
