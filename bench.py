@@ -308,7 +308,7 @@ def run_ours(args, rank, world, dist):
     # correctness of the warm state before timing
     for k in recv:
         assert torch.equal(recv[k], state["src"][k]), f"receiver differs from the sender state: {k}"
-    launches0 = L.crx_ctx_launches(ctx)
+    launches0 = L.crx_ctx_launches(ctx) + L.crx_parse_device_launches()
     evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(args.steps)]
     sizes = []
     with ClockSampler(dev.index) as clk:
@@ -319,7 +319,7 @@ def run_ours(args, rank, world, dist):
             sizes.append(upd.numel())
         barrier()
         t_wall = time.perf_counter() - t_wall0
-    launches = int(L.crx_ctx_launches(ctx) - launches0)
+    launches = int(L.crx_ctx_launches(ctx) + L.crx_parse_device_launches() - launches0)   # + the device parses' table checks
     enc = [e[0].elapsed_time(e[1]) for e in evs]
     ex = [e[1].elapsed_time(e[2]) for e in evs]
     app = [e[2].elapsed_time(e[3]) for e in evs]

@@ -17,7 +17,8 @@ LIB_PATH = os.path.join(_HERE, "libcrukx_b200.so")
 CRX_OK, CRX_VALUE_ERROR, CRX_CORRUPT, CRX_CUDA_ERROR, CRX_NO_MEMORY, CRX_BAD_ARGUMENT, CRX_NEED_MORE = range(7)
 
 EXPORTS = [
-    "crx_wire_version", "crx_ctx_create", "crx_ctx_destroy", "crx_ctx_launches", "crx_ctx_profile",
+    "crx_wire_version", "crx_ctx_create", "crx_ctx_destroy", "crx_ctx_launches", "crx_parse_device_launches",
+    "crx_ctx_profile",
     "crx_ctx_kernel_times", "crx_encode", "crx_encoded_size", "crx_encoded_copy",
     "crx_encoded_changes", "crx_encoded_checksums", "crx_encoded_free", "crx_parse", "crx_update_n_tensors",
     "crx_update_changes", "crx_update_tensor", "crx_update_group", "crx_update_tensor_table", "crx_update_n_tables", "crx_update_table",
@@ -56,6 +57,7 @@ def load():
             "crx_ctx_create": ([ctypes.c_int, ctypes.POINTER(P), CP, SZ], ctypes.c_int),
             "crx_ctx_destroy": ([P], None),
             "crx_ctx_launches": ([P], U64),
+            "crx_parse_device_launches": ([], U64),
             "crx_ctx_profile": ([P, ctypes.c_int], ctypes.c_int),
             "crx_ctx_kernel_times": ([P, CP, SZ, P, P, I32], I32),
             "crx_encode": ([P, I32, P, P, P, P, P, P, P, P, ctypes.POINTER(P), CP, SZ], ctypes.c_int),

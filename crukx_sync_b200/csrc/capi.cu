@@ -1,5 +1,6 @@
 // extern "C" entry points (include/crukx_b200.h) over the C++ drivers; no exception crosses.
 #include <algorithm>
+#include <atomic>
 #include <chrono>
 #include <cstdio>
 #include <cstdlib>
@@ -605,6 +606,7 @@ size_t g_head_cap = 0;
 // zero fill and page faults on every parse
 std::vector<std::vector<uint8_t>> g_head_pool;
 constexpr size_t kHeadPoolMax = 8;
+std::atomic<uint64_t> g_parse_launches{0};   // kernels crx_parse_device launched
 
 }  // namespace
 
@@ -696,6 +698,7 @@ int check_device_block_table(crx::Update* u, const uint8_t* table, uint8_t last,
         if (ok) {
             const int64_t grid = crx::tmin<int64_t>((u->n_blocks + 255) / 256, 148 * 8);
             k_check_block_table<<<unsigned(grid), 256, 0, st>>>(table, u->n_blocks, dfb, dcr, ns);
+            ++g_parse_launches;
             ok = cudaGetLastError() == cudaSuccess &&
                  cudaMemcpyAsync(g_head_pinned, dtot, 8, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
                  cudaMemcpyAsync(g_head_pinned + 8, dshort, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess;
@@ -955,6 +958,7 @@ int crx_huffman_lengths(const uint64_t* counts, int64_t n, uint8_t* lengths) {
 }
 
 uint64_t crx_ctx_launches(crx_ctx* ctx) { return ctx ? ctx->c.launches : 0; }
+uint64_t crx_parse_device_launches(void) { return g_parse_launches.load(); }
 
 int crx_ctx_profile(crx_ctx* ctx, int enable) {
     if (!ctx) return CRX_BAD_ARGUMENT;

@@ -48,6 +48,9 @@ int crx_ctx_create(int device, crx_ctx** out, char* err, size_t errlen);
 void crx_ctx_destroy(crx_ctx* ctx);
 /* Kernels launched by this context so far (no reference counterpart: instrumentation). */
 uint64_t crx_ctx_launches(crx_ctx* ctx);
+/* Kernels launched by crx_parse_device (its block-table check), process-wide: crx_parse_device
+ * takes no context, so these are not in crx_ctx_launches. */
+uint64_t crx_parse_device_launches(void);
 /* Per-kernel timing with CUDA events on the caller's stream while enabled (instrumentation, no
  * reference counterpart).  Enabling clears earlier records.  crx_ctx_kernel_times returns the
  * number of distinct kernels, writes their names ('\n'-separated) and total ms / launch counts
