@@ -10,9 +10,10 @@
 //                  64-bit window are followed inside the block's own bits only.
 //   k_locals       group-local index = running sum of gap + 1 (codec.py:640-642), range checks
 //                  (codec.py:696-697).
-//   k_map          per super-tile: in-CTA stable counting sort of the old exponents, then every
-//                  change is placed by (exponent, local rank) -> position (codec.py:654-694), the
-//                  new value staged and the checksum delta accumulated (codec.py:698-700).
+//   k_map          per super-tile: per-lane masks of the old exponents over a 16-exponent window,
+//                  then every change is placed by (exponent, local rank) -> position through
+//                  selection on the masks' counts (codec.py:654-694), the new value staged and the
+//                  checksum delta accumulated (codec.py:698-700).
 //   host verdict   one synchronisation: decode/range flags and per-tensor checksums.
 //   k_commit       scatter of the staged values, only after the verdict (codec.py:713-714).
 #include <algorithm>

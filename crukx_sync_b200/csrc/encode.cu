@@ -14,7 +14,7 @@
 //                  (exponent, zigzag residual) symbol histogram (codec.py:355-367).
 //   host           Rice choice, length-limited Huffman per exponent (codec.py:71-111, 369-392).
 //   k_block_bits   bits per 256-change block (codec.py:411-416), then an exclusive scan.
-//   k_pack         one warp per block writes its bits MSB-first (codec.py:218-257).
+//   k_pack         one warp per block assembles its bits MSB-first (codec.py:218-257).
 #include <algorithm>
 #include <cstring>
 #include <string>
