@@ -209,6 +209,48 @@ struct QuadReader {
     }
 };
 
+// The generic step of k_decode: a unary run that does not fit the bit buffer (more than ~30 ones,
+// or a large Rice parameter) is followed window by window at absolute positions, never past the
+// block's end or past q_max, so hostile updates cost at most their own bits.  ok = false on a
+// decode error; otherwise pos is past the change.  (Inlined: a call costs the main loop registers.)
+struct GenericStep {
+    uint64_t pos, gap;
+    uint32_t sym;
+    bool ok;
+};
+
+__device__ __forceinline__ GenericStep decode_generic(const uint64_t* __restrict__ W, uint64_t p, uint64_t end, uint64_t qmax,
+                                                      int rice, const DecTable* __restrict__ tab,
+                                                      const uint32_t* __restrict__ SY, uint32_t nsym1) {
+    GenericStep r{p, 0, 0, false};
+    uint64_t y = ~read64(W, p);
+    uint64_t qq;
+    if (y) {
+        qq = uint64_t(__clzll(y));
+    } else {
+        qq = 64;
+        while (qq <= qmax && p + qq < end) {
+            y = ~read64(W, p + qq);
+            if (y) { qq += uint64_t(__clzll(y)); break; }
+            qq += 64;
+        }
+    }
+    if (qq > qmax || p + qq >= end) return r;
+    const uint64_t c = p + qq + 1;
+    const uint64_t x = read64(W, c);
+    const uint64_t rem = rice ? (x >> (64 - rice)) : 0;
+    int L;
+    uint32_t idx;
+    if (!find_code(tab, uint32_t((x << rice) >> (64 - kMaxCodeLen)), L, idx)) return r;
+    r.sym = SY[tmin(idx, nsym1)];
+    r.gap = (qq << rice) | rem;
+    r.pos = c + uint64_t(rice) + uint64_t(L);
+    r.ok = true;
+    return r;
+}
+
+__device__ __forceinline__ uint32_t clamp32(uint64_t v) { return v > 0xFFFFFFFFull ? 0xFFFFFFFFu : uint32_t(v); }
+
 __global__ void __launch_bounds__(DEC_THREADS) k_decode(const uint64_t* __restrict__ W, uint64_t n32,
                                                         const uint32_t* __restrict__ bb, const uint64_t* __restrict__ boff,
                                                         int64_t n_blocks, const AppGroup* __restrict__ G,
@@ -243,25 +285,18 @@ __global__ void __launch_bounds__(DEC_THREADS) k_decode(const uint64_t* __restri
         wi += 2;
     };
     fill();
-    uint64_t sum = 0;
-    bool ok = true;
-    // outputs go out four at a time as 16-byte stores at indices that are multiples of 4 (the
-    // buffers are 256-byte aligned); the unaligned head and tail of the block are stored singly
-    uint4 gq = make_uint4(0, 0, 0, 0), zq = make_uint4(0, 0, 0, 0);
-    int step = 0;
-    for (; step < cnt; ++step) {
-        if (pos >= end) { ok = false; break; }
+    // one change: Rice gap and canonical-code symbol, with the reference's validation; false on error
+    auto one = [&](uint64_t& gap, uint32_t& sym) -> bool {
+        if (pos >= end) return false;
         const int q = __clzll(~buf);   // ones ahead; bits past `avail` are zeros, so q < avail when it fits
-        uint64_t gap;
-        uint32_t sym;
         if (q + 1 + rice + kMaxCodeLen <= avail) {
-            if (uint64_t(q) > qmax || pos + uint64_t(q) >= end) { ok = false; break; }
+            if (uint64_t(q) > qmax || pos + uint64_t(q) >= end) return false;
             uint64_t t = buf << (q + 1);
             const uint64_t rem = rice ? (t >> (64 - rice)) : 0;
             t <<= rice;
             int L;
             uint32_t idx;
-            if (!find_code(tab, uint32_t(t >> (64 - kMaxCodeLen)), L, idx)) { ok = false; break; }
+            if (!find_code(tab, uint32_t(t >> (64 - kMaxCodeLen)), L, idx)) return false;
             sym = SY[tmin(idx, nsym1)];
             gap = (uint64_t(q) << rice) | rem;
             const int used = q + 1 + rice + L;
@@ -272,55 +307,52 @@ __global__ void __launch_bounds__(DEC_THREADS) k_decode(const uint64_t* __restri
                 buf |= uint64_t(R.word(wi++)) << (32 - avail);
                 avail += 32;
             }
-        } else {
-            // generic step: a unary run of more than 64 ones is followed window by window, never
-            // past this block's end or past q_max, so hostile updates cost at most their own bits
-            uint64_t y = ~read64(W, pos);
-            uint64_t qq;
-            if (y) {
-                qq = uint64_t(__clzll(y));
-            } else {
-                qq = 64;
-                while (qq <= qmax && pos + qq < end) {
-                    y = ~read64(W, pos + qq);
-                    if (y) { qq += uint64_t(__clzll(y)); break; }
-                    qq += 64;
-                }
-            }
-            if (qq > qmax || pos + qq >= end) { ok = false; break; }
-            const uint64_t c = pos + qq + 1;
-            const uint64_t x = read64(W, c);
-            const uint64_t rem = rice ? (x >> (64 - rice)) : 0;
-            int L;
-            uint32_t idx;
-            if (!find_code(tab, uint32_t((x << rice) >> (64 - kMaxCodeLen)), L, idx)) { ok = false; break; }
-            sym = SY[tmin(idx, nsym1)];
-            gap = (qq << rice) | rem;
-            pos = c + uint64_t(rice) + uint64_t(L);
-            fill();
+            return true;
         }
-        gq = make_uint4(gq.y, gq.z, gq.w, gap > 0xFFFFFFFFull ? 0xFFFFFFFFu : uint32_t(gap));
-        zq = make_uint4(zq.y, zq.z, zq.w, sym);
-        const uint64_t i = ebase + uint64_t(step);
-        if ((i & 3) == 3) {
-            if (step >= 3) {
-                *reinterpret_cast<uint4*>(gaps + i - 3) = gq;
-                *reinterpret_cast<uint4*>(zz + i - 3) = zq;
-            } else {   // head: steps 0..step
-                if (step >= 2) { gaps[i - 2] = gq.y; zz[i - 2] = zq.y; }
-                if (step >= 1) { gaps[i - 1] = gq.z; zz[i - 1] = zq.z; }
-                gaps[i] = gq.w;
-                zz[i] = zq.w;
-            }
+        const GenericStep r = decode_generic(W, pos, end, qmax, rice, tab, SY, nsym1);
+        if (!r.ok) return false;
+        pos = r.pos;
+        gap = r.gap;
+        sym = r.sym;
+        fill();
+        return true;
+    };
+    uint64_t sum = 0;
+    bool ok = true;
+    // outputs: singly up to a multiple-of-4 index, then four at a time as 16-byte stores (the
+    // buffers are 256-byte aligned), then the tail singly
+    int step = 0;
+    const int head = tmin(cnt, int((4 - (ebase & 3)) & 3));
+    for (; step < head && ok; ++step) {
+        uint64_t gp;
+        uint32_t sy;
+        ok = one(gp, sy);
+        if (ok) {
+            gaps[ebase + step] = clamp32(gp);
+            zz[ebase + step] = sy;
+            sum += gp + 1;
         }
-        sum += gap + 1;
     }
-    if (ok) {   // tail: the last (ebase + cnt) % 4 outputs, unless already in the head
-        const uint64_t e = ebase + uint64_t(cnt);
-        const int r = tmin(int(e & 3), cnt);
-        if (r >= 3) { gaps[e - 3] = gq.y; zz[e - 3] = zq.y; }
-        if (r >= 2) { gaps[e - 2] = gq.z; zz[e - 2] = zq.z; }
-        if (r >= 1) { gaps[e - 1] = gq.w; zz[e - 1] = zq.w; }
+    const int body = head + ((cnt - head) & ~3);
+    for (; step < body && ok; step += 4) {
+        uint64_t g0, g1, g2, g3;
+        uint32_t s0, s1, s2, s3;
+        ok = one(g0, s0) && one(g1, s1) && one(g2, s2) && one(g3, s3);
+        if (ok) {
+            *reinterpret_cast<uint4*>(gaps + ebase + step) = make_uint4(clamp32(g0), clamp32(g1), clamp32(g2), clamp32(g3));
+            *reinterpret_cast<uint4*>(zz + ebase + step) = make_uint4(s0, s1, s2, s3);
+            sum += g0 + g1 + g2 + g3 + 4;
+        }
+    }
+    for (; step < cnt && ok; ++step) {
+        uint64_t gp;
+        uint32_t sy;
+        ok = one(gp, sy);
+        if (ok) {
+            gaps[ebase + step] = clamp32(gp);
+            zz[ebase + step] = sy;
+            sum += gp + 1;
+        }
     }
     ok = ok && pos == end;
     bsum[b] = ok ? sum : 0;
