@@ -26,7 +26,7 @@ EXPORTS = [
     "crx_update_free", "crx_apply", "crx_huffman_lengths", "crx_checksum", "crx_checksum_noalloc",
     "crx_encode_device", "crx_encoded_copy_device", "crx_parse_head", "crx_parse_device",
     "crx_encode_global", "crx_encoded_part", "crx_encoded_part_copy", "crx_apply_versioned",
-    "crx_ctx_hist_cache_hits",
+    "crx_ctx_hist_cache_hits", "crx_alloc_calls",
 ]
 
 # collective callbacks of crx_encode_global
@@ -94,6 +94,7 @@ def load():
             "crx_encoded_part_copy": ([P, P, P, P, P], ctypes.c_int),
             "crx_apply_versioned": ([P, P, P, P, P, P, P, P, P, CP, SZ], ctypes.c_int),
             "crx_ctx_hist_cache_hits": ([P], U64),
+            "crx_alloc_calls": ([], U64),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

@@ -1049,32 +1049,52 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
                                                            total);
     }
     CRX_CUDA(cudaGetLastError());
-    // ---- the new weights' histograms for the next apply (tagged version + 1: the caller bumps it)
+    // ---- the new weights' histograms for the next apply (tagged version + 1: the caller bumps it).
+    //      Rows of dropped entries go to a free list and are reused; nothing is freed here (a
+    //      cudaFree would synchronize the device and stall every other stream).
+    auto retire = [&](DevBuf& b) {
+        if (b.p) C.hist_free.push_back(b);
+        b = DevBuf{};
+    };
     for (int t = 0; t < nt; ++t) {
         const auto key = reinterpret_cast<uintptr_t>(weights[t]);
         if (!(keep_hist && has_version[t])) {   // written without a tag: forget what was cached
             const auto it = C.hist_cache.find(key);
             if (it != C.hist_cache.end()) {
-                if (it->second.rows.p) cudaFree(it->second.rows.p);
+                retire(it->second.rows);
                 C.hist_cache.erase(it);
             }
         }
     }
     if (keep_hist) {
-        size_t cached_bytes = 0;
-        for (auto& kv : C.hist_cache) cached_bytes += kv.second.rows.cap;
-        if (cached_bytes > (size_t(4) << 30)) {   // bound the cache: start over
-            for (auto& kv : C.hist_cache)
-                if (kv.second.rows.p) cudaFree(kv.second.rows.p);
-            C.hist_cache.clear();
-        }
+        constexpr size_t kHistBound = size_t(4) << 30;   // cached rows plus free rows
+        size_t held = 0;
+        for (auto& kv : C.hist_cache) held += kv.second.rows.cap;
+        for (auto& d : C.hist_free) held += d.cap;
         std::vector<uint32_t*> dst;
         std::vector<int64_t> row0, rows;
         for (int t = 0; t < nt; ++t) {
             if (!has_version[t]) continue;
             auto& ent = C.hist_cache[reinterpret_cast<uintptr_t>(weights[t])];
             const int64_t nr = (T[size_t(t)].numel + SUPER_N - 1) / SUPER_N;
-            CRX_CUDA(ensure_dev(ent.rows, sizeof(uint32_t) * 256 * size_t(nr), st));
+            const size_t need = sizeof(uint32_t) * 256 * size_t(nr);
+            if (ent.rows.cap < need) {
+                retire(ent.rows);
+                size_t best = C.hist_free.size();   // the smallest free rows that fit
+                for (size_t k = 0; k < C.hist_free.size(); ++k)
+                    if (C.hist_free[k].cap >= need && (best == C.hist_free.size() || C.hist_free[k].cap < C.hist_free[best].cap))
+                        best = k;
+                if (best < C.hist_free.size()) {
+                    ent.rows = C.hist_free[best];
+                    C.hist_free.erase(C.hist_free.begin() + std::ptrdiff_t(best));
+                } else if (held + need <= kHistBound) {
+                    CRX_CUDA(ensure_dev(ent.rows, need, st));
+                    held += ent.rows.cap;
+                } else {   // over the bound: this tensor is not cached (its next apply reads the weights)
+                    C.hist_cache.erase(reinterpret_cast<uintptr_t>(weights[t]));
+                    continue;
+                }
+            }
             ent.numel = T[size_t(t)].numel;
             ent.tag = versions[t] + 1;
             ent.checksum = u.tensors[size_t(t)].checksum;

@@ -5,7 +5,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <memory>
 #include <new>
+#include <unordered_map>
 #include <string>
 
 #include "../../include/crukx_b200.h"
@@ -25,6 +27,9 @@ struct crx_update {
 };
 
 namespace crx {
+
+std::atomic<uint64_t> g_alloc_calls{0};
+void note_alloc() { g_alloc_calls.fetch_add(1, std::memory_order_relaxed); }
 
 static cudaEvent_t pooled_event(Ctx& c) {
     if (c.ev_used == c.ev_pool.size()) {
@@ -88,6 +93,8 @@ Ctx::~Ctx() {
         if (d.p) cudaFree(d.p);
     for (auto& kv : hist_cache)
         if (kv.second.rows.p) cudaFree(kv.second.rows.p);
+    for (auto& d : hist_free)
+        if (d.p) cudaFree(d.p);
     if (host) cudaFreeHost(host);
     if (out_host.p) cudaFreeHost(out_host.p);
     if (in_host.p) cudaFreeHost(in_host.p);
@@ -102,13 +109,16 @@ cudaError_t ensure_dev(DevBuf& buf, size_t bytes, cudaStream_t s) {
     if (buf.p) {
         cudaError_t e = cudaStreamSynchronize(s);
         if (e != cudaSuccess) return e;
+        note_alloc();
         cudaFree(buf.p);
         buf.p = nullptr;
         buf.cap = 0;
     }
+    note_alloc();
     cudaError_t e = cudaMalloc(&buf.p, cap);
     if (e != cudaSuccess) {
         cudaGetLastError();
+        note_alloc();
         e = cudaMalloc(&buf.p, bytes);   // retry without headroom
         if (e != cudaSuccess) { buf.p = nullptr; return e; }
         cap = bytes;
@@ -124,10 +134,12 @@ cudaError_t ensure_host(Ctx& c, size_t bytes, cudaStream_t s) {
     if (c.host) {
         cudaError_t e = cudaStreamSynchronize(s);
         if (e != cudaSuccess) return e;
+        note_alloc();
         cudaFreeHost(c.host);
         c.host = nullptr;
         c.host_cap = 0;
     }
+    note_alloc();
     cudaError_t e = cudaMallocHost(&c.host, cap);
     if (e != cudaSuccess) { c.host = nullptr; return e; }
     c.host_cap = cap;
@@ -141,10 +153,12 @@ cudaError_t ensure_pinned(DevBuf& buf, size_t bytes, cudaStream_t s) {
     if (buf.p) {
         cudaError_t e = cudaStreamSynchronize(s);
         if (e != cudaSuccess) return e;
+        note_alloc();
         cudaFreeHost(buf.p);
         buf.p = nullptr;
         buf.cap = 0;
     }
+    note_alloc();
     cudaError_t e = cudaMallocHost(&buf.p, cap);
     if (e != cudaSuccess) { buf.p = nullptr; return e; }
     buf.cap = cap;
@@ -327,6 +341,8 @@ extern "C" {
 
 int crx_wire_version(void) { return 2; }
 
+uint64_t crx_alloc_calls(void) { return crx::g_alloc_calls.load(std::memory_order_relaxed); }
+
 int crx_ctx_create(int device, crx_ctx** out, char* err, size_t errlen) {
     if (!out) return CRX_BAD_ARGUMENT;
     *out = nullptr;
@@ -337,6 +353,7 @@ int crx_ctx_create(int device, crx_ctx** out, char* err, size_t errlen) {
     c->c.trace = tr && *tr && *tr != '0';
     DeviceGuard g(device);
     cudaError_t e = cudaSetDevice(device);
+    crx::note_alloc();
     if (e == cudaSuccess) e = cudaMallocHost(reinterpret_cast<void**>(&c->c.small), 4096);
     if (e != cudaSuccess) {
         put_err(err, errlen, std::string("crx_ctx_create: ") + cudaGetErrorString(e));
@@ -597,13 +614,30 @@ int crx_parse_head(const uint8_t* head, int64_t head_len, int64_t len, uint8_t l
 
 namespace {
 
-// pinned staging for the heads crx_parse_device copies back (one buffer for the process, grown on
-// demand; device -> pageable copies run at a fraction of the link's bandwidth)
-std::mutex g_head_mu;
-uint8_t* g_head_pinned = nullptr;
-size_t g_head_cap = 0;
+// What crx_parse_device keeps per device: its lock (the block-table check's accumulators below are
+// per device, so parses on different devices run concurrently), pinned staging for the heads it
+// copies back (device -> pageable copies run at a fraction of the link's bandwidth) and the group
+// spans of the last checked table, both grown on demand and kept for the process.
+struct DevParse {
+    std::mutex mu;
+    uint8_t* pinned = nullptr;
+    size_t cap = 0;
+    void* spans = nullptr;
+    size_t spans_cap = 0;
+};
+std::mutex g_devparse_mu;                                   // guards the map only
+std::unordered_map<int, std::unique_ptr<DevParse>> g_devparse;
+
+DevParse& dev_parse(int dev) {
+    std::lock_guard<std::mutex> lock(g_devparse_mu);
+    auto& p = g_devparse[dev];
+    if (!p) p.reset(new DevParse);
+    return *p;
+}
+
 // host buffers of freed device-update heads, reused: a fresh multi-megabyte vector costs its
 // zero fill and page faults on every parse
+std::mutex g_pool_mu;
 std::vector<std::vector<uint8_t>> g_head_pool;
 constexpr size_t kHeadPoolMax = 8;
 std::atomic<uint64_t> g_parse_launches{0};   // kernels crx_parse_device launched
@@ -612,7 +646,7 @@ std::atomic<uint64_t> g_parse_launches{0};   // kernels crx_parse_device launche
 
 crx_update::~crx_update() {
     if (head.capacity() == 0) return;
-    std::lock_guard<std::mutex> lock(g_head_mu);
+    std::lock_guard<std::mutex> lock(g_pool_mu);
     if (g_head_pool.size() < kHeadPoolMax) g_head_pool.push_back(std::move(head));
 }
 
@@ -650,15 +684,24 @@ __global__ void __launch_bounds__(256) k_check_block_table(const uint8_t* __rest
     }
 }
 
-// per device: the group spans of the last checked table (grown on demand, kept for the process)
-struct SpanBuf {
-    void* p = nullptr;
-    size_t cap = 0;
-};
-std::unordered_map<int, SpanBuf> g_span_bufs;
+// pinned staging of at least `bytes` in P (the caller holds P.mu)
+bool stage_pinned(DevParse& P, size_t bytes) {
+    if (bytes <= P.cap) return true;
+    crx::note_alloc();
+    if (P.pinned) cudaFreeHost(P.pinned);
+    P.pinned = nullptr;
+    P.cap = 0;
+    const size_t cap = std::max(bytes, size_t(1) << 20);
+    crx::note_alloc();
+    if (cudaMallocHost(reinterpret_cast<void**>(&P.pinned), cap) != cudaSuccess) return false;
+    P.cap = cap;
+    return true;
+}
 
-// sums and checks u's block table at `table` in device memory (stream-ordered, one synchronisation)
-int check_device_block_table(crx::Update* u, const uint8_t* table, uint8_t last, cudaStream_t st, std::string* msg) {
+// sums and checks u's block table at `table` in device memory (stream-ordered, one synchronisation;
+// the caller holds P.mu)
+int check_device_block_table(DevParse& P, crx::Update* u, const uint8_t* table, uint8_t last, cudaStream_t st,
+                             std::string* msg) {
     uint64_t total = 0;
     bool short_block = false;
     if (u->n_blocks > 0) {
@@ -666,32 +709,25 @@ int check_device_block_table(crx::Update* u, const uint8_t* table, uint8_t last,
         crx::block_spans(*u, &fb, &cr);
         const int64_t ns = int64_t(fb.size());
         const size_t span_bytes = 16 * size_t(ns);
-        if (span_bytes + 16 > g_head_cap) {
-            if (g_head_pinned) cudaFreeHost(g_head_pinned);
-            g_head_pinned = nullptr;
-            g_head_cap = 0;
-            if (cudaMallocHost(reinterpret_cast<void**>(&g_head_pinned), span_bytes + 16) != cudaSuccess) return CRX_CUDA_ERROR;
-            g_head_cap = span_bytes + 16;
-        }
-        std::memcpy(g_head_pinned, fb.data(), 8 * size_t(ns));
-        std::memcpy(g_head_pinned + 8 * size_t(ns), cr.data(), 8 * size_t(ns));
-        int dev = 0;
-        if (cudaGetDevice(&dev) != cudaSuccess) return CRX_CUDA_ERROR;
-        SpanBuf& sb = g_span_bufs[dev];
-        if (sb.cap < span_bytes) {
-            if (sb.p && cudaFree(sb.p) != cudaSuccess) return CRX_CUDA_ERROR;
-            sb.p = nullptr;
-            sb.cap = 0;
+        if (!stage_pinned(P, span_bytes + 16)) return CRX_CUDA_ERROR;
+        std::memcpy(P.pinned, fb.data(), 8 * size_t(ns));
+        std::memcpy(P.pinned + 8 * size_t(ns), cr.data(), 8 * size_t(ns));
+        if (P.spans_cap < span_bytes) {
+            crx::note_alloc();
+            if (P.spans && cudaFree(P.spans) != cudaSuccess) return CRX_CUDA_ERROR;
+            P.spans = nullptr;
+            P.spans_cap = 0;
             const size_t cap = std::max(span_bytes, size_t(1) << 20);
-            if (cudaMalloc(&sb.p, cap) != cudaSuccess) return CRX_CUDA_ERROR;
-            sb.cap = cap;
+            crx::note_alloc();
+            if (cudaMalloc(&P.spans, cap) != cudaSuccess) return CRX_CUDA_ERROR;
+            P.spans_cap = cap;
         }
-        void* dspan = sb.p;
+        void* dspan = P.spans;
         void* dtot = nullptr;
         void* dshort = nullptr;
         const uint64_t* dfb = static_cast<const uint64_t*>(dspan);
         const uint64_t* dcr = dfb + ns;
-        bool ok = cudaMemcpyAsync(dspan, g_head_pinned, span_bytes, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+        bool ok = cudaMemcpyAsync(dspan, P.pinned, span_bytes, cudaMemcpyHostToDevice, st) == cudaSuccess &&
                   cudaGetSymbolAddress(&dtot, g_bt_total) == cudaSuccess &&
                   cudaGetSymbolAddress(&dshort, g_bt_short) == cudaSuccess &&
                   cudaMemsetAsync(dtot, 0, 8, st) == cudaSuccess && cudaMemsetAsync(dshort, 0, 4, st) == cudaSuccess;
@@ -700,14 +736,14 @@ int check_device_block_table(crx::Update* u, const uint8_t* table, uint8_t last,
             k_check_block_table<<<unsigned(grid), 256, 0, st>>>(table, u->n_blocks, dfb, dcr, ns);
             ++g_parse_launches;
             ok = cudaGetLastError() == cudaSuccess &&
-                 cudaMemcpyAsync(g_head_pinned, dtot, 8, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
-                 cudaMemcpyAsync(g_head_pinned + 8, dshort, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess;
+                 cudaMemcpyAsync(P.pinned, dtot, 8, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+                 cudaMemcpyAsync(P.pinned + 8, dshort, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess;
         }
         ok = cudaStreamSynchronize(st) == cudaSuccess && ok;
         if (!ok) return CRX_CUDA_ERROR;
-        std::memcpy(&total, g_head_pinned, 8);
+        std::memcpy(&total, P.pinned, 8);
         uint32_t sh = 0;
-        std::memcpy(&sh, g_head_pinned + 8, 4);
+        std::memcpy(&sh, P.pinned + 8, 4);
         short_block = sh != 0;
     }
     return int(crx::finish_block_table_checks(u, total, short_block, last, msg));
@@ -720,23 +756,23 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
     *out = nullptr;
     try {
         const cudaStream_t st = static_cast<cudaStream_t>(stream);
-        std::lock_guard<std::mutex> lock(g_head_mu);
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess) return CRX_CUDA_ERROR;
+        DevParse& P = dev_parse(dev);
+        std::lock_guard<std::mutex> lock(P.mu);
         std::vector<uint8_t> head;
-        if (!g_head_pool.empty()) {
-            head.swap(g_head_pool.back());
-            g_head_pool.pop_back();
+        {
+            std::lock_guard<std::mutex> pl(g_pool_mu);
+            if (!g_head_pool.empty()) {
+                head.swap(g_head_pool.back());
+                g_head_pool.pop_back();
+            }
         }
-        auto keep = [&]() { if (g_head_pool.size() < kHeadPoolMax) g_head_pool.push_back(std::move(head)); };
-        auto stage = [&](size_t bytes) {   // pinned staging of at least `bytes`
-            if (bytes <= g_head_cap) return true;
-            if (g_head_pinned) cudaFreeHost(g_head_pinned);
-            g_head_pinned = nullptr;
-            g_head_cap = 0;
-            const size_t cap = std::max(bytes, size_t(1) << 20);
-            if (cudaMallocHost(reinterpret_cast<void**>(&g_head_pinned), cap) != cudaSuccess) return false;
-            g_head_cap = cap;
-            return true;
+        auto keep = [&]() {
+            std::lock_guard<std::mutex> pl(g_pool_mu);
+            if (g_head_pool.size() < kHeadPoolMax) g_head_pool.push_back(std::move(head));
         };
+        auto stage = [&](size_t bytes) { return stage_pinned(P, bytes); };
         uint8_t last = 0;
         int64_t have = std::min<int64_t>(len, int64_t(1) << 16);
         int64_t got = 0;      // bytes [0, got) of the update are in `head`
@@ -744,15 +780,15 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
         for (;;) {   // copy a head, parse it, copy more when the header reaches past it
             if (have > got) {
                 if (!stage(size_t(have - got) + 1)) return CRX_CUDA_ERROR;
-                if (cudaMemcpyAsync(g_head_pinned, data + got, size_t(have - got), cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                if (cudaMemcpyAsync(P.pinned, data + got, size_t(have - got), cudaMemcpyDeviceToHost, st) != cudaSuccess)
                     return CRX_CUDA_ERROR;
                 if (got == 0 && len &&
-                    cudaMemcpyAsync(g_head_pinned + (have - got), data + len - 1, 1, cudaMemcpyDeviceToHost, st) != cudaSuccess)
+                    cudaMemcpyAsync(P.pinned + (have - got), data + len - 1, 1, cudaMemcpyDeviceToHost, st) != cudaSuccess)
                     return CRX_CUDA_ERROR;
                 if (cudaStreamSynchronize(st) != cudaSuccess) return CRX_CUDA_ERROR;
-                if (got == 0 && len) last = g_head_pinned[have];
+                if (got == 0 && len) last = P.pinned[have];
                 if (head.size() < size_t(have)) head.resize(size_t(have));   // a reused buffer keeps its size
-                crx::parallel_copy(head.data() + got, g_head_pinned, size_t(have - got));
+                crx::parallel_copy(head.data() + got, P.pinned, size_t(have - got));
                 got = have;
                 avail = std::max(avail, got);
             }
@@ -762,7 +798,7 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
             const crx::Status s = crx::parse_head_device_table(head.data(), avail, len, last, &u->u, &nd, &msg);
             if (s == crx::kOk) {
                 const int64_t t0 = u->u.block_table_offset;
-                const int rc = check_device_block_table(&u->u, data + t0, last, st, &msg);
+                const int rc = check_device_block_table(P, &u->u, data + t0, last, st, &msg);
                 if (rc != CRX_OK) {
                     delete u;
                     keep();
@@ -790,11 +826,11 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
                 const int64_t w1 = std::min(len, t1 + 16);
                 if (w1 <= avail) return CRX_CUDA_ERROR;   // no progress: cannot happen
                 if (!stage(size_t(w1 - t1))) return CRX_CUDA_ERROR;
-                if (cudaMemcpyAsync(g_head_pinned, data + t1, size_t(w1 - t1), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+                if (cudaMemcpyAsync(P.pinned, data + t1, size_t(w1 - t1), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
                     cudaStreamSynchronize(st) != cudaSuccess)
                     return CRX_CUDA_ERROR;
                 if (head.size() < size_t(w1)) head.resize(size_t(w1));
-                std::memcpy(head.data() + t1, g_head_pinned, size_t(w1 - t1));
+                std::memcpy(head.data() + t1, P.pinned, size_t(w1 - t1));
                 avail = w1;
                 continue;
             }

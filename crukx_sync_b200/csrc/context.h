@@ -22,6 +22,10 @@ struct DevBuf {
 
 struct Ctx;
 
+// Counts one device or pinned-host allocation or free made by this library (process-wide; read by
+// crx_alloc_calls, so tests can check that an entry point allocates nothing).
+void note_alloc();
+
 // Grow `buf` to at least `bytes` (contents not preserved).  Synchronizes `s` before freeing.
 cudaError_t ensure_dev(DevBuf& buf, size_t bytes, cudaStream_t s);
 cudaError_t ensure_host(Ctx& c, size_t bytes, cudaStream_t s);
@@ -94,6 +98,9 @@ struct Ctx {
         DevBuf rows;   // [super-tiles of the tensor][256] u32
     };
     std::unordered_map<uintptr_t, HistEntry> hist_cache;
+    // rows of evicted entries, reused by capacity for new ones: apply never calls cudaFree, which
+    // would synchronize the whole device (freed only with the context)
+    std::vector<DevBuf> hist_free;
     uint64_t hist_hits = 0;   // tensors whose histogram pass was skipped
     DevBuf hstore_table;      // pinned: the table of the last histogram store, read by an async copy
     cudaEvent_t hstore_ev = nullptr;   // recorded after that copy

@@ -79,11 +79,27 @@ int fail(char* err, size_t errlen, int status, const char* msg, cudaError_t e = 
     return status;
 }
 
+// true when p is memory a kernel on device `dev` can use as plain device memory: allocated on that
+// device, or managed.  cudaPointerGetAttributes looks the pointer up and allocates nothing.
+bool on_device(const void* p, int dev) {
+    cudaPointerAttributes a{};
+    if (cudaPointerGetAttributes(&a, p) != cudaSuccess) {
+        cudaGetLastError();   // an unknown pointer is an argument error, not a sticky one
+        return false;
+    }
+    return a.type == cudaMemoryTypeManaged || (a.type == cudaMemoryTypeDevice && a.device == dev);
+}
+
 }  // namespace
 
 extern "C" int crx_checksum_noalloc(const int16_t* data, int64_t n, void* stream, uint64_t* out, char* err,
                                     size_t errlen) {
     if (n < 0 || (n && !data) || !out) return fail(err, errlen, CRX_BAD_ARGUMENT, "null pointer or negative size");
+    // a misaligned or host pointer would make the kernels fault (a sticky error for the whole
+    // context), so both are rejected here, before anything is launched
+    if (reinterpret_cast<uintptr_t>(out) & 7) return fail(err, errlen, CRX_BAD_ARGUMENT, "out is not 8-byte aligned");
+    if (n && (reinterpret_cast<uintptr_t>(data) & 1))
+        return fail(err, errlen, CRX_BAD_ARGUMENT, "data is not 2-byte aligned");
     if (n > CRX_CHECKSUM_NOALLOC_MAX) {
         char msg[160];
         std::snprintf(msg, sizeof msg, "%lld elements exceed the limit of %lld (a fixed %d KiB scratch); use crx_checksum",
@@ -95,6 +111,9 @@ extern "C" int crx_checksum_noalloc(const int16_t* data, int64_t n, void* stream
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return fail(err, errlen, CRX_CUDA_ERROR, "cudaGetDevice", e);
     if (dev < 0 || dev >= kMaxDevices) return fail(err, errlen, CRX_BAD_ARGUMENT, "device index out of range");
+    if (!on_device(out, dev)) return fail(err, errlen, CRX_BAD_ARGUMENT, "out is not device memory of the current device");
+    if (n && !on_device(data, dev))
+        return fail(err, errlen, CRX_BAD_ARGUMENT, "data is not device memory of the current device");
     unsigned long long* partials;
     {
         std::lock_guard<std::mutex> g(g_setup_mu);

@@ -48,6 +48,10 @@ int crx_ctx_create(int device, crx_ctx** out, char* err, size_t errlen);
 void crx_ctx_destroy(crx_ctx* ctx);
 /* Kernels launched by this context so far (no reference counterpart: instrumentation). */
 uint64_t crx_ctx_launches(crx_ctx* ctx);
+/* Device and pinned-host allocations and frees this library has made so far, process-wide
+ * (instrumentation, no reference counterpart): a test reads it around calls of an entry point that
+ * must allocate nothing. */
+uint64_t crx_alloc_calls(void);
 /* Kernels launched by crx_parse_device (its block-table check), process-wide: crx_parse_device
  * takes no context, so these are not in crx_ctx_launches. */
 uint64_t crx_parse_device_launches(void);
@@ -198,9 +202,10 @@ int crx_checksum(crx_ctx* ctx, const int16_t* data, int64_t n, void* stream, uin
  * KV-cache (a cudaMalloc in steady state fails or breaks the budget), code inside an allocator
  * callback or out-of-memory handler (re-entering the allocator can deadlock), or a loop that must
  * not stall other streams (cudaFree synchronizes the device).  It needs no crx_ctx, allocates
- * nothing and does not synchronize: data (n int16 elements) and out (8 bytes, 8-byte aligned)
- * are device memory on the current device, and the result is in *out once the work on `stream`
- * is done.
+ * nothing and does not synchronize: data (n int16 elements, 2-byte aligned) and out (8 bytes,
+ * 8-byte aligned) are device memory on the current device (or managed memory), and the result is
+ * in *out once the work on `stream` is done.  A misaligned pointer, or one that is not device
+ * memory of the current device, returns CRX_BAD_ARGUMENT before anything is launched.
  *
  * Limit: n <= CRX_CHECKSUM_NOALLOC_MAX (2^30 elements); larger n returns CRX_VALUE_ERROR — use
  * crx_checksum.  Its scratch is one fixed 128 KiB device array per device: the first call on a

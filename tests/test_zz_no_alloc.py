@@ -11,7 +11,7 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
-CRX_OK, CRX_VALUE_ERROR = 0, 1
+CRX_OK, CRX_VALUE_ERROR, CRX_BAD_ARGUMENT = 0, 1, 5
 LIMIT = 1 << 30
 
 
@@ -93,9 +93,54 @@ def test_no_device_memory_is_allocated(lib):
     out = torch.zeros(1, dtype=torch.int64, device="cuda")
     assert noalloc(lib, x, out)[0] == CRX_OK          # set-up done on this device
     torch.cuda.synchronize()
-    free0, _ = torch.cuda.mem_get_info()
+    calls0 = lib.crx_alloc_calls()                    # every allocation and free the library makes
+    alloc0, reserved0 = torch.cuda.memory_allocated(), torch.cuda.memory_reserved()
     for _ in range(3):
         assert noalloc(lib, x, out)[0] == CRX_OK
     torch.cuda.synchronize()
-    free1, _ = torch.cuda.mem_get_info()
-    assert free1 == free0
+    assert lib.crx_alloc_calls() == calls0
+    assert torch.cuda.memory_allocated() == alloc0 and torch.cuda.memory_reserved() == reserved0
+
+
+def test_the_counter_sees_allocations(lib):
+    """crx_alloc_calls is not blind: the context-based checksum's first call on a fresh context grows
+    its workspace."""
+    h = ctypes.c_void_p()
+    err = ctypes.create_string_buffer(256)
+    before = lib.crx_alloc_calls()
+    assert lib.crx_ctx_create(torch.cuda.current_device(), ctypes.byref(h), err, 256) == CRX_OK, err.value
+    try:
+        x = tensor(4096, 5)
+        out = ctypes.c_uint64()
+        st = lib.crx_checksum(h, ctypes.c_void_p(x.data_ptr()), x.numel(),
+                              ctypes.c_void_p(torch.cuda.current_stream().cuda_stream), ctypes.byref(out), err, 256)
+        assert st == CRX_OK, err.value
+        assert lib.crx_alloc_calls() > before
+        assert out.value == with_ctx(lib, x)
+    finally:
+        lib.crx_ctx_destroy(h)
+
+
+def test_bad_pointers_are_rejected_before_any_launch(lib):
+    """A misaligned out or data, or a host out, would fault the kernels and lose the context: each
+    returns CRX_BAD_ARGUMENT and nothing runs (the result buffer keeps its contents)."""
+    x = tensor(10_000, 4)
+    raw = torch.full((4,), 7, dtype=torch.int64, device="cuda")
+    misaligned = ctypes.c_void_p(raw.data_ptr() + 4)          # 4-byte aligned only
+    err = ctypes.create_string_buffer(256)
+    stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    st = lib.crx_checksum_noalloc(ctypes.c_void_p(x.data_ptr()), x.numel(), stream, misaligned, err, 256)
+    assert st == CRX_BAD_ARGUMENT and b"aligned" in err.value
+    host_out = ctypes.c_uint64(123)                          # the context-based call's host out
+    st = lib.crx_checksum_noalloc(ctypes.c_void_p(x.data_ptr()), x.numel(), stream, ctypes.byref(host_out), err, 256)
+    assert st == CRX_BAD_ARGUMENT and b"device memory" in err.value
+    assert host_out.value == 123
+    odd = ctypes.c_void_p(x.data_ptr() + 1)                  # an int16 pointer at an odd byte
+    st = lib.crx_checksum_noalloc(odd, 100, stream, ctypes.c_void_p(raw.data_ptr()), err, 256)
+    assert st == CRX_BAD_ARGUMENT and b"aligned" in err.value
+    host_data = torch.zeros(100, dtype=torch.int16)          # pageable host memory as data
+    st = lib.crx_checksum_noalloc(ctypes.c_void_p(host_data.data_ptr()), 100, stream, ctypes.c_void_p(raw.data_ptr()),
+                                  err, 256)
+    assert st == CRX_BAD_ARGUMENT and b"device memory" in err.value
+    torch.cuda.synchronize()
+    assert raw.tolist() == [7, 7, 7, 7]
