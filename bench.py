@@ -242,6 +242,36 @@ def time_oracle(prev, cur, steps=1, threads=None, warmup=0):
     return sum(times) / len(times), threads
 
 
+def parity_check(A, B, threads):
+    """The first step's update (no caches) through encode_update_device, against the CPU oracle's
+    whole-dict update of the same state: SHA-256 of both.  Run once, outside the timed region.
+    Raises when they differ: a wrong encoder produces no bench line."""
+    import hashlib
+
+    import psutil
+
+    import crukx_sync_b200 as crx
+    from oracle import oracle
+    need = 2.6 * sum(v.numel() * 2 for v in A.values())   # host copies of both states + the oracle's lists
+    if psutil.virtual_memory().available < need:
+        return {"checked": False, "why": "not enough free host memory for the oracle"}
+    t0 = time.perf_counter()
+    dev_upd = crx.encode_update_device(A, B, None)
+    ours = dev_upd.cpu().numpy().tobytes()
+    del dev_upd
+    hA = {k: v.cpu() for k, v in A.items()}
+    hB = {k: v.cpu() for k, v in B.items()}
+    oracle.set_threads(threads)
+    want = oracle.encode_update(hA, hB)
+    del hA, hB
+    a, b = hashlib.sha256(ours).hexdigest(), hashlib.sha256(want).hexdigest()
+    if (len(ours), a) != (len(want), b):
+        raise AssertionError(f"update differs from the CPU oracle: {len(ours)} B {a[:16]} vs {len(want)} B {b[:16]}")
+    return {"checked": True, "sha256": a, "bytes": len(ours), "result": "sha256 matches oracle",
+            "what": "first update of this rank's tensors (no caches) vs the CPU oracle's whole-dict update of the "
+                    "same state", "oracle_threads": threads, "seconds": round(time.perf_counter() - t0, 1)}
+
+
 def log(*a):
     if os.environ.get("CRUKX_B200_TRACE"):
         print(f"[bench {time.strftime('%H:%M:%S')}]", *a, file=sys.stderr, flush=True)
@@ -266,6 +296,11 @@ def run_ours(args, rank, world, dist):
     A, B = make_states(shapes, cfg["lr"], dev, seed=0)
     log("generated")
     changed = sum(int((A[k].view(torch.int16) != B[k].view(torch.int16)).sum()) for k in A)
+    parity = None
+    if not args.no_parity:
+        log("parity check against the oracle")
+        parity = parity_check(A, B, max(1, host_threads() // max(world, 1)))
+        log("parity", parity)
     recv = {k: v.clone() for k, v in A.items()}
     sender, receiver = {}, {}
     ctx = _ext.context(dev.index)
@@ -440,7 +475,7 @@ def run_ours(args, rank, world, dist):
         "update_bytes": int(upd_bytes), "bytes_per_changed": round(upd_bytes / max(changed_all, 1), 4),
         "wall_s_timed": round(t_wall, 3),
         "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e, "bytes_api": bytes_api,
-        "gpu_launches": launches, "clocks": clk.summary(),
+        "gpu_launches": launches, "clocks": clk.summary(), "parity": parity,
     }
     return result
 
@@ -521,6 +556,7 @@ def main():
     ap.add_argument("--no-bytes-api", action="store_true", help="skip the host-bytes API measurement")
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the first update")
     ap.add_argument("--cpu-sample", type=int, default=1_000_000_000, help="elements in the CPU-baseline sample")
     ap.add_argument("--ref-sample", type=int, default=1_000_000_000, help="elements per reference-arm step")
     args = ap.parse_args()

@@ -21,8 +21,13 @@
  *
  * Status codes: 0 ok, 1 ValueError, 2 CorruptUpdate, 3 internal (allocation) error.
  */
+#define _GNU_SOURCE
+#include <pthread.h>
+#include <sched.h>
+#include <stdatomic.h>
 #include <stdint.h>
 #include <stdlib.h>
+#include <unistd.h>
 #include <string.h>
 #include <stdio.h>
 #include <math.h>
@@ -40,6 +45,44 @@
 
 static void set_err(char *err, size_t n, const char *msg) {
     if (err && n) { snprintf(err, n, "%s", msg); }
+}
+
+/* Threads of the per-tensor and per-exponent passes (0 = every processor this process may run
+ * on).  The passes split independent tensors or exponents only, so the bytes never depend on it. */
+static int g_threads = 0;
+void orc_set_threads(int n) { g_threads = n > 0 ? n : 0; }
+static int orc_threads(void) {
+    if (g_threads) return g_threads;
+    cpu_set_t set;
+    if (sched_getaffinity(0, sizeof(set), &set) == 0) return CPU_COUNT(&set) > 0 ? CPU_COUNT(&set) : 1;
+    long n = sysconf(_SC_NPROCESSORS_ONLN);
+    return n > 0 ? (int)n : 1;
+}
+
+/* fn(ctx, i) for i in [0, n) on up to orc_threads() threads, indices handed out one at a time */
+typedef void (*orc_task_fn)(void *ctx, int64_t i);
+typedef struct { orc_task_fn fn; void *ctx; int64_t n; atomic_llong next; } pfor_t;
+static void *pfor_worker(void *arg) {
+    pfor_t *p = arg;
+    for (;;) {
+        int64_t i = atomic_fetch_add(&p->next, 1);
+        if (i >= p->n) break;
+        p->fn(p->ctx, i);
+    }
+    return NULL;
+}
+static void parallel_for(int64_t n, orc_task_fn fn, void *ctx) {
+    int nt = orc_threads();
+    if (nt > 256) nt = 256;
+    if (n < nt) nt = (int)n;
+    pfor_t p = {fn, ctx, n, 0};
+    atomic_init(&p.next, 0);
+    pthread_t th[256];
+    int started = 0;
+    for (int k = 1; k < nt; k++)
+        if (pthread_create(&th[started], NULL, pfor_worker, &p) == 0) started++;
+    pfor_worker(&p);   /* this thread works too; with no extra thread it does everything */
+    for (int k = 0; k < started; k++) pthread_join(th[k], NULL);
 }
 
 /* ------------------------------------------------------------------ checksum (FORMAT.md:59-68) */
@@ -269,6 +312,102 @@ static void free_tstate(tstate_t *ts, int n) {
     free(ts);
 }
 
+typedef struct {
+    tstate_t *ts;
+    etab_t *tabs;
+    const int16_t *const *prev, *const *cur;
+    const int64_t *numel;
+    const uint64_t *cache_chk;
+    const uint8_t *has_cache;
+    uint64_t *new_chk;
+    uint8_t *chk_present;
+    int n;
+    bits_t *tbits;
+    const int64_t *tblock;
+    uint32_t *block_bits;
+    atomic_int fail, too_long;
+} enc_ctx_t;
+
+/* pass 1 for tensor t: its changes per old exponent, the new checksum, the Rice parameters */
+static void enc_pass1(void *vc, int64_t t) {
+    enc_ctx_t *c = vc;
+    tstate_t *ts = &c->ts[t];
+    c->chk_present[t] = 0;
+    ts->numel = c->numel[t];
+    int64_t counter[256] = {0};
+    const int16_t *a = c->prev[t], *b = c->cur[t];
+    for (int64_t i = 0; i < c->numel[t]; i++) {
+        int e = ((uint16_t)a[i] >> 7) & 0xFF;
+        if (a[i] != b[i]) {
+            if (group_push(&ts->g[e], counter[e], a[i], b[i])) { atomic_store(&c->fail, 1); return; }
+            ts->present = 1;
+        }
+        counter[e]++;
+    }
+    if (!ts->present) return;
+    /* checksum of the new tensor: cached + delta, else a full pass (codec.py:344-352) */
+    uint64_t chk;
+    if (c->has_cache && c->has_cache[t]) {
+        uint64_t d = 0;
+        for (int64_t i = 0; i < c->numel[t]; i++)
+            if (a[i] != b[i])
+                d += ((uint64_t)(uint16_t)b[i] - (uint64_t)(uint16_t)a[i]) * splitmix_weight((uint64_t)i);
+        chk = c->cache_chk[t] + d;
+    } else {
+        chk = orc_checksum(b, c->numel[t]);
+    }
+    c->new_chk[t] = chk;
+    c->chk_present[t] = 1;
+    for (int e = 0; e < 256; e++) {
+        group_t *g = &ts->g[e];
+        g->exp = e;
+        if (g->count) g->rice = rice_param(g);
+    }
+}
+
+/* pass 2 for exponent e: its symbol counts over every tensor of the update */
+static void enc_pass2(void *vc, int64_t e) {
+    enc_ctx_t *c = vc;
+    for (int t = 0; t < c->n; t++) {
+        if (!c->ts[t].present) continue;
+        const group_t *g = &c->ts[t].g[e];
+        if (!g->count) continue;
+        if (!c->tabs[e].count) {
+            c->tabs[e].count = calloc(SYM_SPACE, sizeof(uint64_t));
+            if (!c->tabs[e].count) { atomic_store(&c->fail, 1); return; }
+        }
+        for (int64_t j = 0; j < g->count; j++) c->tabs[e].count[zigzag_res(g->va[j], g->vb[j])]++;
+    }
+}
+
+/* pass 3 for tensor t: its bits from bit 0 of its own buffer, its blocks' bit counts */
+static void enc_pass3(void *vc, int64_t t) {
+    enc_ctx_t *c = vc;
+    bits_t *tw = &c->tbits[t];
+    int64_t bi = c->tblock[t];
+    for (int e = 0; e < 256; e++) {
+        const group_t *g = &c->ts[t].g[e];
+        if (!g->count) continue;
+        const etab_t *tb = &c->tabs[e];
+        for (int64_t k0 = 0; k0 < g->count; k0 += BLOCK) {
+            uint64_t start = tw->nbits;
+            int64_t k1 = k0 + BLOCK < g->count ? k0 + BLOCK : g->count;
+            for (int64_t j = k0; j < k1; j++) {
+                uint64_t gap = (uint64_t)gap_at(g, j);
+                uint64_t q = gap >> g->rice;
+                bits_ones(tw, q);
+                bits_put(tw, 0, 1);
+                if (g->rice) bits_put(tw, gap & ((1ULL << g->rice) - 1), g->rice);
+                uint32_t z = zigzag_res(g->va[j], g->vb[j]);
+                bits_put(tw, tb->code[z], tb->len[z]);
+            }
+            uint64_t nb = tw->nbits - start;
+            if (nb >= (1ULL << 32)) atomic_store(&c->too_long, 1);
+            c->block_bits[bi++] = (uint32_t)nb;
+        }
+    }
+}
+
 /*
  * Encode n tensors (old = prev[t], new = cur[t], numel[t] elements, names[t] of name_len[t]
  * bytes).  cache_chk/has_cache: the sender's cached checksum of prev[t] (codec.py:345-352).
@@ -286,53 +425,20 @@ int orc_encode(int n, const int16_t *const *prev, const int16_t *const *cur, con
     int status = ORC_NOMEM;
     buf_t b = {0};
     bits_t w = {0};
+    bits_t *tbits = NULL;
     uint32_t *block_bits = NULL;
     if (!ts || !tabs) goto done;
 
-    /* pass 1: changed elements per (tensor, old exponent) in index order = stable rank order */
-    for (int t = 0; t < n; t++) {
-        chk_present[t] = 0;
-        ts[t].numel = numel[t];
-        int64_t counter[256] = {0};
-        const int16_t *a = prev[t], *c = cur[t];
-        for (int64_t i = 0; i < numel[t]; i++) {
-            int e = ((uint16_t)a[i] >> 7) & 0xFF;
-            if (a[i] != c[i]) {
-                if (group_push(&ts[t].g[e], counter[e], a[i], c[i])) goto done;
-                ts[t].present = 1;
-            }
-            counter[e]++;
-        }
-        if (!ts[t].present) continue;
-        /* checksum of the new tensor: cached + delta, else a full pass (codec.py:344-352) */
-        uint64_t chk;
-        if (has_cache && has_cache[t]) {
-            uint64_t d = 0;
-            for (int64_t i = 0; i < numel[t]; i++)
-                if (a[i] != c[i])
-                    d += ((uint64_t)(uint16_t)c[i] - (uint64_t)(uint16_t)a[i]) * splitmix_weight((uint64_t)i);
-            chk = cache_chk[t] + d;
-        } else {
-            chk = orc_checksum(c, numel[t]);
-        }
-        new_chk[t] = chk; chk_present[t] = 1;
-        for (int e = 0; e < 256; e++) {
-            group_t *g = &ts[t].g[e];
-            g->exp = e;
-            if (g->count) g->rice = rice_param(g);
-        }
-    }
+    /* pass 1: changed elements per (tensor, old exponent) in index order = stable rank order.
+     * Tensors are independent until the Huffman tables: one task per tensor. */
+    enc_ctx_t ec = {ts, tabs, prev, cur, numel, cache_chk, has_cache, new_chk, chk_present, n, NULL, NULL, NULL, 0, 0};
+    parallel_for(n, enc_pass1, &ec);
+    if (ec.fail) goto done;
 
-    /* pass 2: one Huffman table per exponent over the whole update (codec.py:355-392) */
-    for (int t = 0; t < n; t++) {
-        if (!ts[t].present) continue;
-        for (int e = 0; e < 256; e++) {
-            group_t *g = &ts[t].g[e];
-            if (!g->count) continue;
-            if (!tabs[e].count) { tabs[e].count = calloc(SYM_SPACE, sizeof(uint64_t)); if (!tabs[e].count) goto done; }
-            for (int64_t j = 0; j < g->count; j++) tabs[e].count[zigzag_res(g->va[j], g->vb[j])]++;
-        }
-    }
+    /* pass 2: one Huffman table per exponent over the whole update (codec.py:355-392); the
+     * exponents are independent: one task per exponent */
+    parallel_for(256, enc_pass2, &ec);
+    if (ec.fail) goto done;
     for (int e = 0; e < 256; e++) {
         etab_t *tb = &tabs[e];
         if (!tb->count) continue;
@@ -354,39 +460,51 @@ int orc_encode(int n, const int16_t *const *prev, const int16_t *const *cur, con
         free(cnt); free(ln); free(cd);
     }
 
-    /* pass 3: bits, in (tensor, group, element) order; block sizes per 256-run of a group */
+    /* pass 3: bits, in (tensor, group, element) order; block sizes per 256-run of a group.  Each
+     * tensor's bits are written by one task into its own buffer from bit 0; the buffers are then
+     * joined in tensor order at their running bit offsets (the reference's carry, codec.py:405-410). */
     int64_t n_blocks = 0;
-    for (int t = 0; t < n; t++)
-        for (int e = 0; e < 256; e++) n_blocks += (ts[t].g[e].count + BLOCK - 1) / BLOCK;
-    block_bits = malloc(sizeof(uint32_t) * (n_blocks ? n_blocks : 1));
-    if (!block_bits) goto done;
-    int64_t bi = 0;
+    int64_t *tblock = calloc((size_t)n + 1, sizeof(int64_t));   /* first block of each tensor */
+    tbits = calloc(n > 0 ? (size_t)n : 1, sizeof(bits_t));
+    if (!tblock || !tbits) { free(tblock); goto done; }
     for (int t = 0; t < n; t++) {
-        for (int e = 0; e < 256; e++) {
-            group_t *g = &ts[t].g[e];
-            if (!g->count) continue;
-            const etab_t *tb = &tabs[e];
-            for (int64_t k0 = 0; k0 < g->count; k0 += BLOCK) {
-                uint64_t start = w.nbits;
-                int64_t k1 = k0 + BLOCK < g->count ? k0 + BLOCK : g->count;
-                for (int64_t j = k0; j < k1; j++) {
-                    uint64_t gap = (uint64_t)gap_at(g, j);
-                    uint64_t q = gap >> g->rice;
-                    bits_ones(&w, q);
-                    bits_put(&w, 0, 1);
-                    if (g->rice) bits_put(&w, gap & ((1ULL << g->rice) - 1), g->rice);
-                    uint32_t z = zigzag_res(g->va[j], g->vb[j]);
-                    bits_put(&w, tb->code[z], tb->len[z]);
+        tblock[t] = n_blocks;
+        for (int e = 0; e < 256; e++) n_blocks += (ts[t].g[e].count + BLOCK - 1) / BLOCK;
+    }
+    tblock[n] = n_blocks;
+    block_bits = malloc(sizeof(uint32_t) * (n_blocks ? n_blocks : 1));
+    if (!block_bits) { free(tblock); goto done; }
+    ec.tbits = tbits;
+    ec.tblock = tblock;
+    ec.block_bits = block_bits;
+    parallel_for(n, enc_pass3, &ec);
+    const int too_long = ec.too_long;
+    free(tblock);
+    for (int t = 0; t < n; t++) if (tbits[t].fail) goto done;
+    if (too_long) {
+        status = ORC_VALUE;
+        set_err(err, errlen, "a block exceeds 2^32 bits; the update cannot be represented");
+        goto done;
+    }
+    {   /* join: tensor t's bits start at bit w.nbits of the whole payload */
+        uint64_t total = 0;
+        for (int t = 0; t < n; t++) total += tbits[t].nbits;
+        bits_reserve(&w, total);
+        if (w.fail) goto done;
+        for (int t = 0; t < n; t++) {
+            const bits_t *tw = &tbits[t];
+            uint64_t nbytes = (tw->nbits + 7) / 8;
+            uint64_t at = w.nbits >> 3;
+            int sh = (int)(w.nbits & 7);
+            if (sh == 0) {
+                if (nbytes) memcpy(w.p + at, tw->p, nbytes);
+            } else {
+                for (uint64_t k = 0; k < nbytes; k++) {
+                    w.p[at + k] |= (uint8_t)(tw->p[k] >> sh);
+                    w.p[at + k + 1] |= (uint8_t)(tw->p[k] << (8 - sh));
                 }
-                if (w.fail) goto done;
-                uint64_t nb = w.nbits - start;
-                if (nb >= (1ULL << 32)) {
-                    status = ORC_VALUE;
-                    set_err(err, errlen, "a block exceeds 2^32 bits; the update cannot be represented");
-                    goto done;
-                }
-                block_bits[bi++] = (uint32_t)nb;
             }
+            w.nbits += tw->nbits;
         }
     }
 
@@ -433,6 +551,7 @@ int orc_encode(int n, const int16_t *const *prev, const int16_t *const *cur, con
 done:
     if (status == ORC_NOMEM) set_err(err, errlen, "oracle: out of memory");
     free(b.p); free(w.p); free(block_bits);
+    if (tbits) { for (int t = 0; t < n; t++) free(tbits[t].p); free(tbits); }
     free_tstate(ts, n);
     if (tabs) for (int e = 0; e < 256; e++) { free(tabs[e].count); free(tabs[e].code); free(tabs[e].len); free(tabs[e].syms); }
     free(tabs);
@@ -688,6 +807,125 @@ static inline uint64_t read_bits(const uint8_t *p, int64_t nbytes, uint64_t pos,
     return v;
 }
 
+typedef struct {
+    pupdate_t *u;
+    int16_t *const *weights;
+    const uint64_t *old_chk;
+    const uint8_t *has_chk;
+    const dtab_t *dt;
+    const int *tab_of;
+    const int64_t *tb0;
+    const uint64_t *tbit0;
+    int64_t **pos;
+    int16_t **val;
+    int *tbad;
+    int64_t *tchanged;
+    atomic_int nomem;
+} app_ctx_t;
+
+/* decode, place and verify tensor t (nothing is written to the weights here) */
+static void app_tensor(void *vc, int64_t t) {
+    app_ctx_t *c = vc;
+    pupdate_t *u = c->u;
+    int bad = 0;
+    uint64_t bitpos = c->tbit0[t];
+    int64_t b = c->tb0[t];
+    ptensor_t *h = &u->tens[t];
+    const int16_t *a = c->weights[t];
+    int64_t size[256] = {0};
+    for (int64_t i = 0; i < h->numel; i++) size[((uint16_t)a[i] >> 7) & 0xFF]++;
+    int64_t tot = 0;
+    for (int k = 0; k < h->ng; k++) tot += h->g[k].count;
+    c->pos[t] = malloc(sizeof(int64_t) * (tot ? tot : 1));
+    c->val[t] = malloc(sizeof(int16_t) * (tot ? tot : 1));
+    int64_t *local = malloc(sizeof(int64_t) * (tot ? tot : 1));
+    uint32_t *zz = malloc(sizeof(uint32_t) * (tot ? tot : 1));
+    int *gexp = malloc(sizeof(int) * (tot ? tot : 1));
+    if (!c->pos[t] || !c->val[t] || !local || !zz || !gexp) {
+        free(local); free(zz); free(gexp);
+        atomic_store(&c->nomem, 1);
+        return;
+    }
+    int64_t o = 0;
+    for (int k = 0; k < h->ng && !bad; k++) {
+        pgroup_t *g = &h->g[k];
+        const dtab_t *d = &c->dt[c->tab_of[g->exp]];
+        int64_t gsize = size[g->exp];
+        uint64_t qmax = (uint64_t)gsize >> g->rice;
+        int64_t prev_local = -1;
+        for (int64_t j0 = 0; j0 < g->count && !bad; j0 += BLOCK, b++) {
+            uint64_t cur = bitpos, end = bitpos + u->block_bits[b];
+            bitpos = end;
+            int64_t j1 = j0 + BLOCK < g->count ? j0 + BLOCK : g->count;
+            for (int64_t j = j0; j < j1; j++) {
+                if (cur >= end) { bad = 1; break; }
+                /* unary run, bounded by the block's own end and by qmax (_triton.py:54-62) */
+                uint64_t q = 0;
+                while (bit_at(u->payload, u->payload_len, cur + q)) {
+                    q++;
+                    if (q > qmax || cur + q >= end) break;
+                }
+                if (q > qmax || cur + q >= end) { bad = 1; break; }
+                uint64_t c = cur + q + 1;
+                uint64_t rem = g->rice ? read_bits(u->payload, u->payload_len, c, g->rice) : 0;
+                uint64_t peek = read_bits(u->payload, u->payload_len, c + g->rice, MAX_CODE_LEN);
+                int L = 0;
+                for (int ln = 1; ln <= MAX_CODE_LEN; ln++) {
+                    uint64_t code = peek >> (MAX_CODE_LEN - ln);
+                    if (code >= d->first[ln] && code < d->first[ln] + d->cnt[ln]) { L = ln; break; }
+                }
+                if (!L) { bad = 1; break; }
+                uint64_t code = peek >> (MAX_CODE_LEN - L);
+                int64_t sym = d->sorted[d->base[L] + code - d->first[L]];
+                uint64_t gap = (q << g->rice) | rem;
+                if ((int64_t)gap >= gsize) { bad = 1; break; }
+                int64_t loc = prev_local + (int64_t)gap + 1;
+                if (loc >= gsize) { bad = 1; break; }
+                prev_local = loc;
+                local[o] = loc; zz[o] = (uint32_t)sym; gexp[o] = g->exp; o++;
+                cur = c + g->rice + L;
+            }
+            if (!bad && cur != end) bad = 1;
+        }
+    }
+    if (!bad) {
+        /* (exponent, rank) -> position: one walk with running counters (codec.py:636-694) */
+        int64_t counter[256] = {0};
+        int64_t ptr[256], gend[256], gbeg[256];
+        for (int e = 0; e < 256; e++) { ptr[e] = -1; gend[e] = -1; }
+        int64_t oo = 0;
+        for (int k = 0; k < h->ng; k++) { gbeg[h->g[k].exp] = oo; ptr[h->g[k].exp] = oo; oo += h->g[k].count; gend[h->g[k].exp] = oo; }
+        uint64_t delta = 0;
+        for (int64_t i = 0; i < h->numel; i++) {
+            int e = ((uint16_t)a[i] >> 7) & 0xFF;
+            if (ptr[e] >= 0 && ptr[e] < gend[e] && local[ptr[e]] == counter[e]) {
+                int64_t j = ptr[e]++;
+                uint32_t z = zz[j];
+                int64_t res = (int64_t)(z >> 1) ^ -(int64_t)(z & 1);
+                uint64_t old_u = (uint16_t)a[i];
+                uint64_t new_u = (old_u + (uint64_t)res) & 0xFFFF;
+                delta += (new_u - old_u) * splitmix_weight((uint64_t)i);
+                c->pos[t][j] = i; c->val[t][j] = (int16_t)(uint16_t)new_u;
+            }
+            counter[e]++;
+        }
+        (void)gbeg;
+        uint64_t base = (c->has_chk && c->has_chk[t]) ? c->old_chk[t] : orc_checksum(a, h->numel);
+        if (base + delta != h->chk) { bad = 2; }
+    }
+    free(local); free(zz); free(gexp);
+    c->tbad[t] = bad;
+    c->tchanged[t] = tot;
+}
+
+/* the verified changes of tensor t into its weights */
+static void app_commit(void *vc, int64_t t) {
+    app_ctx_t *c = vc;
+    int64_t tot = 0;
+    for (int k = 0; k < c->u->tens[t].ng; k++) tot += c->u->tens[t].g[k].count;
+    for (int64_t j = 0; j < tot; j++) c->weights[t][c->pos[t][j]] = c->val[t][j];
+}
+
 /*
  * Apply a parsed update.  weights[t] / old_chk[t] / has_chk[t] are given per update tensor
  * (the caller matched names and numel).  Writes nothing unless every block decodes exactly,
@@ -707,91 +945,35 @@ int orc_apply(void *handle, int16_t *const *weights, const uint64_t *old_chk, co
     if (!dt || !pos || !val) goto done;
     for (int t = 0; t < u->n_tables; t++) { tab_of[u->tab[t].exp] = t; if (build_dtab(&u->tab[t], &dt[t])) goto done; }
 
-    uint64_t bitpos = 0;   /* blocks are consecutive in the payload (FORMAT.md:39-44) */
-    int64_t b = 0;
-    for (int64_t t = 0; t < u->n_tensors && !bad; t++) {
-        ptensor_t *h = &u->tens[t];
-        const int16_t *a = weights[t];
-        int64_t size[256] = {0};
-        for (int64_t i = 0; i < h->numel; i++) size[((uint16_t)a[i] >> 7) & 0xFF]++;
-        int64_t tot = 0;
-        for (int k = 0; k < h->ng; k++) tot += h->g[k].count;
-        pos[t] = malloc(sizeof(int64_t) * (tot ? tot : 1));
-        val[t] = malloc(sizeof(int16_t) * (tot ? tot : 1));
-        int64_t *local = malloc(sizeof(int64_t) * (tot ? tot : 1));
-        uint32_t *zz = malloc(sizeof(uint32_t) * (tot ? tot : 1));
-        int *gexp = malloc(sizeof(int) * (tot ? tot : 1));
-        if (!pos[t] || !val[t] || !local || !zz || !gexp) { free(local); free(zz); free(gexp); goto done; }
-        int64_t o = 0;
-        for (int k = 0; k < h->ng && !bad; k++) {
-            pgroup_t *g = &h->g[k];
-            const dtab_t *d = &dt[tab_of[g->exp]];
-            int64_t gsize = size[g->exp];
-            uint64_t qmax = (uint64_t)gsize >> g->rice;
-            int64_t prev_local = -1;
-            for (int64_t j0 = 0; j0 < g->count && !bad; j0 += BLOCK, b++) {
-                uint64_t cur = bitpos, end = bitpos + u->block_bits[b];
-                bitpos = end;
-                int64_t j1 = j0 + BLOCK < g->count ? j0 + BLOCK : g->count;
-                for (int64_t j = j0; j < j1; j++) {
-                    if (cur >= end) { bad = 1; break; }
-                    /* unary run, bounded by the block's own end and by qmax (_triton.py:54-62) */
-                    uint64_t q = 0;
-                    while (bit_at(u->payload, u->payload_len, cur + q)) {
-                        q++;
-                        if (q > qmax || cur + q >= end) break;
-                    }
-                    if (q > qmax || cur + q >= end) { bad = 1; break; }
-                    uint64_t c = cur + q + 1;
-                    uint64_t rem = g->rice ? read_bits(u->payload, u->payload_len, c, g->rice) : 0;
-                    uint64_t peek = read_bits(u->payload, u->payload_len, c + g->rice, MAX_CODE_LEN);
-                    int L = 0;
-                    for (int ln = 1; ln <= MAX_CODE_LEN; ln++) {
-                        uint64_t code = peek >> (MAX_CODE_LEN - ln);
-                        if (code >= d->first[ln] && code < d->first[ln] + d->cnt[ln]) { L = ln; break; }
-                    }
-                    if (!L) { bad = 1; break; }
-                    uint64_t code = peek >> (MAX_CODE_LEN - L);
-                    int64_t sym = d->sorted[d->base[L] + code - d->first[L]];
-                    uint64_t gap = (q << g->rice) | rem;
-                    if ((int64_t)gap >= gsize) { bad = 1; break; }
-                    int64_t loc = prev_local + (int64_t)gap + 1;
-                    if (loc >= gsize) { bad = 1; break; }
-                    prev_local = loc;
-                    local[o] = loc; zz[o] = (uint32_t)sym; gexp[o] = g->exp; o++;
-                    cur = c + g->rice + L;
-                }
-                if (!bad && cur != end) bad = 1;
+    /* blocks are consecutive in the payload (FORMAT.md:39-44): each tensor's first block and bit,
+     * so that tensors decode independently (one thread per tensor) */
+    int64_t *tb0 = malloc(sizeof(int64_t) * (size_t)(u->n_tensors + 1));
+    uint64_t *tbit0 = malloc(sizeof(uint64_t) * (size_t)(u->n_tensors + 1));
+    int *tbad = calloc((size_t)(u->n_tensors + 1), sizeof(int));
+    int64_t *tchanged = calloc((size_t)(u->n_tensors + 1), sizeof(int64_t));
+    if (!tb0 || !tbit0 || !tbad || !tchanged) { free(tb0); free(tbit0); free(tbad); free(tchanged); goto done; }
+    {
+        int64_t bb = 0;
+        uint64_t bits = 0;
+        for (int64_t t = 0; t < u->n_tensors; t++) {
+            tb0[t] = bb;
+            tbit0[t] = bits;
+            for (int k = 0; k < u->tens[t].ng; k++) {
+                int64_t nbk = (u->tens[t].g[k].count + BLOCK - 1) / BLOCK;
+                for (int64_t q = 0; q < nbk; q++) bits += u->block_bits[bb + q];
+                bb += nbk;
             }
         }
-        if (!bad) {
-            /* (exponent, rank) -> position: one walk with running counters (codec.py:636-694) */
-            int64_t counter[256] = {0};
-            int64_t ptr[256], gend[256], gbeg[256];
-            for (int e = 0; e < 256; e++) { ptr[e] = -1; gend[e] = -1; }
-            int64_t oo = 0;
-            for (int k = 0; k < h->ng; k++) { gbeg[h->g[k].exp] = oo; ptr[h->g[k].exp] = oo; oo += h->g[k].count; gend[h->g[k].exp] = oo; }
-            uint64_t delta = 0;
-            for (int64_t i = 0; i < h->numel; i++) {
-                int e = ((uint16_t)a[i] >> 7) & 0xFF;
-                if (ptr[e] >= 0 && ptr[e] < gend[e] && local[ptr[e]] == counter[e]) {
-                    int64_t j = ptr[e]++;
-                    uint32_t z = zz[j];
-                    int64_t res = (int64_t)(z >> 1) ^ -(int64_t)(z & 1);
-                    uint64_t old_u = (uint16_t)a[i];
-                    uint64_t new_u = (old_u + (uint64_t)res) & 0xFFFF;
-                    delta += (new_u - old_u) * splitmix_weight((uint64_t)i);
-                    pos[t][j] = i; val[t][j] = (int16_t)(uint16_t)new_u;
-                }
-                counter[e]++;
-            }
-            (void)gbeg;
-            uint64_t base = (has_chk && has_chk[t]) ? old_chk[t] : orc_checksum(a, h->numel);
-            if (base + delta != h->chk) { bad = 2; }
-        }
-        free(local); free(zz); free(gexp);
-        *changed += tot;
     }
+    app_ctx_t ac = {u, weights, old_chk, has_chk, dt, tab_of, tb0, tbit0, pos, val, tbad, tchanged, 0};
+    parallel_for(u->n_tensors, app_tensor, &ac);
+    const int nomem = ac.nomem;
+    for (int64_t t = 0; t < u->n_tensors; t++) {   /* a decode or range error outranks a checksum one */
+        if (tbad[t] == 1 || (tbad[t] == 2 && bad == 0)) bad = tbad[t];
+        *changed += tchanged[t];
+    }
+    free(tb0); free(tbit0); free(tbad); free(tchanged);
+    if (nomem) goto done;
     if (bad) {
         status = ORC_CORRUPT;
         set_err(err, errlen, bad == 2 ? "update does not verify (checksum mismatch)" : "payload positions outside their exponent groups");
@@ -799,11 +981,7 @@ int orc_apply(void *handle, int16_t *const *weights, const uint64_t *old_chk, co
         goto done;
     }
     /* commit only now (codec.py:713-714) */
-    for (int64_t t = 0; t < u->n_tensors; t++) {
-        int64_t tot = 0;
-        for (int k = 0; k < u->tens[t].ng; k++) tot += u->tens[t].g[k].count;
-        for (int64_t j = 0; j < tot; j++) weights[t][pos[t][j]] = val[t][j];
-    }
+    parallel_for(u->n_tensors, app_commit, &ac);
     status = ORC_OK;
 done:
     if (status == ORC_NOMEM) set_err(err, errlen, "oracle: out of memory");

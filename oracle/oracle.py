@@ -61,6 +61,8 @@ def lib():
         L.orc_update_free.argtypes = [P]
         L.orc_apply.argtypes = [P, P, P, P, P, ctypes.c_char_p, ctypes.c_size_t]
         L.orc_apply.restype = ctypes.c_int
+        L.orc_set_threads.argtypes = [ctypes.c_int]
+        L.orc_set_threads.restype = None
         _lib = L
     return _lib
 
@@ -89,6 +91,12 @@ def _bits(name, t) -> np.ndarray:
 
 def _version(t):
     return getattr(t, "_version", None)
+
+
+def set_threads(n: int) -> None:
+    """Threads of the oracle's per-tensor and per-exponent passes (0: every processor this process
+    may run on, the default).  The bytes do not depend on it."""
+    lib().orc_set_threads(int(n))
 
 
 def checksum(a) -> int:
