@@ -71,23 +71,42 @@ def allgather_updates(update: bytes, group=None, device: torch.device | None = N
     return [out[r * mx: r * mx + sizes[r]].cpu().numpy().tobytes() for r in want]
 
 
-def allgather_updates_device(update, group=None, ranks: Sequence[int] | None = None) -> list:
+def host_size_group():
+    """A gloo group over the same ranks, for the update sizes: the sizes are known on the host as
+    soon as encode_update_device returns, so exchanging them there never waits for the GPU."""
+    import torch.distributed as td
+    return td.new_group(backend="gloo")
+
+
+def allgather_updates_device(update, group=None, ranks: Sequence[int] | None = None, size_group=None) -> list:
     """allgather_updates for device-resident updates (uint8 CUDA tensors from
-    encode_update_device): the sizes, then the padded updates, gathered into one device buffer
-    over NCCL; returns device views of the requested ranks' updates, ready for apply_update."""
+    encode_update_device): every rank's size, then the updates padded to the largest, gathered into
+    one device buffer over NCCL; returns device views of the requested ranks' updates, ready for
+    apply_update.  With ``size_group`` (a gloo group, see host_size_group) the sizes are exchanged
+    between the hosts, so nothing waits for the device; otherwise they take a small NCCL gather
+    that the host reads back."""
     import torch.distributed as td
 
     world = td.get_world_size(group) if td.is_initialized() else 1
     if world == 1:
         return [update]
     device = update.device
-    n = torch.tensor([update.numel()], dtype=torch.int64, device=device)
-    sizes_t = torch.empty(world, dtype=torch.int64, device=device)
-    td.all_gather_into_tensor(sizes_t, n, group=group)
+    if size_group is not None:
+        n = torch.tensor([update.numel()], dtype=torch.int64)
+        sizes_t = torch.empty(world, dtype=torch.int64)
+        td.all_gather_into_tensor(sizes_t, n, group=size_group)
+    else:
+        n = torch.tensor([update.numel()], dtype=torch.int64, device=device)
+        sizes_t = torch.empty(world, dtype=torch.int64, device=device)
+        td.all_gather_into_tensor(sizes_t, n, group=group)
     sizes = sizes_t.tolist()
     mx = max(max(sizes), 1)
-    buf = torch.zeros(mx, dtype=torch.uint8, device=device)
-    buf[: update.numel()].copy_(update)
+    if update.numel() == mx:
+        buf = update
+    else:
+        buf = torch.empty(mx, dtype=torch.uint8, device=device)
+        buf[: update.numel()].copy_(update)
+        buf[update.numel():].zero_()
     out = torch.empty(world * mx, dtype=torch.uint8, device=device)
     td.all_gather_into_tensor(out, buf, group=group)
     want = range(world) if ranks is None else ranks

@@ -84,6 +84,15 @@ def _worker(rank, world, port, outdir):
         assert changed <= seen <= set(prev)
         for k in prev:
             assert torch.equal(weights[k], cur[k]), k
+        # the device-resident exchange's host logic, on CPU tensors: sizes through a separate gloo
+        # group (host_size_group) or through the data group, uneven sizes padded and cut back
+        t = torch.frombuffer(bytearray(upd), dtype=torch.uint8)
+        sg = cdist.host_size_group()
+        for size_group in (sg, None):
+            views = cdist.allgather_updates_device(t, size_group=size_group)
+            assert [bytes(v.numpy().tobytes()) for v in views] == got
+            mine_only = cdist.allgather_updates_device(t, ranks=[rank], size_group=size_group)
+            assert bytes(mine_only[0].numpy().tobytes()) == upd
         with open(os.path.join(outdir, f"ok{rank}"), "w") as f:
             f.write(str(len(upd)))
     finally:
