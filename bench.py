@@ -12,8 +12,15 @@ step, caches stay valid), so all K steps run back to back between two barriers. 
 15 GB, far larger than L2, so no flush is needed between steps.
 
 N > 1 (torchrun): tensors are partitioned by LPT on numel; each rank encodes its partition, the
-compressed payloads are all-gathered over NCCL, and each rank applies its own partition's update
-taken from the gathered buffer.  The reported time is the max over ranks.
+compressed payloads are all-gathered over NCCL (their sizes between the hosts over gloo), and each
+rank applies its own partition's update taken from the gathered buffer (the headline's receiver).
+The reported time is the max over ranks.  Beside the headline the line carries:
+  roofline_step   whole encode and whole apply against the HBM roofline, per GPU
+  full_replica    (N > 1) every rank applies all N gathered updates to a whole copy of the model
+  tp8_32b         BASELINE config 4: each rank encodes and applies its own 32B 8-way TP shard
+  parity          the first update's SHA-256 against the CPU oracle's whole-dict update
+  cpu_baseline    the oracle port on the host cores, and the reference's own torch code beside it
+  reference_gpu   the reference's own GPU path (torch CUDA + Triton) on the same GPU (secondary)
 """
 
 from __future__ import annotations
@@ -206,39 +213,92 @@ def host_threads():
         return os.cpu_count() or 1
 
 
-def time_oracle(prev, cur, steps=1, threads=None, warmup=0):
-    """The CPU oracle (the C restatement of the reference) on one sample, with all host threads:
-    tensors cut into pieces of at most 2^24 elements, one update per piece, pieces spread over a
-    thread pool (the C calls release the GIL); the per-element work is the reference's.
-    `warmup` untimed steps come first.  Returns seconds per timed step (encode + apply, whole
-    sample) and the threads used."""
+def time_oracle(prev, cur, steps=1, threads=None, warmup=0, whole=False):
+    """The CPU oracle (the C restatement of the reference) on one sample, on every host thread.
+    Default: tensors cut into pieces of at most 2^24 elements, one update per piece, the pieces
+    spread over a thread pool (the C calls release the GIL) -- the per-element work of the
+    reference with the parallelism of a CPU implementation that splits large tensors.
+    whole=True: one whole-dict update per step, the oracle's per-tensor and per-exponent passes on
+    the threads (a step then waits for its largest tensor on one thread).  `warmup` untimed steps
+    come first.  Returns seconds per timed step (encode + apply) and the threads used."""
     import concurrent.futures
 
     from oracle import oracle
     threads = threads or host_threads()
     sender, receiver = {}, {}
     recv = {k: v.clone() for k, v in prev.items()}
-    piece = 1 << 24
-    pieces = [(k, a, min(a + piece, prev[k].numel())) for k in prev for a in range(0, prev[k].numel(), piece)]
-    pieces.sort(key=lambda p: p[1] - p[2])   # big pieces first: better balance
     state = {"a": prev, "b": cur}
+    if whole:
+        oracle.set_threads(threads)
 
-    def one(p):
-        k, lo, hi = p
-        name = f"{k}#{lo}"
-        upd = oracle.encode_update({name: state["a"][k].view(-1)[lo:hi]}, {name: state["b"][k].view(-1)[lo:hi]}, sender)
-        oracle.apply_update({name: recv[k].view(-1)[lo:hi]}, upd, receiver)
+        def run_step():
+            upd = oracle.encode_update(state["a"], state["b"], sender)
+            oracle.apply_update(recv, upd, receiver)
+    else:
+        oracle.set_threads(1)
+        piece = 1 << 24
+        pieces = [(k, a, min(a + piece, prev[k].numel())) for k in prev for a in range(0, prev[k].numel(), piece)]
+        pieces.sort(key=lambda p: p[1] - p[2])   # big pieces first: better balance
+        pool = concurrent.futures.ThreadPoolExecutor(max_workers=threads)
 
+        def one(p):
+            k, lo, hi = p
+            name = f"{k}#{lo}"
+            upd = oracle.encode_update({name: state["a"][k].view(-1)[lo:hi]}, {name: state["b"][k].view(-1)[lo:hi]},
+                                       sender)
+            oracle.apply_update({name: recv[k].view(-1)[lo:hi]}, upd, receiver)
+
+        def run_step():
+            list(pool.map(one, pieces))
     times = []
-    with concurrent.futures.ThreadPoolExecutor(max_workers=threads) as pool:
+    try:
         for i in range(warmup + steps):
             t0 = time.perf_counter()
-            list(pool.map(one, pieces))
+            run_step()
             if i >= warmup:
                 times.append(time.perf_counter() - t0)
             state["a"], state["b"] = state["b"], state["a"]
+    finally:
+        if not whole:
+            pool.shutdown()
+        oracle.set_threads(0)
     for k in recv:   # the oracle reproduced the sender's state
         assert torch.equal(recv[k], state["a"][k]), k
+    return sum(times) / len(times), threads
+
+
+def reference_src():
+    """Import path of the reference package installed beside this repository (baseline/_ref), or
+    None when it is not there."""
+    p = os.path.join(ROOT, "baseline", "_ref")
+    return p if os.path.exists(os.path.join(p, "crukx_sync", "__init__.py")) else None
+
+
+def time_reference_torch(prev, cur, steps=1, threads=None):
+    """The reference's own torch implementation (crukx_sync, unmodified, from baseline/_ref) on CPU
+    tensors with every host thread: seconds per steady-state step (encode_update + apply_update,
+    checksum caches kept, after one untimed step that fills them), or None without the package."""
+    src = reference_src()
+    if src is None:
+        return None, 0
+    if src not in sys.path:
+        sys.path.insert(0, src)
+    import crukx_sync as ref   # the reference, unchanged
+    threads = threads or host_threads()
+    torch.set_num_threads(threads)
+    sender, receiver = {}, {}
+    recv = {k: v.clone() for k, v in prev.items()}
+    state = {"a": prev, "b": cur}
+    times = []
+    for i in range(1 + steps):
+        t0 = time.perf_counter()
+        upd = ref.encode_update(state["a"], state["b"], sender)
+        ref.apply_update(recv, upd, receiver)
+        if i >= 1:
+            times.append(time.perf_counter() - t0)
+        state["a"], state["b"] = state["b"], state["a"]
+    for k in recv:
+        assert torch.equal(recv[k].view(torch.int16), state["a"][k].view(torch.int16)), k
     return sum(times) / len(times), threads
 
 
@@ -277,6 +337,19 @@ def log(*a):
         print(f"[bench {time.strftime('%H:%M:%S')}]", *a, file=sys.stderr, flush=True)
 
 
+def step_roofline(my_params, changed, upd_bytes, ms_enc, ms_app, peak):
+    """Whole encode and whole apply of one rank against the HBM roofline: algorithmic bytes (encode:
+    prev + cur, 4 B per element; apply: the old weights 2 B per element + the update + 2 B per
+    changed element) over the rank's measured time."""
+    enc_b = 4.0 * my_params
+    app_b = 2.0 * my_params + upd_bytes + 2.0 * changed
+    enc = enc_b / (ms_enc * 1e-3) / 1e9
+    app = app_b / (ms_app * 1e-3) / 1e9
+    return {"encode": {"achieved": round(enc, 1), "frac": round(enc / peak, 4), "algorithmic_bytes": enc_b},
+            "apply": {"achieved": round(app, 1), "frac": round(app / peak, 4), "algorithmic_bytes": app_b},
+            "peak": peak, "unit": "GB/s", "per": "GPU (max over ranks of its time)"}
+
+
 def run_ours(args, rank, world, dist):
     import crukx_sync_b200 as crx
     from crukx_sync_b200 import _ext
@@ -289,11 +362,15 @@ def run_ours(args, rank, world, dist):
     if cfg.get("drop_embed"):
         shapes_all = {k: v for k, v in shapes_all.items() if "embed" not in k}
     owner = cdist.partition({k: int(torch.tensor(v).prod()) for k, v in shapes_all.items()}, world)
-    shapes = {k: v for k, v in shapes_all.items() if owner[k] == rank}
+    mine = [k for k in shapes_all if owner[k] == rank]
     total_params = sum(int(torch.tensor(s).prod()) for s in shapes_all.values())
-    my_params = sum(int(torch.tensor(s).prod()) for s in shapes.values())
-    log("generating", len(shapes), "tensors,", my_params, "params")
-    A, B = make_states(shapes, cfg["lr"], dev, seed=0)
+    my_params = sum(int(torch.tensor(shapes_all[k]).prod()) for k in mine)
+    # every rank holds the whole model's two states (same seed everywhere): its own tensors are the
+    # partition it encodes and applies; the whole states serve the full-replica receiver
+    log("generating", len(shapes_all), "tensors,", total_params, "params")
+    A_full, B_full = make_states(shapes_all, cfg["lr"], dev, seed=0)
+    A = {k: A_full[k] for k in mine}
+    B = {k: B_full[k] for k in mine}
     log("generated")
     changed = sum(int((A[k].view(torch.int16) != B[k].view(torch.int16)).sum()) for k in A)
     parity = None
@@ -306,34 +383,40 @@ def run_ours(args, rank, world, dist):
     ctx = _ext.context(dev.index)
     L = _ext.load()
     stream = torch.cuda.current_stream(dev)
+    size_group = cdist.host_size_group() if dist is not None else None
 
     def barrier():
         if dist is not None:
             dist.barrier()
         torch.cuda.synchronize(dev)
 
-    def exchange(upd):
-        """All-gather of the device-resident updates over NCCL; this rank's update from the gather."""
-        return cdist.allgather_updates_device(upd, ranks=[rank])[0]
+    def exchange(upd, ranks=(rank,)):
+        """All-gather of the device-resident updates over NCCL (sizes between the hosts); the
+        requested ranks' updates from the gathered buffer."""
+        return cdist.allgather_updates_device(upd, ranks=list(ranks), size_group=size_group)
 
-    state = {"src": A, "dst": B}
+    state = {"src": A, "dst": B, "src_is_A": True}
+
+    def flip():
+        state["src"], state["dst"] = state["dst"], state["src"]
+        state["src_is_A"] = not state["src_is_A"]
 
     def step(events=None):
         """One sync step with the updates resident in HBM: encode_update_device (the reference's
-        bytes, in device memory), NCCL all-gather, apply_update of the device update."""
+        bytes, in device memory), NCCL all-gather, apply_update of this rank's update."""
         src, dst = state["src"], state["dst"]
         if events:
             events[0].record(stream)
         upd = crx.encode_update_device(src, dst, sender)
         if events:
             events[1].record(stream)
-        mine = exchange(upd)
+        mine_u = exchange(upd)[0]
         if events:
             events[2].record(stream)
-        st = crx.apply_update(recv, mine, receiver)
+        st = crx.apply_update(recv, mine_u, receiver)
         if events:
             events[3].record(stream)
-        state["src"], state["dst"] = dst, src
+        flip()
         return upd, st
 
     for i in range(args.warmup):
@@ -363,17 +446,22 @@ def run_ours(args, rank, world, dist):
         assert torch.equal(recv[k], state["src"][k]), f"receiver differs after timing: {k}"
     ms_step = sum(tot) / len(tot)
     ms_enc, ms_ex, ms_app = (sum(x) / len(x) for x in (enc, ex, app))
+    my_upd = sum(sizes) / len(sizes)
     if dist is not None:
         t = torch.tensor([ms_step, ms_enc, ms_app, ms_ex], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms_step, ms_enc, ms_app, ms_ex = t.tolist()
-        c = torch.tensor([changed, sum(sizes) / len(sizes)], dtype=torch.float64, device=dev)
+        c = torch.tensor([changed, my_upd], dtype=torch.float64, device=dev)
         dist.all_reduce(c)
         changed_all, upd_bytes = c.tolist()
     else:
-        changed_all, upd_bytes = changed, sum(sizes) / len(sizes)
+        changed_all, upd_bytes = changed, my_upd
     weight_bytes = 2.0 * total_params
     value = weight_bytes / (ms_step * 1e-3) / 1e9
+    peak, peak_kind = measured_peak()
+    # this rank's share against the slowest rank's time
+    per_rank = step_roofline(my_params, changed, my_upd, ms_enc, ms_app, peak)
+    per_rank["peak_kind"] = peak_kind
 
     # ---- the same steps through the host-bytes API (encode_update -> bytes -> apply_update), the
     #      reference's own interface: the update crosses PCIe twice; each rank applies its own
@@ -387,7 +475,7 @@ def run_ours(args, rank, world, dist):
             events[1].record(stream)
             crx.apply_update(recv, u, receiver)
             events[2].record(stream)
-            state["src"], state["dst"] = dst, src
+            flip()
 
         for _ in range(2):
             bstep([torch.cuda.Event(enable_timing=True) for _ in range(3)])
@@ -415,7 +503,6 @@ def run_ours(args, rank, world, dist):
     torch.cuda.synchronize(dev)
     kt = kernel_times(ctx)
     L.crx_ctx_profile(ctx, 0)
-    peak, peak_kind = measured_peak()
     algo = {"k_enc_rank": 4.0 * my_params, "k_map": 2.0 * my_params, "k_app_hist": 2.0 * my_params}
     kernels = {}
     for nm, (ms, n) in sorted(kt.items(), key=lambda x: -x[1][0]):
@@ -441,22 +528,99 @@ def run_ours(args, rank, world, dist):
             pass
         roofline = {"kernel": dom, "bound": "hbm", "achieved": round(achieved, 1), "peak": peak,
                     "peak_kind": peak_kind, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": traffic,
+                    "traffic_source": "scaled from profiles/traffic.json: ncu dram__bytes_read.sum + "
+                                      "dram__bytes_write.sum per element of the kernel's 7b-2l capture, times this "
+                                      "launch's elements (not measured in this run)",
                     "algorithmic_bytes": algo[dom]}
+
+    # ---- full-replica receiver (N > 1): every rank applies all N gathered updates to a whole copy
+    #      of the model (inference replicas that each hold the whole model)
+    full_replica = None
+    if dist is not None and not args.no_receivers:
+        src_full = A_full if state["src_is_A"] else B_full
+        replica = {k: v.clone() for k, v in src_full.items()}
+        rep_chk = {}
+
+        def rstep(events=None):
+            src, dst = state["src"], state["dst"]
+            if events:
+                events[0].record(stream)
+            upd = crx.encode_update_device(src, dst, sender)
+            allu = exchange(upd, ranks=range(world))
+            if events:
+                events[1].record(stream)
+            for u in allu:
+                crx.apply_update(replica, u, rep_chk)
+            if events:
+                events[2].record(stream)
+            flip()
+
+        for _ in range(2):
+            rstep()
+        nrep = max(3, min(args.steps, 10))
+        revs = [[torch.cuda.Event(enable_timing=True) for _ in range(3)] for _ in range(nrep)]
+        barrier()
+        for k in range(nrep):
+            rstep(revs[k])
+        barrier()
+        src_full = A_full if state["src_is_A"] else B_full
+        for k in replica:
+            assert torch.equal(replica[k], src_full[k]), f"replica differs from the sender state: {k}"
+        rt = torch.tensor([sum(e[0].elapsed_time(e[2]) for e in revs) / nrep,
+                           sum(e[0].elapsed_time(e[1]) for e in revs) / nrep,
+                           sum(e[1].elapsed_time(e[2]) for e in revs) / nrep], dtype=torch.float64, device=dev)
+        dist.all_reduce(rt, op=dist.ReduceOp.MAX)
+        r_step, r_encx, r_app = rt.tolist()
+        full_replica = {"value": round(2.0 * total_params / (r_step * 1e-3) / 1e9, 2), "unit": "GB/s",
+                        "ms_per_step": round(r_step, 4), "encode_exchange_ms": round(r_encx, 4),
+                        "apply_all_ms": round(r_app, 4), "steps": nrep, "scaling": "strong",
+                        "receiver": "full replica: every rank applies all N updates to a whole copy of the model",
+                        "note": "GB/s of bf16 weights per sync step (the model's bytes over the step time)"}
+        del replica
+    del A_full, B_full
+    torch.cuda.empty_cache()
 
     # ---- end to end through the public API with host (pinned) buffers
     e2e = None
     if not args.no_e2e:
         e2e = run_e2e(args, A, B, dev, weight_bytes, exchange, barrier, dist)
 
-    # ---- CPU baseline: the oracle on a bounded sample of the same workload (rank 0, N = 1)
+    # ---- 32B shape, 8-way tensor parallel: every rank encodes and applies its
+    #      own TP shard (weak scaling: one shard per GPU)
+    tp8 = None
+    if not args.no_receivers:
+        state.clear()
+        del A, B, recv
+        torch.cuda.empty_cache()
+        tp8 = run_tp8_shard(args, rank, world, dev, dist, exchange, barrier, peak)
+
+    # ---- CPU baselines on a bounded sample of the same workload (rank 0, N = 1): the oracle port
+    #      (one whole-dict update per step on every host thread) and the reference's own torch code
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         prev_s, cur_s, n_s = cpu_baseline_sample(shapes_all, cfg["lr"], args.cpu_sample)
         t_step, thr = time_oracle(prev_s, cur_s, steps=2)
         cpu = {"value": round(2.0 * n_s / t_step / 1e9, 4), "unit": "GB/s", "cores": thr, "kind": "port",
-               "sample": f"{len(prev_s)} whole tensors of the workload ({n_s / 1e6:.0f}M params), encode + apply "
-                         f"per tensor on {thr} threads, {t_step:.2f} s per step (mean of 2)"}
-    del A, B, recv
+               "sample": f"{len(prev_s)} whole tensors of the workload ({n_s / 1e6:.0f}M params), cut into pieces of at "
+                         f"most 2^24 elements with one update each, encode + apply on {thr} threads, {t_step:.2f} s "
+                         f"per step (mean of 2)"}
+        t_whole, _ = time_oracle(prev_s, cur_s, steps=1, whole=True)
+        cpu["whole_dict_update"] = {
+            "value": round(2.0 * n_s / t_whole / 1e9, 4), "unit": "GB/s", "cores": thr,
+            "note": "the same sample as one whole-dict update per step (the oracle's passes run one tensor or exponent "
+                    "per thread, so a step waits for its largest tensor); the piecewise figure above is the baseline"}
+        tprev, tcur, tn = cpu_baseline_sample(shapes_all, cfg["lr"], args.torch_sample)
+        t_ref, thr_ref = time_reference_torch(tprev, tcur, steps=1)
+        if t_ref is not None:
+            cpu["reference_torch"] = {
+                "value": round(2.0 * tn / t_ref / 1e9, 4), "unit": "GB/s", "cores": thr_ref, "kind": "reference",
+                "sample": f"{len(tprev)} whole tensors ({tn / 1e6:.0f}M params), the reference's own torch code "
+                          f"(crukx_sync from baseline/_ref, unmodified) on CPU tensors with {thr_ref} threads, one "
+                          f"steady-state step after one that fills the checksum caches, {t_ref:.2f} s"}
+    ref_gpu = None
+    if rank == 0 and world == 1 and not args.no_ref_gpu:
+        ref_gpu = run_reference_gpu_line(args)
+
     result = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 4), "higher_is_better": True,
@@ -466,18 +630,131 @@ def run_ours(args, rank, world, dist):
                    "lr": cfg["lr"], "changed_frac": round(changed_all / total_params, 5),
                    "parallelism": f"tensor partition x{world} (LPT on numel), NCCL all-gather of the device-resident updates"
                    if world > 1 else "single GPU",
-                   "path": "encode_update_device -> (NCCL all-gather) -> apply_update of the device update; "
-                           "the reference's bytes, kept in HBM",
+                   "receiver": "partitioned: every rank applies the update of its own tensors, taken from the "
+                               "gathered buffer" if world > 1 else "single GPU: the sender's GPU applies the update",
+                   "path": "encode_update_device -> (NCCL all-gather, sizes between the hosts) -> apply_update of "
+                           "the device update; the reference's bytes, kept in HBM",
                    "l2": "inputs larger than L2 (each state 2 B x params; no flush needed)"},
         "encode_gbs": round(weight_bytes / (ms_enc * 1e-3) / 1e9, 2),
         "apply_gbs": round(weight_bytes / (ms_app * 1e-3) / 1e9, 2),
         "exchange_ms": round(ms_ex, 4), "encode_ms": round(ms_enc, 4), "apply_ms": round(ms_app, 4),
         "update_bytes": int(upd_bytes), "bytes_per_changed": round(upd_bytes / max(changed_all, 1), 4),
-        "wall_s_timed": round(t_wall, 3),
+        "wall_s_timed": round(t_wall, 3), "roofline_step": per_rank,
         "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e, "bytes_api": bytes_api,
+        "full_replica": full_replica, "tp8_32b": tp8, "reference_gpu": ref_gpu,
         "gpu_launches": launches, "clocks": clk.summary(), "parity": parity,
     }
     return result
+
+
+def run_tp8_shard(args, rank, world, dev, dist, exchange, barrier, peak):
+    """Qwen2.5-32B shapes cut 8 ways tensor-parallel; rank r holds shard r
+    (seed 100 + r) and encodes and applies it, the updates crossing an NCCL all-gather."""
+    import crukx_sync_b200 as crx
+    shapes = CONFIGS["32b-tp8"]["shapes"]()
+    params = sum(int(torch.tensor(s).prod()) for s in shapes.values())
+    A, B = make_states(shapes, CONFIGS["32b-tp8"]["lr"], dev, seed=100 + rank)
+    changed = sum(int((A[k].view(torch.int16) != B[k].view(torch.int16)).sum()) for k in A)
+    recv = {k: v.clone() for k, v in A.items()}
+    sender, receiver = {}, {}
+    stream = torch.cuda.current_stream(dev)
+    st = {"src": A, "dst": B}
+
+    def one(events=None):
+        if events:
+            events[0].record(stream)
+        upd = crx.encode_update_device(st["src"], st["dst"], sender)
+        if events:
+            events[1].record(stream)
+        u = exchange(upd)[0]
+        if events:
+            events[2].record(stream)
+        crx.apply_update(recv, u, receiver)
+        if events:
+            events[3].record(stream)
+        st["src"], st["dst"] = st["dst"], st["src"]
+        return upd.numel()
+
+    for _ in range(args.warmup):
+        one()
+    n = max(3, min(args.steps, 10))
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(n)]
+    barrier()
+    sizes = [one(evs[k]) for k in range(n)]
+    barrier()
+    for k in recv:
+        assert torch.equal(recv[k], st["src"][k]), f"tp8 receiver differs: {k}"
+    t = torch.tensor([sum(e[0].elapsed_time(e[3]) for e in evs) / n, sum(e[0].elapsed_time(e[1]) for e in evs) / n,
+                      sum(e[1].elapsed_time(e[2]) for e in evs) / n, sum(e[2].elapsed_time(e[3]) for e in evs) / n],
+                     dtype=torch.float64, device=dev)
+    if dist is not None:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms, ms_e, ms_x, ms_a = t.tolist()
+    upd = sum(sizes) / len(sizes)
+    out = {"value": round(world * 2.0 * params / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
+           "encode_ms": round(ms_e, 4), "exchange_ms": round(ms_x, 4), "apply_ms": round(ms_a, 4), "steps": n,
+           "params_per_rank": params, "changed_frac": round(changed / params, 5), "update_bytes_per_rank": int(upd),
+           "scaling": "weak", "workload": "qwen2.5-32b-shape, 8-way TP shard per rank (seed 100 + rank)",
+           "receiver": "per shard: every rank applies its own shard's update, taken from the gathered buffer",
+           "roofline_step": step_roofline(params, changed, upd, ms_e, ms_a, peak)}
+    del A, B, recv
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_reference_gpu_line(args):
+    """The reference's own GPU path (crukx_sync from baseline/_ref, unmodified: torch CUDA ops and
+    its Triton block decoder) on this B200, same workload and steps of encode_update (bytes) and
+    apply_update, in a child process with a time limit; a secondary line, not a target."""
+    if reference_src() is None or args.config not in ("7b", "1.5b", "toy", "7b-2l"):
+        return None
+    cmd = [sys.executable, os.path.abspath(__file__), "--ref-gpu-child", "--config", args.config]
+    try:
+        r = subprocess.run(cmd, capture_output=True, text=True, timeout=args.ref_gpu_timeout)
+    except subprocess.TimeoutExpired:
+        return {"unavailable": f"did not finish within {args.ref_gpu_timeout} s"}
+    lines = [ln for ln in r.stdout.splitlines() if ln.startswith("{")]
+    if r.returncode != 0 or not lines:
+        return {"unavailable": f"child exited {r.returncode}: {(r.stderr or r.stdout)[-300:]}"}
+    return json.loads(lines[-1])
+
+
+def ref_gpu_child(args):
+    src = reference_src()
+    sys.path.insert(0, src)
+    import crukx_sync as ref   # the reference, unchanged
+    dev = torch.device("cuda", 0)
+    cfg = CONFIGS[args.config]
+    shapes = cfg["shapes"]()
+    if cfg.get("drop_embed"):
+        shapes = {k: v for k, v in shapes.items() if "embed" not in k}
+    params = sum(int(torch.tensor(s).prod()) for s in shapes.values())
+    A, B = make_states(shapes, cfg["lr"], dev, seed=0)
+    recv = {k: v.clone() for k, v in A.items()}
+    sender, receiver = {}, {}
+    st = {"src": A, "dst": B}
+    enc_t, app_t = [], []
+    for i in range(3):
+        torch.cuda.synchronize(dev)
+        t0 = time.perf_counter()
+        upd = ref.encode_update(st["src"], st["dst"], sender)
+        torch.cuda.synchronize(dev)
+        t1 = time.perf_counter()
+        ref.apply_update(recv, upd, receiver)
+        torch.cuda.synchronize(dev)
+        t2 = time.perf_counter()
+        if i:
+            enc_t.append(t1 - t0)
+            app_t.append(t2 - t1)
+        st["src"], st["dst"] = st["dst"], st["src"]
+    for k in recv:
+        assert torch.equal(recv[k], st["src"][k]), k
+    e, a = sum(enc_t) / len(enc_t), sum(app_t) / len(app_t)
+    print(json.dumps({"value": round(2.0 * params / (e + a) / 1e9, 3), "unit": "GB/s", "encode_s": round(e, 3),
+                      "apply_s": round(a, 3), "steps": len(enc_t), "workload": cfg["name"],
+                      "what": "the reference's own GPU path (torch CUDA + its Triton block decoder), host bytes "
+                              "between encode_update and apply_update as in its API, caches kept, wall clock "
+                              "with synchronize; steady-state steps after one that fills the caches"}), flush=True)
 
 
 def run_e2e(args, A, B, dev, weight_bytes, exchange, barrier, dist):
@@ -524,8 +801,8 @@ def run_e2e(args, A, B, dev, weight_bytes, exchange, barrier, dist):
 
 def run_reference(args, rank, world):
     """The reference's algorithm on the host cores: the C restatement in oracle/ (the reference
-    itself is Python/torch and cannot be installed on the GPU box), on a bounded sample of the
-    same workload per step."""
+    itself is Python/torch; its own torch code is timed as a secondary figure in our arm's
+    cpu_baseline.reference_torch), on a bounded sample of the same workload per step."""
     cfg = CONFIGS[args.config]
     shapes_all = cfg["shapes"]()
     total_params = sum(int(torch.tensor(s).prod()) for s in shapes_all.values())
@@ -536,7 +813,8 @@ def run_reference(args, rank, world):
     ms = 1e3 * t_step
     value = 2.0 * n_s / (ms * 1e-3) / 1e9
     sample = (f"{len(prev)} whole tensors of {cfg['name']} ({n_s / 1e6:.0f}M of {total_params / 1e9:.2f}B params) "
-              f"per step, oracle/ C port, encode + apply per tensor on {thr} threads")
+              f"per step, oracle/ C port, cut into pieces of at most 2^24 elements with one update each, "
+              f"encode + apply on {thr} threads")
     return {"metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 2), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16 bits (int16 integer work)",
@@ -557,10 +835,19 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the first update")
+    ap.add_argument("--no-receivers", action="store_true", help="skip the full-replica and 32B-TP8 lines")
+    ap.add_argument("--no-ref-gpu", action="store_true", help="skip the reference's own GPU path line")
+    ap.add_argument("--ref-gpu-timeout", type=int, default=300)
+    ap.add_argument("--ref-gpu-child", action="store_true", help=argparse.SUPPRESS)
+    ap.add_argument("--torch-sample", type=int, default=100_000_000,
+                    help="elements of the sample the reference's torch code runs on the host cores")
     ap.add_argument("--cpu-sample", type=int, default=1_000_000_000, help="elements in the CPU-baseline sample")
     ap.add_argument("--ref-sample", type=int, default=1_000_000_000, help="elements per reference-arm step")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.ref_gpu_child:
+        ref_gpu_child(args)
+        return
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if args.impl == "reference":

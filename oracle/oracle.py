@@ -192,8 +192,11 @@ class _Parsed:
             self.tensors.append(TensorHeader(name, ne.value, ck.value, groups))
 
     def __del__(self):
-        if getattr(self, "h", None) and self.h.value:
-            lib().orc_update_free(self.h)
+        try:
+            if getattr(self, "h", None) and self.h.value:
+                lib().orc_update_free(self.h)
+        except TypeError:   # interpreter shutdown: module globals already cleared
+            pass
 
 
 def parse(data: bytes) -> _Parsed:
