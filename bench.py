@@ -378,6 +378,10 @@ def run_ours(args, rank, world, dist):
         log("parity check against the oracle")
         parity = parity_check(A, B, max(1, host_threads() // max(world, 1)))
         log("parity", parity)
+    size_cmp = None
+    if world == 1:   # the same update in other sparse formats (the reference's bench/compare.py columns)
+        from crukx_sync_b200 import sizes as csizes
+        size_cmp = csizes.update_sizes(A, B)
     recv = {k: v.clone() for k, v in A.items()}
     sender, receiver = {}, {}
     ctx = _ext.context(dev.index)
@@ -642,6 +646,11 @@ def run_ours(args, rank, world, dist):
         "wall_s_timed": round(t_wall, 3), "roofline_step": per_rank,
         "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e, "bytes_api": bytes_api,
         "full_replica": full_replica, "tp8_32b": tp8, "reference_gpu": ref_gpu,
+        "sizes": None if size_cmp is None else dict(size_cmp, crukx=int(upd_bytes), changed=int(changed_all),
+                                                    unit="bytes per update",
+                                                    note="raw, sparserl and ctxfree as the reference's bench/compare.py "
+                                                         "computes them (crx_size_stats); its zstd columns are not "
+                                                         "computed"),
         "gpu_launches": launches, "clocks": clk.summary(), "parity": parity,
     }
     return result
@@ -773,9 +782,11 @@ def run_e2e(args, A, B, dev, weight_bytes, exchange, barrier, dist):
     nsteps = max(1, min(args.steps, args.e2e_steps))
     n_el = sum(v.numel() for v in A.values())
 
+    chg = []
+
     def one():   # each rank applies its own update (host bytes are not exchanged between processes)
         upd = crx.encode_update(st["src"], st["dst"], sender)
-        crx.apply_update(Rh, upd, receiver)
+        chg.append(crx.apply_update(Rh, upd, receiver).changed)
         st["src"], st["dst"] = st["dst"], st["src"]
         return len(upd)
 
@@ -792,9 +803,15 @@ def run_e2e(args, A, B, dev, weight_bytes, exchange, barrier, dist):
     for k in Rh:
         assert torch.equal(Rh[k], st["src"][k])
     ub = sum(sizes) / len(sizes)
+    # down: the update bytes, then the apply's commit list (a bit per element and a span table per
+    # 2^18-element super-tile, the new values of the changed elements), scattered on the host
+    n_super = sum((v.numel() + (1 << 18) - 1) >> 18 for v in A.values())
+    changed = sum(chg[-nsteps:]) / nsteps
     return {"value": round(weight_bytes / dt / 1e9, 3), "unit": "GB/s", "ms_per_step": round(dt * 1e3, 2),
-            "steps": nsteps, "h2d_bytes_per_step": int(6 * n_el + ub), "d2h_bytes_per_step": int(2 * n_el + ub),
-            "note": "public API with pinned host tensors: prev+cur up, weights up and back, update bytes down"}
+            "steps": nsteps, "h2d_bytes_per_step": int(6 * n_el + ub),
+            "d2h_bytes_per_step": int(ub + n_super * (32768 + 2048) + 2 * changed),
+            "note": "public API with pinned host tensors: prev + cur and the receiver's weights up, the update "
+                    "bytes and the apply's commit list down (only changed elements written back on the host)"}
 
 
 # ---------------------------------------------------------------- reference arm

@@ -26,7 +26,7 @@ EXPORTS = [
     "crx_update_free", "crx_apply", "crx_huffman_lengths", "crx_checksum", "crx_checksum_noalloc",
     "crx_encode_device", "crx_encoded_copy_device", "crx_parse_head", "crx_parse_device",
     "crx_encode_global", "crx_encoded_part", "crx_encoded_part_copy", "crx_apply_versioned",
-    "crx_ctx_hist_cache_hits", "crx_alloc_calls",
+    "crx_ctx_hist_cache_hits", "crx_alloc_calls", "crx_size_stats", "crx_apply_to_host",
 ]
 
 # collective callbacks of crx_encode_global
@@ -95,6 +95,8 @@ def load():
             "crx_apply_versioned": ([P, P, P, P, P, P, P, P, P, CP, SZ], ctypes.c_int),
             "crx_ctx_hist_cache_hits": ([P], U64),
             "crx_alloc_calls": ([], U64),
+            "crx_size_stats": ([P, I32, P, P, P, P, P, CP, SZ], ctypes.c_int),
+            "crx_apply_to_host": ([P, P, P, P, P, P, P, P, CP, SZ], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

@@ -268,16 +268,17 @@ def apply(weights: Mapping[str, torch.Tensor], u: ParsedUpdate, checksums: dict 
             tag = _ext.CBuf("B", bytes([1]) * k)
             st = L.crx_apply_versioned(_ext.context(cdev.index), u.handle, ptrs, cache, has, vers, tag,
                                        ctypes.c_void_p(stream), ctypes.byref(changed), err, 1024)
-        else:
+        elif dev.type == "cuda":
             st = L.crx_apply(_ext.context(cdev.index), u.handle, ptrs, cache, has, ctypes.c_void_p(stream),
                              ctypes.byref(changed), err, 1024)
+        else:   # host weights: verified against the device copies, only the changed elements written back
+            hptrs = _ext.ptr_array([a.data_ptr() for a in targets])
+            st = L.crx_apply_to_host(_ext.context(cdev.index), u.handle, ptrs, hptrs, cache, has,
+                                     ctypes.c_void_p(stream), ctypes.byref(changed), err, 1024)
     if st != _ext.CRX_OK:
         _raise(st, err)
-    if dev.type == "cuda":   # the commit wrote through raw pointers: move the version like a[idx] = v
-        torch.autograd.graph.increment_version(targets)
-    else:
-        for a, wk in zip(targets, work):
-            a.copy_(wk)     # in-place copy back: bumps the version and reaches every view
+    # the commit wrote through raw pointers (device or host): move the version like a[idx] = v
+    torch.autograd.graph.increment_version(targets)
     if checksums is not None:   # record the version after our own write
         checksums.update({name: (chk, a._version) for (name, _, chk), a in zip(headers, targets)})
     return int(changed.value)

@@ -468,8 +468,9 @@ __device__ __forceinline__ uint32_t nth_set_bit(uint32_t m, uint32_t r) {
 
 __global__ void __launch_bounds__(MP_THREADS, 4)
 k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, const uint32_t* __restrict__ PS,
-      const uint32_t* __restrict__ local, const uint32_t* __restrict__ zz, unsigned long long* __restrict__ caddr,
-      uint16_t* __restrict__ cval, uint64_t stage_cap, unsigned long long* __restrict__ chk_delta,
+      const uint32_t* __restrict__ local, const uint32_t* __restrict__ zz, uint32_t* __restrict__ marks,
+      unsigned long long* __restrict__ spanbase, uint16_t* __restrict__ cval, uint64_t stage_cap,
+      unsigned long long* __restrict__ chk_delta,
       unsigned long long* __restrict__ staged, const uint64_t* __restrict__ GS, uint32_t* __restrict__ HNEW,
       uint16_t* __restrict__ order_scratch) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -730,6 +731,11 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             unsigned long long sb = 0;
             if (lane == 31 && total) sb = atomicAdd(staged, (unsigned long long)total);
             sb = __shfl_sync(FULL, sb, 31);
+            {   // the commit list: the span's changed-position bits and where its values start
+                const int64_t st_i = s * (SUPER_N / MP_SUB) + (base - e_begin) / MP_SUB;   // sub-tile
+                marks[st_i * (MP_SUB / 32) + (span0 >> 5) + lane] = bits;
+                if (lane == 0) spanbase[st_i * MP_WARPS + w] = sb;
+            }
             uint16_t* lst = reinterpret_cast<uint16_t*>(&S.msk[w][0][0]);
             uint32_t at = incl - c;
             for (uint32_t b = bits; b; b &= b - 1, ++at) lst[at] = uint16_t(lane * 32 + (__ffs(b) - 1));
@@ -737,10 +743,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             for (uint32_t k = lane; k < total; k += 32) {
                 const int i = span0 + lst[k];
                 const uint32_t old = uint16_t(p[i]), nv = (old + S.nval[i]) & 0xFFFFu;
-                if (sb + k < stage_cap) {
-                    caddr[sb + k] = (unsigned long long)(reinterpret_cast<uintptr_t>(p + i));
-                    cval[sb + k] = uint16_t(nv);
-                }
+                if (sb + k < stage_cap) cval[sb + k] = uint16_t(nv);
                 delta += (uint64_t(nv) - uint64_t(old)) * splitmix_weight(uint64_t(base + i));
                 if (HNEW) {
                     const uint32_t eo = (old >> 7) & 0xFFu, en = (nv >> 7) & 0xFFu;
@@ -761,12 +764,70 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
 }
 
 // Runs only after the host verdict, which requires every change to have been staged exactly once.
-__global__ void __launch_bounds__(256) k_commit(const unsigned long long* __restrict__ caddr, const uint16_t* __restrict__ cval,
-                                                uint64_t n) {
-    const uint64_t j = uint64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-    if (j >= n) return;
-    const unsigned long long a = caddr[j];
-    if (a) *reinterpret_cast<uint16_t*>(uintptr_t(a)) = cval[j];
+// One CTA per sub-tile, a warp per span: each lane takes its 32-element run's mark word, its
+// values start at the span's base plus the changed positions of the lanes before it.
+__global__ void __launch_bounds__(MP_THREADS) k_commit(const AppTensor* __restrict__ T, int nT,
+                                                       const uint32_t* __restrict__ marks,
+                                                       const unsigned long long* __restrict__ spanbase,
+                                                       const uint16_t* __restrict__ cval) {
+    const int64_t st_i = blockIdx.x;                      // sub-tile
+    const int64_t s = st_i / (SUPER_N / MP_SUB);
+    const int t = tensor_of_super(T, nT, s);
+    const AppTensor tt = T[t];
+    const int64_t sub0 = (s - tt.super_begin) * SUPER_N + (st_i % (SUPER_N / MP_SUB)) * MP_SUB;
+    if (sub0 >= tt.numel) return;                          // past the tensor's last sub-tile: nothing staged
+    __shared__ uint16_t lst[MP_WARPS][MP_SPAN];   // a span's changed positions, in order
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    const uint32_t bits = marks[st_i * (MP_SUB / 32) + w * 32 + lane];
+    const uint32_t c = __popc(bits);
+    uint32_t incl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint32_t y = __shfl_up_sync(FULL, incl, o);
+        if (lane >= o) incl += y;
+    }
+    const uint32_t total = __shfl_sync(FULL, incl, 31);
+    if (!total) return;
+    uint32_t at = incl - c;
+    for (uint32_t b = bits; b; b &= b - 1, ++at) lst[w][at] = uint16_t(lane * MP_RUN + (__ffs(b) - 1));
+    __syncwarp();
+    // consecutive lanes take consecutive changes: coalesced value reads, neighbouring writes
+    const uint16_t* v = cval + spanbase[st_i * MP_WARPS + w];
+    int16_t* dst = tt.w + sub0 + w * MP_SPAN;
+    for (uint32_t k = lane; k < total; k += 32) dst[lst[w][k]] = int16_t(v[k]);
+}
+
+// The same commit into host memory (weights the caller keeps on the host; the device copies the
+// update was verified against are temporaries): the commit list comes down once, host threads
+// scatter it.  `mk`, `sbase`, `vals` are host copies of marks, spanbase and cval.
+void commit_host(const std::vector<AppTensor>& T, int16_t* const* host, const uint32_t* mk, const uint64_t* sbase,
+                 const uint16_t* vals, int64_t n_super) {
+    const int nt = int(T.size());
+    parallel_for(size_t(n_super), [&](size_t si) {
+        const int64_t s = int64_t(si);
+        int t = 0;
+        {
+            int lo = 0, hi = nt - 1;
+            while (lo < hi) {
+                const int mid = (lo + hi + 1) >> 1;
+                if (T[size_t(mid)].super_begin <= s) lo = mid; else hi = mid - 1;
+            }
+            t = lo;
+        }
+        const AppTensor& tt = T[size_t(t)];
+        for (int sub = 0; sub < int(SUPER_N / MP_SUB); ++sub) {
+            const int64_t sub0 = (s - tt.super_begin) * SUPER_N + int64_t(sub) * MP_SUB;
+            if (sub0 >= tt.numel) break;
+            const int64_t st_i = s * (SUPER_N / MP_SUB) + sub;
+            for (int w = 0; w < MP_WARPS; ++w) {
+                const uint16_t* v = vals + sbase[st_i * MP_WARPS + w];
+                const uint32_t* m = mk + st_i * (MP_SUB / 32) + w * 32;
+                int16_t* dst = host[t] + sub0 + w * MP_SPAN;
+                for (int l = 0; l < 32; ++l)
+                    for (uint32_t b = m[l]; b; b &= b - 1) dst[l * MP_RUN + __builtin_ctz(b)] = int16_t(*v++);
+            }
+        }
+    });
 }
 
 __global__ void k_widen(const uint32_t* __restrict__ a, uint64_t* __restrict__ b, int64_t n) {
@@ -808,7 +869,7 @@ __global__ void k_hist_store(const uint32_t* __restrict__ src, uint32_t* const* 
 
 Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64_t* old_chk, const uint8_t* has_chk,
                   cudaStream_t st, int64_t* changed, std::string* err, const uint64_t* versions,
-                  const uint8_t* has_version) {
+                  const uint8_t* has_version, int16_t* const* host_weights) {
     *changed = 0;
     const int nt = int(u.tensors.size());
     if (u.payload_len && !u.payload && !u.payload_device) {
@@ -903,7 +964,11 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     CRX_CUDA(ensure_dev(C.b[S_A_GAPS], sizeof(uint32_t) * total, st));
     CRX_CUDA(ensure_dev(C.b[S_A_ZZ], sizeof(uint32_t) * total, st));
     CRX_CUDA(ensure_dev(C.b[S_A_LOCAL], sizeof(uint32_t) * total, st));
-    CRX_CUDA(ensure_dev(C.b[S_A_CADDR], sizeof(uint64_t) * total, st));
+    // commit list: a bit per element, the span's first value slot, the values in position order
+    const size_t mark_words = size_t(n_super) * (SUPER_N / 32);
+    const size_t span_slots = size_t(n_super) * (SUPER_N / MP_SUB) * MP_WARPS;
+    CRX_CUDA(ensure_dev(C.b[S_A_CADDR], sizeof(uint32_t) * mark_words, st));
+    CRX_CUDA(ensure_dev(C.b[S_A_SPANB], sizeof(uint64_t) * span_slots, st));
     CRX_CUDA(ensure_dev(C.b[S_A_CVAL], sizeof(uint16_t) * total, st));
     CRX_CUDA(ensure_dev(C.b[S_A_HS], sizeof(uint32_t) * 256 * size_t(n_super), st));
     bool keep_hist = false;   // some tensor asks for its histogram to be cached
@@ -1000,7 +1065,8 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     CRX_CUDA(cudaFuncSetAttribute(k_map, cudaFuncAttributeMaxDynamicSharedMemorySize, int(map_smem)));
     { KernelScope ks_(C, "k_map", st);
     k_map<<<unsigned(n_super), MP_THREADS, map_smem, st>>>(dT, nt, dG, dev<uint32_t>(C, S_A_HS), dev<uint32_t>(C, S_A_LOCAL),
-                                                            dev<uint32_t>(C, S_A_ZZ), dev<unsigned long long>(C, S_A_CADDR),
+                                                            dev<uint32_t>(C, S_A_ZZ), dev<uint32_t>(C, S_A_CADDR),
+                                                            dev<unsigned long long>(C, S_A_SPANB),
                                                             dev<uint16_t>(C, S_A_CVAL), total, chk_delta, counters + 2,
                                                             dev<uint64_t>(C, S_A_TOT), hnew, dev<uint16_t>(C, S_A_ORDER));
     }
@@ -1044,9 +1110,23 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
         *err = "update does not verify (checksum mismatch: " + bad_names + ")";
         return kCorrupt;
     }
+    if (host_weights) {   // the weights live on the host: bring the commit list down and scatter it there
+        const size_t mb = sizeof(uint32_t) * mark_words, sb = sizeof(uint64_t) * span_slots, vb = sizeof(uint16_t) * total;
+        CRX_CUDA(ensure_pinned(C.in_host, mb + sb + vb + 16, st));
+        uint8_t* hb = static_cast<uint8_t*>(C.in_host.p);
+        CRX_CUDA(cudaMemcpyAsync(hb, C.b[S_A_CADDR].p, mb, cudaMemcpyDeviceToHost, st));
+        CRX_CUDA(cudaMemcpyAsync(hb + mb, C.b[S_A_SPANB].p, sb, cudaMemcpyDeviceToHost, st));
+        if (vb) CRX_CUDA(cudaMemcpyAsync(hb + mb + sb, C.b[S_A_CVAL].p, vb, cudaMemcpyDeviceToHost, st));
+        CRX_CUDA(cudaStreamSynchronize(st));
+        commit_host(T, host_weights, reinterpret_cast<const uint32_t*>(hb), reinterpret_cast<const uint64_t*>(hb + mb),
+                    reinterpret_cast<const uint16_t*>(hb + mb + sb), n_super);
+        *changed = int64_t(total);
+        return kOk;
+    }
     { KernelScope ks_(C, "k_commit", st);
-    k_commit<<<unsigned((total + 255) / 256), 256, 0, st>>>(dev<unsigned long long>(C, S_A_CADDR), dev<uint16_t>(C, S_A_CVAL),
-                                                           total);
+    k_commit<<<unsigned(n_super * (SUPER_N / MP_SUB)), MP_THREADS, 0, st>>>(dT, nt, dev<uint32_t>(C, S_A_CADDR),
+                                                                          dev<unsigned long long>(C, S_A_SPANB),
+                                                                          dev<uint16_t>(C, S_A_CVAL));
     }
     CRX_CUDA(cudaGetLastError());
     // ---- the new weights' histograms for the next apply (tagged version + 1: the caller bumps it).

@@ -950,6 +950,38 @@ int crx_apply(crx_ctx* ctx, const crx_update* u, int16_t* const* weights, const 
     }
 }
 
+int crx_apply_to_host(crx_ctx* ctx, const crx_update* u, int16_t* const* device_copies, int16_t* const* host_weights,
+                      const uint64_t* cached_checksums, const uint8_t* has_cached, void* stream, int64_t* changed,
+                      char* err, size_t errlen) {
+    if (!ctx || !u || !changed || (!u->u.tensors.empty() && (!device_copies || !host_weights))) {
+        put_err(err, errlen, "crx_apply_to_host: bad argument");
+        return CRX_BAD_ARGUMENT;
+    }
+    if (has_cached && !cached_checksums) {
+        put_err(err, errlen, "crx_apply_to_host: has_cached without cached_checksums");
+        return CRX_BAD_ARGUMENT;
+    }
+    try {
+        std::lock_guard<std::mutex> lock(ctx->c.mu);
+        DeviceGuard g(ctx->c.device);
+        std::string msg;
+        const crx::Status s = crx::apply_impl(ctx->c, u->u, device_copies, cached_checksums, has_cached,
+                                              static_cast<cudaStream_t>(stream), changed, &msg, nullptr, nullptr,
+                                              host_weights);
+        if (s != crx::kOk) {
+            put_err(err, errlen, msg);
+            return int(s);
+        }
+        return CRX_OK;
+    } catch (const std::bad_alloc&) {
+        put_err(err, errlen, "crx_apply_to_host: out of host memory");
+        return CRX_NO_MEMORY;
+    } catch (const std::exception& ex) {
+        put_err(err, errlen, std::string("crx_apply_to_host: ") + ex.what());
+        return CRX_CUDA_ERROR;
+    }
+}
+
 int crx_apply_versioned(crx_ctx* ctx, const crx_update* u, int16_t* const* weights, const uint64_t* cached_checksums,
                         const uint8_t* has_cached, const uint64_t* versions, const uint8_t* has_version, void* stream,
                         int64_t* changed, char* err, size_t errlen) {
@@ -1053,6 +1085,28 @@ int crx_checksum(crx_ctx* ctx, const int16_t* data, int64_t n, void* stream, uin
         return CRX_OK;
     } catch (const std::exception& ex) {
         put_err(err, errlen, std::string("crx_checksum: ") + ex.what());
+        return CRX_CUDA_ERROR;
+    }
+}
+
+int crx_size_stats(crx_ctx* ctx, int32_t n_tensors, const int16_t* const* prev, const int16_t* const* cur,
+                   const int64_t* numel, void* stream, uint64_t* out, char* err, size_t errlen) {
+    if (!ctx || !out || n_tensors < 0 || (n_tensors && (!prev || !cur || !numel))) return CRX_BAD_ARGUMENT;
+    static_assert(CRX_SIZE_STATS_WORDS == 3 + 64 + 2 * 65536, "stats layout");
+    try {
+        if (crx::size_stats_words() != CRX_SIZE_STATS_WORDS) return CRX_CUDA_ERROR;
+        std::lock_guard<std::mutex> lock(ctx->c.mu);
+        DeviceGuard g(ctx->c.device);
+        std::string msg;
+        const crx::Status s = crx::size_stats_impl(ctx->c, n_tensors, prev, cur, numel, static_cast<cudaStream_t>(stream),
+                                                   out, &msg);
+        if (s != crx::kOk) {
+            put_err(err, errlen, msg);
+            return int(s);
+        }
+        return CRX_OK;
+    } catch (const std::exception& ex) {
+        put_err(err, errlen, std::string("crx_size_stats: ") + ex.what());
         return CRX_CUDA_ERROR;
     }
 }

@@ -74,9 +74,14 @@ Status encode_impl(Ctx& C, int n, const int16_t* const* prev, const int16_t* con
 // success.  old_chk/has_chk: the receiver's trusted checksum of each tensor's current contents.
 Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64_t* old_chk, const uint8_t* has_chk,
                   cudaStream_t st, int64_t* changed, std::string* err, const uint64_t* versions = nullptr,
-                  const uint8_t* has_version = nullptr);
+                  const uint8_t* has_version = nullptr, int16_t* const* host_weights = nullptr);
 
 // Full checksum of one device tensor (reference codec.checksum).
 Status checksum_impl(Ctx& C, const int16_t* data, int64_t n, cudaStream_t st, uint64_t* out, std::string* err);
+
+// Histograms behind the size comparison (sizes.cu); `out` (host) receives size_stats_words() u64.
+int size_stats_words();
+Status size_stats_impl(Ctx& C, int n, const int16_t* const* prev, const int16_t* const* cur, const int64_t* numel,
+                       cudaStream_t st, uint64_t* out, std::string* err);
 
 }  // namespace crx

@@ -56,6 +56,10 @@ enum Slot : int {
     S_A_TENS, S_A_GROUPS, S_A_TABLES, S_A_SYMS, S_A_PAYLOAD, S_A_BB, S_A_BOFF, S_A_GAPS, S_A_ZZ, S_A_BSUM,
     S_A_LOCAL, S_A_CADDR, S_A_CVAL, S_A_HS, S_A_TOT, S_A_CHUNK_ROWS, S_A_CHUNK_SUMS, S_A_COUNTERS, S_A_SCAN_TMP,
     S_CHK, S_REC_POS, S_SUPER_T, S_A_HNEW, S_A_HSTORE, S_A_ORDER,
+    // size statistics
+    S_SZ_STATS, S_SZ_TILES,
+    // apply: first value slot of every span of the commit list
+    S_A_SPANB,
     S_NSLOTS
 };
 

@@ -187,6 +187,18 @@ int crx_apply(crx_ctx* ctx, const crx_update* u, int16_t* const* weights, const 
 int crx_apply_versioned(crx_ctx* ctx, const crx_update* u, int16_t* const* weights, const uint64_t* cached_checksums,
                         const uint8_t* has_cached, const uint64_t* versions, const uint8_t* has_version, void* stream,
                         int64_t* changed, char* err, size_t errlen);
+/*
+ * crx_apply for weights the caller keeps in host memory (the reference accepts CPU tensors,
+ * src/crukx_sync/codec.py:578-592, and writes them in place, :713-714).  device_copies[i] hold
+ * the same bits as host_weights[i] (the caller uploaded them); the update is decoded, placed and
+ * verified against the copies exactly as crx_apply does, and on success only the changed elements
+ * are written into host_weights (the commit list -- a bit per element and the new values -- comes
+ * down once and host threads scatter it).  The device copies are left as they were.  On any error
+ * nothing is written.  host_weights[i] must stay valid and unused by others until it returns.
+ */
+int crx_apply_to_host(crx_ctx* ctx, const crx_update* u, int16_t* const* device_copies, int16_t* const* host_weights,
+                      const uint64_t* cached_checksums, const uint8_t* has_cached, void* stream, int64_t* changed,
+                      char* err, size_t errlen);
 /* Tensors whose histogram pass was skipped by the cache so far (instrumentation). */
 uint64_t crx_ctx_hist_cache_hits(crx_ctx* ctx);
 
@@ -214,6 +226,20 @@ int crx_checksum(crx_ctx* ctx, const int16_t* data, int64_t n, void* stream, uin
  * device (two streams or unordered host threads) race on the scratch; order them. */
 #define CRX_CHECKSUM_NOALLOC_MAX (INT64_C(1) << 30)
 int crx_checksum_noalloc(const int16_t* data, int64_t n, void* stream, uint64_t* out, char* err, size_t errlen);
+
+/*
+ * Histograms behind the update-size comparison of the reference's bench/compare.py (:56-100, its
+ * raw, sparserl and ctxfree columns), over n tensors of old/new bits on the context's device, in
+ * one pass.  out (host) receives CRX_SIZE_STATS_WORDS u64: [0] changed elements, [1] changes
+ * whose position delta needs more than 16 bits, [2] the sum over changes of
+ * max(bit_length(gap) - 1, 0), [3, 67) changes per gap bit length, then 65536 counts of the new
+ * values' bit patterns and 65536 counts of old ^ new.  The gap of a change is its distance to the
+ * tensor's previous change minus one; the tensor's first change has gap = delta = its index.
+ * crukx_sync_b200.sizes turns these into the three sizes with compare.py's formulas.
+ */
+#define CRX_SIZE_STATS_WORDS (3 + 64 + 2 * 65536)
+int crx_size_stats(crx_ctx* ctx, int32_t n_tensors, const int16_t* const* prev, const int16_t* const* cur,
+                   const int64_t* numel, void* stream, uint64_t* out, char* err, size_t errlen);
 
 #ifdef __cplusplus
 }
