@@ -388,6 +388,7 @@ def run_ours(args, rank, world, dist):
     L = _ext.load()
     stream = torch.cuda.current_stream(dev)
     size_group = cdist.host_size_group() if dist is not None else None
+    side = torch.cuda.Stream(dev)   # the all-gather runs here, beside the apply
 
     def barrier():
         if dist is not None:
@@ -399,6 +400,12 @@ def run_ours(args, rank, world, dist):
         requested ranks' updates from the gathered buffer."""
         return cdist.allgather_updates_device(upd, ranks=list(ranks), size_group=size_group)
 
+    def start_exchange(upd):
+        """The same all-gather on the side stream, overlapping the caller's next work (N > 1)."""
+        if dist is None:
+            return None
+        return cdist.allgather_updates_device_async(upd, size_group=size_group, side_stream=side)
+
     state = {"src": A, "dst": B, "src_is_A": True}
 
     def flip():
@@ -407,21 +414,29 @@ def run_ours(args, rank, world, dist):
 
     def step(events=None):
         """One sync step with the updates resident in HBM: encode_update_device (the reference's
-        bytes, in device memory), NCCL all-gather, apply_update of this rank's update."""
+        bytes, in device memory); the NCCL all-gather that gives every rank every update, on a side
+        stream while this rank applies its own update (which it holds); the step ends when both
+        are done.  events: start, encode done, apply done, step done (gather included)."""
         src, dst = state["src"], state["dst"]
         if events:
             events[0].record(stream)
         upd = crx.encode_update_device(src, dst, sender)
         if events:
             events[1].record(stream)
-        mine_u = exchange(upd)[0]
+        pg = start_exchange(upd)
+        st = crx.apply_update(recv, upd, receiver)
         if events:
             events[2].record(stream)
-        st = crx.apply_update(recv, mine_u, receiver)
+        if pg is not None:
+            pg.wait()
+            if events is not None:
+                gathers.append((events[1], pg.event))
         if events:
             events[3].record(stream)
         flip()
         return upd, st
+
+    gathers = []   # (encode done, gather done) per timed step
 
     for i in range(args.warmup):
         log("warmup step", i)
@@ -443,9 +458,10 @@ def run_ours(args, rank, world, dist):
         t_wall = time.perf_counter() - t_wall0
     launches = int(L.crx_ctx_launches(ctx) + L.crx_parse_device_launches() - launches0)   # + the device parses' table checks
     enc = [e[0].elapsed_time(e[1]) for e in evs]
-    ex = [e[1].elapsed_time(e[2]) for e in evs]
-    app = [e[2].elapsed_time(e[3]) for e in evs]
+    app = [e[1].elapsed_time(e[2]) for e in evs]
     tot = [e[0].elapsed_time(e[3]) for e in evs]
+    # the gather: from the end of the encode to the end of the NCCL all-gather (it overlaps the apply)
+    ex = [a.elapsed_time(b) for a, b in gathers[-args.steps:]] or [0.0]
     for k in recv:
         assert torch.equal(recv[k], state["src"][k]), f"receiver differs after timing: {k}"
     ms_step = sum(tot) / len(tot)
@@ -550,11 +566,14 @@ def run_ours(args, rank, world, dist):
             if events:
                 events[0].record(stream)
             upd = crx.encode_update_device(src, dst, sender)
-            allu = exchange(upd, ranks=range(world))
+            pg = start_exchange(upd)
             if events:
                 events[1].record(stream)
-            for u in allu:
-                crx.apply_update(replica, u, rep_chk)
+            crx.apply_update(replica, upd, rep_chk)   # its own update first, while the others arrive
+            pg.wait()
+            for r, u in enumerate(pg.views()):
+                if r != rank:
+                    crx.apply_update(replica, u, rep_chk)
             if events:
                 events[2].record(stream)
             flip()
@@ -576,7 +595,7 @@ def run_ours(args, rank, world, dist):
         dist.all_reduce(rt, op=dist.ReduceOp.MAX)
         r_step, r_encx, r_app = rt.tolist()
         full_replica = {"value": round(2.0 * total_params / (r_step * 1e-3) / 1e9, 2), "unit": "GB/s",
-                        "ms_per_step": round(r_step, 4), "encode_exchange_ms": round(r_encx, 4),
+                        "ms_per_step": round(r_step, 4), "encode_ms": round(r_encx, 4),
                         "apply_all_ms": round(r_app, 4), "steps": nrep, "scaling": "strong",
                         "receiver": "full replica: every rank applies all N updates to a whole copy of the model",
                         "note": "GB/s of bf16 weights per sync step (the model's bytes over the step time)"}
@@ -596,7 +615,7 @@ def run_ours(args, rank, world, dist):
         state.clear()
         del A, B, recv
         torch.cuda.empty_cache()
-        tp8 = run_tp8_shard(args, rank, world, dev, dist, exchange, barrier, peak)
+        tp8 = run_tp8_shard(args, rank, world, dev, dist, start_exchange, barrier, peak)
 
     # ---- CPU baselines on a bounded sample of the same workload (rank 0, N = 1): the oracle port
     #      (one whole-dict update per step on every host thread) and the reference's own torch code
@@ -636,12 +655,14 @@ def run_ours(args, rank, world, dist):
                    if world > 1 else "single GPU",
                    "receiver": "partitioned: every rank applies the update of its own tensors, taken from the "
                                "gathered buffer" if world > 1 else "single GPU: the sender's GPU applies the update",
-                   "path": "encode_update_device -> (NCCL all-gather, sizes between the hosts) -> apply_update of "
-                           "the device update; the reference's bytes, kept in HBM",
+                   "path": "encode_update_device -> apply_update of the device update; at N > 1 the NCCL all-gather "
+                           "that gives every rank every update (sizes between the hosts) runs on a side stream beside "
+                           "the apply, and the step ends when both are done; the reference's bytes, kept in HBM",
                    "l2": "inputs larger than L2 (each state 2 B x params; no flush needed)"},
         "encode_gbs": round(weight_bytes / (ms_enc * 1e-3) / 1e9, 2),
         "apply_gbs": round(weight_bytes / (ms_app * 1e-3) / 1e9, 2),
-        "exchange_ms": round(ms_ex, 4), "encode_ms": round(ms_enc, 4), "apply_ms": round(ms_app, 4),
+        "exchange_ms": round(ms_ex, 4), "exchange_note": "encode end to all-gather end, overlapping the apply",
+        "encode_ms": round(ms_enc, 4), "apply_ms": round(ms_app, 4),
         "update_bytes": int(upd_bytes), "bytes_per_changed": round(upd_bytes / max(changed_all, 1), 4),
         "wall_s_timed": round(t_wall, 3), "roofline_step": per_rank,
         "roofline": roofline, "kernels": kernels, "cpu_baseline": cpu, "e2e": e2e, "bytes_api": bytes_api,
@@ -656,7 +677,7 @@ def run_ours(args, rank, world, dist):
     return result
 
 
-def run_tp8_shard(args, rank, world, dev, dist, exchange, barrier, peak):
+def run_tp8_shard(args, rank, world, dev, dist, start_exchange, barrier, peak):
     """Qwen2.5-32B shapes cut 8 ways tensor-parallel; rank r holds shard r
     (seed 100 + r) and encodes and applies it, the updates crossing an NCCL all-gather."""
     import crukx_sync_b200 as crx
@@ -675,10 +696,12 @@ def run_tp8_shard(args, rank, world, dev, dist, exchange, barrier, peak):
         upd = crx.encode_update_device(st["src"], st["dst"], sender)
         if events:
             events[1].record(stream)
-        u = exchange(upd)[0]
+        pg = start_exchange(upd)
+        crx.apply_update(recv, upd, receiver)
         if events:
             events[2].record(stream)
-        crx.apply_update(recv, u, receiver)
+        if pg is not None:
+            pg.wait()
         if events:
             events[3].record(stream)
         st["src"], st["dst"] = st["dst"], st["src"]
@@ -695,13 +718,13 @@ def run_tp8_shard(args, rank, world, dev, dist, exchange, barrier, peak):
         assert torch.equal(recv[k], st["src"][k]), f"tp8 receiver differs: {k}"
     t = torch.tensor([sum(e[0].elapsed_time(e[3]) for e in evs) / n, sum(e[0].elapsed_time(e[1]) for e in evs) / n,
                       sum(e[1].elapsed_time(e[2]) for e in evs) / n, sum(e[2].elapsed_time(e[3]) for e in evs) / n],
-                     dtype=torch.float64, device=dev)
+                     dtype=torch.float64, device=dev)   # step, encode, apply, gather tail after the apply
     if dist is not None:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms, ms_e, ms_x, ms_a = t.tolist()
+    ms, ms_e, ms_a, ms_x = t.tolist()
     upd = sum(sizes) / len(sizes)
     out = {"value": round(world * 2.0 * params / (ms * 1e-3) / 1e9, 2), "unit": "GB/s", "ms_per_step": round(ms, 4),
-           "encode_ms": round(ms_e, 4), "exchange_ms": round(ms_x, 4), "apply_ms": round(ms_a, 4), "steps": n,
+           "encode_ms": round(ms_e, 4), "apply_ms": round(ms_a, 4), "gather_tail_ms": round(ms_x, 4), "steps": n,
            "params_per_rank": params, "changed_frac": round(changed / params, 5), "update_bytes_per_rank": int(upd),
            "scaling": "weak", "workload": "qwen2.5-32b-shape, 8-way TP shard per rank (seed 100 + rank)",
            "receiver": "per shard: every rank applies its own shard's update, taken from the gathered buffer",

@@ -113,6 +113,67 @@ def allgather_updates_device(update, group=None, ranks: Sequence[int] | None = N
     return [out[r * mx: r * mx + sizes[r]] for r in want]
 
 
+class PendingGather:
+    """An all-gather of device updates in flight on a side stream (allgather_updates_device_async).
+    views() are valid for work ordered after wait(); wait() makes the caller's current stream (or
+    `stream`) wait for the gather."""
+
+    def __init__(self, out, sizes, mx, event):
+        self.out, self.sizes, self.mx, self.event = out, sizes, mx, event
+
+    def views(self, ranks: Sequence[int] | None = None) -> list:
+        want = range(len(self.sizes)) if ranks is None else ranks
+        return [self.out[r * self.mx: r * self.mx + self.sizes[r]] for r in want]
+
+    def wait(self, stream=None):
+        if self.event is not None:
+            (stream or torch.cuda.current_stream(self.out.device)).wait_event(self.event)
+
+
+def allgather_updates_device_async(update, group=None, size_group=None, side_stream=None) -> PendingGather:
+    """allgather_updates_device that does not hold up the caller's stream: the sizes go between
+    the hosts first (size_group, a gloo group: nothing waits for the device), then the NCCL gather
+    runs on `side_stream` after the work already queued on the current stream (the encode that
+    produced `update`), so the caller can go on -- e.g. apply its own update, which it holds
+    locally -- while the updates cross NVLink."""
+    import torch.distributed as td
+
+    world = td.get_world_size(group) if td.is_initialized() else 1
+    if world == 1 or update.device.type != "cuda" or side_stream is None:
+        views = allgather_updates_device(update, group=group, size_group=size_group)
+        sizes = [v.numel() for v in views]
+        mx = max(max(sizes), 1)
+        out = torch.zeros(world * mx, dtype=torch.uint8, device=update.device)
+        for r, v in enumerate(views):
+            out[r * mx: r * mx + v.numel()].copy_(v)
+        return PendingGather(out, sizes, mx, None)
+    if size_group is not None:
+        n = torch.tensor([update.numel()], dtype=torch.int64)
+        sizes_t = torch.empty(world, dtype=torch.int64)
+        td.all_gather_into_tensor(sizes_t, n, group=size_group)
+    else:
+        n = torch.tensor([update.numel()], dtype=torch.int64, device=update.device)
+        sizes_t = torch.empty(world, dtype=torch.int64, device=update.device)
+        td.all_gather_into_tensor(sizes_t, n, group=group)
+    sizes = sizes_t.tolist()
+    mx = max(max(sizes), 1)
+    main = torch.cuda.current_stream(update.device)
+    side_stream.wait_stream(main)
+    with torch.cuda.stream(side_stream):
+        if update.numel() == mx:
+            buf = update
+        else:
+            buf = torch.empty(mx, dtype=torch.uint8, device=update.device)
+            buf[: update.numel()].copy_(update)
+            buf[update.numel():].zero_()
+        out = torch.empty(world * mx, dtype=torch.uint8, device=update.device)
+        td.all_gather_into_tensor(out, buf, group=group)
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(side_stream)
+    update.record_stream(side_stream)
+    return PendingGather(out, sizes, mx, ev)
+
+
 def partition_contiguous(numels: Sequence[int], world: int) -> list[tuple[int, int]]:
     """Split tensors 0..n-1 (update order) into `world` contiguous ranges of about equal elements;
     range r = (first, end) for rank r (possibly empty)."""

@@ -93,6 +93,9 @@ def _worker(rank, world, port, outdir):
             assert [bytes(v.numpy().tobytes()) for v in views] == got
             mine_only = cdist.allgather_updates_device(t, ranks=[rank], size_group=size_group)
             assert bytes(mine_only[0].numpy().tobytes()) == upd
+            pg = cdist.allgather_updates_device_async(t, size_group=size_group)   # CPU: completes at once
+            pg.wait()
+            assert [bytes(v.numpy().tobytes()) for v in pg.views()] == got
         with open(os.path.join(outdir, f"ok{rank}"), "w") as f:
             f.write(str(len(upd)))
     finally:
