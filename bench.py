@@ -190,6 +190,16 @@ def kernel_times(ctx):
     return out
 
 
+def kernel_gaps(ctx):
+    """Per kernel: ms its stream sat idle before it (host work and round trips in between)."""
+    from crukx_sync_b200 import _ext
+    L = _ext.load()
+    names = ctypes.create_string_buffer(8192)
+    ms = (ctypes.c_double * 64)()
+    n = L.crx_ctx_kernel_gaps(ctx, names, 8192, ms, 64)
+    return {nm: ms[i] for i, nm in enumerate(names.value.decode().split("\n")[:n])}
+
+
 def cpu_baseline_sample(shapes, lr, budget_elems, seed=1):
     """A bounded sample of the workload (whole tensors, in order, up to budget) on the CPU."""
     names, tot = [], 0
@@ -361,6 +371,10 @@ def run_ours(args, rank, world, dist):
     shapes_all = cfg["shapes"]()
     if cfg.get("drop_embed"):
         shapes_all = {k: v for k, v in shapes_all.items() if "embed" not in k}
+    if args.emulate:   # one rank's share of an N-way run, alone on this GPU (no exchange)
+        er, en = (int(x) for x in args.emulate.split("/"))
+        owner = cdist.partition({k: int(torch.tensor(v).prod()) for k, v in shapes_all.items()}, en)
+        shapes_all = {k: v for k, v in shapes_all.items() if owner[k] == er}
     owner = cdist.partition({k: int(torch.tensor(v).prod()) for k, v in shapes_all.items()}, world)
     mine = [k for k in shapes_all if owner[k] == rank]
     total_params = sum(int(torch.tensor(s).prod()) for s in shapes_all.values())
@@ -522,12 +536,14 @@ def run_ours(args, rank, world, dist):
         step()
     torch.cuda.synchronize(dev)
     kt = kernel_times(ctx)
+    kg = kernel_gaps(ctx)
     L.crx_ctx_profile(ctx, 0)
     algo = {"k_enc_rank": 4.0 * my_params, "k_map": 2.0 * my_params, "k_app_hist": 2.0 * my_params}
     kernels = {}
     for nm, (ms, n) in sorted(kt.items(), key=lambda x: -x[1][0]):
         per = ms / max(n, 1)
-        row = {"ms_per_launch": round(per, 4), "launches": n, "share": None}
+        row = {"ms_per_launch": round(per, 4), "launches": n, "share": None,
+               "idle_before_ms": round(kg.get(nm, 0.0) / max(n, 1), 4)}
         if nm in algo:
             row["algo_gbs"] = round(algo[nm] / (per * 1e-3) / 1e9, 1)
         kernels[nm] = row
@@ -876,6 +892,8 @@ def main():
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-parity", action="store_true", help="skip the oracle check of the first update")
     ap.add_argument("--no-receivers", action="store_true", help="skip the full-replica and 32B-TP8 lines")
+    ap.add_argument("--emulate", default="", help="R/N: time rank R's tensors of an N-way partition on one GPU "
+                                                   "(a development aid; the line then describes that share)")
     ap.add_argument("--no-ref-gpu", action="store_true", help="skip the reference's own GPU path line")
     ap.add_argument("--ref-gpu-timeout", type=int, default=300)
     ap.add_argument("--ref-gpu-child", action="store_true", help=argparse.SUPPRESS)

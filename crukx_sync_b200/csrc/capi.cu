@@ -60,6 +60,7 @@ KernelScope::KernelScope(Ctx& ctx, const char* name, cudaStream_t st) : c(ctx), 
     }
     if (c.profile) {
         m.name = name;
+        m.s = s;
         m.a = pooled_event(c);
         m.b = pooled_event(c);
         if (m.a) cudaEventRecord(m.a, s);
@@ -624,6 +625,10 @@ struct DevParse {
     size_t cap = 0;
     void* spans = nullptr;
     size_t spans_cap = 0;
+    uint8_t* res = nullptr;     // pinned: the block-table check's results (bit total, short flag)
+    uint8_t* spin = nullptr;    // pinned: the group spans going up for the check
+    size_t spin_cap = 0;
+    int64_t last_head = 0;      // header length of the last update parsed here: the next first copy's size
 };
 std::mutex g_devparse_mu;                                   // guards the map only
 std::unordered_map<int, std::unique_ptr<DevParse>> g_devparse;
@@ -698,55 +703,70 @@ bool stage_pinned(DevParse& P, size_t bytes) {
     return true;
 }
 
-// sums and checks u's block table at `table` in device memory (stream-ordered, one synchronisation;
-// the caller holds P.mu)
-int check_device_block_table(DevParse& P, crx::Update* u, const uint8_t* table, uint8_t last, cudaStream_t st,
-                             std::string* msg) {
-    uint64_t total = 0;
-    bool short_block = false;
-    if (u->n_blocks > 0) {
-        std::vector<uint64_t> fb, cr;
-        crx::block_spans(*u, &fb, &cr);
-        const int64_t ns = int64_t(fb.size());
-        const size_t span_bytes = 16 * size_t(ns);
-        if (!stage_pinned(P, span_bytes + 16)) return CRX_CUDA_ERROR;
-        std::memcpy(P.pinned, fb.data(), 8 * size_t(ns));
-        std::memcpy(P.pinned + 8 * size_t(ns), cr.data(), 8 * size_t(ns));
-        if (P.spans_cap < span_bytes) {
-            crx::note_alloc();
-            if (P.spans && cudaFree(P.spans) != cudaSuccess) return CRX_CUDA_ERROR;
-            P.spans = nullptr;
-            P.spans_cap = 0;
-            const size_t cap = std::max(span_bytes, size_t(1) << 20);
-            crx::note_alloc();
-            if (cudaMalloc(&P.spans, cap) != cudaSuccess) return CRX_CUDA_ERROR;
-            P.spans_cap = cap;
-        }
-        void* dspan = P.spans;
-        void* dtot = nullptr;
-        void* dshort = nullptr;
-        const uint64_t* dfb = static_cast<const uint64_t*>(dspan);
-        const uint64_t* dcr = dfb + ns;
-        bool ok = cudaMemcpyAsync(dspan, P.pinned, span_bytes, cudaMemcpyHostToDevice, st) == cudaSuccess &&
-                  cudaGetSymbolAddress(&dtot, g_bt_total) == cudaSuccess &&
-                  cudaGetSymbolAddress(&dshort, g_bt_short) == cudaSuccess &&
-                  cudaMemsetAsync(dtot, 0, 8, st) == cudaSuccess && cudaMemsetAsync(dshort, 0, 4, st) == cudaSuccess;
-        if (ok) {
-            const int64_t grid = crx::tmin<int64_t>((u->n_blocks + 255) / 256, 148 * 8);
-            k_check_block_table<<<unsigned(grid), 256, 0, st>>>(table, u->n_blocks, dfb, dcr, ns);
-            ++g_parse_launches;
-            ok = cudaGetLastError() == cudaSuccess &&
-                 cudaMemcpyAsync(P.pinned, dtot, 8, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
-                 cudaMemcpyAsync(P.pinned + 8, dshort, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess;
-        }
-        ok = cudaStreamSynchronize(st) == cudaSuccess && ok;
-        if (!ok) return CRX_CUDA_ERROR;
-        std::memcpy(&total, P.pinned, 8);
-        uint32_t sh = 0;
-        std::memcpy(&sh, P.pinned + 8, 4);
-        short_block = sh != 0;
+// queues the check of u's block table at `table` in device memory: its bit total and whether some
+// block is shorter than its symbols could be, into P.res (read after the caller's next
+// synchronisation of `st`); the caller holds P.mu
+int issue_block_table_check(DevParse& P, const crx::Update& u, const uint8_t* table, cudaStream_t st) {
+    if (!P.res) {
+        crx::note_alloc();
+        if (cudaMallocHost(reinterpret_cast<void**>(&P.res), 64) != cudaSuccess) { P.res = nullptr; return CRX_CUDA_ERROR; }
     }
-    return int(crx::finish_block_table_checks(u, total, short_block, last, msg));
+    std::memset(P.res, 0, 16);
+    if (u.n_blocks <= 0) return CRX_OK;
+    std::vector<uint64_t> fb, cr;
+    crx::block_spans(u, &fb, &cr);
+    const int64_t ns = int64_t(fb.size());
+    const size_t span_bytes = 16 * size_t(ns);
+    if (P.spans_cap < span_bytes + 16) {
+        crx::note_alloc();
+        if (P.spans && cudaFree(P.spans) != cudaSuccess) return CRX_CUDA_ERROR;
+        P.spans = nullptr;
+        P.spans_cap = 0;
+        const size_t cap = std::max(span_bytes + 16, size_t(1) << 20);
+        crx::note_alloc();
+        if (cudaMalloc(&P.spans, cap) != cudaSuccess) return CRX_CUDA_ERROR;
+        P.spans_cap = cap;
+    }
+    // the spans go up from their own pinned buffer (a pageable source would synchronise the stream;
+    // head and window copies use P.pinned); it is reused only after the caller's synchronisation
+    if (P.spin_cap < span_bytes) {
+        crx::note_alloc();
+        if (P.spin) cudaFreeHost(P.spin);
+        P.spin = nullptr;
+        P.spin_cap = 0;
+        const size_t cap = std::max(span_bytes, size_t(1) << 20);
+        crx::note_alloc();
+        if (cudaMallocHost(reinterpret_cast<void**>(&P.spin), cap) != cudaSuccess) { P.spin = nullptr; return CRX_CUDA_ERROR; }
+        P.spin_cap = cap;
+    }
+    std::memcpy(P.spin, fb.data(), 8 * size_t(ns));
+    std::memcpy(P.spin + 8 * size_t(ns), cr.data(), 8 * size_t(ns));
+    const uint64_t* dfb = static_cast<const uint64_t*>(P.spans);
+    const uint64_t* dcr = dfb + ns;
+    void* dtot = nullptr;
+    void* dshort = nullptr;
+    bool ok = cudaMemcpyAsync(P.spans, P.spin, span_bytes, cudaMemcpyHostToDevice, st) == cudaSuccess &&
+              cudaGetSymbolAddress(&dtot, g_bt_total) == cudaSuccess &&
+              cudaGetSymbolAddress(&dshort, g_bt_short) == cudaSuccess &&
+              cudaMemsetAsync(dtot, 0, 8, st) == cudaSuccess && cudaMemsetAsync(dshort, 0, 4, st) == cudaSuccess;
+    if (ok) {
+        const int64_t grid = crx::tmin<int64_t>((u.n_blocks + 255) / 256, 148 * 8);
+        k_check_block_table<<<unsigned(grid), 256, 0, st>>>(table, u.n_blocks, dfb, dcr, ns);
+        ++g_parse_launches;
+        ok = cudaGetLastError() == cudaSuccess &&
+             cudaMemcpyAsync(P.res, dtot, 8, cudaMemcpyDeviceToHost, st) == cudaSuccess &&
+             cudaMemcpyAsync(P.res + 8, dshort, 4, cudaMemcpyDeviceToHost, st) == cudaSuccess;
+    }
+    return ok ? CRX_OK : CRX_CUDA_ERROR;
+}
+
+// after the synchronisation that follows issue_block_table_check: the table's verdict
+int finish_block_table_check(DevParse& P, crx::Update* u, uint8_t last, std::string* msg) {
+    uint64_t total = 0;
+    uint32_t sh = 0;
+    std::memcpy(&total, P.res, 8);
+    std::memcpy(&sh, P.res + 8, 4);
+    return int(crx::finish_block_table_checks(u, total, sh != 0, last, msg));
 }
 
 }  // namespace
@@ -774,9 +794,11 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
         };
         auto stage = [&](size_t bytes) { return stage_pinned(P, bytes); };
         uint8_t last = 0;
-        int64_t have = std::min<int64_t>(len, int64_t(1) << 16);
+        // the first copy: as long as the last header parsed here (updates of one model are alike)
+        int64_t have = std::min<int64_t>(len, std::max<int64_t>(int64_t(1) << 16, P.last_head + 4096));
         int64_t got = 0;      // bytes [0, got) of the update are in `head`
         int64_t avail = 0;    // what the parser may read: [0, got), and past the block table a window after it
+        bool checked = false; // the block table's check is queued (its results land with the window)
         for (;;) {   // copy a head, parse it, copy more when the header reaches past it
             if (have > got) {
                 if (!stage(size_t(have - got) + 1)) return CRX_CUDA_ERROR;
@@ -798,7 +820,13 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
             const crx::Status s = crx::parse_head_device_table(head.data(), avail, len, last, &u->u, &nd, &msg);
             if (s == crx::kOk) {
                 const int64_t t0 = u->u.block_table_offset;
-                const int rc = check_device_block_table(P, &u->u, data + t0, last, st, &msg);
+                P.last_head = t0;
+                int rc = CRX_OK;
+                if (!checked) {
+                    rc = issue_block_table_check(P, u->u, data + t0, st);
+                    if (rc == CRX_OK && cudaStreamSynchronize(st) != cudaSuccess) rc = CRX_CUDA_ERROR;
+                }
+                if (rc == CRX_OK) rc = finish_block_table_check(P, &u->u, last, &msg);
                 if (rc != CRX_OK) {
                     delete u;
                     keep();
@@ -814,6 +842,17 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
             }
             const int64_t t0 = u->u.block_table_offset;
             const int64_t t1 = t0 >= 0 ? t0 + 4 * u->u.n_blocks : -1;
+            if (s == crx::kNeedMore && t0 >= 0 && nd > t0 && got >= t0 && !checked) {
+                // the header is complete: queue the block table's check now, so that its results
+                // come back with the window copied below (one synchronisation for both)
+                const int rc = issue_block_table_check(P, u->u, data + t0, st);
+                if (rc != CRX_OK) {
+                    delete u;
+                    keep();
+                    return rc;
+                }
+                checked = true;
+            }
             delete u;
             if (s != crx::kNeedMore) {
                 keep();
@@ -1064,6 +1103,35 @@ int32_t crx_ctx_kernel_times(crx_ctx* ctx, char* names, size_t names_len, double
             if (ms) ms[k] = tot[k];
             if (counts) counts[k] = cnt[k];
         }
+        joined += order[k];
+        joined += '\n';
+    }
+    if (names && names_len) std::snprintf(names, names_len, "%s", joined.c_str());
+    return int32_t(order.size());
+}
+
+int32_t crx_ctx_kernel_gaps(crx_ctx* ctx, char* names, size_t names_len, double* gap_ms, int32_t max) {
+    if (!ctx) return -1;
+    std::lock_guard<std::mutex> lock(ctx->c.mu);
+    DeviceGuard g(ctx->c.device);
+    std::vector<std::string> order;
+    std::vector<double> tot;
+    const crx::ProfMark* prev = nullptr;
+    for (const crx::ProfMark& m : ctx->c.marks) {
+        float t = 0.f;
+        const bool ok = prev && prev->s == m.s && cudaEventSynchronize(m.a) == cudaSuccess &&
+                        cudaEventElapsedTime(&t, prev->b, m.a) == cudaSuccess;
+        if (!ok) cudaGetLastError();
+        prev = &m;
+        if (!ok) continue;
+        size_t k = 0;
+        while (k < order.size() && order[k] != m.name) ++k;
+        if (k == order.size()) { order.push_back(m.name); tot.push_back(0.0); }
+        tot[k] += t > 0.f ? t : 0.f;
+    }
+    std::string joined;
+    for (size_t k = 0; k < order.size(); ++k) {
+        if (int32_t(k) < max && gap_ms) gap_ms[k] = tot[k];
         joined += order[k];
         joined += '\n';
     }

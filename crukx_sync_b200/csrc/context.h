@@ -66,6 +66,7 @@ enum Slot : int {
 struct ProfMark {
     const char* name;
     cudaEvent_t a, b;
+    cudaStream_t s = nullptr;   // the stream the kernel ran on
 };
 
 struct Encoded;

@@ -16,6 +16,7 @@
 //   k_block_bits   bits per 256-change block (codec.py:411-416), then an exclusive scan.
 //   k_pack         one warp per block assembles its bits MSB-first (codec.py:218-257).
 #include <algorithm>
+#include <cstdio>
 #include <cstring>
 #include <string>
 #include <vector>
@@ -944,14 +945,21 @@ void build_tables(const std::vector<uint64_t>& dense, const std::vector<std::pai
     for (int e = 0; e < 256; ++e)
         if (!tabs->sym[e].empty()) todo.push_back(e);
     std::sort(todo.begin(), todo.end(), [&](int a, int b) { return tabs->sym[a].size() > tabs->sym[b].size(); });
-    parallel_for(todo.size(), [&](size_t k) {
+    size_t total = 0;
+    for (int e : todo) total += tabs->sym[e].size();
+    auto one = [&](size_t k) {
         const int e = todo[k];
         const size_t ns = tabs->sym[e].size();
         tabs->len[e].resize(ns);
         tabs->code[e].resize(ns);
         huffman_lengths(tabs->cnt[e].data(), int64_t(ns), tabs->len[e].data());
         canonical_codes(tabs->len[e].data(), int64_t(ns), tabs->code[e].data());
-    });
+    };
+    if (total < 8192) {   // small alphabets: waking the pool costs more than the work
+        for (size_t k = 0; k < todo.size(); ++k) one(k);
+    } else {
+        parallel_for(todo.size(), one);
+    }
 }
 
 // Global mode: the histogram summed over ranks (dense part by sum, rare pairs gathered and merged)
@@ -1228,7 +1236,10 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     const size_t off_cost = off_gc + 8 * size_t(ng), off_dense = off_cost + 24 * size_t(ng);
     const size_t off_rc = off_dense + 8 * 256 * DENSE_SYM, off_rb = off_rc + 4 * 256, off_chk = off_rb + 8 * 256;
     const size_t off_ctr = off_chk + 16 * size_t(nt), off_cand = off_ctr + 8 * 16;
-    const size_t down1 = off_cand + 4 * size_t(ng);
+    // the first rare-symbol pairs come down in the same round trip (most updates have few)
+    const size_t off_rare = (off_cand + 4 * size_t(ng) + 7) & ~size_t(7);
+    const uint64_t rare_eager = std::min<uint64_t>(rare_cap, 65536);
+    const size_t down1 = off_rare + 8 * size_t(rare_eager);
     CRX_CUDA(ensure_host(C, down1, st));
     uint8_t* h = static_cast<uint8_t*>(C.host);
     CRX_CUDA(cudaMemcpyAsync(h + off_gt, g_tensor, 4 * size_t(ng), cudaMemcpyDeviceToHost, st));
@@ -1241,6 +1252,8 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     CRX_CUDA(cudaMemcpyAsync(h + off_chk, chk_delta, 16 * size_t(nt), cudaMemcpyDeviceToHost, st));
     CRX_CUDA(cudaMemcpyAsync(h + off_ctr, counters, 8 * 16, cudaMemcpyDeviceToHost, st));
     CRX_CUDA(cudaMemcpyAsync(h + off_cand, g_cand, 4 * size_t(ng), cudaMemcpyDeviceToHost, st));
+    if (rare_eager)
+        CRX_CUDA(cudaMemcpyAsync(h + off_rare, C.b[S_RARE_OUT].p, 8 * size_t(rare_eager), cudaMemcpyDeviceToHost, st));
     CRX_CUDA(cudaStreamSynchronize(st));
     std::vector<uint32_t> hcand(static_cast<size_t>(ng));
     std::memcpy(hcand.data(), h + off_cand, 4 * size_t(ng));
@@ -1262,7 +1275,9 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     const uint64_t rare_total = hctr[4];
     if (rare_total > rare_cap) { *err = "internal: rare symbol overflow"; return kCudaError; }
     std::vector<uint64_t> hrare(rare_total);
-    if (rare_total) {
+    if (rare_total && rare_total <= rare_eager) {
+        std::memcpy(hrare.data(), h + off_rare, 8 * rare_total);
+    } else if (rare_total) {
         CRX_CUDA(ensure_host(C, 8 * rare_total, st));
         CRX_CUDA(cudaMemcpyAsync(C.host, C.b[S_RARE_OUT].p, 8 * rare_total, cudaMemcpyDeviceToHost, st));
         CRX_CUDA(cudaStreamSynchronize(st));
@@ -1305,6 +1320,13 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     trace_phase(C, "encode: rice, rare pairs");
     HostTables tabs;
     build_tables(hdense, rare_pairs, &tabs);
+    if (C.trace) {
+        size_t nsym = 0, ntab = 0, biggest = 0;
+        for (int e = 0; e < 256; ++e)
+            if (!tabs.sym[e].empty()) { ++ntab; nsym += tabs.sym[e].size(); biggest = std::max(biggest, tabs.sym[e].size()); }
+        std::fprintf(stderr, "[crx-host] tables: %zu, symbols %zu (largest %zu), rare pairs %zu, groups %lld\n", ntab, nsym,
+                     biggest, rare_pairs.size(), static_cast<long long>(ng));
+    }
 
     trace_phase(C, "encode: huffman (host)");
     // ---- upload rice, block starts, code tables
@@ -1347,6 +1369,7 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     std::memcpy(h + o, rice.data(), size_t(ng));
     CRX_CUDA(cudaMemcpyAsync(g_rice, h + o, size_t(ng), cudaMemcpyHostToDevice, st));
     o += size_t(ng);
+    trace_phase(C, "encode: code tables up");
 
     // ---- block lengths, offsets, payload
     CRX_CUDA(ensure_dev(C.b[S_BLOCK_BITS], sizeof(uint64_t) * size_t(n_blocks), st));

@@ -352,13 +352,58 @@ void huffman_unlimited(const std::vector<uint64_t>& counts, std::vector<int>& de
     for (int64_t i = 0; i < n; ++i) depth_out[size_t(i)] = depth[size_t(i)];
 }
 
+// huffman_unlimited with the leaves sorted as packed 64-bit keys (count << 20 | id): the same
+// (count, id) order, an order of magnitude cheaper to sort than Items; needs every count < 2^44 and
+// n <= 2^20 (the caller checks).  Scratch buffers are reused across the length-limit rounds.
+struct HuffScratch {
+    std::vector<uint64_t> keys, mcount;
+    std::vector<int32_t> parent, depth;
+};
+
+void huffman_unlimited_packed(const std::vector<uint64_t>& counts, std::vector<int>& depth_out, HuffScratch& w) {
+    const int64_t n = int64_t(counts.size());
+    depth_out.assign(size_t(n), 1);
+    if (n == 1) return;
+    w.keys.resize(size_t(n));
+    for (int64_t i = 0; i < n; ++i) w.keys[size_t(i)] = (counts[size_t(i)] << 20) | uint64_t(i);
+    std::sort(w.keys.begin(), w.keys.end());
+    w.mcount.clear();
+    w.mcount.reserve(size_t(n));
+    w.parent.assign(size_t(2 * n - 1), 0);
+    size_t li = 0, mi = 0;
+    // a leaf and a merged node of equal count: the leaf first (leaf ids are below merged ids)
+    auto pop = [&](uint64_t& c) -> int64_t {
+        if (li < size_t(n) && (mi >= w.mcount.size() || (w.keys[li] >> 20) <= w.mcount[mi])) {
+            c = w.keys[li] >> 20;
+            return int64_t(w.keys[li++] & 0xFFFFFu);
+        }
+        c = w.mcount[mi];
+        return n + int64_t(mi++);
+    };
+    for (int64_t k = 0; k < n - 1; ++k) {
+        uint64_t ca, cb;
+        const int64_t a = pop(ca), b = pop(cb);
+        const int64_t id = n + int64_t(w.mcount.size());
+        w.parent[size_t(a)] = int32_t(id);
+        w.parent[size_t(b)] = int32_t(id);
+        w.mcount.push_back(ca + cb);
+    }
+    w.depth.assign(size_t(2 * n - 1), 0);
+    for (int64_t node = 2 * n - 3; node >= 0; --node) w.depth[size_t(node)] = w.depth[size_t(w.parent[size_t(node)])] + 1;
+    for (int64_t i = 0; i < n; ++i) depth_out[size_t(i)] = w.depth[size_t(i)];
+}
+
 }  // namespace
 
 void huffman_lengths(const uint64_t* counts_in, int64_t n, uint8_t* lengths) {
     std::vector<uint64_t> c(counts_in, counts_in + n);
     std::vector<int> d;
+    bool packed = n <= (int64_t(1) << 20);
+    for (int64_t i = 0; i < n && packed; ++i) packed = counts_in[i] < (uint64_t(1) << 44);
+    HuffScratch w;
     for (int round = 0; round < 8; ++round) {          // codec.py:71-78
-        huffman_unlimited(c, d);
+        if (packed) huffman_unlimited_packed(c, d, w);
+        else huffman_unlimited(c, d);
         if (*std::max_element(d.begin(), d.end()) <= kMaxCodeLen) {
             for (int64_t i = 0; i < n; ++i) lengths[i] = uint8_t(d[size_t(i)]);
             return;

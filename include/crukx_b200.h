@@ -61,6 +61,10 @@ uint64_t crx_parse_device_launches(void);
  * for the first `max` of them. */
 int crx_ctx_profile(crx_ctx* ctx, int enable);
 int32_t crx_ctx_kernel_times(crx_ctx* ctx, char* names, size_t names_len, double* ms, int32_t* counts, int32_t max);
+/* While profiling: per kernel, the total time its stream sat idle between the previous profiled
+ * kernel's end and its start (host work, synchronisations and copies in between); names as for
+ * crx_ctx_kernel_times.  Instrumentation, no reference counterpart. */
+int32_t crx_ctx_kernel_gaps(crx_ctx* ctx, char* names, size_t names_len, double* gap_ms, int32_t max);
 
 /*
  * Encode old -> new for n tensors of bf16/int16 bits on the context's device.
