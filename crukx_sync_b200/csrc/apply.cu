@@ -57,7 +57,7 @@ struct DecTable {
     uint32_t limit[kMaxCodeLen + 1];
     uint32_t sym_off;
     uint32_t nsym;
-    uint32_t lut[1 << LUT_BITS];   // len << 24 | symbol index for codes of <= LUT_BITS bits, else 0
+    uint32_t lut[1 << LUT_BITS];   // len << 24 | symbol for codes of <= LUT_BITS bits, else 0
 };
 
 __device__ __forceinline__ int tensor_of_super(const AppTensor* T, int nT, int64_t s) {
@@ -168,46 +168,22 @@ __global__ void __launch_bounds__(HIST_THREADS) k_app_hist(const AppTensor* __re
 
 constexpr int DEC_THREADS = 256;
 
-// canonical code at the top of `peek` (17 bits): length and symbol-table index; false if none
-__device__ __forceinline__ bool find_code(const DecTable* __restrict__ tab, uint32_t peek, int& L, uint32_t& idx) {
+// canonical code at the top of `peek` (17 bits): its length and symbol; false if none.  Codes of
+// up to LUT_BITS bits (nearly all) take one table load; longer ones search the lengths.
+__device__ __forceinline__ bool find_code(const DecTable* __restrict__ tab, const uint32_t* __restrict__ SY,
+                                          uint32_t nsym1, uint32_t peek, int& L, uint32_t& sym) {
     const uint32_t lv = tab->lut[peek >> (kMaxCodeLen - LUT_BITS)];
     if (lv) {
         L = int(lv >> 24);
-        idx = lv & 0xFFFFFFu;
+        sym = lv & 0xFFFFFFu;
         return true;
     }
     L = LUT_BITS + 1;   // no code of <= LUT_BITS bits starts with these bits
     while (L <= kMaxCodeLen && peek >= tab->limit[L]) ++L;
     if (L > kMaxCodeLen) return false;
-    idx = tab->base[L] + (peek >> (kMaxCodeLen - L)) - tab->first[L];
+    sym = SY[tmin(tab->base[L] + (peek >> (kMaxCodeLen - L)) - tab->first[L], nsym1)];
     return true;
 }
-
-// Payload words for one lane: 32-bit big-endian words read through a window of two 16-byte
-// quads held in registers; moving past the first quad loads the one after the second, so each
-// load is issued about 128 bits before its words are needed.
-struct QuadReader {
-    const uint4* __restrict__ W4;
-    uint64_t n4;   // 16-byte quads in the buffer
-    uint64_t qa;   // index of quad a
-    uint4 a, b;
-    __device__ __forceinline__ uint4 load(uint64_t i) const { return __ldg(W4 + tmin(i, n4 - 1)); }
-    __device__ __forceinline__ void seek(uint64_t word) {   // window starts at the quad holding `word`
-        qa = word >> 2;
-        a = load(qa);
-        b = load(qa + 1);
-    }
-    __device__ __forceinline__ uint32_t word(uint64_t i) {   // i >= 4 * qa; advances the window as needed
-        while (i >= 4 * qa + 4) {
-            a = b;
-            ++qa;
-            b = load(qa + 1);
-        }
-        const uint32_t k = uint32_t(i & 3);
-        const uint32_t v = k == 0 ? a.x : k == 1 ? a.y : k == 2 ? a.z : a.w;
-        return bswap32(v);
-    }
-};
 
 // The generic step of k_decode: a unary run that does not fit the bit buffer (more than ~30 ones,
 // or a large Rice parameter) is followed window by window at absolute positions, never past the
@@ -240,9 +216,7 @@ __device__ __forceinline__ GenericStep decode_generic(const uint64_t* __restrict
     const uint64_t x = read64(W, c);
     const uint64_t rem = rice ? (x >> (64 - rice)) : 0;
     int L;
-    uint32_t idx;
-    if (!find_code(tab, uint32_t((x << rice) >> (64 - kMaxCodeLen)), L, idx)) return r;
-    r.sym = SY[tmin(idx, nsym1)];
+    if (!find_code(tab, SY, nsym1, uint32_t((x << rice) >> (64 - kMaxCodeLen)), L, r.sym)) return r;
     r.gap = (qq << rice) | rem;
     r.pos = c + uint64_t(rice) + uint64_t(L);
     r.ok = true;
@@ -266,52 +240,58 @@ __global__ void __launch_bounds__(DEC_THREADS) k_decode(const uint64_t* __restri
     const uint64_t kb = uint64_t(b) - gblock[g];
     const int cnt = int(tmin<uint64_t>(kBlock, grp.count - kb * kBlock));
     const uint64_t ebase = grp.start + kb * kBlock;
-    uint64_t pos = boff[b];
-    const uint64_t end = pos + bb[b];
+    const uint64_t pos0 = boff[b];
     const uint64_t qmax = GS[int64_t(grp.tensor) * 256 + grp.exp] >> grp.rice;
+    const uint32_t qmax32 = uint32_t(tmin<uint64_t>(qmax, 0xFFFFFFFFull));   // the fast path's q is below 64
     const int rice = grp.rice;
     const DecTable* tab = TB + grp.table;
     const uint32_t* SY = SYMS + tab->sym_off;
     const uint32_t nsym1 = tab->nsym - 1;
-    QuadReader R{reinterpret_cast<const uint4*>(W), n32 / 4, 0, {}, {}};
-
-    uint64_t wi, buf;   // wi: the payload word that follows the buffered bits
+    const uint32_t* W32 = reinterpret_cast<const uint32_t*>(W);
+    const uint64_t last32 = n32 - 1;
+    // bits [pos0 + rel, pos0 + rel + avail) of the payload sit MSB-aligned in buf (zeros below);
+    // the next word to enter it is `nextw`, loaded one refill ahead; blen = the block's bits
+    const uint64_t blen = bb[b];
+    uint64_t rel = 0;
+    uint64_t wi, buf;
+    uint32_t nextw;
     int avail;
+    auto word = [&](uint64_t i) { return bswap32(__ldg(W32 + tmin(i, last32))); };
     auto fill = [&]() {   // buffer := 64 - (pos & 31) bits from pos
-        wi = pos >> 5;
-        R.seek(wi);
-        buf = ((uint64_t(R.word(wi)) << 32) | R.word(wi + 1)) << (pos & 31);
-        avail = 64 - int(pos & 31);
-        wi += 2;
+        const uint64_t p = pos0 + rel;
+        wi = p >> 5;
+        buf = ((uint64_t(word(wi)) << 32) | word(wi + 1)) << (p & 31);
+        avail = 64 - int(p & 31);
+        nextw = word(wi + 2);
+        wi += 3;
     };
     fill();
     // one change: Rice gap and canonical-code symbol, with the reference's validation; false on error
     auto one = [&](uint64_t& gap, uint32_t& sym) -> bool {
-        if (pos >= end) return false;
+        if (rel >= blen) return false;
         const int q = __clzll(~buf);   // ones ahead; bits past `avail` are zeros, so q < avail when it fits
         if (q + 1 + rice + kMaxCodeLen <= avail) {
-            if (uint64_t(q) > qmax || pos + uint64_t(q) >= end) return false;
+            if (uint32_t(q) > qmax32 || rel + uint64_t(q) >= blen) return false;
             uint64_t t = buf << (q + 1);
             const uint64_t rem = rice ? (t >> (64 - rice)) : 0;
             t <<= rice;
             int L;
-            uint32_t idx;
-            if (!find_code(tab, uint32_t(t >> (64 - kMaxCodeLen)), L, idx)) return false;
-            sym = SY[tmin(idx, nsym1)];
+            if (!find_code(tab, SY, nsym1, uint32_t(t >> (64 - kMaxCodeLen)), L, sym)) return false;
             gap = (uint64_t(q) << rice) | rem;
             const int used = q + 1 + rice + L;
             buf = t << L;
             avail -= used;
-            pos += uint64_t(used);
-            while (avail <= 32) {
-                buf |= uint64_t(R.word(wi++)) << (32 - avail);
+            rel += uint64_t(used);
+            if (avail <= 32) {   // used <= avail before, so one word brings it above 32 again
+                buf |= uint64_t(nextw) << (32 - avail);
                 avail += 32;
+                nextw = word(wi++);
             }
             return true;
         }
-        const GenericStep r = decode_generic(W, pos, end, qmax, rice, tab, SY, nsym1);
+        const GenericStep r = decode_generic(W, pos0 + rel, pos0 + blen, qmax, rice, tab, SY, nsym1);
         if (!r.ok) return false;
-        pos = r.pos;
+        rel = r.pos - pos0;
         gap = r.gap;
         sym = r.sym;
         fill();
@@ -354,7 +334,7 @@ __global__ void __launch_bounds__(DEC_THREADS) k_decode(const uint64_t* __restri
             sum += gp + 1;
         }
     }
-    ok = ok && pos == end;
+    ok = ok && rel == blen;
     bsum[b] = ok ? sum : 0;
     if (!ok) atomicOr(&counters[1], (unsigned long long)ERR_DECODE);
 }
@@ -846,12 +826,12 @@ __global__ void __launch_bounds__(512) k_checksum(const int16_t* __restrict__ p,
 template <class T>
 T* dev(Ctx& c, Slot s) { return reinterpret_cast<T*>(c.b[s].p); }
 
-void build_lut(const DecodeTable& d, uint32_t* lut) {
+void build_lut(const DecodeTable& d, const uint32_t* sorted_syms, uint32_t* lut) {
     for (uint32_t p = 0; p < (1u << LUT_BITS); ++p) {
         const uint32_t lo = p << (kMaxCodeLen - LUT_BITS);
         int L = 1;
         while (L <= kMaxCodeLen && lo >= d.limit[L]) ++L;
-        if (L <= LUT_BITS) lut[p] = (uint32_t(L) << 24) | (d.base[L] + (lo >> (kMaxCodeLen - L)) - d.first[L]);
+        if (L <= LUT_BITS) lut[p] = (uint32_t(L) << 24) | sorted_syms[d.base[L] + (lo >> (kMaxCodeLen - L)) - d.first[L]];
         else lut[p] = 0;
     }
 }
@@ -942,7 +922,7 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
             std::memcpy(x.limit, d.limit, sizeof(x.limit));
             x.sym_off = uint32_t(offs[k]);
             x.nsym = uint32_t(u.tables[k].symbols.size());
-            build_lut(d, x.lut);
+            build_lut(d, syms.data() + offs[k], x.lut);
         };
         if (u.tables.size() > 4) parallel_for(u.tables.size(), one);
         else for (size_t k = 0; k < u.tables.size(); ++k) one(k);
