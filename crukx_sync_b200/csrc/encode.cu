@@ -72,12 +72,13 @@ __device__ __forceinline__ int64_t group_of(const uint64_t* __restrict__ start, 
 
 constexpr int ER_THREADS = 256;
 constexpr int ER_WARPS = ER_THREADS / 32;
-constexpr int ER_SUB = 8192;                 // elements per sub-tile
-constexpr int ER_SPAN = ER_SUB / ER_WARPS;   // 1024 per warp
+constexpr int ER_MINB = 1024 / ER_THREADS;   // CTAs per SM at 64 registers a thread
+constexpr int ER_SPAN = 1024;                // elements per warp
+constexpr int ER_SUB = ER_SPAN * ER_WARPS;   // elements per sub-tile
 constexpr int ER_RUN = ER_SPAN / 32;         // 32 per lane
 constexpr int WIN = 16;                      // window rows
 constexpr int WLIST = 256;                   // in-window changes of a span listed for the CTA's record writes
-static_assert(ER_SUB * 32 == SUPER_N, "32 sub-tiles per super-tile");
+static_assert(SUPER_N % ER_SUB == 0 && ER_SUB <= 0xFFFF, "whole sub-tiles per super-tile; 16-bit packed counts");
 
 struct RankSmem {
     uint32_t texp[ER_SUB / 32 * 9];       // old exponent bytes; run r (32 elements) in words 9r..9r+7
@@ -139,7 +140,7 @@ __device__ __forceinline__ void scan_change_starts(const uint32_t* tot, uint32_t
     for (int k = 0; k < 8; ++k) { cstart[lane * 8 + k] = run; run += v[k]; }
 }
 
-__global__ void __launch_bounds__(ER_THREADS, 4)
+__global__ void __launch_bounds__(ER_THREADS, ER_MINB)
 k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_key, uint32_t* __restrict__ rec_val,
            uint64_t rec_cap, unsigned long long* __restrict__ counters, uint32_t* __restrict__ HS,
            uint32_t* __restrict__ CS, unsigned long long* __restrict__ chk_delta, unsigned long long* __restrict__ chk_full) {
@@ -155,8 +156,10 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
     const int span0 = w * ER_SPAN;
     uint64_t full = 0, delta = 0;   // checksum of cur (no cache) / checksum delta of the changes
 
-    S.runA[tid] = 0;
-    S.runC[tid] = 0;
+    for (int e = tid; e < 256; e += ER_THREADS) {
+        S.runA[e] = 0;
+        S.runC[e] = 0;
+    }
     if (tid == 0) { S.emax[0] = 0; S.emax[1] = 0; }
     __syncthreads();
 
@@ -210,7 +213,7 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
             mx = tmax(mx & 0xFFFFu, mx >> 16);
         } else {
             uint8_t* tb = reinterpret_cast<uint8_t*>(S.texp);
-            S.chm[tid] = 0;
+            for (int k = tid; k < ER_SUB / 32; k += ER_THREADS) S.chm[k] = 0;
             __syncthreads();
             for (int i = tid; i < n; i += ER_THREADS) {
                 const uint32_t x = bits_of(i);
@@ -241,11 +244,19 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
             const uint32_t* ew = &S.texp[(w * 32 + lane) * 9];
             uint32_t* mine = &S.msk[w][0][lane];
             if (vn == ER_RUN) {
+                // two exponent bytes per word at once: 16-bit halves hold e + 256 - ebase (no carry
+                // out), flipping bit 8 turns window exponents into 0..15 and all others into 272 and
+                // up, and a halfword minimum with 16 gives the row (row_of for both)
+                const uint32_t kofs = (256u - ebase) * 0x00010001u;
 #pragma unroll
                 for (int g = 0; g < ER_RUN / 4; ++g) {
                     const uint32_t eb = ew[g];
-#pragma unroll
-                    for (int h = 0; h < 4; ++h) mine[row_of((eb >> (8 * h)) & 0xFFu) * 32] |= 1u << (4 * g + h);
+                    const uint32_t r02 = __vimin3_u16x2(((eb & 0x00FF00FFu) + kofs) ^ 0x01000100u, 0x00100010u, 0x00100010u);
+                    const uint32_t r13 = __vimin3_u16x2((((eb >> 8) & 0x00FF00FFu) + kofs) ^ 0x01000100u, 0x00100010u, 0x00100010u);
+                    atomicOr(mine + (r02 & 0xFFFFu) * 32, 1u << (4 * g));
+                    atomicOr(mine + (r13 & 0xFFFFu) * 32, 2u << (4 * g));
+                    atomicOr(mine + (r02 >> 16) * 32, 4u << (4 * g));
+                    atomicOr(mine + (r13 >> 16) * 32, 8u << (4 * g));
                 }
             } else {
                 for (int k = 0; k < vn; ++k) mine[row_of((ew[k >> 2] >> (8 * (k & 3))) & 0xFFu) * 32] |= 1u << k;
@@ -323,8 +334,7 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
             if (w == 0) rank_outside(false);
             __syncthreads();
         }
-        {   // warp bases of the window rows and the sub-tile's totals (all | changed << 16)
-            const int e = tid;
+        for (int e = tid; e < 256; e += ER_THREADS) {   // warp bases of the window rows and the sub-tile's totals (all | changed << 16)
             uint32_t o = any_out ? S.ocnt[e] : 0u;
             const uint32_t d = uint32_t(e) - ebase;
             if (d < uint32_t(WIN)) {
@@ -337,11 +347,11 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
                 o += a;
             }
             S.tot[e] = o;
-            if (tid == 0) {
-                uint32_t r = 0;
-                for (int ww = 0; ww < ER_WARPS; ++ww) { S.lbase[ww] = r; r += S.wcnt[ww]; }
-                S.lbase[ER_WARPS] = r;
-            }
+        }
+        if (tid == 0) {
+            uint32_t r = 0;
+            for (int ww = 0; ww < ER_WARPS; ++ww) { S.lbase[ww] = r; r += S.wcnt[ww]; }
+            S.lbase[ER_WARPS] = r;
         }
         __syncthreads();
         if (w == 0) {   // record slots: the sub-tile's changes sorted by exponent, one atomic
@@ -395,11 +405,15 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
             }
         }
         __syncthreads();
-        S.runA[tid] += S.tot[tid] & 0xFFFFu;
-        S.runC[tid] += S.tot[tid] >> 16;
+        for (int e = tid; e < 256; e += ER_THREADS) {
+            S.runA[e] += S.tot[e] & 0xFFFFu;
+            S.runC[e] += S.tot[e] >> 16;
+        }
     }
-    HS[s * 256 + tid] = S.runA[tid];
-    CS[s * 256 + tid] = S.runC[tid];
+    for (int e = tid; e < 256; e += ER_THREADS) {
+        HS[s * 256 + e] = S.runA[e];
+        CS[s * 256 + e] = S.runC[e];
+    }
     block_add_u64<ER_THREADS>(delta, &chk_delta[t], S.red);
     if (tt.want_full) block_add_u64<ER_THREADS>(full, &chk_full[t], S.red);
 }
