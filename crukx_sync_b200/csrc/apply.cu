@@ -752,8 +752,8 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
 __global__ void __launch_bounds__(MP_THREADS) k_commit(const AppTensor* __restrict__ T, int nT,
                                                        const uint32_t* __restrict__ marks,
                                                        const unsigned long long* __restrict__ spanbase,
-                                                       const uint16_t* __restrict__ cval) {
-    const int64_t st_i = blockIdx.x;                      // sub-tile
+                                                       const uint16_t* __restrict__ cval, int64_t st0) {
+    const int64_t st_i = st0 + blockIdx.x;                // sub-tile
     const int64_t s = st_i / (SUPER_N / MP_SUB);
     const int t = tensor_of_super(T, nT, s);
     const AppTensor tt = T[t];
@@ -784,7 +784,7 @@ __global__ void __launch_bounds__(MP_THREADS) k_commit(const AppTensor* __restri
 // update was verified against are temporaries): the commit list comes down once, host threads
 // scatter it.  `mk`, `sbase`, `vals` are host copies of marks, spanbase and cval.
 void commit_host(const std::vector<AppTensor>& T, int16_t* const* host, const uint32_t* mk, const uint64_t* sbase,
-                 const uint16_t* vals, int64_t n_super) {
+                 const uint16_t* vals, int64_t n_super) {   // super-tiles [0, n_super)
     const int nt = int(T.size());
     parallel_for(size_t(n_super), [&](size_t si) {
         const int64_t s = int64_t(si);
@@ -1093,23 +1093,71 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
         *err = "update does not verify (checksum mismatch: " + bad_names + ")";
         return kCorrupt;
     }
-    if (host_weights) {   // the weights live on the host: bring the commit list down and scatter it there
-        const size_t mb = sizeof(uint32_t) * mark_words, sb = sizeof(uint64_t) * span_slots, vb = sizeof(uint16_t) * total;
+    if (host_weights) {   // the weights live on the host
+        // Two ways down, run at once.  The last tensors, while their host memory is pinned and up to
+        // kDmaShare of the elements, are committed on the device and copied down whole by DMA (2 B
+        // an element over PCIe); the others get the commit list (a bit an element + the changed
+        // values) and are scattered by the host threads, which costs them the host's memory traffic
+        // of every touched line.  Measured on a 16-core host at 7.6e9 elements and 5.8 % changed:
+        // DMA ~35 ps an element, list + scatter ~29 ps, so about 45 % goes by DMA.
+        constexpr double kDmaShare = 0.45;
+        int64_t all = 0;
+        for (int t = 0; t < nt; ++t) all += T[size_t(t)].numel;
+        int t_split = nt;
+        int64_t dma = 0;
+        while (t_split > 0) {
+            const int t = t_split - 1;
+            cudaPointerAttributes pa{};
+            const bool pinned = cudaPointerGetAttributes(&pa, host_weights[t]) == cudaSuccess && pa.type == cudaMemoryTypeHost;
+            (void)cudaGetLastError();   // an unregistered pointer may leave an error behind
+            if (!pinned || double(dma + T[size_t(t)].numel) > kDmaShare * double(all)) break;
+            dma += T[size_t(t)].numel;
+            t_split = t;
+        }
+        const int64_t s_split = t_split < nt ? T[size_t(t_split)].super_begin : n_super;
+        const size_t mb = sizeof(uint32_t) * size_t(s_split) * (SUPER_N / 32);
+        const size_t sb = sizeof(uint64_t) * size_t(s_split) * (SUPER_N / MP_SUB) * MP_WARPS;
+        const size_t vb = s_split ? sizeof(uint16_t) * total : 0;   // value slots are spread over the whole list
         CRX_CUDA(ensure_pinned(C.in_host, mb + sb + vb + 16, st));
         uint8_t* hb = static_cast<uint8_t*>(C.in_host.p);
-        CRX_CUDA(cudaMemcpyAsync(hb, C.b[S_A_CADDR].p, mb, cudaMemcpyDeviceToHost, st));
-        CRX_CUDA(cudaMemcpyAsync(hb + mb, C.b[S_A_SPANB].p, sb, cudaMemcpyDeviceToHost, st));
+        if (mb) CRX_CUDA(cudaMemcpyAsync(hb, C.b[S_A_CADDR].p, mb, cudaMemcpyDeviceToHost, st));
+        if (sb) CRX_CUDA(cudaMemcpyAsync(hb + mb, C.b[S_A_SPANB].p, sb, cudaMemcpyDeviceToHost, st));
         if (vb) CRX_CUDA(cudaMemcpyAsync(hb + mb + sb, C.b[S_A_CVAL].p, vb, cudaMemcpyDeviceToHost, st));
+        cudaEvent_t list_down = nullptr;
+        CRX_CUDA(cudaEventCreateWithFlags(&list_down, cudaEventDisableTiming));
+        const cudaError_t rec = cudaEventRecord(list_down, st);
+        if (rec != cudaSuccess) { cudaEventDestroy(list_down); CRX_CUDA(rec); }
+        if (s_split < n_super) {   // the DMA share: commit on the device, then copy down tensors that changed
+            const int64_t st0 = s_split * (SUPER_N / MP_SUB);
+            { KernelScope ks_(C, "k_commit", st);
+            k_commit<<<unsigned((n_super - s_split) * (SUPER_N / MP_SUB)), MP_THREADS, 0, st>>>(
+                dT, nt, dev<uint32_t>(C, S_A_CADDR), dev<unsigned long long>(C, S_A_SPANB), dev<uint16_t>(C, S_A_CVAL), st0);
+            }
+            cudaError_t e = cudaGetLastError();
+            for (int t = t_split; t < nt && e == cudaSuccess; ++t) {
+                uint64_t cnt = 0;
+                for (const Group& g : u.tensors[size_t(t)].groups) cnt += uint64_t(g.count);
+                if (cnt) e = cudaMemcpyAsync(host_weights[t], weights[t], sizeof(int16_t) * size_t(T[size_t(t)].numel),
+                                             cudaMemcpyDeviceToHost, st);
+            }
+            if (e != cudaSuccess) { cudaEventDestroy(list_down); CRX_CUDA(e); }
+        }
+        const cudaError_t ew = cudaEventSynchronize(list_down);
+        cudaEventDestroy(list_down);
+        CRX_CUDA(ew);
+        trace_phase(C, "apply: commit list down");
+        if (s_split) commit_host(T, host_weights, reinterpret_cast<const uint32_t*>(hb), reinterpret_cast<const uint64_t*>(hb + mb),
+                                 reinterpret_cast<const uint16_t*>(hb + mb + sb), s_split);
+        trace_phase(C, "apply: host scatter");
         CRX_CUDA(cudaStreamSynchronize(st));
-        commit_host(T, host_weights, reinterpret_cast<const uint32_t*>(hb), reinterpret_cast<const uint64_t*>(hb + mb),
-                    reinterpret_cast<const uint16_t*>(hb + mb + sb), n_super);
+        trace_phase(C, "apply: DMA share down");
         *changed = int64_t(total);
         return kOk;
     }
     { KernelScope ks_(C, "k_commit", st);
     k_commit<<<unsigned(n_super * (SUPER_N / MP_SUB)), MP_THREADS, 0, st>>>(dT, nt, dev<uint32_t>(C, S_A_CADDR),
                                                                           dev<unsigned long long>(C, S_A_SPANB),
-                                                                          dev<uint16_t>(C, S_A_CVAL));
+                                                                          dev<uint16_t>(C, S_A_CVAL), 0);
     }
     CRX_CUDA(cudaGetLastError());
     // ---- the new weights' histograms for the next apply (tagged version + 1: the caller bumps it).
