@@ -410,6 +410,7 @@ constexpr int MP_SUB = 8192;
 constexpr int MP_SPAN = MP_SUB / MP_WARPS;   // 1024
 constexpr int MP_RUN = MP_SPAN / 32;         // 32
 constexpr int MWIN = 16;
+constexpr int MP_PRE = 4;                    // groups per warp whose first changes are loaded ahead
 static_assert(MP_SUB * 32 == SUPER_N, "32 sub-tiles per super-tile");
 
 struct MapSmem {
@@ -426,7 +427,6 @@ struct MapSmem {
     int32_t hdelta[256];                   // this super-tile's histogram, then plus its exponent moves
     uint8_t gexp[256];
     uint32_t oowm[MP_WARPS];               // per warp: its runs that hold outside-window elements
-    uint32_t qnext;                        // next group to place (taken from the largest exponent down)
     unsigned long long wkey[MP_WARPS];
     uint32_t ebase;
     uint64_t red[MP_WARPS];
@@ -514,6 +514,22 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
         const int span_n = tmax(0, tmin(MP_SPAN, n - span0));
         const int r0 = lane * MP_RUN;
         const int vn = tmax(0, tmin(MP_RUN, span_n - r0));
+        // the first 32 changes of this warp's groups (group k belongs to warp k % MP_WARPS), loaded
+        // now so that they arrive while the sub-tile is marked and scanned
+        uint32_t pl[MP_PRE], pz[MP_PRE];
+#pragma unroll
+        for (int j = 0; j < MP_PRE; ++j) {
+            const int k = w + MP_WARPS * j;
+            pl[j] = 0xFFFFFFFFu;
+            pz[j] = 0;
+            if (k < ngt) {
+                const uint64_t c = S.cursor[k] + uint64_t(lane);
+                if (c < S.gend[k]) {   // issued here (volatile), consumed after the marking and scans
+                    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(pl[j]) : "l"(local + c));
+                    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(pz[j]) : "l"(zz + c));
+                }
+            }
+        }
         // ---- this warp's masks to zero, then each lane marks its run
         {
             uint4* m4 = reinterpret_cast<uint4*>(&S.msk[w][0][0]);
@@ -607,7 +623,6 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                 o += a;
             }
             S.tot[e] = uint16_t(o);
-            if (tid == 0) S.qnext = 0;
         }
         __syncthreads();
         if (any_out) {   // second pass: bucket starts, then every outside element's slot
@@ -628,24 +643,19 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             }
             __syncthreads();
         }
-        // ---- place this sub-tile's changes: warps take groups from a queue, largest exponents (the
-        //      most changes) first; groups whose next change lies beyond this sub-tile are skipped
-        //      from shared memory.  A change leaves its residual and its mark; the old value is read
-        //      when the span is staged.  The next chunk of a group is loaded while this one is placed.
-        for (;;) {
-            int q = 0;
-            if (lane == 0) q = int(atomicAdd(&S.qnext, 1u));
-            q = __shfl_sync(FULL, q, 0);
-            if (q >= ngt) break;
-            const int k = ngt - 1 - q;
+        // ---- place this sub-tile's changes: group k is placed by warp k % MP_WARPS, which knows its
+        //      groups' first changes already; groups whose next change lies beyond this sub-tile are
+        //      skipped from shared memory.  A change leaves its residual and its mark; the old value
+        //      is read when the span is staged.  The next chunk of a group is loaded while this one is
+        //      placed.
+        auto place_group = [&](int k, uint32_t lc, uint32_t z) {
             const uint32_t e = S.gexp[k];
             const uint32_t lo = S.pcur[e], tot = S.tot[e];
-            if (S.nextloc[k] - lo >= tot) continue;
+            if (S.nextloc[k] - lo >= tot) return;
             const uint32_t d = row_of(e);
             const uint64_t ge = S.gend[k];
             uint64_t cur = S.cursor[k];
-            uint32_t lc = 0xFFFFFFFFu, z = 0, next;
-            if (cur + lane < ge) { lc = local[cur + lane]; z = zz[cur + lane]; }
+            uint32_t next;
             for (;;) {
                 const uint64_t jn = cur + 32 + lane;
                 uint32_t lcn = 0xFFFFFFFFu, zn = 0;
@@ -687,6 +697,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                 lc = lcn;
                 z = zn;
             }
+            __syncwarp();
             if (lane == 0) {
                 S.cursor[k] = cur;
                 S.nextloc[k] = next;
@@ -696,6 +707,18 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                     prefetch_l2(zz + cur, 4 * nb);
                 }
             }
+            __syncwarp();
+        };
+#pragma unroll
+        for (int j = 0; j < MP_PRE; ++j) {
+            const int k = w + MP_WARPS * j;
+            if (k < ngt) place_group(k, pl[j], pz[j]);
+        }
+        for (int k = w + MP_WARPS * MP_PRE; k < ngt; k += MP_WARPS) {
+            const uint64_t c = S.cursor[k] + uint64_t(lane);
+            uint32_t lc = 0xFFFFFFFFu, z = 0;
+            if (c < S.gend[k]) { lc = local[c]; z = zz[c]; }
+            place_group(k, lc, z);
         }
         __syncthreads();
         // ---- stage this warp span's new values in position order, one atomic per warp: the
