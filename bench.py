@@ -821,11 +821,15 @@ def run_e2e(args, A, B, dev, weight_bytes, exchange, barrier, dist):
     nsteps = max(1, min(args.steps, args.e2e_steps))
     n_el = sum(v.numel() for v in A.values())
 
-    chg = []
+    chg, t_enc, t_app = [], [], []
 
     def one():   # each rank applies its own update (host bytes are not exchanged between processes)
+        t0 = time.perf_counter()
         upd = crx.encode_update(st["src"], st["dst"], sender)
+        t1 = time.perf_counter()
         chg.append(crx.apply_update(Rh, upd, receiver).changed)
+        t_enc.append(t1 - t0)
+        t_app.append(time.perf_counter() - t1)
         st["src"], st["dst"] = st["dst"], st["src"]
         return len(upd)
 
@@ -847,6 +851,7 @@ def run_e2e(args, A, B, dev, weight_bytes, exchange, barrier, dist):
     n_super = sum((v.numel() + (1 << 18) - 1) >> 18 for v in A.values())
     changed = sum(chg[-nsteps:]) / nsteps
     return {"value": round(weight_bytes / dt / 1e9, 3), "unit": "GB/s", "ms_per_step": round(dt * 1e3, 2),
+            "encode_ms": round(1e3 * sum(t_enc[-nsteps:]) / nsteps, 2), "apply_ms": round(1e3 * sum(t_app[-nsteps:]) / nsteps, 2),
             "steps": nsteps, "h2d_bytes_per_step": int(6 * n_el + ub),
             "d2h_bytes_per_step": int(ub + n_super * (32768 + 2048) + 2 * changed),
             "note": "public API with pinned host tensors: prev + cur and the receiver's weights up, the update "
