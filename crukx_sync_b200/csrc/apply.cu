@@ -416,7 +416,7 @@ static_assert(MP_SUB * 32 == SUPER_N, "32 sub-tiles per super-tile");
 struct MapSmem {
     uint32_t msk[MP_WARPS][MWIN + 1][32];  // per lane and window row: its run's elements of that exponent (row MWIN: outside)
     uint16_t pre[MP_WARPS][MWIN][32];      // exclusive prefixes over the lanes of the masks' counts
-    uint16_t nval[MP_SUB];                 // new bits of every changed position
+    uint8_t nz8[MP_SUB];                   // zigzag residual of every changed position; 255: in the escape list
     uint32_t mark[MP_SUB / 32];            // changed positions
     uint32_t ocnt[256];                    // outside-window counts per exponent (index order over the sub-tile)
     uint32_t wwin[MP_WARPS][MWIN];         // per-warp window totals, then warp bases
@@ -446,13 +446,13 @@ __device__ __forceinline__ uint32_t nth_set_bit(uint32_t m, uint32_t r) {
     return pos;
 }
 
-__global__ void __launch_bounds__(MP_THREADS, 4)
+__global__ void __launch_bounds__(MP_THREADS, 5)
 k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, const uint32_t* __restrict__ PS,
       const uint32_t* __restrict__ local, const uint32_t* __restrict__ zz, uint32_t* __restrict__ marks,
       unsigned long long* __restrict__ spanbase, uint16_t* __restrict__ cval, uint64_t stage_cap,
       unsigned long long* __restrict__ chk_delta,
       unsigned long long* __restrict__ staged, const uint64_t* __restrict__ GS, uint32_t* __restrict__ HNEW,
-      uint16_t* __restrict__ order_scratch) {
+      uint16_t* __restrict__ order_scratch, uint16_t* __restrict__ esc_scratch) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     MapSmem& S = *reinterpret_cast<MapSmem*>(smem_raw);
     const int64_t s = blockIdx.x;
@@ -465,6 +465,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
     const int ngt = tt.g_end - tt.g_begin;
     const int span0 = w * MP_SPAN;
     uint16_t* const order = order_scratch + s * MP_SUB;   // outside-window positions in (exponent, index) order
+    uint16_t* const esc = esc_scratch + s * MP_SUB;       // residuals whose zigzag is 255 or more, by position
     S.pcur[tid] = PS[s * 256 + tid];
     {   // this super-tile's histogram: the next row's prefix (or the tensor's total) minus this one's
         const bool last = e_end >= tt.numel;
@@ -682,7 +683,8 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                         i = order[S.estart[e] + r];
                     }
                     if (unsigned(i) < unsigned(n)) {
-                        S.nval[i] = uint16_t(int32_t(z >> 1) ^ -int32_t(z & 1));   // residual, mod 2^16
+                        S.nz8[i] = uint8_t(tmin(z, 255u));
+                        if (z >= 255u) esc[i] = uint16_t(int32_t(z >> 1) ^ -int32_t(z & 1));   // residual, mod 2^16
                         atomicOr(&S.mark[i >> 5], 1u << (i & 31));
                     }
                 }
@@ -748,7 +750,9 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             __syncwarp();
             for (uint32_t k = lane; k < total; k += 32) {
                 const int i = span0 + lst[k];
-                const uint32_t old = uint16_t(p[i]), nv = (old + S.nval[i]) & 0xFFFFu;
+                const uint32_t z8 = S.nz8[i];
+                const uint32_t res = z8 < 255u ? uint32_t(int32_t(z8 >> 1) ^ -int32_t(z8 & 1)) : uint32_t(esc[i]);
+                const uint32_t old = uint16_t(p[i]), nv = (old + res) & 0xFFFFu;
                 if (sb + k < stage_cap) cval[sb + k] = uint16_t(nv);
                 delta += (uint64_t(nv) - uint64_t(old)) * splitmix_weight(uint64_t(base + i));
                 if (HNEW) {
@@ -982,6 +986,7 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     if (keep_hist) CRX_CUDA(ensure_dev(C.b[S_A_HNEW], sizeof(uint32_t) * 256 * size_t(n_super), st));
     uint32_t* hnew = keep_hist ? dev<uint32_t>(C, S_A_HNEW) : nullptr;
     CRX_CUDA(ensure_dev(C.b[S_A_ORDER], sizeof(uint16_t) * MP_SUB * size_t(n_super), st));
+    CRX_CUDA(ensure_dev(C.b[S_A_ESC], sizeof(uint16_t) * MP_SUB * size_t(n_super), st));
     CRX_CUDA(ensure_dev(C.b[S_A_TOT], sizeof(uint64_t) * cells, st));
     CRX_CUDA(ensure_dev(C.b[S_A_CHUNK_ROWS], sizeof(int64_t) * 2 * (size_t(nt) + 1), st));
     CRX_CUDA(ensure_dev(C.b[S_A_CHUNK_SUMS], sizeof(uint32_t) * 256 * size_t(n_chunks), st));
@@ -1074,7 +1079,8 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
                                                             dev<uint32_t>(C, S_A_ZZ), dev<uint32_t>(C, S_A_CADDR),
                                                             dev<unsigned long long>(C, S_A_SPANB),
                                                             dev<uint16_t>(C, S_A_CVAL), total, chk_delta, counters + 2,
-                                                            dev<uint64_t>(C, S_A_TOT), hnew, dev<uint16_t>(C, S_A_ORDER));
+                                                            dev<uint64_t>(C, S_A_TOT), hnew, dev<uint16_t>(C, S_A_ORDER),
+                                                            dev<uint16_t>(C, S_A_ESC));
     }
     CRX_CUDA(cudaGetLastError());
     // ---- verdict (one synchronisation for the whole update)

@@ -60,6 +60,8 @@ enum Slot : int {
     S_SZ_STATS, S_SZ_TILES,
     // apply: first value slot of every span of the commit list
     S_A_SPANB,
+    // apply: k_map's large residuals, by sub-tile position, one sub-tile per super-tile at a time
+    S_A_ESC,
     S_NSLOTS
 };
 
