@@ -553,7 +553,7 @@ struct StatsSmem {
 // symbol counts (codec.py:355-367).  Lanes take consecutive changes; each lane keeps its sums and
 // a packed count of the symbols 0..7 in registers while its group stays the same, so atomics are
 // needed only at group boundaries and for larger symbols.
-__global__ void __launch_bounds__(256) k_stats(const uint64_t* __restrict__ g_start, const int32_t* __restrict__ g_exp,
+__global__ void __launch_bounds__(256, 5) k_stats(const uint64_t* __restrict__ g_start, const int32_t* __restrict__ g_exp,
                                                const uint32_t* __restrict__ g_cand, int64_t ng, uint64_t total,
                                                const uint32_t* __restrict__ local, const uint32_t* __restrict__ vals,
                                                unsigned long long* __restrict__ costs, unsigned long long* __restrict__ dense_hist,
@@ -808,7 +808,7 @@ constexpr int PACK_WORDS = 512;   // a warp assembles blocks of up to 16 Kbit in
 // fits is assembled in shared memory, then its words are stored (the two edge words, which it may
 // share with its neighbours, by atomic OR into the zeroed payload); a longer block writes its bits
 // straight to the payload by atomic OR.
-__global__ void __launch_bounds__(256) k_pack(const uint64_t* __restrict__ g_start, const int32_t* __restrict__ g_exp,
+__global__ void __launch_bounds__(256, 5) k_pack(const uint64_t* __restrict__ g_start, const int32_t* __restrict__ g_exp,
                                               const uint8_t* __restrict__ g_rice, const uint64_t* __restrict__ g_block,
                                               int64_t ng, int64_t n_blocks, const uint32_t* __restrict__ local,
                                               const uint32_t* __restrict__ vals, const uint32_t* __restrict__ dense_code,
