@@ -415,14 +415,14 @@ static_assert(MP_SUB * 32 == SUPER_N, "32 sub-tiles per super-tile");
 
 struct MapSmem {
     uint32_t msk[MP_WARPS][MWIN + 1][32];  // per lane and window row: its run's elements of that exponent (row MWIN: outside)
-    uint16_t pre[MP_WARPS][MWIN][32];      // exclusive prefixes over the lanes of the masks' counts
-    uint8_t nz8[MP_SUB];                   // zigzag residual of every changed position; 255: in the escape list
+    uint8_t nz8[MP_SUB];                   // zigzag residual of every changed position; 255: in the escape list.
+                                           // Before the placement its first KB holds the outside-window counts.
+    uint16_t pre[MP_WARPS][MWIN][16];      // exclusive prefixes over the lanes of the masks' counts, at even lanes
     uint32_t mark[MP_SUB / 32];            // changed positions
-    uint32_t ocnt[256];                    // outside-window counts per exponent (index order over the sub-tile)
     uint32_t wwin[MP_WARPS][MWIN];         // per-warp window totals, then warp bases
     uint16_t tot[256], estart[256];
     uint32_t pcur[256];
-    uint64_t cursor[256], gend[256];
+    uint32_t cursor[256], gend[256];      // per group: next change and end, relative to the tensor's first change
     uint32_t nextloc[256];                 // group-local index of each group's next change (~0: none)
     int32_t hdelta[256];                   // this super-tile's histogram, then plus its exponent moves
     uint8_t gexp[256];
@@ -446,7 +446,7 @@ __device__ __forceinline__ uint32_t nth_set_bit(uint32_t m, uint32_t r) {
     return pos;
 }
 
-__global__ void __launch_bounds__(MP_THREADS, 5)
+__global__ void __launch_bounds__(MP_THREADS, 6)
 k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, const uint32_t* __restrict__ PS,
       const uint32_t* __restrict__ local, const uint32_t* __restrict__ zz, uint32_t* __restrict__ marks,
       unsigned long long* __restrict__ spanbase, uint16_t* __restrict__ cval, uint64_t stage_cap,
@@ -466,6 +466,8 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
     const int span0 = w * MP_SPAN;
     uint16_t* const order = order_scratch + s * MP_SUB;   // outside-window positions in (exponent, index) order
     uint16_t* const esc = esc_scratch + s * MP_SUB;       // residuals whose zigzag is 255 or more, by position
+    uint32_t* const ocnt = reinterpret_cast<uint32_t*>(S.nz8);   // outside-window counts per exponent (before placement)
+    const uint64_t tg0 = ngt ? G[tt.g_begin].start : 0;   // the tensor's first change: group cursors are relative to it
     S.pcur[tid] = PS[s * 256 + tid];
     {   // this super-tile's histogram: the next row's prefix (or the tensor's total) minus this one's
         const bool last = e_end >= tt.numel;
@@ -492,8 +494,8 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             const uint64_t mid = (lo + hi) >> 1;
             if (local[mid] < p0) lo = mid + 1; else hi = mid;
         }
-        S.cursor[tid] = lo;
-        S.gend[tid] = grp.start + grp.count;
+        S.cursor[tid] = uint32_t(lo - tg0);
+        S.gend[tid] = uint32_t(grp.start + grp.count - tg0);
         S.gexp[tid] = uint8_t(grp.exp);
         S.nextloc[tid] = lo < grp.start + grp.count ? local[lo] : 0xFFFFFFFFu;
     }
@@ -524,8 +526,8 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             pl[j] = 0xFFFFFFFFu;
             pz[j] = 0;
             if (k < ngt) {
-                const uint64_t c = S.cursor[k] + uint64_t(lane);
-                if (c < S.gend[k]) {   // issued here (volatile), consumed after the marking and scans
+                const uint64_t c = tg0 + S.cursor[k] + uint64_t(lane);
+                if (c < tg0 + S.gend[k]) {   // issued here (volatile), consumed after the marking and scans
                     asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(pl[j]) : "l"(local + c));
                     asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(pz[j]) : "l"(zz + c));
                 }
@@ -581,8 +583,10 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                 if (lane >= o) incl += y;
             }
             const uint32_t ex = incl - v;
-            S.pre[w][2 * j][lane] = uint16_t(ex & 0xFFFFu);
-            S.pre[w][2 * j + 1][lane] = uint16_t(ex >> 16);
+            if (!(lane & 1)) {
+                S.pre[w][2 * j][lane >> 1] = uint16_t(ex & 0xFFFFu);
+                S.pre[w][2 * j + 1][lane >> 1] = uint16_t(ex >> 16);
+            }
             if (lane == 31) {
                 S.wwin[w][2 * j] = incl & 0xFFFFu;
                 S.wwin[w][2 * j + 1] = incl >> 16;
@@ -593,7 +597,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
         // outside-window elements of the whole sub-tile in index order, by one warp (they are rare):
         // slots from warp matching over the counters
         auto rank_outside = [&](bool list) {
-            for (int k = lane; k < 256; k += 32) S.ocnt[k] = 0;
+            for (int k = lane; k < 256; k += 32) ocnt[k] = 0;
             __syncwarp();
             for (int ww = 0; ww < MP_WARPS; ++ww) {
                 const int sn = tmax(0, tmin(MP_SPAN, n - ww * MP_SPAN));
@@ -601,7 +605,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                     const int ii = (__ffs(m) - 1) * MP_RUN + lane;
                     const uint32_t e = ii < sn ? exp_at(ww * MP_SPAN + ii) : 0u;
                     const bool outside = ii < sn && row_of(e) == uint32_t(MWIN);
-                    const uint32_t r = warp_rank(S.ocnt, e, outside, lt, lane);
+                    const uint32_t r = warp_rank(ocnt, e, outside, lt, lane);
                     if (list && outside) order[S.estart[e] + r] = uint16_t(ww * MP_SPAN + ii);
                 }
             }
@@ -612,7 +616,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
         }
         {   // warp bases of the window rows and the sub-tile's totals
             const int e = tid;
-            uint32_t o = any_out ? S.ocnt[e] : 0u;
+            uint32_t o = any_out ? ocnt[e] : 0u;
             const uint32_t d = uint32_t(e) - ebase;
             if (d < uint32_t(MWIN)) {
                 uint32_t a = 0;
@@ -654,8 +658,8 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             const uint32_t lo = S.pcur[e], tot = S.tot[e];
             if (S.nextloc[k] - lo >= tot) return;
             const uint32_t d = row_of(e);
-            const uint64_t ge = S.gend[k];
-            uint64_t cur = S.cursor[k];
+            const uint64_t ge = tg0 + S.gend[k];
+            uint64_t cur = tg0 + S.cursor[k];
             uint32_t next;
             for (;;) {
                 const uint64_t jn = cur + 32 + lane;
@@ -671,11 +675,17 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                         for (int st = MP_WARPS / 2; st; st >>= 1) ww += S.wwin[ww + st][d] <= r ? st : 0;
                         r -= S.wwin[ww][d];
                         const uint16_t* pr = &S.pre[ww][d][0];
-                        int l = 0;                   // last lane whose prefix is <= r
+                        int l = 0;                   // last even lane whose prefix is <= r, then maybe the next
 #pragma unroll
-                        for (int st = 16; st; st >>= 1) l += pr[l + st] <= r ? st : 0;
+                        for (int st = 8; st; st >>= 1) l += pr[l + st] <= r ? st : 0;
                         r -= pr[l];
-                        const uint32_t m = S.msk[ww][d][l];
+                        l *= 2;
+                        uint32_t m = S.msk[ww][d][l];
+                        const uint32_t c0 = uint32_t(__popc(m));
+                        if (r >= c0) {
+                            r -= c0;
+                            m = S.msk[ww][d][++l];
+                        }
                         // a selection past the mask's bits leaves the change unplaced: the host then
                         // reports that not every change was placed
                         i = r < uint32_t(__popc(m)) ? ww * MP_SPAN + l * MP_RUN + int(nth_set_bit(m, r)) : -1;
@@ -701,7 +711,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             }
             __syncwarp();
             if (lane == 0) {
-                S.cursor[k] = cur;
+                S.cursor[k] = uint32_t(cur - tg0);
                 S.nextloc[k] = next;
                 if (cur < ge) {   // the group's next changes, for a later sub-tile
                     const size_t nb = size_t(tmin<uint64_t>(ge - cur, 128));
@@ -717,9 +727,9 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             if (k < ngt) place_group(k, pl[j], pz[j]);
         }
         for (int k = w + MP_WARPS * MP_PRE; k < ngt; k += MP_WARPS) {
-            const uint64_t c = S.cursor[k] + uint64_t(lane);
+            const uint64_t c = tg0 + S.cursor[k] + uint64_t(lane);
             uint32_t lc = 0xFFFFFFFFu, z = 0;
-            if (c < S.gend[k]) { lc = local[c]; z = zz[c]; }
+            if (c < tg0 + S.gend[k]) { lc = local[c]; z = zz[c]; }
             place_group(k, lc, z);
         }
         __syncthreads();
