@@ -72,7 +72,7 @@ __device__ __forceinline__ int64_t group_of(const uint64_t* __restrict__ start, 
 
 constexpr int ER_THREADS = 256;
 constexpr int ER_WARPS = ER_THREADS / 32;
-constexpr int ER_MINB = 1024 / ER_THREADS;   // CTAs per SM at 64 registers a thread
+constexpr int ER_MINB = 5;                   // CTAs per SM (48 registers a thread, 45 KB of shared memory)
 constexpr int ER_SPAN = 1024;                // elements per warp
 constexpr int ER_SUB = ER_SPAN * ER_WARPS;   // elements per sub-tile
 constexpr int ER_RUN = ER_SPAN / 32;         // 32 per lane
@@ -84,12 +84,12 @@ struct RankSmem {
     uint32_t texp[ER_SUB / 32 * 9];       // old exponent bytes; run r (32 elements) in words 9r..9r+7
     uint32_t chm[ER_SUB / 32];            // changed bit of every element, one word per run
     uint32_t msk[ER_WARPS][WIN + 1][32];  // per lane and window row: its run's elements of that exponent (row WIN: below)
-    uint32_t pre[ER_WARPS][WIN][32];      // exclusive lane prefixes of the rows' counts, all | changed << 16
+    uint32_t pre[ER_WARPS][WIN][16];      // exclusive lane prefixes of the rows' counts at even lanes, all | changed << 16
     uint32_t wwin[ER_WARPS][WIN];         // per-warp row totals, then warp bases (all | changed << 16)
     uint32_t ocnt[256];                   // below-window counts per exponent, all | changed << 16
     uint32_t runA[256], runC[256];        // super-tile running totals
     uint32_t tot[256];                    // this sub-tile's totals, all | changed << 16
-    uint32_t cstart[256];                 // exclusive scan of the changed totals: records sorted by exponent
+    uint16_t cstart[256];                 // exclusive scan of the changed totals: records sorted by exponent
     uint16_t wl[ER_WARPS][WLIST];         // a warp's in-window changes (sub-tile indices)
     uint32_t wcnt[ER_WARPS];              // listed changes per warp, then (lbase) their exclusive prefix
     uint32_t lbase[ER_WARPS + 1];
@@ -126,7 +126,7 @@ __device__ __forceinline__ bool changed_bits(uint32_t x) { return ((x ^ (x >> 16
 
 // warp 0: cstart[e] = number of this sub-tile's changed elements with a smaller exponent, so each
 // sub-tile's records land sorted by (exponent, rank) and k_place writes runs of consecutive changes
-__device__ __forceinline__ void scan_change_starts(const uint32_t* tot, uint32_t* cstart, int lane) {
+__device__ __forceinline__ void scan_change_starts(const uint32_t* tot, uint16_t* cstart, int lane) {
     uint32_t v[8], sum = 0;
 #pragma unroll
     for (int k = 0; k < 8; ++k) { v[k] = tot[lane * 8 + k] >> 16; sum += v[k]; }
@@ -301,7 +301,7 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
                 const uint32_t y = __shfl_up_sync(FULL, incl, o);
                 if (lane >= o) incl += y;
             }
-            S.pre[w][d][lane] = incl - v;
+            if (!(lane & 1)) S.pre[w][d][lane >> 1] = incl - v;
             if (lane == 31) S.wwin[w][d] = incl;
         }
         const bool any_out = __syncthreads_or(oowm != 0);
@@ -375,7 +375,12 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
                 const uint32_t below = (1u << k) - 1u;
                 const uint32_t m = S.msk[ww][d][l];
                 const uint32_t c = S.chm[i >> 5];
-                const uint32_t pr = S.pre[ww][d][l], wb = S.wwin[ww][d];
+                uint32_t pr = S.pre[ww][d][l >> 1];   // even lanes' prefixes: an odd lane adds its neighbour's counts
+                if (l & 1) {
+                    const uint32_t mp = S.msk[ww][d][l - 1];
+                    pr += uint32_t(__popc(mp)) | (uint32_t(__popc(mp & S.chm[(i >> 5) - 1])) << 16);
+                }
+                const uint32_t wb = S.wwin[ww][d];
                 const uint32_t rA = (wb & 0xFFFFu) + (pr & 0xFFFFu) + uint32_t(__popc(m & below));
                 const uint32_t rC = (wb >> 16) + (pr >> 16) + uint32_t(__popc(m & c & below));
                 put_record(rec_key, rec_val, rec_cap, rb + S.cstart[e] + rC, s, S.runA[e] + rA, S.runC[e] + rC, x);
