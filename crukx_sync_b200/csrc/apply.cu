@@ -225,6 +225,12 @@ __device__ __forceinline__ GenericStep decode_generic(const uint64_t* __restrict
 
 __device__ __forceinline__ uint32_t clamp32(uint64_t v) { return v > 0xFFFFFFFFull ? 0xFFFFFFFFu : uint32_t(v); }
 
+// One thread per 256-change block.  Outputs go through shared memory: every DEC_CH changes a lane's
+// values wait in its row, then the warp stores them with consecutive lanes on consecutive indices
+// (16 lanes per block row), so a store instruction writes two runs of 64 bytes instead of 32
+// scattered words.
+constexpr int DEC_CH = 16;
+
 __global__ void __launch_bounds__(DEC_THREADS) k_decode(const uint64_t* __restrict__ W, uint64_t n32,
                                                         const uint32_t* __restrict__ bb, const uint64_t* __restrict__ boff,
                                                         int64_t n_blocks, const AppGroup* __restrict__ G,
@@ -233,29 +239,32 @@ __global__ void __launch_bounds__(DEC_THREADS) k_decode(const uint64_t* __restri
                                                         const uint64_t* __restrict__ GS, uint32_t* __restrict__ gaps,
                                                         uint32_t* __restrict__ zz, uint64_t* __restrict__ bsum,
                                                         unsigned long long* __restrict__ counters) {
+    __shared__ uint32_t sg[DEC_THREADS / 32][32 * (DEC_CH + 1)];   // per warp: each lane's staged gaps (rows padded)
+    __shared__ uint32_t sz[DEC_THREADS / 32][32 * (DEC_CH + 1)];   // and residual symbols
+    const int lane = threadIdx.x & 31, wq = threadIdx.x >> 5;
     const int64_t b = int64_t(blockIdx.x) * DEC_THREADS + threadIdx.x;
-    if (b >= n_blocks) return;
-    const int64_t g = last_le(gblock, ng, uint64_t(b));
-    const AppGroup grp = G[g];
-    const uint64_t kb = uint64_t(b) - gblock[g];
-    const int cnt = int(tmin<uint64_t>(kBlock, grp.count - kb * kBlock));
+    const bool live = b < n_blocks;   // lanes past the last block only take part in the warp's stores
+    const int64_t g = live ? last_le(gblock, ng, uint64_t(b)) : 0;
+    const AppGroup grp = live ? G[g] : AppGroup{};
+    const uint64_t kb = live ? uint64_t(b) - gblock[g] : 0;
+    const int cnt = live ? int(tmin<uint64_t>(kBlock, grp.count - kb * kBlock)) : 0;
     const uint64_t ebase = grp.start + kb * kBlock;
-    const uint64_t pos0 = boff[b];
-    const uint64_t qmax = GS[int64_t(grp.tensor) * 256 + grp.exp] >> grp.rice;
+    const uint64_t pos0 = live ? boff[b] : 0;
+    const uint64_t qmax = live ? GS[int64_t(grp.tensor) * 256 + grp.exp] >> grp.rice : 0;
     const uint32_t qmax32 = uint32_t(tmin<uint64_t>(qmax, 0xFFFFFFFFull));   // the fast path's q is below 64
     const int rice = grp.rice;
-    const DecTable* tab = TB + grp.table;
-    const uint32_t* SY = SYMS + tab->sym_off;
-    const uint32_t nsym1 = tab->nsym - 1;
+    const DecTable* tab = TB + (live ? grp.table : 0);
+    const uint32_t* SY = SYMS + (live ? tab->sym_off : 0);
+    const uint32_t nsym1 = live ? tab->nsym - 1 : 0;
     const uint32_t* W32 = reinterpret_cast<const uint32_t*>(W);
     const uint64_t last32 = n32 - 1;
     // bits [pos0 + rel, pos0 + rel + avail) of the payload sit MSB-aligned in buf (zeros below);
     // the next word to enter it is `nextw`, loaded one refill ahead; blen = the block's bits
-    const uint64_t blen = bb[b];
+    const uint64_t blen = live ? bb[b] : 0;
     uint64_t rel = 0;
-    uint64_t wi, buf;
-    uint32_t nextw;
-    int avail;
+    uint64_t wi = 0, buf = 0;
+    uint32_t nextw = 0;
+    int avail = 0;
     auto word = [&](uint64_t i) { return bswap32(__ldg(W32 + tmin(i, last32))); };
     auto fill = [&]() {   // buffer := 64 - (pos & 31) bits from pos
         const uint64_t p = pos0 + rel;
@@ -265,7 +274,7 @@ __global__ void __launch_bounds__(DEC_THREADS) k_decode(const uint64_t* __restri
         nextw = word(wi + 2);
         wi += 3;
     };
-    fill();
+    if (live) fill();
     // one change: Rice gap and canonical-code symbol, with the reference's validation; false on error
     auto one = [&](uint64_t& gap, uint32_t& sym) -> bool {
         if (rel >= blen) return false;
@@ -298,42 +307,37 @@ __global__ void __launch_bounds__(DEC_THREADS) k_decode(const uint64_t* __restri
         return true;
     };
     uint64_t sum = 0;
-    bool ok = true;
-    // outputs: singly up to a multiple-of-4 index, then four at a time as 16-byte stores (the
-    // buffers are 256-byte aligned), then the tail singly
-    int step = 0;
-    const int head = tmin(cnt, int((4 - (ebase & 3)) & 3));
-    for (; step < head && ok; ++step) {
-        uint64_t gp;
-        uint32_t sy;
-        ok = one(gp, sy);
-        if (ok) {
-            gaps[ebase + step] = clamp32(gp);
-            zz[ebase + step] = sy;
+    bool ok = live;
+    uint32_t* mg = &sg[wq][lane * (DEC_CH + 1)];
+    uint32_t* mz = &sz[wq][lane * (DEC_CH + 1)];
+    for (int c0 = 0; __any_sync(FULL, ok && c0 < cnt); c0 += DEC_CH) {
+        const int n = ok ? tmax(0, tmin(DEC_CH, cnt - c0)) : 0;
+        int got = 0;
+        for (; got < n; ++got) {
+            uint64_t gp;
+            uint32_t sy;
+            ok = one(gp, sy);
+            if (!ok) break;
+            mg[got] = clamp32(gp);
+            mz[got] = sy;
             sum += gp + 1;
         }
-    }
-    const int body = head + ((cnt - head) & ~3);
-    for (; step < body && ok; step += 4) {
-        uint64_t g0, g1, g2, g3;
-        uint32_t s0, s1, s2, s3;
-        ok = one(g0, s0) && one(g1, s1) && one(g2, s2) && one(g3, s3);
-        if (ok) {
-            *reinterpret_cast<uint4*>(gaps + ebase + step) = make_uint4(clamp32(g0), clamp32(g1), clamp32(g2), clamp32(g3));
-            *reinterpret_cast<uint4*>(zz + ebase + step) = make_uint4(s0, s1, s2, s3);
-            sum += g0 + g1 + g2 + g3 + 4;
+        __syncwarp();
+        // lanes 0-15 store lane 2i's staged values, lanes 16-31 lane 2i+1's
+        const int k2 = lane & 15;
+#pragma unroll 4
+        for (int i = 0; i < 16; ++i) {
+            const int t = 2 * i + (lane >> 4);
+            const int gt = __shfl_sync(FULL, got, t);
+            const uint64_t dst = __shfl_sync(FULL, ebase, t) + uint64_t(c0 + k2);
+            if (k2 < gt) {
+                gaps[dst] = sg[wq][t * (DEC_CH + 1) + k2];
+                zz[dst] = sz[wq][t * (DEC_CH + 1) + k2];
+            }
         }
+        __syncwarp();
     }
-    for (; step < cnt && ok; ++step) {
-        uint64_t gp;
-        uint32_t sy;
-        ok = one(gp, sy);
-        if (ok) {
-            gaps[ebase + step] = clamp32(gp);
-            zz[ebase + step] = sy;
-            sum += gp + 1;
-        }
-    }
+    if (!live) return;
     ok = ok && rel == blen;
     bsum[b] = ok ? sum : 0;
     if (!ok) atomicOr(&counters[1], (unsigned long long)ERR_DECODE);
