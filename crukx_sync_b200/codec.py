@@ -100,17 +100,20 @@ def encode(old: Mapping[str, torch.Tensor], new: Mapping[str, torch.Tensor],
     names = list(old)
     olds = [old[n] for n in names]
     news = [new[n] for n in names]
-    for name, a, b in zip(names, olds, news):     # the reference's order of checks
-        check16(name, a)
-        check16(name, b)
+    T = torch.Tensor
+    for name, a, b in zip(names, olds, news):     # the reference's order of checks (check16 inlined)
+        if not isinstance(a, T) or a.dtype not in _BITS16 or not a.is_contiguous():
+            check16(name, a)
+        if not isinstance(b, T) or b.dtype not in _BITS16 or not b.is_contiguous():
+            check16(name, b)
         if a.numel() != b.numel():
             raise ValueError(f"{name}: old and new differ in shape")
     if not names:
         return _encode_on(torch.device("cpu"), [], [], [], None, device_result)
-    devs = {t.device for t in olds} | {t.device for t in news}
-    if len(devs) != 1:
+    d0 = olds[0].get_device()
+    if any(t.get_device() != d0 for t in olds) or any(t.get_device() != d0 for t in news):
         raise ValueError("all tensors must be on one device")
-    return _encode_on(next(iter(devs)), names, olds, news, checksums, device_result)
+    return _encode_on(olds[0].device, names, olds, news, checksums, device_result)
 
 
 def _encode_on(dev, names, olds, news, checksums, device_result=False) -> EncodedUpdate:
@@ -235,16 +238,18 @@ def apply(weights: Mapping[str, torch.Tensor], u: ParsedUpdate, checksums: dict 
     if not headers:
         return 0
     targets = []
-    for name, numel, _ in headers:
+    for name, numel, _ in headers:   # check16 inlined: this loop runs once per tensor per apply
         if name not in weights:
             raise ValueError(f"update has tensor {name!r} that the receiver does not have")
         a = weights[name]
-        check16(name, a)
+        if not isinstance(a, torch.Tensor) or a.dtype not in _BITS16 or not a.is_contiguous():
+            check16(name, a)
         if a.numel() != numel:
             raise ValueError(f"{name}: update is for {numel} elements, receiver has {a.numel()}")
         targets.append(a)
     dev = targets[0].device
-    if any(a.device != dev for a in targets):
+    di = targets[0].get_device()
+    if any(a.get_device() != di for a in targets):
         raise ValueError("all updated tensors must be on one device")
     cdev = _cuda_device(dev)
     work = targets if dev.type == "cuda" else [a.to(cdev) for a in targets]

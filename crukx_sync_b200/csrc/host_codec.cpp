@@ -5,6 +5,8 @@
 
 #include <algorithm>
 #include <cstring>
+#include <string_view>
+#include <unordered_set>
 
 namespace crx {
 
@@ -161,6 +163,8 @@ Status parse_core(const uint8_t* data, int64_t avail, int64_t len, uint8_t last,
     if (!r.varint(&n_tensors)) return bad("update is truncated or has a bad varint");
     if (n_tensors > r.remaining()) return bad("too many tensors");
     u->tensors.resize(size_t(n_tensors));
+    std::unordered_set<std::string_view> names_seen;   // a tensor named twice is corrupt (wire.py's check)
+    names_seen.reserve(size_t(n_tensors) * 2);
     unsigned __int128 total_blocks = 0;
     unsigned __int128 per_exp[256] = {};
     for (int64_t t = 0; t < n_tensors; ++t) {
@@ -170,10 +174,7 @@ Status parse_core(const uint8_t* data, int64_t avail, int64_t len, uint8_t last,
         if (!valid_utf8(p, nl)) return bad("tensor name is not valid UTF-8");
         h.name = p;
         h.name_len = nl;
-        for (int64_t s = 0; s < t; ++s) {
-            const TensorHeader& o = u->tensors[size_t(s)];
-            if (o.name_len == nl && std::memcmp(o.name, p, size_t(nl)) == 0) return bad("tensor appears twice");
-        }
+        if (!names_seen.emplace(reinterpret_cast<const char*>(p), size_t(nl)).second) return bad("tensor appears twice");
         if (!r.varint(&h.numel)) return bad("update is truncated or has a bad varint");
         if (!r.take(8, &p)) return bad("update is truncated");
         h.checksum = 0;

@@ -233,8 +233,14 @@ class ParsedUpdate:
             numels = (ctypes.c_int64 * max(n, 1))()
             chks = (ctypes.c_uint64 * max(n, 1))()
             L.crx_update_tensor_table(self._h, names, lens, numels, chks)
-            self._table = [(ctypes.string_at(names[i], lens[i]).decode("utf-8"), int(numels[i]), int(chks[i]))
-                           for i in range(n)]
+            if n == 0:
+                self._table = []
+            else:   # the names lie in one header buffer: one copy, then a slice per name
+                ptrs, ls = names[:n], lens[:n]
+                base = min(ptrs)
+                blob = ctypes.string_at(base, max(q + k for q, k in zip(ptrs, ls)) - base)
+                self._table = [(blob[q - base:q - base + k].decode("utf-8"), e, c)
+                               for q, k, e, c in zip(ptrs, ls, numels[:n], chks[:n])]
         return self._table
 
     @property
