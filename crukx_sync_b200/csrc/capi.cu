@@ -799,8 +799,12 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
         int64_t got = 0;      // bytes [0, got) of the update are in `head`
         int64_t avail = 0;    // what the parser may read: [0, got), and past the block table a window after it
         bool checked = false; // the block table's check is queued (its results land with the window)
+        crx_update* held = nullptr;         // a parse that stopped just past the block table
+        const uint8_t* held_at = nullptr;   // the head buffer its names point into
         for (;;) {   // copy a head, parse it, copy more when the header reaches past it
             if (have > got) {
+                delete held;   // a new head: parse from the start
+                held = nullptr;
                 if (!stage(size_t(have - got) + 1)) return CRX_CUDA_ERROR;
                 if (cudaMemcpyAsync(P.pinned, data + got, size_t(have - got), cudaMemcpyDeviceToHost, st) != cudaSuccess)
                     return CRX_CUDA_ERROR;
@@ -814,10 +818,19 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
                 got = have;
                 avail = std::max(avail, got);
             }
-            crx_update* u = new crx_update;
+            crx_update* u;
             std::string msg;
             int64_t nd = 0;
-            const crx::Status s = crx::parse_head_device_table(head.data(), avail, len, last, &u->u, &nd, &msg);
+            crx::Status s;
+            if (held && held_at == head.data()) {   // only the bytes after the table were missing
+                u = held;
+                s = crx::resume_head_device_table(head.data(), avail, len, &u->u, &nd, &msg);
+            } else {
+                delete held;
+                u = new crx_update;
+                s = crx::parse_head_device_table(head.data(), avail, len, last, &u->u, &nd, &msg);
+            }
+            held = nullptr;
             if (s == crx::kOk) {
                 const int64_t t0 = u->u.block_table_offset;
                 P.last_head = t0;
@@ -853,26 +866,32 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
                 }
                 checked = true;
             }
-            delete u;
             if (s != crx::kNeedMore) {
+                delete u;
                 keep();
                 put_err(err, errlen, msg);
                 return int(s);
             }
             if (t0 >= 0 && nd > t0 && got >= t0) {
                 // the header is here; past the table comes at most a 10-byte length varint: copy
-                // that window only (the table itself is checked on the device)
+                // that window only (the table itself is checked on the device), then resume the
+                // parse there (it is redone from the start only if the head buffer moved)
                 const int64_t w1 = std::min(len, t1 + 16);
-                if (w1 <= avail) return CRX_CUDA_ERROR;   // no progress: cannot happen
-                if (!stage(size_t(w1 - t1))) return CRX_CUDA_ERROR;
-                if (cudaMemcpyAsync(P.pinned, data + t1, size_t(w1 - t1), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
-                    cudaStreamSynchronize(st) != cudaSuccess)
+                const bool failed = w1 <= avail || !stage(size_t(w1 - t1)) ||
+                                   cudaMemcpyAsync(P.pinned, data + t1, size_t(w1 - t1), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+                                   cudaStreamSynchronize(st) != cudaSuccess;
+                if (failed) {   // no progress (cannot happen) or a failed copy
+                    delete u;
                     return CRX_CUDA_ERROR;
-                if (head.size() < size_t(w1)) head.resize(size_t(w1));
+                }
+                held = u;
+                held_at = head.data();   // the buffer the parse read (and its names point into)
+                if (head.size() < size_t(w1)) head.resize(size_t(w1));   // may move it: then parse anew
                 std::memcpy(head.data() + t1, P.pinned, size_t(w1 - t1));
                 avail = w1;
                 continue;
             }
+            delete u;
             have = std::min(len, std::max(nd + 16, 4 * have));
         }
     } catch (const std::bad_alloc&) {

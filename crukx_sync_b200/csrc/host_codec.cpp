@@ -97,6 +97,25 @@ namespace {
 
 // The whole parse over the first `avail` of `len` bytes; `last` is the update's final byte (the
 // padding check needs it).  kNeedMore with *need set when the head does not fit in `avail`.
+// What follows a block table kept elsewhere: the payload length, the payload's place, nothing after
+// it.  `r` stands just past the table.
+template <class Bad>
+Status parse_after_table(Reader& r, const uint8_t* data, int64_t avail, Update* u, Bad& bad) {
+    int64_t pl;
+    if (!r.varint(&pl)) return bad("update is truncated");
+    u->payload_offset = r.pos;
+    if (!r.skip(pl)) return bad("update is truncated");
+    u->payload = r.pos <= avail ? data + u->payload_offset : nullptr;
+    u->payload_len = pl;
+    if (r.remaining() != 0) return bad("trailing bytes after the payload");
+    int64_t changes = 0;
+    for (const TensorHeader& h : u->tensors)
+        for (const Group& g : h.groups) changes += g.count;
+    u->total_changes = changes;
+    u->total_bits = 0;
+    return kOk;
+}
+
 Status parse_core(const uint8_t* data, int64_t avail, int64_t len, uint8_t last, Update* u, int64_t* need,
                   std::string* err, bool table_elsewhere = false) {
     Reader r{data, len, avail};
@@ -210,6 +229,7 @@ Status parse_core(const uint8_t* data, int64_t avail, int64_t len, uint8_t last,
     } else if (!r.take(4 * u->n_blocks, &u->block_table)) {
         return bad("update is truncated");
     }
+    if (table_elsewhere) return parse_after_table(r, data, avail, u, bad);
     int64_t pl;
     if (!r.varint(&pl)) return bad("update is truncated");
     u->payload_offset = r.pos;
@@ -217,14 +237,6 @@ Status parse_core(const uint8_t* data, int64_t avail, int64_t len, uint8_t last,
     u->payload = r.pos <= avail ? data + u->payload_offset : nullptr;
     u->payload_len = pl;
     if (r.remaining() != 0) return bad("trailing bytes after the payload");
-    if (table_elsewhere) {
-        int64_t changes = 0;
-        for (const TensorHeader& h : u->tensors)
-            for (const Group& g : h.groups) changes += g.count;
-        u->total_changes = changes;
-        u->total_bits = 0;
-        return kOk;
-    }
     // block table, one pass split over the worker threads: the bit total, and every change costs
     // at least 2 + rice bits (wire.py:204-211)
     struct Span { int64_t b0, count; int rice; };
@@ -286,6 +298,21 @@ Status parse_head(const uint8_t* head, int64_t head_len, int64_t len, uint8_t la
 Status parse_head_device_table(const uint8_t* head, int64_t head_len, int64_t len, uint8_t last, Update* u,
                                int64_t* need, std::string* err) {
     return parse_core(head, std::min(head_len, len), len, last, u, need, err, true);
+}
+
+Status resume_head_device_table(const uint8_t* head, int64_t head_len, int64_t len, Update* u, int64_t* need,
+                                std::string* err) {
+    Reader r{head, len, std::min(head_len, len)};
+    r.pos = u->block_table_offset + 4 * u->n_blocks;
+    auto bad = [&](const char* m) {
+        if (r.need > 0) {
+            if (need) *need = r.need;
+            return kNeedMore;
+        }
+        if (err) *err = m;
+        return kCorrupt;
+    };
+    return parse_after_table(r, head, r.avail, u, bad);
 }
 
 Status finish_block_table_checks(Update* u, uint64_t total_bits, bool short_block, uint8_t last, std::string* err) {

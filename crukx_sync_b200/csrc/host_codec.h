@@ -84,6 +84,12 @@ Status parse_head(const uint8_t* head, int64_t head_len, int64_t len, uint8_t la
 // finish_block_table_checks.
 Status parse_head_device_table(const uint8_t* head, int64_t head_len, int64_t len, uint8_t last, Update* out,
                                int64_t* need, std::string* err);
+// Resumes a parse_head_device_table that stopped with kNeedMore past the block table (every check
+// before it done, u->block_table_offset and u->n_blocks set): reads what follows the table from
+// `head`, which now holds bytes [0, head_len) at least where they are needed, and gives the verdict
+// the whole parse would give.  `u` must still point into `head` (its names do).
+Status resume_head_device_table(const uint8_t* head, int64_t head_len, int64_t len, Update* u, int64_t* need,
+                                std::string* err);
 // The block table's checks from its bit total and whether some block is shorter than its symbols
 // could be (same messages and order as parse_update's); sets u->total_bits on kOk.
 Status finish_block_table_checks(Update* u, uint64_t total_bits, bool short_block, uint8_t last, std::string* err);

@@ -154,6 +154,26 @@ def test_large_header_needs_several_head_copies():
         assert eq(w[k], new[k])
 
 
+def test_block_table_past_the_first_head_copy():
+    """A block table longer than parse_device's first head copy: the parse stops past the table and
+    resumes on the few bytes after it.  The first apply in a process grows its head buffer, which
+    moves it, so the header is parsed anew; the later ones resume.  All must give the sender's state."""
+    c = crx()
+    g = torch.Generator().manual_seed(21)
+    states = [{"a": (0.02 * torch.randn(6_000_000, generator=g)).bfloat16(),
+               "b": (0.02 * torch.randn(3_000_000, generator=g)).bfloat16()}]
+    for _ in range(3):   # most elements change: about 29 K blocks, a 113 KB table after a small header
+        states.append({k: (v.float() + 2e-4 * torch.randn(v.numel(), generator=g)).bfloat16() for k, v in states[-1].items()})
+    w = cu(states[0])
+    send, recv = {}, {}
+    for i in range(1, len(states)):
+        t = c.encode_update_device(cu(states[i - 1]), cu(states[i]), send)
+        st = c.apply_update(w, t, recv)
+        assert st.changed > 0
+        for k in w:
+            assert eq(w[k], states[i][k]), (i, k)
+
+
 def test_head_only_update_cannot_be_applied():
     from crukx_sync_b200 import codec
     from crukx_sync_b200.wire import parse, parse_head
