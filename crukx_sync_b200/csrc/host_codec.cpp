@@ -153,7 +153,29 @@ Status parse_core(const uint8_t* data, int64_t avail, int64_t len, uint8_t last,
         tb.symbols.resize(size_t(n_sym));
         tb.lengths.resize(size_t(n_sym));
         bool sym_range_ok = true;
-        for (int64_t k = 0; k < n_sym; ++k) {
+        int64_t k = 0;
+        // fast path while 4 bytes are at hand: a symbol of at most 3 varint bytes and its length
+        // byte, read straight from the buffer (the same values and verdicts as the reader below,
+        // which takes over at the first longer varint or near the end of the bytes)
+        while (k < n_sym && r.avail - r.pos >= 4) {
+            const uint8_t* q = r.d + r.pos;
+            uint32_t v = q[0], nb = 1;
+            if (v & 0x80) {
+                v = (v & 0x7Fu) | (uint32_t(q[1] & 0x7F) << 7);
+                nb = 2;
+                if (q[1] & 0x80) {
+                    if (q[2] & 0x80) break;
+                    v |= uint32_t(q[2]) << 14;
+                    nb = 3;
+                }
+            }
+            if (v > kMaxSymbol) sym_range_ok = false;
+            tb.symbols[size_t(k)] = std::min<uint32_t>(v, kMaxSymbol + 1);
+            tb.lengths[size_t(k)] = q[nb];
+            r.pos += nb + 1;
+            ++k;
+        }
+        for (; k < n_sym; ++k) {
             int64_t s;
             int L;
             if (!r.varint(&s) || !r.u8(&L)) return bad("update is truncated or has a bad varint");
