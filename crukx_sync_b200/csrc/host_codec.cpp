@@ -406,9 +406,30 @@ void huffman_unlimited(const std::vector<uint64_t>& counts, std::vector<int>& de
 // (count, id) order, an order of magnitude cheaper to sort than Items; needs every count < 2^44 and
 // n <= 2^20 (the caller checks).  Scratch buffers are reused across the length-limit rounds.
 struct HuffScratch {
-    std::vector<uint64_t> keys, mcount;
+    std::vector<uint64_t> keys, mcount, tmp;
     std::vector<int32_t> parent, depth;
 };
+
+// Ascending LSD radix sort of distinct 64-bit keys, a byte per pass; bytes that are the same in
+// every key are skipped (the length-limit rounds shrink the counts, so fewer bytes vary).
+void radix_sort_keys(std::vector<uint64_t>& a, std::vector<uint64_t>& tmp) {
+    const size_t n = a.size();
+    if (n < 256) {
+        std::sort(a.begin(), a.end());
+        return;
+    }
+    uint64_t diff = 0;
+    for (const uint64_t x : a) diff |= x ^ a[0];
+    tmp.resize(n);
+    for (int sh = 0; sh < 64; sh += 8) {
+        if (((diff >> sh) & 0xFFu) == 0) continue;
+        size_t cnt[257] = {};
+        for (const uint64_t x : a) ++cnt[((x >> sh) & 0xFFu) + 1];
+        for (int i = 0; i < 256; ++i) cnt[i + 1] += cnt[i];
+        for (const uint64_t x : a) tmp[cnt[(x >> sh) & 0xFFu]++] = x;
+        a.swap(tmp);
+    }
+}
 
 void huffman_unlimited_packed(const std::vector<uint64_t>& counts, std::vector<int>& depth_out, HuffScratch& w) {
     const int64_t n = int64_t(counts.size());
@@ -416,7 +437,7 @@ void huffman_unlimited_packed(const std::vector<uint64_t>& counts, std::vector<i
     if (n == 1) return;
     w.keys.resize(size_t(n));
     for (int64_t i = 0; i < n; ++i) w.keys[size_t(i)] = (counts[size_t(i)] << 20) | uint64_t(i);
-    std::sort(w.keys.begin(), w.keys.end());
+    radix_sort_keys(w.keys, w.tmp);
     w.mcount.clear();
     w.mcount.reserve(size_t(n));
     w.parent.assign(size_t(2 * n - 1), 0);
