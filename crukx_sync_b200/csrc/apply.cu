@@ -456,7 +456,7 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
       unsigned long long* __restrict__ spanbase, uint16_t* __restrict__ cval, uint64_t stage_cap,
       unsigned long long* __restrict__ chk_delta,
       unsigned long long* __restrict__ staged, const uint64_t* __restrict__ GS, uint32_t* __restrict__ HNEW,
-      uint16_t* __restrict__ order_scratch, uint16_t* __restrict__ esc_scratch) {
+      uint16_t* __restrict__ order_scratch, uint16_t* __restrict__ esc_scratch, int inplace) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     MapSmem& S = *reinterpret_cast<MapSmem*>(smem_raw);
     const int64_t s = blockIdx.x;
@@ -762,12 +762,20 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             uint32_t at = incl - c;
             for (uint32_t b = bits; b; b &= b - 1, ++at) lst[at] = uint16_t(lane * 32 + (__ffs(b) - 1));
             __syncwarp();
+            int16_t* const pw = tt.w + base;
             for (uint32_t k = lane; k < total; k += 32) {
                 const int i = span0 + lst[k];
                 const uint32_t z8 = S.nz8[i];
                 const uint32_t res = z8 < 255u ? uint32_t(int32_t(z8 >> 1) ^ -int32_t(z8 & 1)) : uint32_t(esc[i]);
                 const uint32_t old = uint16_t(p[i]), nv = (old + res) & 0xFFFFu;
-                if (sb + k < stage_cap) cval[sb + k] = uint16_t(nv);
+                if (sb + k < stage_cap) {
+                    if (inplace) {   // written now; the list keeps the old value, to put back if the update fails
+                        pw[i] = int16_t(nv);
+                        cval[sb + k] = uint16_t(old);
+                    } else {
+                        cval[sb + k] = uint16_t(nv);
+                    }
+                }
                 delta += (uint64_t(nv) - uint64_t(old)) * splitmix_weight(uint64_t(base + i));
                 if (HNEW) {
                     const uint32_t eo = (old >> 7) & 0xFFu, en = (nv >> 7) & 0xFFu;
@@ -787,13 +795,16 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
     block_add_u64<MP_THREADS>(delta, &chk_delta[t], S.red);
 }
 
-// Runs only after the host verdict, which requires every change to have been staged exactly once.
-// One CTA per sub-tile, a warp per span: each lane takes its 32-element run's mark word, its
-// values start at the span's base plus the changed positions of the lanes before it.
+// Writes the list's values at its positions: the new values for weights that k_map staged (host
+// weights, after a passing verdict), the old ones to undo k_map's in-place writes after a failing
+// one.  Slots at or past cap were never written by k_map (only a hostile update over-fills the
+// list) and are skipped.  One CTA per sub-tile, a warp per span: each lane takes its 32-element
+// run's mark word, its values start at the span's base plus the changed positions of the lanes
+// before it.
 __global__ void __launch_bounds__(MP_THREADS) k_commit(const AppTensor* __restrict__ T, int nT,
                                                        const uint32_t* __restrict__ marks,
                                                        const unsigned long long* __restrict__ spanbase,
-                                                       const uint16_t* __restrict__ cval, int64_t st0) {
+                                                       const uint16_t* __restrict__ cval, int64_t st0, uint64_t cap) {
     const int64_t st_i = st0 + blockIdx.x;                // sub-tile
     const int64_t s = st_i / (SUPER_N / MP_SUB);
     const int t = tensor_of_super(T, nT, s);
@@ -816,9 +827,11 @@ __global__ void __launch_bounds__(MP_THREADS) k_commit(const AppTensor* __restri
     for (uint32_t b = bits; b; b &= b - 1, ++at) lst[w][at] = uint16_t(lane * MP_RUN + (__ffs(b) - 1));
     __syncwarp();
     // consecutive lanes take consecutive changes: coalesced value reads, neighbouring writes
-    const uint16_t* v = cval + spanbase[st_i * MP_WARPS + w];
+    const uint64_t vb = spanbase[st_i * MP_WARPS + w];
+    const uint16_t* v = cval + vb;
     int16_t* dst = tt.w + sub0 + w * MP_SPAN;
-    for (uint32_t k = lane; k < total; k += 32) dst[lst[w][k]] = int16_t(v[k]);
+    for (uint32_t k = lane; k < total; k += 32)
+        if (vb + k < cap) dst[lst[w][k]] = int16_t(v[k]);   // slots past the list: never staged
 }
 
 // The same commit into host memory (weights the caller keeps on the host; the device copies the
@@ -1085,7 +1098,10 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
                                                                    dev<uint32_t>(C, S_A_LOCAL), counters);
     }
     CRX_CUDA(cudaGetLastError());
-    // ---- positions, staged values, checksum deltas
+    // ---- positions, staged values, checksum deltas.  Device weights are written here, in place,
+    //      with the old values kept in the list; the host's verdict then either keeps them or has
+    //      k_commit put the old values back.  Host weights get the new values in the list.
+    const bool inplace = host_weights == nullptr;
     const size_t map_smem = sizeof(MapSmem);
     CRX_CUDA(cudaFuncSetAttribute(k_map, cudaFuncAttributeMaxDynamicSharedMemorySize, int(map_smem)));
     { KernelScope ks_(C, "k_map", st);
@@ -1094,7 +1110,7 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
                                                             dev<unsigned long long>(C, S_A_SPANB),
                                                             dev<uint16_t>(C, S_A_CVAL), total, chk_delta, counters + 2,
                                                             dev<uint64_t>(C, S_A_TOT), hnew, dev<uint16_t>(C, S_A_ORDER),
-                                                            dev<uint16_t>(C, S_A_ESC));
+                                                            dev<uint16_t>(C, S_A_ESC), inplace ? 1 : 0);
     }
     CRX_CUDA(cudaGetLastError());
     // ---- verdict (one synchronisation for the whole update)
@@ -1112,13 +1128,29 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
         std::memcpy(hv.data(), C.host, 8 * nsmall);
     }
     trace_phase(C, "apply: verdict (sync)");
+    // A failed verdict leaves the weights as they were: the old values go back over what k_map
+    // wrote (each written element is listed once, with its old value in the slot k_map used).
+    auto undo = [&](Status s) -> Status {
+        if (!inplace) return s;
+        { KernelScope ks_(C, "k_commit", st);
+        k_commit<<<unsigned(n_super * (SUPER_N / MP_SUB)), MP_THREADS, 0, st>>>(
+            dT, nt, dev<uint32_t>(C, S_A_CADDR), dev<unsigned long long>(C, S_A_SPANB), dev<uint16_t>(C, S_A_CVAL), 0, total);
+        }
+        const cudaError_t e1 = cudaGetLastError();
+        const cudaError_t e2 = cudaStreamSynchronize(st);
+        if (e1 != cudaSuccess || e2 != cudaSuccess) {
+            *err += std::string("; restoring the weights failed: ") + cudaGetErrorString(e1 != cudaSuccess ? e1 : e2);
+            return kCudaError;
+        }
+        return s;
+    };
     if (hv[1] & (ERR_DECODE | ERR_RANGE)) {
         *err = "payload positions outside their exponent groups";
-        return kCorrupt;
+        return undo(kCorrupt);
     }
     if (hv[2] != total) {   // every in-range change lands in exactly one sub-tile
         *err = "internal: not every change was placed";
-        return kCudaError;
+        return undo(kCudaError);
     }
     std::string bad_names;
     int n_bad = 0;
@@ -1134,7 +1166,7 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     }
     if (n_bad) {
         *err = "update does not verify (checksum mismatch: " + bad_names + ")";
-        return kCorrupt;
+        return undo(kCorrupt);
     }
     if (host_weights) {   // the weights live on the host
         // Two ways down, run at once.  The last tensors, while their host memory is pinned and up to
@@ -1174,7 +1206,8 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
             const int64_t st0 = s_split * (SUPER_N / MP_SUB);
             { KernelScope ks_(C, "k_commit", st);
             k_commit<<<unsigned((n_super - s_split) * (SUPER_N / MP_SUB)), MP_THREADS, 0, st>>>(
-                dT, nt, dev<uint32_t>(C, S_A_CADDR), dev<unsigned long long>(C, S_A_SPANB), dev<uint16_t>(C, S_A_CVAL), st0);
+                dT, nt, dev<uint32_t>(C, S_A_CADDR), dev<unsigned long long>(C, S_A_SPANB), dev<uint16_t>(C, S_A_CVAL), st0,
+                total);
             }
             cudaError_t e = cudaGetLastError();
             for (int t = t_split; t < nt && e == cudaSuccess; ++t) {
@@ -1197,12 +1230,6 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
         *changed = int64_t(total);
         return kOk;
     }
-    { KernelScope ks_(C, "k_commit", st);
-    k_commit<<<unsigned(n_super * (SUPER_N / MP_SUB)), MP_THREADS, 0, st>>>(dT, nt, dev<uint32_t>(C, S_A_CADDR),
-                                                                          dev<unsigned long long>(C, S_A_SPANB),
-                                                                          dev<uint16_t>(C, S_A_CVAL), 0);
-    }
-    CRX_CUDA(cudaGetLastError());
     // ---- the new weights' histograms for the next apply (tagged version + 1: the caller bumps it).
     //      Rows of dropped entries go to a free list and are reused; nothing is freed here (a
     //      cudaFree would synchronize the device and stall every other stream).

@@ -197,8 +197,10 @@ int crx_apply_versioned(crx_ctx* ctx, const crx_update* u, int16_t* const* weigh
  * the same bits as host_weights[i] (the caller uploaded them); the update is decoded, placed and
  * verified against the copies exactly as crx_apply does, and on success only the changed elements
  * are written into host_weights (the commit list -- a bit per element and the new values -- comes
- * down once and host threads scatter it).  The device copies are left as they were.  On any error
- * nothing is written.  host_weights[i] must stay valid and unused by others until it returns.
+ * down once and host threads scatter it; tensors whose host memory is pinned may instead be
+ * committed into their device copy and copied down whole).  The device copies are scratch: after a
+ * success some may hold the new values.  On any error nothing is written to either.
+ * host_weights[i] must stay valid and unused by others until it returns.
  */
 int crx_apply_to_host(crx_ctx* ctx, const crx_update* u, int16_t* const* device_copies, int16_t* const* host_weights,
                       const uint64_t* cached_checksums, const uint8_t* has_cached, void* stream, int64_t* changed,
