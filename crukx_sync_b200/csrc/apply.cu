@@ -422,6 +422,7 @@ struct MapSmem {
     uint8_t nz8[MP_SUB];                   // zigzag residual of every changed position; 255: in the escape list.
                                            // Before the placement its first KB holds the outside-window counts.
     uint16_t pre[MP_WARPS][MWIN][16];      // exclusive prefixes over the lanes of the masks' counts, at even lanes
+                                           // (first the lanes' counts as bytes, in the same 32 bytes a row)
     uint32_t mark[MP_SUB / 32];            // changed positions
     uint32_t wwin[MP_WARPS][MWIN];         // per-warp window totals, then warp bases
     uint16_t tot[256], estart[256];
@@ -435,6 +436,8 @@ struct MapSmem {
     uint32_t ebase;
     uint64_t red[MP_WARPS];
 };
+
+static_assert(offsetof(MapSmem, pre) % 16 == 0, "16-byte prefix pieces");
 
 // position of the r-th (0-based) set bit of m; m has more than r set bits
 __device__ __forceinline__ uint32_t nth_set_bit(uint32_t m, uint32_t r) {
@@ -576,25 +579,32 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
         __syncwarp();
         const uint32_t oowm = __ballot_sync(FULL, S.msk[w][MWIN][lane] != 0);   // runs with outside elements
         if (lane == 0) S.oowm[w] = oowm;
-        // ---- lane prefixes of the window rows, two rows per scan (16-bit halves)
+        // ---- lane prefixes of the window rows.  Every lane writes its run's count of each row as a
+        //      byte, into the row's prefix slots; then lane 2d + h turns the 16 bytes of row d's
+        //      lanes 16h..16h+15 in place into the exclusive prefixes of its even lanes (16 bits
+        //      each: per 4 lanes one byte-dot-product to the middle lane and one over all four)
+        {
+            uint8_t* const cb = reinterpret_cast<uint8_t*>(&S.pre[w][0][0]);
 #pragma unroll
-        for (int j = 0; j < MWIN / 2; ++j) {
-            const uint32_t v = uint32_t(__popc(S.msk[w][2 * j][lane])) | (uint32_t(__popc(S.msk[w][2 * j + 1][lane])) << 16);
-            uint32_t incl = v;
+            for (int d = 0; d < MWIN; ++d) cb[d * 32 + lane] = uint8_t(__popc(S.msk[w][d][lane]));
+            __syncwarp();
+            const int d = lane >> 1, h = lane & 1;
+            uint4* const q = reinterpret_cast<uint4*>(cb + d * 32 + h * 16);   // this lane's 16 bytes, in and out
+            const uint4 c = *q;
+            const uint32_t wd[4] = {c.x, c.y, c.z, c.w};
+            uint32_t run = 0, out[4];
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t y = __shfl_up_sync(FULL, incl, o);
-                if (lane >= o) incl += y;
+            for (int k = 0; k < 4; ++k) {
+                out[k] = run | (__dp4a(wd[k], 0x0101u, run) << 16);   // lanes 4k and 4k + 2
+                run = __dp4a(wd[k], 0x01010101u, run);
             }
-            const uint32_t ex = incl - v;
-            if (!(lane & 1)) {
-                S.pre[w][2 * j][lane >> 1] = uint16_t(ex & 0xFFFFu);
-                S.pre[w][2 * j + 1][lane >> 1] = uint16_t(ex >> 16);
+            const uint32_t lo = __shfl_xor_sync(FULL, run, 1);   // at odd lanes: the first 16 lanes' total
+            if (h) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) out[k] += lo * 0x00010001u;
+                S.wwin[w][d] = run + lo;
             }
-            if (lane == 31) {
-                S.wwin[w][2 * j] = incl & 0xFFFFu;
-                S.wwin[w][2 * j + 1] = incl >> 16;
-            }
+            *q = make_uint4(out[0], out[1], out[2], out[3]);
         }
         const bool any_out = __syncthreads_or(oowm != 0);
         auto exp_at = [&](int i) { return (uint32_t(uint16_t(p[i])) >> 7) & 0xFFu; };

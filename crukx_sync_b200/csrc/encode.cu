@@ -85,6 +85,7 @@ struct RankSmem {
     uint32_t chm[ER_SUB / 32];            // changed bit of every element, one word per run
     uint32_t msk[ER_WARPS][WIN + 1][32];  // per lane and window row: its run's elements of that exponent (row WIN: below)
     uint32_t pre[ER_WARPS][WIN][16];      // exclusive lane prefixes of the rows' counts at even lanes, all | changed << 16
+                                          // (first every lane's counts as a halfword, in the same 64 bytes a row)
     uint32_t wwin[ER_WARPS][WIN];         // per-warp row totals, then warp bases (all | changed << 16)
     uint32_t ocnt[256];                   // below-window counts per exponent, all | changed << 16
     uint32_t runA[256], runC[256];        // super-tile running totals
@@ -98,6 +99,8 @@ struct RankSmem {
     int emax[2];                          // largest old exponent, alternating between sub-tiles
     uint64_t red[ER_WARPS];
 };
+
+static_assert(offsetof(RankSmem, pre) % 16 == 0, "16-byte prefix pieces");
 
 __device__ __forceinline__ void put_record(uint64_t* rec_key, uint32_t* rec_val, uint64_t rec_cap, uint64_t j, int64_t s,
                                            uint32_t rankA, uint32_t rankC, uint32_t x) {
@@ -284,25 +287,36 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
                 S.wl[w][at] = uint16_t(span0 + lane * 32 + (__ffs(b) - 1));
             if (lane == 31) S.wcnt[w] = tmin(incl, uint32_t(WLIST));
         }
-        // ---- lane prefixes per window row of (all, changed) counts.  Records read a row's prefixes
-        //      only where the span has changes in it; other rows need just the warp's total.
+        // ---- lane prefixes per window row of (all, changed) counts.  Every lane writes its run's two
+        //      counts of each row as a halfword (all | changed << 8), into the row's prefix slots;
+        //      then lane 2d + h turns the 32 bytes of row d's lanes 16h..16h+15 in place into the
+        //      exclusive prefixes of its even lanes (all | changed << 16): a word holds two lanes.
+        {
+            uint16_t* const ch = reinterpret_cast<uint16_t*>(&S.pre[w][0][0]);
 #pragma unroll
-        for (int d = 0; d < WIN; ++d) {
-            const uint32_t m = S.msk[w][d][lane];
-            if (!__any_sync(FULL, (m & cm) != 0)) {
-                const uint32_t a = __reduce_add_sync(FULL, uint32_t(__popc(m)));
-                if (lane == 0) S.wwin[w][d] = a;
-                continue;
+            for (int d = 0; d < WIN; ++d) {
+                const uint32_t m = S.msk[w][d][lane];
+                ch[d * 32 + lane] = uint16_t(uint32_t(__popc(m)) | (uint32_t(__popc(m & cm)) << 8));
             }
-            const uint32_t v = uint32_t(__popc(m)) | (uint32_t(__popc(m & cm)) << 16);
-            uint32_t incl = v;
+            __syncwarp();
+            const int d = lane >> 1, h = lane & 1;
+            uint4* const q = reinterpret_cast<uint4*>(&S.pre[w][d][8 * h]);   // this lane's 32 bytes, in and out
+            const uint4 c0 = q[0], c1 = q[1];
+            const uint32_t wd[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+            uint32_t run = 0, out[8];
 #pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t y = __shfl_up_sync(FULL, incl, o);
-                if (lane >= o) incl += y;
+            for (int k = 0; k < 8; ++k) {   // bytes (a0, c0, a1, c1): add a0 + a1 | (c0 + c1) << 16
+                out[k] = run;
+                run += __byte_perm(wd[k], 0u, 0x4140) + __byte_perm(wd[k], 0u, 0x4342);
             }
-            if (!(lane & 1)) S.pre[w][d][lane >> 1] = incl - v;
-            if (lane == 31) S.wwin[w][d] = incl;
+            const uint32_t lo = __shfl_xor_sync(FULL, run, 1);   // at odd lanes: the first 16 lanes' totals
+            if (h) {
+#pragma unroll
+                for (int k = 0; k < 8; ++k) out[k] += lo;
+                S.wwin[w][d] = run + lo;
+            }
+            q[0] = make_uint4(out[0], out[1], out[2], out[3]);
+            q[1] = make_uint4(out[4], out[5], out[6], out[7]);
         }
         const bool any_out = __syncthreads_or(oowm != 0);
         // elements below the window, whole sub-tile in index order, by one warp (they are rare):
