@@ -7,9 +7,10 @@
 //   k_decode       one thread per 256-change block: Golomb-Rice gap + canonical Huffman residual,
 //                  with the reference's validation (codec.py:504-575, _triton.py:34-88): overrun,
 //                  q > q_max, no code, block not consumed exactly.  Unary runs longer than one
-//                  64-bit window are followed inside the block's own bits only.
-//   k_locals       group-local index = running sum of gap + 1 (codec.py:640-642), range checks
-//                  (codec.py:696-697).
+//                  64-bit window are followed inside the block's own bits only.  It writes the
+//                  running sum of gap + 1 inside the block and the block's group.
+//   k_locals       group-local index = the block's base (the group's earlier blocks' sums) + the
+//                  in-block running sum (codec.py:640-642), range checks (codec.py:696-697).
 //   k_map          per super-tile: per-lane masks of the old exponents over a 16-exponent window,
 //                  then every change is placed by (exponent, local rank) -> position through
 //                  selection on the masks' counts (codec.py:654-694), the new value staged and the
@@ -236,15 +237,16 @@ __global__ void __launch_bounds__(DEC_THREADS) k_decode(const uint64_t* __restri
                                                         int64_t n_blocks, const AppGroup* __restrict__ G,
                                                         const uint64_t* __restrict__ gblock, int64_t ng,
                                                         const DecTable* __restrict__ TB, const uint32_t* __restrict__ SYMS,
-                                                        const uint64_t* __restrict__ GS, uint32_t* __restrict__ gaps,
+                                                        const uint64_t* __restrict__ GS, uint32_t* __restrict__ inblk,
                                                         uint32_t* __restrict__ zz, uint64_t* __restrict__ bsum,
-                                                        unsigned long long* __restrict__ counters) {
+                                                        int32_t* __restrict__ bgroup, unsigned long long* __restrict__ counters) {
     __shared__ uint32_t sg[DEC_THREADS / 32][32 * (DEC_CH + 1)];   // per warp: each lane's staged gaps (rows padded)
     __shared__ uint32_t sz[DEC_THREADS / 32][32 * (DEC_CH + 1)];   // and residual symbols
     const int lane = threadIdx.x & 31, wq = threadIdx.x >> 5;
     const int64_t b = int64_t(blockIdx.x) * DEC_THREADS + threadIdx.x;
     const bool live = b < n_blocks;   // lanes past the last block only take part in the warp's stores
     const int64_t g = live ? last_le(gblock, ng, uint64_t(b)) : 0;
+    if (live) bgroup[b] = int32_t(g);
     const AppGroup grp = live ? G[g] : AppGroup{};
     const uint64_t kb = live ? uint64_t(b) - gblock[g] : 0;
     const int cnt = live ? int(tmin<uint64_t>(kBlock, grp.count - kb * kBlock)) : 0;
@@ -318,9 +320,9 @@ __global__ void __launch_bounds__(DEC_THREADS) k_decode(const uint64_t* __restri
             uint32_t sy;
             ok = one(gp, sy);
             if (!ok) break;
-            mg[got] = clamp32(gp);
-            mz[got] = sy;
             sum += gp + 1;
+            mg[got] = clamp32(sum - 1);   // in-block local index: gap 0 is the first change's
+            mz[got] = sy;
         }
         __syncwarp();
         // lanes 0-15 store lane 2i's staged values, lanes 16-31 lane 2i+1's
@@ -331,7 +333,7 @@ __global__ void __launch_bounds__(DEC_THREADS) k_decode(const uint64_t* __restri
             const int gt = __shfl_sync(FULL, got, t);
             const uint64_t dst = __shfl_sync(FULL, ebase, t) + uint64_t(c0 + k2);
             if (k2 < gt) {
-                gaps[dst] = sg[wq][t * (DEC_CH + 1) + k2];
+                inblk[dst] = sg[wq][t * (DEC_CH + 1) + k2];
                 zz[dst] = sz[wq][t * (DEC_CH + 1) + k2];
             }
         }
@@ -343,54 +345,38 @@ __global__ void __launch_bounds__(DEC_THREADS) k_decode(const uint64_t* __restri
     if (!ok) atomicOr(&counters[1], (unsigned long long)ERR_DECODE);
 }
 
-// group-local index of every change: running sum of gap + 1 within its group
+// group-local index of every change: its block's base (the sums of gap + 1 over the group's earlier
+// blocks, from the scan of the blocks' sums) plus the running sum inside the block that k_decode
+// wrote.  An index at or past the group's size is a range error; since indices grow by at least
+// one per change, that also covers every gap at or past the size (codec.py:696-697).  A warp per
+// block, in place.
 __global__ void __launch_bounds__(256) k_locals(const uint64_t* __restrict__ bscan, int64_t n_blocks,
-                                                const AppGroup* __restrict__ G, const uint64_t* __restrict__ gblock, int64_t ng,
-                                                const uint64_t* __restrict__ GS, const uint32_t* __restrict__ gaps,
+                                                const AppGroup* __restrict__ G, const uint64_t* __restrict__ gblock,
+                                                const int32_t* __restrict__ bgroup, const uint64_t* __restrict__ GS,
                                                 uint32_t* __restrict__ local, unsigned long long* __restrict__ counters) {
     const int64_t b = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (b >= n_blocks) return;
-    const int64_t g = last_le(gblock, ng, uint64_t(b));
+    const int32_t g = bgroup[b];
     const AppGroup grp = G[g];
-    const uint64_t k = uint64_t(b) - gblock[g];
-    const uint64_t cnt = tmin<uint64_t>(kBlock, grp.count - k * kBlock);
-    const uint64_t ebase = grp.start + k * kBlock;
+    const uint64_t gb = gblock[g];
+    const uint64_t k = uint64_t(b) - gb;
+    const uint32_t cnt = uint32_t(tmin<uint64_t>(kBlock, grp.count - k * kBlock));
+    uint32_t* const v = local + grp.start + k * kBlock;
     const uint64_t size = GS[int64_t(grp.tensor) * 256 + grp.exp];
-    uint64_t base = bscan[b] - bscan[gblock[g]];
+    const uint64_t base = bscan[b] - bscan[gb];
     bool bad = false;
     static_assert(kBlock == 256, "eight chunks of 32 per block");
-    uint32_t gv[8];
+    uint32_t in[8];
 #pragma unroll
-    for (int u = 0; u < 8; ++u) gv[u] = uint64_t(32 * u + lane) < cnt ? gaps[ebase + 32 * u + lane] : 0u;   // loads together
+    for (int u = 0; u < 8; ++u) in[u] = uint32_t(32 * u + lane) < cnt ? v[32 * u + lane] : 0u;   // loads together
 #pragma unroll
     for (int u = 0; u < 8; ++u) {
-        if (uint64_t(32 * u) >= cnt) break;
-        const uint64_t i = uint64_t(32 * u + lane);
-        const uint64_t gp = gv[u];
-        // 32-bit running sums while every gap of the chunk is below 2^26 (the usual case)
-        uint64_t incl;
-        if (__all_sync(FULL, gp < (1u << 26))) {
-            uint32_t in32 = i < cnt ? uint32_t(gp) + 1u : 0u;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t y = __shfl_up_sync(FULL, in32, o);
-                if (lane >= o) in32 += y;
-            }
-            incl = in32;
-        } else {
-            incl = i < cnt ? gp + 1 : 0;
-            for (int o = 1; o < 32; o <<= 1) {
-                const uint64_t y = __shfl_up_sync(FULL, incl, o);
-                if (lane >= o) incl += y;
-            }
+        if (uint32_t(32 * u + lane) < cnt) {
+            const uint64_t loc = base + in[u];
+            bad |= loc >= size;
+            v[32 * u + lane] = loc > 0xFFFFFFFFull ? 0xFFFFFFFFu : uint32_t(loc);
         }
-        if (i < cnt) {
-            const uint64_t loc = base + incl - 1;
-            if (gp >= size || loc >= size) bad = true;
-            local[ebase + i] = loc > 0xFFFFFFFFull ? 0xFFFFFFFFu : uint32_t(loc);
-        }
-        base += __shfl_sync(FULL, incl, 31);
     }
     if (__any_sync(FULL, bad) && lane == 0) atomicOr(&counters[1], (unsigned long long)ERR_RANGE);
 }
@@ -1008,7 +994,7 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     CRX_CUDA(ensure_dev(C.b[S_A_BOFF], sizeof(uint64_t) * size_t(n_blocks), st));
     CRX_CUDA(ensure_dev(C.b[S_A_BSUM], sizeof(uint64_t) * size_t(n_blocks), st));
     CRX_CUDA(ensure_dev(C.b[S_A_SCAN_TMP], sizeof(uint64_t) * (exclusive_scan_tmp_elems(n_blocks) + 2), st));
-    CRX_CUDA(ensure_dev(C.b[S_A_GAPS], sizeof(uint32_t) * total, st));
+    CRX_CUDA(ensure_dev(C.b[S_A_BGROUP], sizeof(int32_t) * size_t(n_blocks), st));
     CRX_CUDA(ensure_dev(C.b[S_A_ZZ], sizeof(uint32_t) * total, st));
     CRX_CUDA(ensure_dev(C.b[S_A_LOCAL], sizeof(uint32_t) * total, st));
     // commit list: a bit per element, the span's first value slot, the values in position order
@@ -1097,14 +1083,14 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     { KernelScope ks_(C, "k_decode", st);
     k_decode<<<unsigned((n_blocks + DEC_THREADS - 1) / DEC_THREADS), DEC_THREADS, 0, st>>>(
         dev<uint64_t>(C, S_A_PAYLOAD), uint64_t(payload_alloc / 4), dev<uint32_t>(C, S_A_BB), boff, n_blocks, dG, dgblock, ng, dev<DecTable>(C, S_A_TABLES),
-        dev<uint32_t>(C, S_A_SYMS), dev<uint64_t>(C, S_A_TOT), dev<uint32_t>(C, S_A_GAPS), dev<uint32_t>(C, S_A_ZZ),
-        dev<uint64_t>(C, S_A_BSUM), counters);
+        dev<uint32_t>(C, S_A_SYMS), dev<uint64_t>(C, S_A_TOT), dev<uint32_t>(C, S_A_LOCAL), dev<uint32_t>(C, S_A_ZZ),
+        dev<uint64_t>(C, S_A_BSUM), dev<int32_t>(C, S_A_BGROUP), counters);
     }
     CRX_CUDA(cudaGetLastError());
     launch_exclusive_scan_u64(C, dev<uint64_t>(C, S_A_BSUM), n_blocks, scan_tmp, d_total, st);
     { KernelScope ks_(C, "k_locals", st);
-    k_locals<<<unsigned((n_blocks * 32 + 255) / 256), 256, 0, st>>>(dev<uint64_t>(C, S_A_BSUM), n_blocks, dG, dgblock, ng,
-                                                                   dev<uint64_t>(C, S_A_TOT), dev<uint32_t>(C, S_A_GAPS),
+    k_locals<<<unsigned((n_blocks * 32 + 255) / 256), 256, 0, st>>>(dev<uint64_t>(C, S_A_BSUM), n_blocks, dG, dgblock,
+                                                                   dev<int32_t>(C, S_A_BGROUP), dev<uint64_t>(C, S_A_TOT),
                                                                    dev<uint32_t>(C, S_A_LOCAL), counters);
     }
     CRX_CUDA(cudaGetLastError());

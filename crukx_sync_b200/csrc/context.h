@@ -53,7 +53,7 @@ enum Slot : int {
     S_GIDX, S_GROUPS, S_LOCAL, S_VALS, S_COSTS, S_DENSE_HIST, S_RARE_HIST, S_RARE_FLAG, S_RARE_OUT, S_RARE_CNT,
     S_DENSE_CODE, S_BIG_CODE, S_RICE, S_GBLOCK, S_BLOCK_BITS, S_BLOCK_OFF, S_SCAN_TMP, S_PAYLOAD, S_BB32, S_RARE_CODES,
     // apply
-    S_A_TENS, S_A_GROUPS, S_A_TABLES, S_A_SYMS, S_A_PAYLOAD, S_A_BB, S_A_BOFF, S_A_GAPS, S_A_ZZ, S_A_BSUM,
+    S_A_TENS, S_A_GROUPS, S_A_TABLES, S_A_SYMS, S_A_PAYLOAD, S_A_BB, S_A_BOFF, S_A_ZZ, S_A_BSUM,
     S_A_LOCAL, S_A_CADDR, S_A_CVAL, S_A_HS, S_A_TOT, S_A_CHUNK_ROWS, S_A_CHUNK_SUMS, S_A_COUNTERS, S_A_SCAN_TMP,
     S_CHK, S_REC_POS, S_SUPER_T, S_A_HNEW, S_A_HSTORE, S_A_ORDER,
     // size statistics
@@ -62,6 +62,8 @@ enum Slot : int {
     S_A_SPANB,
     // apply: k_map's large residuals, by sub-tile position, one sub-tile per super-tile at a time
     S_A_ESC,
+    // apply: the group of every 256-change block (k_decode finds it, k_locals reads it)
+    S_A_BGROUP,
     S_NSLOTS
 };
 
