@@ -425,18 +425,32 @@ struct MapSmem {
 
 static_assert(offsetof(MapSmem, pre) % 16 == 0, "16-byte prefix pieces");
 
-// position of the r-th (0-based) set bit of m; m has more than r set bits
+// For every byte value: the positions of its set bits, lowest first, four bits each.
+struct NthBitTable {
+    uint32_t v[256];
+};
+constexpr NthBitTable make_nth_bit_table() {
+    NthBitTable t{};
+    for (int m = 0; m < 256; ++m) {
+        uint32_t e = 0;
+        int k = 0;
+        for (int b = 0; b < 8; ++b)
+            if ((m >> b) & 1) e |= uint32_t(b) << (4 * k++);
+        t.v[m] = e;
+    }
+    return t;
+}
+__device__ const NthBitTable kNthBit = make_nth_bit_table();
+
+// position of the r-th (0-based) set bit of m; m has more than r set bits: the half, then the byte
+// by population counts, then the byte's table entry
 __device__ __forceinline__ uint32_t nth_set_bit(uint32_t m, uint32_t r) {
     uint32_t pos = 0;
-#pragma unroll
-    for (int s = 16; s; s >>= 1) {
-        const uint32_t c = __popc(m & ((1u << s) - 1u));
-        const bool up = r >= c;
-        r = up ? r - c : r;
-        m = up ? m >> s : m;
-        pos = up ? pos + uint32_t(s) : pos;
-    }
-    return pos;
+    const uint32_t c16 = __popc(m & 0xFFFFu);
+    if (r >= c16) { r -= c16; m >>= 16; pos = 16; }
+    const uint32_t c8 = __popc(m & 0xFFu);
+    if (r >= c8) { r -= c8; m >>= 8; pos += 8; }
+    return pos + ((__ldg(&kNthBit.v[m & 0xFFu]) >> (4 * r)) & 0xFu);
 }
 
 __global__ void __launch_bounds__(MP_THREADS, 6)
@@ -461,6 +475,8 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
     uint16_t* const esc = esc_scratch + s * MP_SUB;       // residuals whose zigzag is 255 or more, by position
     uint32_t* const ocnt = reinterpret_cast<uint32_t*>(S.nz8);   // outside-window counts per exponent (before placement)
     const uint64_t tg0 = ngt ? G[tt.g_begin].start : 0;   // the tensor's first change: group cursors are relative to it
+    const uint32_t* const lrel = local + tg0;               // indexed by those 32-bit cursors (a tensor has < 2^32 changes)
+    const uint32_t* const zrel = zz + tg0;
     S.pcur[tid] = PS[s * 256 + tid];
     {   // this super-tile's histogram: the next row's prefix (or the tensor's total) minus this one's
         const bool last = e_end >= tt.numel;
@@ -519,10 +535,10 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             pl[j] = 0xFFFFFFFFu;
             pz[j] = 0;
             if (k < ngt) {
-                const uint64_t c = tg0 + S.cursor[k] + uint64_t(lane);
-                if (c < tg0 + S.gend[k]) {   // issued here (volatile), consumed after the marking and scans
-                    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(pl[j]) : "l"(local + c));
-                    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(pz[j]) : "l"(zz + c));
+                const uint32_t c = S.cursor[k];
+                if (uint32_t(lane) < S.gend[k] - c) {   // issued here (volatile), consumed after the marking and scans
+                    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(pl[j]) : "l"(lrel + c + lane));
+                    asm volatile("ld.global.nc.u32 %0, [%1];" : "=r"(pz[j]) : "l"(zrel + c + lane));
                 }
             }
         }
@@ -658,13 +674,12 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             const uint32_t lo = S.pcur[e], tot = S.tot[e];
             if (S.nextloc[k] - lo >= tot) return;
             const uint32_t d = row_of(e);
-            const uint64_t ge = tg0 + S.gend[k];
-            uint64_t cur = tg0 + S.cursor[k];
+            const uint32_t ge = S.gend[k];
+            uint32_t cur = S.cursor[k];   // <= ge, so ge - cur does not wrap
             uint32_t next;
             for (;;) {
-                const uint64_t jn = cur + 32 + lane;
                 uint32_t lcn = 0xFFFFFFFFu, zn = 0;
-                if (jn < ge) { lcn = local[jn]; zn = zz[jn]; }
+                if (32u + uint32_t(lane) < ge - cur) { lcn = lrel[cur + 32u + lane]; zn = zrel[cur + 32u + lane]; }
                 const bool valid = lc != 0xFFFFFFFFu && lc >= lo && lc - lo < tot;
                 if (valid) {
                     uint32_t r = lc - lo;
@@ -701,22 +716,22 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                 const uint32_t m = __ballot_sync(FULL, valid);
                 const int taken = __popc(~m) ? __ffs(~m) - 1 : 32;   // consumed changes are a prefix
                 if (taken < 32) {
-                    cur += uint64_t(taken);
+                    cur += uint32_t(taken);
                     next = __shfl_sync(FULL, lc, taken);   // local[cur], or ~0 past the group's end
                     break;
                 }
-                cur += 32;
+                cur += 32u;
                 lc = lcn;
                 z = zn;
             }
             __syncwarp();
             if (lane == 0) {
-                S.cursor[k] = uint32_t(cur - tg0);
+                S.cursor[k] = cur;
                 S.nextloc[k] = next;
                 if (cur < ge) {   // the group's next changes, for a later sub-tile
-                    const size_t nb = size_t(tmin<uint64_t>(ge - cur, 128));
-                    prefetch_l2(local + cur, 4 * nb);
-                    prefetch_l2(zz + cur, 4 * nb);
+                    const size_t nb = size_t(tmin(ge - cur, 128u));
+                    prefetch_l2(lrel + cur, 4 * nb);
+                    prefetch_l2(zrel + cur, 4 * nb);
                 }
             }
             __syncwarp();
@@ -727,9 +742,9 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
             if (k < ngt) place_group(k, pl[j], pz[j]);
         }
         for (int k = w + MP_WARPS * MP_PRE; k < ngt; k += MP_WARPS) {
-            const uint64_t c = tg0 + S.cursor[k] + uint64_t(lane);
+            const uint32_t c = S.cursor[k];
             uint32_t lc = 0xFFFFFFFFu, z = 0;
-            if (c < tg0 + S.gend[k]) { lc = local[c]; z = zz[c]; }
+            if (uint32_t(lane) < S.gend[k] - c) { lc = lrel[c + lane]; z = zrel[c + lane]; }
             place_group(k, lc, z);
         }
         __syncthreads();
