@@ -23,7 +23,7 @@ from dataclasses import dataclass
 import torch
 
 from . import codec
-from .wire import CorruptUpdate, parse, parse_device, serialize
+from .wire import CorruptUpdate, encoder_parse, parse, parse_device, serialize
 
 __all__ = ["encode_update", "apply_update", "encode_update_device", "UpdateStats", "CorruptUpdate"]
 
@@ -78,7 +78,14 @@ def apply_update(weights: Mapping[str, torch.Tensor], update,
     bytes encode_update returned, or (no reference counterpart) the uint8 CUDA tensor that
     encode_update_device returned, read where it lies."""
     t0 = time.perf_counter()
-    u = parse_device(update) if isinstance(update, torch.Tensor) else parse(update)
+    if isinstance(update, torch.Tensor):
+        # a device update from encode_update_device in this process comes with the encoder's parse:
+        # no header copy down, so nothing waits for the encode to finish
+        u = encoder_parse(update)
+        if u is None:
+            u = parse_device(update)
+    else:
+        u = parse(update)
     codec._trace("parse", t0)
     t1 = time.perf_counter()
     with torch.no_grad():

@@ -27,7 +27,7 @@ EXPORTS = [
     "crx_encode_device", "crx_encoded_copy_device", "crx_parse_head", "crx_parse_device",
     "crx_encode_global", "crx_encoded_part", "crx_encoded_part_copy", "crx_apply_versioned",
     "crx_ctx_hist_cache_hits", "crx_alloc_calls", "crx_size_stats", "crx_apply_to_host",
-    "crx_ctx_kernel_gaps",
+    "crx_ctx_kernel_gaps", "crx_encoded_parse_device",
 ]
 
 # collective callbacks of crx_encode_global
@@ -99,6 +99,7 @@ def load():
             "crx_size_stats": ([P, I32, P, P, P, P, P, CP, SZ], ctypes.c_int),
             "crx_apply_to_host": ([P, P, P, P, P, P, P, P, CP, SZ], ctypes.c_int),
             "crx_ctx_kernel_gaps": ([P, CP, SZ, P, I32], I32),
+            "crx_encoded_parse_device": ([P, P, ctypes.POINTER(P), CP, SZ], ctypes.c_int),
         }
         for name, (args, res) in sig.items():
             fn = getattr(L, name)

@@ -88,6 +88,8 @@ Ctx::~Ctx() {
     if (ev_main) cudaEventDestroy(ev_main);
     if (hstore_ev) cudaEventDestroy(hstore_ev);
     if (hstore_table.p) cudaFreeHost(hstore_table.p);
+    if (wd_ev) cudaEventDestroy(wd_ev);
+    if (head_host.p) cudaFreeHost(head_host.p);
     if (ev_copy) cudaEventDestroy(ev_copy);
     if (copy_stream) cudaStreamDestroy(copy_stream);
     for (auto& d : b)
@@ -257,19 +259,31 @@ cudaError_t Encoded::write_part(uint8_t* prefix, uint8_t* tensors, uint8_t* tbl,
 cudaError_t Encoded::write_device(uint8_t* dst, cudaStream_t s) const {
     const size_t bt = 4 * size_t(n_blocks);
     cudaError_t e = cudaSuccess;
-    if (device) {
-        e = cudaEventSynchronize(ctx->copy_ev[0]);
+    if (device) {   // stream-ordered: nothing waits for the device here
+        // after the encoder's last kernel (its stream may not be `s`); its consistency checks were
+        // read back before the encode returned
+        e = cudaStreamWaitEvent(s, ctx->copy_ev[0], 0);
         if (e != cudaSuccess) return e;
-        if (ctx->small[kEncStatusWord] & ERR_INTERNAL) return cudaErrorUnknown;
-        // the header and the length varint are a few KB of host bytes; the rest moves on the device
-        e = cudaMemcpyAsync(dst, head.data(), head.size(), cudaMemcpyHostToDevice, s);
+        // the header and the length varint are a few KB of host bytes, sent from pinned memory that
+        // the previous call's copies have finished reading; the rest moves on the device
+        if (ctx->wd_busy) {
+            e = cudaEventSynchronize(ctx->wd_ev);
+            if (e != cudaSuccess) return e;
+            ctx->wd_busy = false;
+        }
+        if (!ctx->wd_ev && (e = cudaEventCreateWithFlags(&ctx->wd_ev, cudaEventDisableTiming)) != cudaSuccess) return e;
+        if ((e = ensure_pinned(ctx->head_host, head.size() + len_varint.size(), s)) != cudaSuccess) return e;
+        uint8_t* hh = static_cast<uint8_t*>(ctx->head_host.p);
+        std::memcpy(hh, head.data(), head.size());
+        std::memcpy(hh + head.size(), len_varint.data(), len_varint.size());
+        e = cudaMemcpyAsync(dst, hh, head.size(), cudaMemcpyHostToDevice, s);
         if (e == cudaSuccess && bt) e = cudaMemcpyAsync(dst + head.size(), dtable, bt, cudaMemcpyDeviceToDevice, s);
         if (e == cudaSuccess)
-            e = cudaMemcpyAsync(dst + head.size() + bt, len_varint.data(), len_varint.size(), cudaMemcpyHostToDevice, s);
+            e = cudaMemcpyAsync(dst + head.size() + bt, hh + head.size(), len_varint.size(), cudaMemcpyHostToDevice, s);
         if (e == cudaSuccess && payload_len)
             e = cudaMemcpyAsync(dst + head.size() + bt + len_varint.size(), dpay, payload_len, cudaMemcpyDeviceToDevice, s);
-        // pageable host sources: make sure they were read before head/len_varint can go away
-        if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+        if (e == cudaSuccess) e = cudaEventRecord(ctx->wd_ev, s);
+        if (e == cudaSuccess) ctx->wd_busy = true;
         return e;
     }
     if (pending) {
@@ -556,8 +570,9 @@ void crx_encoded_free(crx_encoded* enc) {
     if (!enc) return;
     if (enc->e.ctx) {
         std::lock_guard<std::mutex> lock(enc->e.ctx->mu);
-        // copies still landing in the context's pinned buffer must finish before it is reused
-        if (enc->e.pending || enc->e.device) {
+        // copies still landing in the context's pinned buffer must finish before it is reused (a
+        // device result's copies are ordered by the context's wd_ev instead)
+        if (enc->e.pending) {
             DeviceGuard g(enc->e.ctx->device);
             cudaStreamSynchronize(enc->e.stream);
         }
@@ -896,6 +911,53 @@ int crx_parse_device(const uint8_t* data, int64_t len, void* stream, crx_update*
         }
     } catch (const std::bad_alloc&) {
         put_err(err, errlen, "crx_parse_device: out of host memory");
+        return CRX_NO_MEMORY;
+    }
+}
+
+int crx_encoded_parse_device(const crx_encoded* enc, const uint8_t* data, crx_update** out, char* err, size_t errlen) {
+    if (!enc || !out || !data || enc->e.part || !enc->e.device) return CRX_BAD_ARGUMENT;
+    *out = nullptr;
+    const crx::Encoded& E = enc->e;
+    try {
+        // the update's bytes as the host parser sees them in a device parse: the header, then (past
+        // the block table, which it does not read) the length varint
+        const int64_t len = int64_t(E.size());
+        const int64_t t0 = int64_t(E.head.size()), t1 = t0 + 4 * E.n_blocks;
+        const int64_t w1 = t1 + int64_t(E.len_varint.size());
+        std::vector<uint8_t> head;
+        {
+            std::lock_guard<std::mutex> pl(g_pool_mu);
+            if (!g_head_pool.empty()) {
+                head.swap(g_head_pool.back());
+                g_head_pool.pop_back();
+            }
+        }
+        if (head.size() < size_t(w1)) head.resize(size_t(w1));
+        std::memcpy(head.data(), E.head.data(), size_t(t0));
+        std::memcpy(head.data() + t1, E.len_varint.data(), E.len_varint.size());
+        crx_update* u = new crx_update;
+        std::string msg;
+        int64_t nd = 0;
+        crx::Status s = crx::parse_head_device_table(head.data(), t0, len, 0, &u->u, &nd, &msg);
+        if (s == crx::kNeedMore && u->u.block_table_offset == t0)
+            s = crx::resume_head_device_table(head.data(), w1, len, &u->u, &nd, &msg);
+        if (s != crx::kOk || u->u.payload_offset != w1 || uint64_t(u->u.payload_len) != E.payload_len) {
+            delete u;
+            std::lock_guard<std::mutex> pl(g_pool_mu);
+            if (g_head_pool.size() < kHeadPoolMax) g_head_pool.push_back(std::move(head));
+            put_err(err, errlen, "crx_encoded_parse_device: internal: the encoder's header does not parse (" + msg + ")");
+            return CRX_CUDA_ERROR;
+        }
+        u->u.total_bits = E.total_bits;
+        u->u.block_table_device = data + t0;
+        u->u.payload_device = data + w1;
+        u->u.payload = nullptr;
+        u->head.swap(head);   // the header's pointers stay valid: the vector's buffer moves with it
+        *out = u;
+        return CRX_OK;
+    } catch (const std::bad_alloc&) {
+        put_err(err, errlen, "crx_encoded_parse_device: out of host memory");
         return CRX_NO_MEMORY;
     }
 }

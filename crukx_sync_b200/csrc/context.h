@@ -113,6 +113,13 @@ struct Ctx {
     uint64_t hist_hits = 0;   // tensors whose histogram pass was skipped
     DevBuf hstore_table;      // pinned: the table of the last histogram store, read by an async copy
     cudaEvent_t hstore_ev = nullptr;   // recorded after that copy
+    // device results (Encoded::write_device): the header and length varint go up from head_host on
+    // the caller's stream; wd_ev is recorded after that call's copies.  Until it has passed, the
+    // host does not rewrite head_host and the next encode's stream does not rewrite the workspace's
+    // block table and payload, which those copies read.
+    DevBuf head_host;
+    cudaEvent_t wd_ev = nullptr;
+    bool wd_busy = false;
     ~Ctx();
 };
 

@@ -1085,6 +1085,8 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
         C.live = nullptr;
         if (de != cudaSuccess) { *err = std::string("detaching the previous update: ") + cudaGetErrorString(de); return kCudaError; }
     }
+    // copies of an earlier device result may still read the block table and payload workspace
+    if (C.wd_busy) CRX_CUDA(cudaStreamWaitEvent(st, C.wd_ev, 0));
     out->ctx = &C;
     out->head.clear();
     out->len_varint.assign(1, 0);
@@ -1494,6 +1496,7 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     out->n_blocks = n_blocks;
     out->payload_len = payload_len;
     out->changes = total;
+    if (!gx) out->total_bits = total_bits;
     if (device_result) {   // block table and payload stay on the device; only the error flags come back
         CRX_CUDA(chunk_events(C, 1));
         CRX_CUDA(cudaMemcpyAsync(C.small + kEncStatusWord, counters + 1, 8, cudaMemcpyDeviceToHost, st));

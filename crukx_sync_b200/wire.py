@@ -138,6 +138,11 @@ class EncodedUpdate:
         st = stream if stream is not None else torch.cuda.current_stream(out.device).cuda_stream
         if n and L.crx_encoded_copy_device(self._h, ctypes.c_void_p(out.data_ptr()), n, ctypes.c_void_p(st)) != _ext.CRX_OK:
             raise RuntimeError("crukx_sync_b200: encoded update device copy failed")
+        if n:   # the encoder's own parse of these bytes, for apply_update while they stay unchanged
+            h = ctypes.c_void_p()
+            err = ctypes.create_string_buffer(256)
+            if L.crx_encoded_parse_device(self._h, ctypes.c_void_p(out.data_ptr()), ctypes.byref(h), err, 256) == _ext.CRX_OK:
+                out._crx_parsed = (ParsedUpdate(_handle=h), out._version, out.data_ptr(), n)
         return out
 
     def part(self) -> dict:
@@ -318,6 +323,15 @@ class ParsedUpdate:
 def parse(data: bytes) -> ParsedUpdate:
     """Parse and structurally validate an update (every limit of the format); CorruptUpdate if not."""
     return ParsedUpdate(data)
+
+
+def encoder_parse(update):
+    """The parse that to_device attached to a device update, while the tensor is the one it wrote
+    and was not modified since (same address, size and version counter); else None."""
+    pre = getattr(update, "_crx_parsed", None)
+    if pre is not None and pre[1] == update._version and pre[2] == update.data_ptr() and pre[3] == update.numel():
+        return pre[0]
+    return None
 
 
 def parse_device(update, stream=None) -> ParsedUpdate:

@@ -90,15 +90,26 @@ void crx_encoded_free(crx_encoded* enc);
  * Device-resident updates (no reference counterpart: the reference always returns host bytes).
  * crx_encode_device runs the same encoder but leaves the block table and payload in the context's
  * device workspace; crx_encoded_copy_device writes the complete update, byte-identical to
- * crx_encoded_copy's, into device memory `dst` (cap >= crx_encoded_size) on `stream`, reading back
- * only a status word.  Copy (or free) the result before the next encode on the same context, which
- * otherwise first moves it to host memory.  crx_encoded_copy also works on such a result.
+ * crx_encoded_copy's, into device memory `dst` (cap >= crx_encoded_size) on `stream`, ordered after
+ * the encode; it returns without waiting for the device (the encoder's consistency checks were
+ * read back before crx_encode_device returned).  Copy (or free) the result before the next encode
+ * on the same context, which otherwise first moves it to host memory.  crx_encoded_copy also works
+ * on such a result.
  */
 int crx_encode_device(crx_ctx* ctx, int32_t n_tensors, const int16_t* const* prev, const int16_t* const* cur,
                       const int64_t* numel, const uint8_t* const* names, const int64_t* name_len,
                       const uint64_t* cached_checksums, const uint8_t* has_cached, void* stream,
                       crx_encoded** out, char* err, size_t errlen);
 int crx_encoded_copy_device(const crx_encoded* enc, void* dst, int64_t cap, void* stream);
+/*
+ * The parsed form of the update that crx_encoded_copy_device wrote at device address `data`, built
+ * from the encoder's own host-side header (no reference counterpart): what crx_parse_device would
+ * return for those bytes, without copying the header down or checking the block table, so that a
+ * receiver in the same process (the sender's own replica) applies it without waiting for the
+ * encode to finish.  Only for a device result (crx_encode_device) whose bytes at `data` are
+ * unchanged; free with crx_update_free.
+ */
+int crx_encoded_parse_device(const crx_encoded* enc, const uint8_t* data, crx_update** out, char* err, size_t errlen);
 
 /*
  * One update encoded by several ranks (no reference counterpart; the single-GPU encode of the

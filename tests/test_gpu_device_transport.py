@@ -189,6 +189,36 @@ def test_head_only_update_cannot_be_applied():
         assert torch.equal(w[k], go[k])
 
 
+def test_encoder_parse_until_the_update_is_modified():
+    """A device update carries its encoder's parse: applied as it is, it gives the new weights;
+    after an in-place change of one byte (the tensor's version moves) it is parsed anew from the
+    device and gets the same verdict as the changed bytes do on the host path."""
+    from crukx_sync_b200 import wire
+    c = crx()
+    old, new = cases.case_multi()[0]
+    go, gn = cu(old), cu(new)
+    t = c.encode_update_device(go, gn)
+    assert wire.encoder_parse(t) is not None
+    w = {k: v.clone() for k, v in go.items()}
+    assert c.apply_update(w, t).changed > 0
+    for k in new:
+        assert eq(w[k], new[k])
+    good = host(t)
+    for i in (5, len(good) // 2, len(good) - 1):
+        t2 = c.encode_update_device(go, gn)
+        t2[i] ^= 0x41
+        assert wire.encoder_parse(t2) is None
+        bad = bytearray(good)
+        bad[i] ^= 0x41
+        wh = {k: v.clone() for k, v in go.items()}
+        wd = {k: v.clone() for k, v in go.items()}
+        vh = verdict(lambda: c.apply_update(wh, bytes(bad)))
+        vd = verdict(lambda: c.apply_update(wd, t2))
+        assert vh == vd, i
+        for k in go:
+            assert torch.equal(wh[k], wd[k])
+
+
 def test_empty_update_on_device():
     c = crx()
     a, _ = cases.rl_pair(1000)
