@@ -64,6 +64,8 @@ enum Slot : int {
     S_A_ESC,
     // apply: the group of every 256-change block (k_decode finds it, k_locals reads it)
     S_A_BGROUP,
+    // encode: every block's bits, assembled from bit 0 in a fixed-size slot (k_pack_slots -> k_compact)
+    S_PACK_SLOTS,
     S_NSLOTS
 };
 

@@ -13,8 +13,10 @@
 //   k_r0 / k_stats Golomb-Rice candidate costs per group (codec.py:268-275) and the
 //                  (exponent, zigzag residual) symbol histogram (codec.py:355-367).
 //   host           Rice choice, length-limited Huffman per exponent (codec.py:71-111, 369-392).
-//   k_block_bits   bits per 256-change block (codec.py:411-416), then an exclusive scan.
-//   k_pack         one warp per block assembles its bits MSB-first (codec.py:218-257).
+//   k_pack_slots   one warp per 256-change block assembles its bits MSB-first (codec.py:218-257)
+//                  from bit 0 of the block's slot and records its length (codec.py:411-416);
+//                  an exclusive scan of the lengths gives every block's offset.
+//   k_compact      every block's slot shifted into place in the payload.
 #include <algorithm>
 #include <cstdio>
 #include <cstring>
@@ -741,37 +743,6 @@ __device__ __forceinline__ uint32_t code_of(const uint32_t* __restrict__ dense_c
     return z < DENSE_SYM ? dense_code[e * DENSE_SYM + z] : big_code[int64_t(e) * kSymSpace + z];
 }
 
-// bits of each 256-change block; one warp per block
-__global__ void __launch_bounds__(256) k_block_bits(const uint64_t* __restrict__ g_start, const int32_t* __restrict__ g_exp,
-                                                    const uint8_t* __restrict__ g_rice, const uint64_t* __restrict__ g_block,
-                                                    int64_t ng, int64_t n_blocks, const uint32_t* __restrict__ local,
-                                                    const uint32_t* __restrict__ vals, const uint32_t* __restrict__ dense_code,
-                                                    const uint32_t* __restrict__ big_code, uint64_t* __restrict__ bb64,
-                                                    uint32_t* __restrict__ bb32, unsigned long long* __restrict__ counters) {
-    const int64_t b = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
-    const int lane = threadIdx.x & 31;
-    if (b >= n_blocks) return;
-    const int64_t g = group_of(g_block, ng, uint64_t(b));
-    const uint64_t gs = g_start[g], ge = g_start[g + 1];
-    const uint64_t j0 = gs + uint64_t(b - int64_t(g_block[g])) * kBlock;
-    const uint64_t j1 = tmin<uint64_t>(j0 + kBlock, ge);
-    const int r = g_rice[g];
-    const int e = g_exp[g];
-    uint64_t sum = 0;
-    for (uint64_t j = j0 + lane; j < j1; j += 32) {
-        const uint32_t loc = local[j];
-        const uint64_t gap = j == gs ? loc : uint64_t(loc) - local[j - 1] - 1;
-        const uint32_t cl = code_of(dense_code, big_code, e, zigzag_of(vals[j]));
-        sum += (gap >> r) + 1 + r + (cl >> 24);
-    }
-    for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(FULL, sum, o);
-    if (lane == 0) {
-        bb64[b] = sum;
-        bb32[b] = uint32_t(sum);
-        if (sum >> 32) atomicOr(&counters[1], (unsigned long long)ERR_BLOCK_TOO_LONG);
-    }
-}
-
 __device__ __forceinline__ void or_word(uint32_t* words, uint64_t w, uint32_t v) {
     if (v) atomicOr(&words[w], bswap32(v));
 }
@@ -821,20 +792,21 @@ __device__ __forceinline__ void stage_bits(uint32_t* sw, uint32_t rel, uint64_t 
     }
 }
 
-constexpr int PACK_WORDS = 512;   // a warp assembles blocks of up to 16 Kbit in shared memory
+constexpr int SLOT_WORDS = 128;   // a block of up to 4 Kbit is assembled in shared memory and kept in its slot
 
-// one warp per block: Rice gap then canonical Huffman code per change, MSB first.  A block that
-// fits is assembled in shared memory, then its words are stored (the two edge words, which it may
-// share with its neighbours, by atomic OR into the zeroed payload); a longer block writes its bits
-// straight to the payload by atomic OR.
-__global__ void __launch_bounds__(256, 5) k_pack(const uint64_t* __restrict__ g_start, const int32_t* __restrict__ g_exp,
-                                              const uint8_t* __restrict__ g_rice, const uint64_t* __restrict__ g_block,
-                                              int64_t ng, int64_t n_blocks, const uint32_t* __restrict__ local,
-                                              const uint32_t* __restrict__ vals, const uint32_t* __restrict__ dense_code,
-                                              const uint32_t* __restrict__ big_code, const uint64_t* __restrict__ block_off,
-                                              const uint32_t* __restrict__ block_bits, uint32_t* __restrict__ words,
-                                              uint32_t bit0) {
-    __shared__ uint32_t stage[256 / 32][PACK_WORDS];
+// One warp per 256-change block: Rice gap then canonical Huffman code per change, MSB first
+// (codec.py:218-257).  The block's bit count goes to the block table (bb32, and bb64 for the offset
+// scan; codec.py:411-416).  A block that fits its slot is assembled in shared memory from bit 0 and stored there
+// whole; k_compact later moves it to its place in the payload.  Longer blocks (rare) are encoded
+// again by k_compact straight into the payload.
+__global__ void __launch_bounds__(256, 5) k_pack_slots(const uint64_t* __restrict__ g_start, const int32_t* __restrict__ g_exp,
+                                                    const uint8_t* __restrict__ g_rice, const uint64_t* __restrict__ g_block,
+                                                    int64_t ng, int64_t n_blocks, const uint32_t* __restrict__ local,
+                                                    const uint32_t* __restrict__ vals, const uint32_t* __restrict__ dense_code,
+                                                    const uint32_t* __restrict__ big_code, uint32_t* __restrict__ slots,
+                                                    uint64_t* __restrict__ bb64, uint32_t* __restrict__ bb32,
+                                                    unsigned long long* __restrict__ counters) {
+    __shared__ uint32_t stage[256 / 32][SLOT_WORDS];
     const int64_t b = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
     if (b >= n_blocks) return;
@@ -844,68 +816,118 @@ __global__ void __launch_bounds__(256, 5) k_pack(const uint64_t* __restrict__ g_
     const uint64_t j1 = tmin<uint64_t>(j0 + kBlock, ge);
     const int r = g_rice[g];
     const int e = g_exp[g];
-    uint64_t pos = block_off[b] + bit0;   // bit0: where this part starts inside its first byte
-    const uint32_t o0 = uint32_t(pos & 31);
-    const uint32_t nw = uint32_t((uint64_t(o0) + block_bits[b] + 31) >> 5);   // words the block touches
-    if (nw <= uint32_t(PACK_WORDS)) {
-        uint32_t* sw = stage[threadIdx.x >> 5];
-        for (uint32_t k = lane; k < nw; k += 32) sw[k] = 0;
-        __syncwarp();
-        uint32_t rel = o0;
-        static_assert(kBlock == 256, "eight chunks of 32 per block");
-        uint32_t locs[8], vs[8];   // the block's loads issued together; previous indices by shuffle
+    uint32_t* sw = stage[threadIdx.x >> 5];
+    for (int k = lane; k < SLOT_WORDS; k += 32) sw[k] = 0;
+    __syncwarp();
+    static_assert(kBlock == 256, "eight chunks of 32 per block");
+    uint32_t locs[8], vs[8];   // the block's loads issued together; previous indices by shuffle
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const uint64_t j = j0 + 32 * u + lane;
-            locs[u] = j < j1 ? local[j] : 0u;
-            vs[u] = j < j1 ? vals[j] : 0u;
+    for (int u = 0; u < 8; ++u) {
+        const uint64_t j = j0 + 32 * u + lane;
+        locs[u] = j < j1 ? local[j] : 0u;
+        vs[u] = j < j1 ? vals[j] : 0u;
+    }
+    uint32_t carry = lane == 0 && j0 > gs ? local[j0 - 1] : 0u;
+    uint64_t rel = 0;     // the block's bits so far (warp-uniform)
+    bool fits = true;     // every chunk so far was staged (warp-uniform)
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+        const uint64_t j = j0 + 32 * u + lane;
+        const uint32_t up = __shfl_up_sync(FULL, locs[u], 1);
+        const uint32_t prev = lane ? up : carry;
+        carry = __shfl_sync(FULL, locs[u], 31);
+        uint32_t cl = 0;
+        uint64_t gap = 0, L = 0;
+        if (j < j1) {
+            gap = j == gs ? locs[u] : uint64_t(locs[u]) - prev - 1;
+            cl = code_of(dense_code, big_code, e, zigzag_of(vs[u]));
+            L = (gap >> r) + 1 + uint64_t(r) + (cl >> 24);
         }
-        uint32_t carry = lane == 0 && j0 > gs ? local[j0 - 1] : 0u;
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {
-            const uint64_t j = j0 + 32 * u + lane;
-            const uint32_t up = __shfl_up_sync(FULL, locs[u], 1);
-            const uint32_t prev = lane ? up : carry;
-            carry = __shfl_sync(FULL, locs[u], 31);
-            uint32_t L = 0, cl = 0;
-            uint64_t gap = 0;
-            if (j < j1) {
-                gap = j == gs ? locs[u] : uint64_t(locs[u]) - prev - 1;
-                cl = code_of(dense_code, big_code, e, zigzag_of(vs[u]));
-                L = uint32_t(gap >> r) + 1u + uint32_t(r) + (cl >> 24);   // < 2^14: the block fits
-            }
-            uint32_t incl = L;
+        uint64_t incl;
+        if (__all_sync(FULL, L < (1u << 26))) {   // the usual case: 32-bit sums
+            uint32_t in32 = uint32_t(L);
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
-                const uint32_t y = __shfl_up_sync(FULL, incl, o);
+                const uint32_t y = __shfl_up_sync(FULL, in32, o);
+                if (lane >= o) in32 += y;
+            }
+            incl = in32;
+        } else {
+            incl = L;
+            for (int o = 1; o < 32; o <<= 1) {
+                const uint64_t y = __shfl_up_sync(FULL, incl, o);
                 if (lane >= o) incl += y;
             }
-            if (j < j1) {
-                uint32_t at = rel + incl - L;
-                uint32_t q = uint32_t(gap >> r);
-                const int hl = int(cl >> 24);
-                const uint64_t rem = r ? (gap & ((1ull << r) - 1)) : 0;
-                const int tail_len = 1 + r + hl;                          // the 0, r remainder bits, code
-                const uint64_t tail = (rem << hl) | (cl & 0xFFFFFFu);     // leading 0 is implicit
-                while (q + uint32_t(tail_len) > 64u) {   // long unary runs: ones 32 at a time
-                    const uint32_t c = tmin(q, 32u);
-                    stage_bits(sw, at, (1ull << c) - 1, int(c));
-                    q -= c;
-                    at += c;
-                }
-                stage_bits(sw, at, q ? ((((1ull << q) - 1) << tail_len) | tail) : tail, int(q) + tail_len);
-            }
-            rel += __shfl_sync(FULL, incl, 31);
         }
+        const uint64_t ctot = __shfl_sync(FULL, incl, 31);
+        fits = fits && rel + ctot <= uint64_t(SLOT_WORDS) * 32;
+        if (fits && j < j1) {
+            uint32_t at = uint32_t(rel + incl - L);
+            uint32_t q = uint32_t(gap >> r);
+            const int hl = int(cl >> 24);
+            const uint64_t rem = r ? (gap & ((1ull << r) - 1)) : 0;
+            const int tail_len = 1 + r + hl;                          // the 0, r remainder bits, code
+            const uint64_t tail = (rem << hl) | (cl & 0xFFFFFFu);     // leading 0 is implicit
+            while (q + uint32_t(tail_len) > 64u) {   // long unary runs: ones 32 at a time
+                const uint32_t c = tmin(q, 32u);
+                stage_bits(sw, at, (1ull << c) - 1, int(c));
+                q -= c;
+                at += c;
+            }
+            stage_bits(sw, at, q ? ((((1ull << q) - 1) << tail_len) | tail) : tail, int(q) + tail_len);
+        }
+        rel += ctot;
+    }
+    if (lane == 0) {
+        bb64[b] = rel;
+        bb32[b] = uint32_t(rel);
+        if (rel >> 32) atomicOr(&counters[1], (unsigned long long)ERR_BLOCK_TOO_LONG);
+    }
+    if (fits) {
         __syncwarp();
+        uint32_t* dst = slots + b * SLOT_WORDS;
+        const uint32_t nw = uint32_t((rel + 31) >> 5);
+        for (uint32_t k = lane; k < nw; k += 32) dst[k] = sw[k];
+    }
+}
+
+// One warp per block: its slot's words shifted to the block's bit offset in the payload (the two
+// edge words, which it may share with its neighbours, by atomic OR into the zeroed payload; the
+// others by plain stores).  A block longer than a slot is encoded here again, straight into the
+// payload.  block_off: exclusive scan of the blocks' bits; bit0: where this part starts inside its
+// first byte (a rank's part of a global update).
+__global__ void __launch_bounds__(256) k_compact(const uint64_t* __restrict__ g_start, const int32_t* __restrict__ g_exp,
+                                                 const uint8_t* __restrict__ g_rice, const uint64_t* __restrict__ g_block,
+                                                 int64_t ng, int64_t n_blocks, const uint32_t* __restrict__ local,
+                                                 const uint32_t* __restrict__ vals, const uint32_t* __restrict__ dense_code,
+                                                 const uint32_t* __restrict__ big_code, const uint32_t* __restrict__ slots,
+                                                 const uint64_t* __restrict__ block_off, const uint32_t* __restrict__ block_bits,
+                                                 uint32_t* __restrict__ words, uint32_t bit0) {
+    const int64_t b = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (b >= n_blocks) return;
+    uint64_t pos = block_off[b] + bit0;
+    const uint32_t bits = block_bits[b];
+    if (bits <= uint32_t(SLOT_WORDS) * 32) {
+        const uint32_t* src = slots + b * SLOT_WORDS;
+        const uint32_t o = uint32_t(pos & 31);
         const uint64_t w0 = pos >> 5;
-        for (uint32_t k = lane; k < nw; k += 32) {
-            const uint32_t v = sw[k];
-            if (k == 0 || k + 1 == nw) or_word(words, w0 + k, v);
+        const uint32_t nin = (bits + 31) >> 5, nout = (o + bits + 31) >> 5;
+        for (uint32_t k = lane; k < nout; k += 32) {
+            const uint32_t hi = k < nin ? src[k] : 0u;
+            const uint32_t lo = k >= 1 && k - 1 < nin ? src[k - 1] : 0u;
+            const uint32_t v = o ? (hi >> o) | (lo << (32 - o)) : hi;
+            if (k == 0 || k + 1 == nout) or_word(words, w0 + k, v);
             else words[w0 + k] = bswap32(v);
         }
         return;
     }
+    const int64_t g = group_of(g_block, ng, uint64_t(b));
+    const uint64_t gs = g_start[g], ge = g_start[g + 1];
+    const uint64_t j0 = gs + uint64_t(b - int64_t(g_block[g])) * kBlock;
+    const uint64_t j1 = tmin<uint64_t>(j0 + kBlock, ge);
+    const int r = g_rice[g];
+    const int e = g_exp[g];
     for (uint64_t jb = j0; jb < j1; jb += 32) {
         const uint64_t j = jb + lane;
         uint64_t L = 0, gap = 0;
@@ -1412,10 +1434,11 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     CRX_CUDA(ensure_dev(C.b[S_SCAN_TMP], sizeof(uint64_t) * (exclusive_scan_tmp_elems(n_blocks) + 2), st));
     const uint32_t* big_code = rare_codes.empty() ? dev<uint32_t>(C, S_DENSE_CODE) : dev<uint32_t>(C, S_BIG_CODE);
     const unsigned warps_grid = unsigned((n_blocks * 32 + 255) / 256);
-    { KernelScope ks_(C, "k_block_bits", st);
-    k_block_bits<<<warps_grid, 256, 0, st>>>(g_start, g_exp, g_rice, g_block, ng, n_blocks, local, vals,
-                                             dev<uint32_t>(C, S_DENSE_CODE), big_code, dev<uint64_t>(C, S_BLOCK_BITS),
-                                             dev<uint32_t>(C, S_BB32), counters);
+    CRX_CUDA(ensure_dev(C.b[S_PACK_SLOTS], sizeof(uint32_t) * SLOT_WORDS * size_t(n_blocks), st));
+    { KernelScope ks_(C, "k_pack_slots", st);
+    k_pack_slots<<<warps_grid, 256, 0, st>>>(g_start, g_exp, g_rice, g_block, ng, n_blocks, local, vals,
+                                             dev<uint32_t>(C, S_DENSE_CODE), big_code, dev<uint32_t>(C, S_PACK_SLOTS),
+                                             dev<uint64_t>(C, S_BLOCK_BITS), dev<uint32_t>(C, S_BB32), counters);
     }
     CRX_CUDA(cudaGetLastError());
     uint64_t* scan_tmp = dev<uint64_t>(C, S_SCAN_TMP);
@@ -1443,10 +1466,11 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     const size_t n_words = size_t((bit0 + total_bits + 31) / 32) + 4;
     CRX_CUDA(ensure_dev(C.b[S_PAYLOAD], 4 * n_words, st));
     CRX_CUDA(cudaMemsetAsync(C.b[S_PAYLOAD].p, 0, 4 * n_words, st));
-    { KernelScope ks_(C, "k_pack", st);
-    k_pack<<<warps_grid, 256, 0, st>>>(g_start, g_exp, g_rice, g_block, ng, n_blocks, local, vals,
-                                       dev<uint32_t>(C, S_DENSE_CODE), big_code, dev<uint64_t>(C, S_BLOCK_BITS),
-                                       dev<uint32_t>(C, S_BB32), dev<uint32_t>(C, S_PAYLOAD), bit0);
+    { KernelScope ks_(C, "k_compact", st);
+    k_compact<<<warps_grid, 256, 0, st>>>(g_start, g_exp, g_rice, g_block, ng, n_blocks, local, vals,
+                                          dev<uint32_t>(C, S_DENSE_CODE), big_code, dev<uint32_t>(C, S_PACK_SLOTS),
+                                          dev<uint64_t>(C, S_BLOCK_BITS), dev<uint32_t>(C, S_BB32),
+                                          dev<uint32_t>(C, S_PAYLOAD), bit0);
     }
     CRX_CUDA(cudaGetLastError());
 
@@ -1508,7 +1532,7 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
         C.live = out;
         return kOk;
     }
-    // block table, error flags and payload go to pinned memory behind k_pack; nothing waits for
+    // block table, error flags and payload go to pinned memory behind k_compact; nothing waits for
     // them here: the serializer pre-faults its destination meanwhile (Encoded::write)
     const size_t bt = 4 * size_t(n_blocks);
     CRX_CUDA(ensure_pinned(C.out_host, bt + payload_len + 16, st));
