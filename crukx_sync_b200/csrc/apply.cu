@@ -558,17 +558,16 @@ k_map(const AppTensor* __restrict__ T, int nT, const AppGroup* __restrict__ G, c
                 uint4 q[4];
 #pragma unroll
                 for (int c = 0; c < 4; ++c) q[c] = rv[c];
-                // both elements of a word at once: 16-bit halves hold e + 256 - ebase (no carry out),
-                // flipping bit 8 turns window exponents into 0..15 and all others into 272 and up,
-                // and a halfword minimum with 16 gives the row (row_of for both)
-                const uint32_t kofs = (256u - ebase) * 0x00010001u;
+                // both elements of a word at once: per 16-bit half, (e - ebase) mod 2^16 then the
+                // minimum with 16 (below the window wraps to 65280 and up) -- row_of for both
+                const uint32_t nb = ((0x10000u - ebase) & 0xFFFFu) * 0x00010001u;
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     const uint32_t wd[4] = {q[c].x, q[c].y, q[c].z, q[c].w};
 #pragma unroll
                     for (int h = 0; h < 4; ++h) {
                         const int k = c * 8 + h * 2;
-                        const uint32_t r2 = __vimin3_u16x2((((wd[h] >> 7) & 0x00FF00FFu) + kofs) ^ 0x01000100u, 0x00100010u, 0x00100010u);
+                        const uint32_t r2 = __viaddmin_u16x2((wd[h] >> 7) & 0x00FF00FFu, nb, 0x00100010u);
                         atomicOr(mine + (r2 & 0xFFFFu) * 32, 1u << k);
                         atomicOr(mine + (r2 >> 16) * 32, 2u << k);
                     }

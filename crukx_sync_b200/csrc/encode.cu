@@ -200,8 +200,9 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
                 // halves plus 0x7FFF carry into bit 15 exactly when nonzero, never into bit 16)
                 auto nzh = [](uint32_t x) { return (((x & 0x7FFF7FFFu) + 0x7FFF7FFFu) | x) & 0x80008000u; };
                 const uint32_t c0 = nzh(a.x ^ b.x), c1 = nzh(a.y ^ b.y), c2 = nzh(a.z ^ b.z), c3 = nzh(a.w ^ b.w);
-                uint32_t cb = ((c0 >> 15) & 1u) | ((c0 >> 30) & 2u) | ((c1 >> 13) & 4u) | ((c1 >> 28) & 8u) |
-                              ((c2 >> 11) & 16u) | ((c2 >> 26) & 32u) | ((c3 >> 9) & 64u) | ((c3 >> 24) & 128u);
+                // word h's two bits (15, 31) to bits 2h and 16 + 2h, then the high ones down to 2h + 1
+                const uint32_t cx = (c0 >> 15) | (c1 >> 13) | (c2 >> 11) | (c3 >> 9);
+                uint32_t cb = (cx | (cx >> 15)) & 0xFFu;
                 cb <<= 8 * q;
                 cb |= __shfl_xor_sync(FULL, cb, 1);
                 cb |= __shfl_xor_sync(FULL, cb, 2);
@@ -249,15 +250,14 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
             const uint32_t* ew = &S.texp[(w * 32 + lane) * 9];
             uint32_t* mine = &S.msk[w][0][lane];
             if (vn == ER_RUN) {
-                // two exponent bytes per word at once: 16-bit halves hold e + 256 - ebase (no carry
-                // out), flipping bit 8 turns window exponents into 0..15 and all others into 272 and
-                // up, and a halfword minimum with 16 gives the row (row_of for both)
-                const uint32_t kofs = (256u - ebase) * 0x00010001u;
+                // two exponent bytes per word at once: per 16-bit half, (e - ebase) mod 2^16 then
+                // the minimum with 16 (below the window wraps to 65280 and up) -- row_of for both
+                const uint32_t nb = ((0x10000u - ebase) & 0xFFFFu) * 0x00010001u;
 #pragma unroll
                 for (int g = 0; g < ER_RUN / 4; ++g) {
                     const uint32_t eb = ew[g];
-                    const uint32_t r02 = __vimin3_u16x2(((eb & 0x00FF00FFu) + kofs) ^ 0x01000100u, 0x00100010u, 0x00100010u);
-                    const uint32_t r13 = __vimin3_u16x2((((eb >> 8) & 0x00FF00FFu) + kofs) ^ 0x01000100u, 0x00100010u, 0x00100010u);
+                    const uint32_t r02 = __viaddmin_u16x2(eb & 0x00FF00FFu, nb, 0x00100010u);
+                    const uint32_t r13 = __viaddmin_u16x2(__byte_perm(eb, 0u, 0x4341), nb, 0x00100010u);
                     atomicOr(mine + (r02 & 0xFFFFu) * 32, 1u << (4 * g));
                     atomicOr(mine + (r13 & 0xFFFFu) * 32, 2u << (4 * g));
                     atomicOr(mine + (r02 >> 16) * 32, 4u << (4 * g));
