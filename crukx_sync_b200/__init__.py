@@ -66,6 +66,9 @@ def encode_update_device(old: Mapping[str, torch.Tensor], new: Mapping[str, torc
         if dev is None or dev.type != "cuda":
             dev = torch.device("cuda", torch.cuda.current_device())
         data = update.to_device(dev)
+        pre = getattr(data, "_crx_parsed", None)
+        if pre is not None:   # its tensor table is the present tensors, in the caller's order
+            pre[0]._table = [(n, old[n].numel(), c) for n, c in update.checksums.items()]
     update.close()
     if checksums is not None:
         checksums.update(update.checksums)

@@ -237,8 +237,10 @@ def apply(weights: Mapping[str, torch.Tensor], u: ParsedUpdate, checksums: dict 
     headers = u.tensor_table()
     if not headers:
         return 0
-    targets = []
-    for name, numel, _ in headers:   # check16 inlined: this loop runs once per tensor per apply
+    # one pass per tensor (check16 and the cache lookup inlined: this runs once per tensor per apply)
+    targets, vers, cvals, hits = [], [], [], []
+    di = None
+    for name, numel, _ in headers:
         if name not in weights:
             raise ValueError(f"update has tensor {name!r} that the receiver does not have")
         a = weights[name]
@@ -246,18 +248,26 @@ def apply(weights: Mapping[str, torch.Tensor], u: ParsedUpdate, checksums: dict 
             check16(name, a)
         if a.numel() != numel:
             raise ValueError(f"{name}: update is for {numel} elements, receiver has {a.numel()}")
+        d = a.get_device()
+        if di is None:
+            di = d
+        elif d != di:
+            raise ValueError("all updated tensors must be on one device")
+        v = a._version
         targets.append(a)
+        vers.append(v)
+        if checksums:   # a cached checksum is trusted only while the tensor's version is the recorded one
+            hit = checksums.get(name)
+            ok = isinstance(hit, tuple) and hit[1] == v and hit[0] is not None
+            cvals.append(hit[0] if ok else 0)
+            hits.append(ok)
     dev = targets[0].device
-    di = targets[0].get_device()
-    if any(a.get_device() != di for a in targets):
-        raise ValueError("all updated tensors must be on one device")
     cdev = _cuda_device(dev)
     work = targets if dev.type == "cuda" else [a.to(cdev) for a in targets]
     k = len(headers)
     if checksums:
-        cached = [_cache_get(checksums, name, a) for (name, _, _), a in zip(headers, targets)]
-        cache = _ext.CBuf("Q", [c if c is not None else 0 for c in cached])
-        has = _ext.CBuf("B", [c is not None for c in cached])
+        cache = _ext.CBuf("Q", cvals)
+        has = _ext.CBuf("B", hits)
     else:
         cache, has = None, None
     ptrs = _ext.ptr_array([a.data_ptr() for a in work])
@@ -269,9 +279,9 @@ def apply(weights: Mapping[str, torch.Tensor], u: ParsedUpdate, checksums: dict 
         if dev.type == "cuda" and checksums is not None:
             # tensors written in place on the device: the library may keep their exponent
             # histograms for the next apply, tagged with the version they will have after it
-            vers = _ext.CBuf("Q", [a._version for a in targets])
+            vtab = _ext.CBuf("Q", vers)
             tag = _ext.CBuf("B", bytes([1]) * k)
-            st = L.crx_apply_versioned(_ext.context(cdev.index), u.handle, ptrs, cache, has, vers, tag,
+            st = L.crx_apply_versioned(_ext.context(cdev.index), u.handle, ptrs, cache, has, vtab, tag,
                                        ctypes.c_void_p(stream), ctypes.byref(changed), err, 1024)
         elif dev.type == "cuda":
             st = L.crx_apply(_ext.context(cdev.index), u.handle, ptrs, cache, has, ctypes.c_void_p(stream),

@@ -920,9 +920,28 @@ int crx_encoded_parse_device(const crx_encoded* enc, const uint8_t* data, crx_up
     *out = nullptr;
     const crx::Encoded& E = enc->e;
     try {
+        const int64_t len = int64_t(E.size());
+        if (E.pre) {   // parsed up to the block table while the encoder's last kernels ran
+            crx_update* u = new crx_update;
+            u->u = std::move(*E.pre);
+            E.pre.reset();
+            u->head = E.head;   // the names move to this copy of the header
+            for (crx::TensorHeader& h : u->u.tensors) h.name = u->head.data() + (h.name - E.head.data());
+            std::string msg;
+            if (crx::resume_after_table(E.len_varint.data(), int64_t(E.len_varint.size()), len, &u->u, &msg) != crx::kOk ||
+                uint64_t(u->u.payload_len) != E.payload_len) {
+                delete u;
+                put_err(err, errlen, "crx_encoded_parse_device: internal: the encoder's header does not parse (" + msg + ")");
+                return CRX_CUDA_ERROR;
+            }
+            u->u.total_bits = E.total_bits;
+            u->u.block_table_device = data + E.head.size();
+            u->u.payload_device = data + u->u.payload_offset;
+            *out = u;
+            return CRX_OK;
+        }
         // the update's bytes as the host parser sees them in a device parse: the header, then (past
         // the block table, which it does not read) the length varint
-        const int64_t len = int64_t(E.size());
         const int64_t t0 = int64_t(E.head.size()), t1 = t0 + 4 * E.n_blocks;
         const int64_t w1 = t1 + int64_t(E.len_varint.size());
         std::vector<uint8_t> head;

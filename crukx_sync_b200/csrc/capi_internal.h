@@ -5,6 +5,7 @@
 
 #include <cstdint>
 #include <cstring>
+#include <memory>
 #include <string>
 #include <vector>
 
@@ -49,6 +50,9 @@ struct Encoded {
     int64_t n_blocks = 0;
     uint64_t payload_len = 0;
     std::vector<uint8_t> len_varint;   // payload_len as LEB128
+    // a device result's header parsed up to its block table while the encoder's last kernels ran
+    // (names point into `head`); crx_encoded_parse_device completes it once, then it is gone
+    mutable std::unique_ptr<Update> pre;
     std::vector<uint64_t> checksums;   // per caller tensor: checksum of `cur` (when present)
     std::vector<uint8_t> present;      // per caller tensor: 1 when the tensor is in the update
     uint64_t changes = 0;

@@ -592,7 +592,8 @@ __global__ void __launch_bounds__(256, 5) k_stats(const uint64_t* __restrict__ g
     __syncthreads();
 
     int64_t g = -1;                    // this lane's current group and its register accumulators
-    uint64_t ge = 0, gs = 0, acc0 = 0, acc1 = 0, acc2 = 0, small = 0;
+    uint64_t ge = 0, gs = 0, acc0 = 0, acc1 = 0, acc2 = 0;
+    uint32_t small_lo = 0, small_hi = 0;   // counts of the symbols 0..3 and 4..7, a byte each
     uint32_t cand = 0;
     int e = 0;
     auto flush = [&]() {
@@ -603,7 +604,7 @@ __global__ void __launch_bounds__(256, 5) k_stats(const uint64_t* __restrict__ g
             if (acc1) atomicAdd(&S.cost[lg][1], (unsigned long long)acc1);
             if (acc2) atomicAdd(&S.cost[lg][2], (unsigned long long)acc2);
             for (int z = 0; z < 8; ++z) {
-                const uint32_t c = uint32_t(small >> (8 * z)) & 0xFFu;
+                const uint32_t c = ((z < 4 ? small_lo : small_hi) >> (8 * (z & 3))) & 0xFFu;
                 if (c) atomicAdd(&S.hist[lg][z], c);
             }
         } else {
@@ -611,11 +612,12 @@ __global__ void __launch_bounds__(256, 5) k_stats(const uint64_t* __restrict__ g
             if (acc1) atomicAdd(&costs[3 * g + 1], (unsigned long long)acc1);
             if (acc2) atomicAdd(&costs[3 * g + 2], (unsigned long long)acc2);
             for (int z = 0; z < 8; ++z) {
-                const uint64_t c = (small >> (8 * z)) & 0xFFu;
+                const uint64_t c = ((z < 4 ? small_lo : small_hi) >> (8 * (z & 3))) & 0xFFu;
                 if (c) atomicAdd(&dense_hist[e * DENSE_SYM + z], (unsigned long long)c);
             }
         }
-        acc0 = acc1 = acc2 = small = 0;
+        acc0 = acc1 = acc2 = 0;
+        small_lo = small_hi = 0;
     };
     // each warp takes a contiguous quarter of the CTA's changes, four chunks of 32 loaded at once
     const uint64_t wb = j0 + uint64_t(threadIdx.x >> 5) * (STATS_PER_CTA / 8);
@@ -647,14 +649,15 @@ __global__ void __launch_bounds__(256, 5) k_stats(const uint64_t* __restrict__ g
                     e = g_exp[g];
                 }
                 const uint32_t prev = lane ? prevw : (j > gs ? pl[u] : 0u);
-                const uint64_t gap = j == gs ? loc : uint64_t(loc) - prev - 1;
+                const uint32_t gap = j == gs ? loc : loc - prev - 1;   // locals ascend within a group
                 const uint32_t c0 = cand & 255, c1 = (cand >> 8) & 255, c2 = (cand >> 16) & 255;
-                acc0 += (gap >> c0) + 1 + c0;
-                acc1 += (gap >> c1) + 1 + c1;
-                acc2 += (gap >> c2) + 1 + c2;
+                acc0 += uint64_t(gap >> c0) + (1 + c0);
+                acc1 += uint64_t(gap >> c1) + (1 + c1);
+                acc2 += uint64_t(gap >> c2) + (1 + c2);
                 const uint32_t z = zigzag_of(vs[u]);
                 if (z < 8) {
-                    small += 1ull << (8 * z);
+                    const uint32_t one = 1u << (8 * (z & 3));
+                    if (z < 4) small_lo += one; else small_hi += one;
                 } else if (z < DENSE_SYM) {
                     const int64_t lg = g - g0;
                     if (lg < STATS_LOCAL_GROUPS) atomicAdd(&S.hist[lg][z], 1u);
@@ -1446,35 +1449,8 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     launch_exclusive_scan_u64(C, dev<uint64_t>(C, S_BLOCK_BITS), n_blocks, scan_tmp, d_total_bits, st);
     CRX_CUDA(cudaMemcpyAsync(hostc, d_total_bits, 8, cudaMemcpyDeviceToHost, st));
     CRX_CUDA(cudaMemcpyAsync(hostc + 1, counters + 1, 8, cudaMemcpyDeviceToHost, st));
-    CRX_CUDA(cudaStreamSynchronize(st));
-    const uint64_t total_bits = hostc[0];
-    trace_phase(C, "encode: block bits (sync 4)");
-    if (hostc[1] & ERR_BLOCK_TOO_LONG) {
-        *err = "a block exceeds 2^32 bits; the update cannot be represented";
-        return kValueError;
-    }
-    uint64_t bit_before = 0, bits_all = total_bits;   // global mode: this part's offset, the update's bits
-    if (gx) {
-        std::vector<uint64_t> bits;
-        const Status xs = exchange_per_rank(*gx, total_bits, &bits, err);
-        if (xs != kOk) return xs;
-        bits_all = 0;
-        for (int r = 0; r < gx->world; ++r) { if (r < gx->rank) bit_before += bits[size_t(r)]; bits_all += bits[size_t(r)]; }
-    }
-    const uint32_t bit0 = uint32_t(bit_before & 7);
-    const uint64_t payload_len = (bit0 + total_bits + 7) / 8;
-    const size_t n_words = size_t((bit0 + total_bits + 31) / 32) + 4;
-    CRX_CUDA(ensure_dev(C.b[S_PAYLOAD], 4 * n_words, st));
-    CRX_CUDA(cudaMemsetAsync(C.b[S_PAYLOAD].p, 0, 4 * n_words, st));
-    { KernelScope ks_(C, "k_compact", st);
-    k_compact<<<warps_grid, 256, 0, st>>>(g_start, g_exp, g_rice, g_block, ng, n_blocks, local, vals,
-                                          dev<uint32_t>(C, S_DENSE_CODE), big_code, dev<uint32_t>(C, S_PACK_SLOTS),
-                                          dev<uint64_t>(C, S_BLOCK_BITS), dev<uint32_t>(C, S_BB32),
-                                          dev<uint32_t>(C, S_PAYLOAD), bit0);
-    }
-    CRX_CUDA(cudaGetLastError());
-
-    // ---- header (wire.py:64-89); block table and payload go to pinned memory in one pass each
+    // ---- header (wire.py:64-89), built while the GPU packs; a device result also gets its parse
+    //      up to the block table now (the rest, the payload length, after the lengths are known)
     out->head.clear();
     out->head.reserve(4096);
     put_prefix(out->head, tabs);
@@ -1510,6 +1486,45 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
             ob.push_back(rice[size_t(g)]);
         }
     }
+    if (device_result && !gx) {
+        out->pre = std::make_unique<Update>();
+        int64_t nd = 0;
+        std::string pmsg;
+        // the update's length is not known yet: any bound past the block table serves here
+        const int64_t t1 = int64_t(out->head.size()) + 4 * n_blocks;
+        const Status ps = parse_head_device_table(out->head.data(), int64_t(out->head.size()), t1 + (int64_t(1) << 60), 0,
+                                                  out->pre.get(), &nd, &pmsg);
+        if (ps != kNeedMore || out->pre->block_table_offset != int64_t(out->head.size()) || out->pre->n_blocks != n_blocks)
+            out->pre.reset();   // (not expected) the parse is then done in full when asked for
+    }
+    CRX_CUDA(cudaStreamSynchronize(st));
+    const uint64_t total_bits = hostc[0];
+    trace_phase(C, "encode: block bits (sync 4)");
+    if (hostc[1] & ERR_BLOCK_TOO_LONG) {
+        *err = "a block exceeds 2^32 bits; the update cannot be represented";
+        return kValueError;
+    }
+    uint64_t bit_before = 0, bits_all = total_bits;   // global mode: this part's offset, the update's bits
+    if (gx) {
+        std::vector<uint64_t> bits;
+        const Status xs = exchange_per_rank(*gx, total_bits, &bits, err);
+        if (xs != kOk) return xs;
+        bits_all = 0;
+        for (int r = 0; r < gx->world; ++r) { if (r < gx->rank) bit_before += bits[size_t(r)]; bits_all += bits[size_t(r)]; }
+    }
+    const uint32_t bit0 = uint32_t(bit_before & 7);
+    const uint64_t payload_len = (bit0 + total_bits + 7) / 8;
+    const size_t n_words = size_t((bit0 + total_bits + 31) / 32) + 4;
+    CRX_CUDA(ensure_dev(C.b[S_PAYLOAD], 4 * n_words, st));
+    CRX_CUDA(cudaMemsetAsync(C.b[S_PAYLOAD].p, 0, 4 * n_words, st));
+    { KernelScope ks_(C, "k_compact", st);
+    k_compact<<<warps_grid, 256, 0, st>>>(g_start, g_exp, g_rice, g_block, ng, n_blocks, local, vals,
+                                          dev<uint32_t>(C, S_DENSE_CODE), big_code, dev<uint32_t>(C, S_PACK_SLOTS),
+                                          dev<uint64_t>(C, S_BLOCK_BITS), dev<uint32_t>(C, S_BB32),
+                                          dev<uint32_t>(C, S_PAYLOAD), bit0);
+    }
+    CRX_CUDA(cudaGetLastError());
+    // block table and payload go to pinned memory in one pass each (below), or stay on the device
     out->len_varint.clear();
     put_varint(out->len_varint, gx ? (bits_all + 7) / 8 : payload_len);
     if (gx) {

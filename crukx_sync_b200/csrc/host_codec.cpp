@@ -337,6 +337,25 @@ Status resume_head_device_table(const uint8_t* head, int64_t head_len, int64_t l
     return parse_after_table(r, head, r.avail, u, bad);
 }
 
+Status resume_after_table(const uint8_t* after, int64_t after_len, int64_t len, Update* u, std::string* err) {
+    const int64_t t1 = u->block_table_offset + 4 * u->n_blocks;
+    if (t1 > len) {
+        if (err) *err = "update is truncated";
+        return kCorrupt;
+    }
+    Reader r{after, len - t1, std::min(after_len, len - t1)};   // offsets relative to t1
+    auto bad = [&](const char* m) {
+        if (err) *err = m;
+        return kCorrupt;
+    };
+    const Status s = parse_after_table(r, after, r.avail, u, bad);
+    if (s == kOk) {
+        u->payload_offset += t1;
+        u->payload = nullptr;
+    }
+    return s;
+}
+
 Status finish_block_table_checks(Update* u, uint64_t total_bits, bool short_block, uint8_t last, std::string* err) {
     auto bad = [&](const char* m) {
         if (err) *err = m;

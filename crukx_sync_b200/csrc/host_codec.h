@@ -90,6 +90,9 @@ Status parse_head_device_table(const uint8_t* head, int64_t head_len, int64_t le
 // the whole parse would give.  `u` must still point into `head` (its names do).
 Status resume_head_device_table(const uint8_t* head, int64_t head_len, int64_t len, Update* u, int64_t* need,
                                 std::string* err);
+// The same completion from the bytes right after the block table alone (`after`, after_len of them,
+// the update being len bytes): for a header whose names point elsewhere.
+Status resume_after_table(const uint8_t* after, int64_t after_len, int64_t len, Update* u, std::string* err);
 // The block table's checks from its bit total and whether some block is shorter than its symbols
 // could be (same messages and order as parse_update's); sets u->total_bits on kOk.
 Status finish_block_table_checks(Update* u, uint64_t total_bits, bool short_block, uint8_t last, std::string* err);

@@ -199,6 +199,8 @@ def test_encoder_parse_until_the_update_is_modified():
     go, gn = cu(old), cu(new)
     t = c.encode_update_device(go, gn)
     assert wire.encoder_parse(t) is not None
+    assert wire.encoder_parse(t).tensor_table() == wire.parse_device(t).tensor_table()
+    assert wire.encoder_parse(t).changes == wire.parse_device(t).changes
     w = {k: v.clone() for k, v in go.items()}
     assert c.apply_update(w, t).changed > 0
     for k in new:
