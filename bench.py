@@ -538,7 +538,8 @@ def run_ours(args, rank, world, dist):
     kt = kernel_times(ctx)
     kg = kernel_gaps(ctx)
     L.crx_ctx_profile(ctx, 0)
-    algo = {"k_enc_rank": 4.0 * my_params, "k_map": 2.0 * my_params, "k_app_hist": 2.0 * my_params}
+    # k_map reads the old weights (2 B/element) and writes every changed element in place (2 B/change)
+    algo = {"k_enc_rank": 4.0 * my_params, "k_map": 2.0 * my_params + 2.0 * changed, "k_app_hist": 2.0 * my_params}
     kernels = {}
     for nm, (ms, n) in sorted(kt.items(), key=lambda x: -x[1][0]):
         per = ms / max(n, 1)

@@ -98,25 +98,31 @@ def encode(old: Mapping[str, torch.Tensor], new: Mapping[str, torch.Tensor],
            checksums: dict | None = None, device_result: bool = False) -> EncodedUpdate:
     """The encoded update (not yet bytes); ``.checksums`` holds what the sender cache commits."""
     names = list(old)
-    olds = [old[n] for n in names]
-    news = [new[n] for n in names]
+    olds, news, numels, devs = [], [], [], set()
     T = torch.Tensor
-    for name, a, b in zip(names, olds, news):     # the reference's order of checks (check16 inlined)
+    for name in names:     # the reference's order of checks (check16 inlined); one pass per tensor
+        a = old[name]
+        b = new[name]
         if not isinstance(a, T) or a.dtype not in _BITS16 or not a.is_contiguous():
             check16(name, a)
         if not isinstance(b, T) or b.dtype not in _BITS16 or not b.is_contiguous():
             check16(name, b)
-        if a.numel() != b.numel():
+        n = a.numel()
+        if n != b.numel():
             raise ValueError(f"{name}: old and new differ in shape")
+        olds.append(a)
+        news.append(b)
+        numels.append(n)
+        devs.add(a.get_device())
+        devs.add(b.get_device())
     if not names:
         return _encode_on(torch.device("cpu"), [], [], [], None, device_result)
-    d0 = olds[0].get_device()
-    if any(t.get_device() != d0 for t in olds) or any(t.get_device() != d0 for t in news):
+    if len(devs) > 1:
         raise ValueError("all tensors must be on one device")
-    return _encode_on(olds[0].device, names, olds, news, checksums, device_result)
+    return _encode_on(olds[0].device, names, olds, news, checksums, device_result, numels)
 
 
-def _encode_on(dev, names, olds, news, checksums, device_result=False) -> EncodedUpdate:
+def _encode_on(dev, names, olds, news, checksums, device_result=False, numels=None) -> EncodedUpdate:
     cdev = _cuda_device(dev)
     if dev.type != "cuda":
         olds = [a.to(cdev) for a in olds]
@@ -125,7 +131,7 @@ def _encode_on(dev, names, olds, news, checksums, device_result=False) -> Encode
     k = len(names)
     prev = _ext.ptr_array([a.data_ptr() for a in olds])
     cur = _ext.ptr_array([b.data_ptr() for b in news])
-    numel = _ext.CBuf("q", [a.numel() for a in olds])
+    numel = _ext.CBuf("q", numels if numels is not None else [a.numel() for a in olds])
     keep, name_ptrs, name_len = _name_table(names)
     if checksums:
         hits = [checksums.get(n) for n in names]
