@@ -74,7 +74,7 @@ __device__ __forceinline__ int64_t group_of(const uint64_t* __restrict__ start, 
 
 constexpr int ER_THREADS = 256;
 constexpr int ER_WARPS = ER_THREADS / 32;
-constexpr int ER_MINB = 5;                   // CTAs per SM (48 registers a thread, 45 KB of shared memory)
+constexpr int ER_MINB = 6;                   // CTAs per SM (40 registers a thread, 37 KB of shared memory)
 constexpr int ER_SPAN = 1024;                // elements per warp
 constexpr int ER_SUB = ER_SPAN * ER_WARPS;   // elements per sub-tile
 constexpr int ER_RUN = ER_SPAN / 32;         // 32 per lane
@@ -83,11 +83,13 @@ constexpr int WLIST = 256;                   // in-window changes of a span list
 static_assert(SUPER_N % ER_SUB == 0 && ER_SUB <= 0xFFFF, "whole sub-tiles per super-tile; 16-bit packed counts");
 
 struct RankSmem {
-    uint32_t texp[ER_SUB / 32 * 9];       // old exponent bytes; run r (32 elements) in words 9r..9r+7
+    // old exponent bytes; run r (32 elements) in words 9r..9r+7.  Once a warp has marked its runs it
+    // reuses their words for its lane prefixes (pre_of): exclusive prefixes of the rows' counts at
+    // even lanes, all | changed << 16 (first every lane's counts as a halfword, in the same 64 bytes
+    // a row).  Exponents needed later are taken from the elements' bits instead.
+    uint32_t texp[ER_SUB / 32 * 9];
     uint32_t chm[ER_SUB / 32];            // changed bit of every element, one word per run
     uint32_t msk[ER_WARPS][WIN + 1][32];  // per lane and window row: its run's elements of that exponent (row WIN: below)
-    uint32_t pre[ER_WARPS][WIN][16];      // exclusive lane prefixes of the rows' counts at even lanes, all | changed << 16
-                                          // (first every lane's counts as a halfword, in the same 64 bytes a row)
     uint32_t wwin[ER_WARPS][WIN];         // per-warp row totals, then warp bases (all | changed << 16)
     uint32_t ocnt[256];                   // below-window counts per exponent, all | changed << 16
     uint32_t runA[256], runC[256];        // super-tile running totals
@@ -102,7 +104,12 @@ struct RankSmem {
     uint64_t red[ER_WARPS];
 };
 
-static_assert(offsetof(RankSmem, pre) % 16 == 0, "16-byte prefix pieces");
+// warp w's lane prefixes: [WIN][16] words in the exponent words of its own 32 runs
+__device__ __forceinline__ uint32_t (*pre_of(RankSmem& S, int w))[16] {
+    return reinterpret_cast<uint32_t(*)[16]>(&S.texp[w * 32 * 9]);
+}
+static_assert(offsetof(RankSmem, texp) % 16 == 0 && (32 * 9 * 4) % 16 == 0, "16-byte prefix pieces");
+static_assert(32 * 9 >= WIN * 16, "a warp's lane prefixes fit in its runs' exponent words");
 
 __device__ __forceinline__ void put_record(uint64_t* rec_key, uint32_t* rec_val, uint64_t rec_cap, uint64_t j, int64_t s,
                                            uint32_t rankA, uint32_t rankC, uint32_t x) {
@@ -242,7 +249,7 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
         if (tid == 0) S.emax[(it + 1) & 1] = 0;   // the next sub-tile's (its atomics come after later barriers)
         const uint32_t ebase = uint32_t(tmax(S.emax[it & 1] - (WIN - 1), 0));
         auto row_of = [&](uint32_t e) { return tmin(e - ebase, uint32_t(WIN)); };   // below: wraps to WIN
-        auto exp_at = [&](int i) { return (S.texp[(i >> 5) * 9 + ((i & 31) >> 2)] >> (8 * (i & 3))) & 0xFFu; };
+        auto exp_at = [&](int i) { return (uint32_t(uint16_t(pp[i])) >> 7) & 0xFFu; };   // (from L1/L2: just staged)
         const int span_n = tmax(0, tmin(ER_SPAN, n - span0));
         const int vn = tmax(0, tmin(ER_RUN, span_n - lane * ER_RUN));
         // ---- lane walk: for every window row, which elements of the lane's run carry it
@@ -294,7 +301,8 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
         //      then lane 2d + h turns the 32 bytes of row d's lanes 16h..16h+15 in place into the
         //      exclusive prefixes of its even lanes (all | changed << 16): a word holds two lanes.
         {
-            uint16_t* const ch = reinterpret_cast<uint16_t*>(&S.pre[w][0][0]);
+            uint32_t (*const pw)[16] = pre_of(S, w);
+            uint16_t* const ch = reinterpret_cast<uint16_t*>(&pw[0][0]);
 #pragma unroll
             for (int d = 0; d < WIN; ++d) {
                 const uint32_t m = S.msk[w][d][lane];
@@ -302,7 +310,7 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
             }
             __syncwarp();
             const int d = lane >> 1, h = lane & 1;
-            uint4* const q = reinterpret_cast<uint4*>(&S.pre[w][d][8 * h]);   // this lane's 32 bytes, in and out
+            uint4* const q = reinterpret_cast<uint4*>(&pw[d][8 * h]);   // this lane's 32 bytes, in and out
             const uint4 c0 = q[0], c1 = q[1];
             const uint32_t wd[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
             uint32_t run = 0, out[8];
@@ -386,12 +394,12 @@ k_enc_rank(const EncTensor* __restrict__ T, int nT, uint64_t* __restrict__ rec_k
             const uint64_t rb = S.rec_base;
             auto record = [&](int i, uint32_t x) {   // i: index in the sub-tile
                 const int ww = i >> 10, l = (i >> 5) & 31, k = i & 31;
-                const uint32_t e = exp_at(i);
+                const uint32_t e = (x >> 7) & 0xFFu;   // the old exponent
                 const uint32_t d = e - ebase;
                 const uint32_t below = (1u << k) - 1u;
                 const uint32_t m = S.msk[ww][d][l];
                 const uint32_t c = S.chm[i >> 5];
-                uint32_t pr = S.pre[ww][d][l >> 1];   // even lanes' prefixes: an odd lane adds its neighbour's counts
+                uint32_t pr = pre_of(S, ww)[d][l >> 1];   // even lanes' prefixes: an odd lane adds its neighbour's counts
                 if (l & 1) {
                     const uint32_t mp = S.msk[ww][d][l - 1];
                     pr += uint32_t(__popc(mp)) | (uint32_t(__popc(mp & S.chm[(i >> 5) - 1])) << 16);
