@@ -245,6 +245,37 @@ def test_byte_parity_with_oracle_at_16m(oracle, n, frac, single):
     assert sender == osender
 
 
+def test_blocks_longer_than_a_pack_slot_match_oracle(oracle):
+    """Blocks of more than 4 Kbit (a pack slot) are encoded a second time straight into the payload:
+    few changes spread over 2^24 elements of one exponent (a large Rice parameter) with random new
+    bits (long codes) make blocks of about 7 Kbit; a second tensor has the usual short blocks.
+    The bytes must be the reference's, on the bytes and the device paths, and apply must round-trip."""
+    c = crx()
+    g = torch.Generator().manual_seed(77)
+    n = 1 << 24
+    sign = torch.randint(0, 2, (n,), generator=g, dtype=torch.int32) << 15
+    old_bits = (sign | 0x3F80 | torch.randint(0, 128, (n,), generator=g, dtype=torch.int32)).to(torch.int16)
+    new_bits = old_bits.clone()
+    pos = torch.randperm(n, generator=g)[:3 * 256 + 17]
+    new_bits[pos] = torch.randint(-32768, 32768, (pos.numel(),), generator=g, dtype=torch.int32).to(torch.int16)
+    a2, b2 = cases.heavy_tail((1 << 20) + 3, 0.05, seed=78)
+    old = {"sparse": old_bits.view(torch.bfloat16), "dense": a2}
+    new = {"sparse": new_bits.view(torch.bfloat16), "dense": b2}
+    upd = c.encode_update(cu(old), cu(new))
+    assert upd == oracle.encode_update(old, new)
+    from crukx_sync_b200 import wire
+    assert max(wire.parse(upd).block_bits) > 4096   # some blocks took the long path
+    assert host_bytes(c.encode_update_device(cu(old), cu(new))) == upd
+    w = {k: v.clone() for k, v in cu(old).items()}
+    c.apply_update(w, upd)
+    for k in new:
+        assert eq(w[k], new[k]), k
+
+
+def host_bytes(t):
+    return t.cpu().numpy().tobytes()
+
+
 @pytest.mark.parametrize("frac", [0.001, 0.01, 0.03, 0.10, 1.0])
 def test_stress_256m_round_trip(frac):
     """BASELINE stress config at 256M elements: size-independent properties (exact round trip,
