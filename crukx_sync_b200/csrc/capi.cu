@@ -920,6 +920,9 @@ int crx_encoded_parse_device(const crx_encoded* enc, const uint8_t* data, crx_up
     *out = nullptr;
     const crx::Encoded& E = enc->e;
     try {
+        // the prepared parse is taken once; the context lock orders calls on one result
+        std::unique_lock<std::mutex> lock;
+        if (E.ctx) lock = std::unique_lock<std::mutex>(E.ctx->mu);
         const int64_t len = int64_t(E.size());
         if (E.pre) {   // parsed up to the block table while the encoder's last kernels ran
             crx_update* u = new crx_update;
