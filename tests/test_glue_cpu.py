@@ -24,3 +24,26 @@ def test_name_table_is_cached_and_points_at_utf8_names():
     assert got == names
     other = codec._name_table(["x"])
     assert other[0] is not blob
+
+
+def test_encoder_parse_is_used_only_while_the_tensor_is_unchanged():
+    """wire.encoder_parse: the parse attached by EncodedUpdate.to_device is returned only for the
+    tensor it was made for, unmodified (same address, size and version counter)."""
+    import torch
+
+    from crukx_sync_b200 import wire
+
+    t = torch.zeros(16, dtype=torch.uint8)
+    assert wire.encoder_parse(t) is None                 # nothing attached
+    marker = object()
+    t._crx_parsed = (marker, t._version, t.data_ptr(), t.numel())
+    assert wire.encoder_parse(t) is marker
+    t[3] ^= 0x41                                         # an in-place change moves the version
+    assert wire.encoder_parse(t) is None
+    u = torch.zeros(16, dtype=torch.uint8)
+    u._crx_parsed = (marker, u._version, u.data_ptr() + 1, u.numel())   # another buffer's parse
+    assert wire.encoder_parse(u) is None
+    v = torch.zeros(16, dtype=torch.uint8)
+    v._crx_parsed = (marker, v._version, v.data_ptr(), 8)              # another length
+    assert wire.encoder_parse(v) is None
+    assert getattr(v.clone(), "_crx_parsed", None) is None             # a copy carries no parse
