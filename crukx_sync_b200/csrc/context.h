@@ -50,12 +50,12 @@ constexpr int kEncStatusWord = 511;
 // Named slots of Ctx::b.
 enum Slot : int {
     S_TENS = 0, S_HS, S_CS, S_CHUNK_ROWS, S_CHUNK_SUMS, S_TOTALS_A, S_TOTALS_C, S_COUNTERS, S_REC_KEY, S_REC_VAL,
-    S_GIDX, S_GROUPS, S_LOCAL, S_VALS, S_COSTS, S_DENSE_HIST, S_RARE_HIST, S_RARE_FLAG, S_RARE_OUT, S_RARE_CNT,
-    S_DENSE_CODE, S_BIG_CODE, S_RICE, S_GBLOCK, S_BLOCK_BITS, S_BLOCK_OFF, S_SCAN_TMP, S_PAYLOAD, S_BB32, S_RARE_CODES,
+    S_GIDX, S_GROUPS, S_LOCAL, S_VALS, S_COSTS, S_DENSE_HIST, S_RARE_HIST, S_RARE_FLAG, S_RARE_OUT,
+    S_DENSE_CODE, S_BIG_CODE, S_BLOCK_BITS, S_SCAN_TMP, S_PAYLOAD, S_BB32, S_RARE_CODES,
     // apply
     S_A_TENS, S_A_GROUPS, S_A_TABLES, S_A_SYMS, S_A_PAYLOAD, S_A_BB, S_A_BOFF, S_A_ZZ, S_A_BSUM,
     S_A_LOCAL, S_A_CADDR, S_A_CVAL, S_A_HS, S_A_TOT, S_A_CHUNK_ROWS, S_A_CHUNK_SUMS, S_A_COUNTERS, S_A_SCAN_TMP,
-    S_CHK, S_REC_POS, S_SUPER_T, S_A_HNEW, S_A_HSTORE, S_A_ORDER,
+    S_CHK, S_SUPER_T, S_A_HNEW, S_A_HSTORE, S_A_ORDER,
     // size statistics
     S_SZ_STATS, S_SZ_TILES,
     // apply: first value slot of every span of the commit list
