@@ -57,6 +57,9 @@ def encode_update_device(old: Mapping[str, torch.Tensor], new: Mapping[str, torc
     """encode_update whose result stays in device memory: a uint8 CUDA tensor holding exactly the
     bytes encode_update returns, on the tensors' device (CPU tensors: the current CUDA device).
     For transports that move updates between GPUs (NCCL, NVLink) without a host round trip.
+    Like any CUDA result, the bytes are written in the order of the current stream: work queued
+    after this call on that stream sees them; another stream must wait for it first.  The tensor
+    carries the encoder's own parse, which apply_update uses while the tensor is unmodified.
     The sender cache follows the same rule: it is updated only once the update exists."""
     if old.keys() != new.keys():
         raise ValueError(f"old and new differ in tensor names: {sorted(old.keys() ^ new.keys())[:5]}")
