@@ -400,7 +400,7 @@ constexpr int MP_SUB = 8192;
 constexpr int MP_SPAN = MP_SUB / MP_WARPS;   // 1024
 constexpr int MP_RUN = MP_SPAN / 32;         // 32
 constexpr int MWIN = 16;
-constexpr int MP_PRE = 4;                    // groups per warp whose first changes are loaded ahead
+constexpr int MP_PRE = 3;                    // groups per warp whose first changes are loaded ahead
 static_assert(MP_SUB * 32 == SUPER_N, "32 sub-tiles per super-tile");
 
 struct MapSmem {
