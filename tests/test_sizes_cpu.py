@@ -50,3 +50,4 @@ def test_restatement_matches_reference(name):
     got = osizes.update_sizes(old, new)
     assert got == {k: row[k] for k in ("raw", "sparserl", "ctxfree")}
     assert psizes.sizes_from_stats(host_stats(old, new)) == got
+
