@@ -23,3 +23,14 @@ def test_bench_reference_arm_prints_the_contract_line():
     e = d["e2e"]
     assert e["value"] == d["value"] and e["unit"] == d["unit"]
     assert e["h2d_bytes_per_step"] == 0 and e["d2h_bytes_per_step"] == 0
+
+
+def test_bench_reference_arm_other_ranks_exit_without_work():
+    """Under torchrun only rank 0 runs the reference arm and prints; the other ranks exit 0."""
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    env = dict(os.environ, RANK="1", WORLD_SIZE="2", LOCAL_RANK="1")
+    out = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--config", "toy", "--gpus", "2",
+                          "--steps", "1", "--warmup", "3"], cwd=root, env=env, capture_output=True, text=True,
+                         timeout=300)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert not [l for l in out.stdout.splitlines() if l.startswith("{")]
