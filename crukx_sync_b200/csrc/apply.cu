@@ -974,35 +974,18 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     const uint64_t total = start;
     const int64_t n_blocks = u.n_blocks;
     if (int64_t(gblock.back()) != n_blocks) { *err = "internal: block count mismatch"; return kCudaError; }
-    std::vector<DecTable> TB(u.tables.size());
-    std::vector<uint32_t> syms;
-    {   // decode tables and their lookup tables, independent per exponent: built on the host pool
-        std::vector<size_t> offs(u.tables.size() + 1, 0);
-        for (size_t k = 0; k < u.tables.size(); ++k) offs[k + 1] = offs[k] + u.tables[k].symbols.size();
-        syms.resize(offs.back());
-        auto one = [&](size_t k) {
-            DecodeTable d;
-            build_decode_table(u.tables[k], &d, syms.data() + offs[k]);
-            DecTable& x = TB[k];
-            std::memcpy(x.first, d.first, sizeof(x.first));
-            std::memcpy(x.base, d.base, sizeof(x.base));
-            std::memcpy(x.limit, d.limit, sizeof(x.limit));
-            x.sym_off = uint32_t(offs[k]);
-            x.nsym = uint32_t(u.tables[k].symbols.size());
-            build_lut(d, syms.data() + offs[k], x.lut);
-        };
-        if (u.tables.size() > 4) parallel_for(u.tables.size(), one);
-        else for (size_t k = 0; k < u.tables.size(); ++k) one(k);
-    }
-
+    // decode tables: their sizes now, their contents once the histogram pass and the copies run
+    std::vector<size_t> toffs(u.tables.size() + 1, 0);
+    for (size_t k = 0; k < u.tables.size(); ++k) toffs[k + 1] = toffs[k] + u.tables[k].symbols.size();
+    const size_t n_tables = u.tables.size(), n_syms = toffs.back();
     trace_phase(C, "apply: host tables");
     // ---- device buffers
     const size_t cells = size_t(nt) * 256;
     const size_t payload_alloc = size_t(u.payload_len) + 64;
     CRX_CUDA(ensure_dev(C.b[S_A_TENS], sizeof(AppTensor) * size_t(nt), st));
     CRX_CUDA(ensure_dev(C.b[S_A_GROUPS], sizeof(AppGroup) * size_t(ng) + sizeof(uint64_t) * (size_t(ng) + 1), st));
-    CRX_CUDA(ensure_dev(C.b[S_A_TABLES], sizeof(DecTable) * TB.size(), st));
-    CRX_CUDA(ensure_dev(C.b[S_A_SYMS], sizeof(uint32_t) * syms.size(), st));
+    CRX_CUDA(ensure_dev(C.b[S_A_TABLES], sizeof(DecTable) * n_tables, st));
+    CRX_CUDA(ensure_dev(C.b[S_A_SYMS], sizeof(uint32_t) * n_syms, st));
     CRX_CUDA(ensure_dev(C.b[S_A_PAYLOAD], payload_alloc, st));
     CRX_CUDA(ensure_dev(C.b[S_A_BB], sizeof(uint32_t) * size_t(n_blocks), st));
     CRX_CUDA(ensure_dev(C.b[S_A_BOFF], sizeof(uint64_t) * size_t(n_blocks), st));
@@ -1030,8 +1013,8 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     CRX_CUDA(ensure_dev(C.b[S_A_COUNTERS], sizeof(uint64_t) * (16 + 2 * size_t(nt)), st));
 
     // ---- uploads: metadata through pinned staging, the payload straight from the caller's buffer
-    const size_t up = sizeof(AppTensor) * nt + sizeof(AppGroup) * ng + 8 * (ng + 1) + sizeof(DecTable) * TB.size() +
-                      4 * syms.size() + 16 * (nt + 1) + 256;
+    const size_t up = sizeof(AppTensor) * nt + sizeof(AppGroup) * ng + 8 * (ng + 1) + sizeof(DecTable) * n_tables +
+                      4 * n_syms + 16 * (nt + 1) + 256;
     CRX_CUDA(ensure_host(C, up, st));
     uint8_t* h = static_cast<uint8_t*>(C.host);
     size_t o = 0;
@@ -1048,8 +1031,6 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
     CRX_CUDA(upload(C.b[S_A_TENS].p, T.data(), sizeof(AppTensor) * size_t(nt)));
     CRX_CUDA(upload(dG, G.data(), sizeof(AppGroup) * size_t(ng)));
     CRX_CUDA(upload(dgblock, gblock.data(), 8 * (size_t(ng) + 1)));
-    CRX_CUDA(upload(C.b[S_A_TABLES].p, TB.data(), sizeof(DecTable) * TB.size()));
-    CRX_CUDA(upload(C.b[S_A_SYMS].p, syms.data(), 4 * syms.size()));
     CRX_CUDA(upload(drows, row_begin.data(), 8 * (size_t(nt) + 1)));
     CRX_CUDA(upload(drows + nt + 1, chunk_begin.data(), 8 * (size_t(nt) + 1)));
     CRX_CUDA(cudaMemsetAsync(static_cast<uint8_t*>(C.b[S_A_PAYLOAD].p) + u.payload_len, 0, 64, st));
@@ -1085,6 +1066,29 @@ Status apply_impl(Ctx& C, const Update& u, int16_t* const* weights, const uint64
         CRX_CUDA(cudaMemcpyAsync(C.b[S_A_PAYLOAD].p, u.payload_device, size_t(u.payload_len), cudaMemcpyDeviceToDevice,
                                  C.copy_stream));
     CRX_CUDA(cudaEventRecord(C.ev_copy, C.copy_stream));
+    std::vector<DecTable> TB(n_tables);
+    std::vector<uint32_t> syms;
+    {   // decode tables and their lookup tables, independent per exponent: built on the host pool
+        //  while the histogram pass and the update's copies run
+        const std::vector<size_t>& offs = toffs;
+        syms.resize(n_syms);
+        auto one = [&](size_t k) {
+            DecodeTable d;
+            build_decode_table(u.tables[k], &d, syms.data() + offs[k]);
+            DecTable& x = TB[k];
+            std::memcpy(x.first, d.first, sizeof(x.first));
+            std::memcpy(x.base, d.base, sizeof(x.base));
+            std::memcpy(x.limit, d.limit, sizeof(x.limit));
+            x.sym_off = uint32_t(offs[k]);
+            x.nsym = uint32_t(u.tables[k].symbols.size());
+            build_lut(d, syms.data() + offs[k], x.lut);
+        };
+        if (u.tables.size() > 4) parallel_for(u.tables.size(), one);
+        else for (size_t k = 0; k < u.tables.size(); ++k) one(k);
+    }
+    CRX_CUDA(upload(C.b[S_A_TABLES].p, TB.data(), sizeof(DecTable) * n_tables));
+    CRX_CUDA(upload(C.b[S_A_SYMS].p, syms.data(), 4 * n_syms));
+    trace_phase(C, "apply: decode tables up");
     CRX_CUDA(cudaStreamWaitEvent(st, C.ev_copy, 0));
     // ---- block offsets and decode
     uint64_t* boff = dev<uint64_t>(C, S_A_BOFF);
