@@ -421,16 +421,18 @@ void huffman_unlimited(const std::vector<uint64_t>& counts, std::vector<int>& de
     for (int64_t i = 0; i < n; ++i) depth_out[size_t(i)] = depth[size_t(i)];
 }
 
-// huffman_unlimited with the leaves sorted as packed 64-bit keys (count << 20 | id): the same
-// (count, id) order, an order of magnitude cheaper to sort than Items; needs every count < 2^44 and
-// n <= 2^20 (the caller checks).  Scratch buffers are reused across the length-limit rounds.
+// huffman_unlimited with the leaves sorted as packed 64-bit keys (count << 24 | id): the same
+// (count, id) order, an order of magnitude cheaper to sort than Items; needs every count < 2^40 and
+// n <= 2^24 (the caller checks).  Scratch buffers are reused across the length-limit rounds.
 struct HuffScratch {
     std::vector<uint64_t> keys, mcount, tmp;
     std::vector<int32_t> parent, depth;
 };
 
-// Ascending LSD radix sort of distinct 64-bit keys, a byte per pass; bytes that are the same in
-// every key are skipped (the length-limit rounds shrink the counts, so fewer bytes vary).
+// Ascending sort of distinct keys (count << 24 | id) that arrive in id order: an LSD radix sort
+// over the count bytes only, a byte per pass (the passes over the id bytes would keep the order the
+// keys already have, and each later pass is stable); bytes that are the same in every key are
+// skipped (the length-limit rounds shrink the counts, so fewer bytes vary).
 void radix_sort_keys(std::vector<uint64_t>& a, std::vector<uint64_t>& tmp) {
     const size_t n = a.size();
     if (n < 256) {
@@ -440,7 +442,7 @@ void radix_sort_keys(std::vector<uint64_t>& a, std::vector<uint64_t>& tmp) {
     uint64_t diff = 0;
     for (const uint64_t x : a) diff |= x ^ a[0];
     tmp.resize(n);
-    for (int sh = 0; sh < 64; sh += 8) {
+    for (int sh = 24; sh < 64; sh += 8) {
         if (((diff >> sh) & 0xFFu) == 0) continue;
         size_t cnt[257] = {};
         for (const uint64_t x : a) ++cnt[((x >> sh) & 0xFFu) + 1];
@@ -455,7 +457,7 @@ void huffman_unlimited_packed(const std::vector<uint64_t>& counts, std::vector<i
     depth_out.assign(size_t(n), 1);
     if (n == 1) return;
     w.keys.resize(size_t(n));
-    for (int64_t i = 0; i < n; ++i) w.keys[size_t(i)] = (counts[size_t(i)] << 20) | uint64_t(i);
+    for (int64_t i = 0; i < n; ++i) w.keys[size_t(i)] = (counts[size_t(i)] << 24) | uint64_t(i);   // in id order
     radix_sort_keys(w.keys, w.tmp);
     w.mcount.clear();
     w.mcount.reserve(size_t(n));
@@ -463,9 +465,9 @@ void huffman_unlimited_packed(const std::vector<uint64_t>& counts, std::vector<i
     size_t li = 0, mi = 0;
     // a leaf and a merged node of equal count: the leaf first (leaf ids are below merged ids)
     auto pop = [&](uint64_t& c) -> int64_t {
-        if (li < size_t(n) && (mi >= w.mcount.size() || (w.keys[li] >> 20) <= w.mcount[mi])) {
-            c = w.keys[li] >> 20;
-            return int64_t(w.keys[li++] & 0xFFFFFu);
+        if (li < size_t(n) && (mi >= w.mcount.size() || (w.keys[li] >> 24) <= w.mcount[mi])) {
+            c = w.keys[li] >> 24;
+            return int64_t(w.keys[li++] & 0xFFFFFFu);
         }
         c = w.mcount[mi];
         return n + int64_t(mi++);
@@ -488,8 +490,8 @@ void huffman_unlimited_packed(const std::vector<uint64_t>& counts, std::vector<i
 void huffman_lengths(const uint64_t* counts_in, int64_t n, uint8_t* lengths) {
     std::vector<uint64_t> c(counts_in, counts_in + n);
     std::vector<int> d;
-    bool packed = n <= (int64_t(1) << 20);
-    for (int64_t i = 0; i < n && packed; ++i) packed = counts_in[i] < (uint64_t(1) << 44);
+    bool packed = n <= (int64_t(1) << 24);
+    for (int64_t i = 0; i < n && packed; ++i) packed = counts_in[i] < (uint64_t(1) << 40);
     HuffScratch w;
     for (int round = 0; round < 8; ++round) {          // codec.py:71-78
         if (packed) huffman_unlimited_packed(c, d, w);

@@ -111,6 +111,27 @@ def test_huffman_lengths_match_oracle(lib, oracle):
         assert list(out) == oracle.huffman_lengths(counts), trial
 
 
+def test_huffman_lengths_match_oracle_on_large_tables(lib, oracle):
+    """Alphabets of thousands of symbols (the radix-sorted path), with counts that need several
+    length-limit rounds, the flat fallback, runs of equal counts, and counts on both sides of the
+    packed-key limit (2^40)."""
+    rng = random.Random(11)
+    cases = []
+    for n in (256, 257, 1000, 4247, 9000, 20000):
+        cases.append([rng.randint(1, 1 << 30) for _ in range(n)])                      # flat fallback
+        cases.append([rng.choice([1, 2, 3, 4, 5, 8, 13, 1000, rng.randint(1, 10**7)]) for _ in range(n)])
+        cases.append([int(1.3 ** (i % 60)) + rng.randint(0, 3) for i in range(n)])   # a few rounds
+        cases.append([7] * n)                                                          # all tied
+    cases.append([rng.randint(1, 1 << 30) for _ in range(999)] + [(1 << 40) + 5])       # one count too big to pack
+    cases.append([(1 << 40) - 1] + [rng.randint(1, 99) for _ in range(3000)])
+    for k, counts in enumerate(cases):
+        n = len(counts)
+        c = (ctypes.c_uint64 * n)(*counts)
+        out = (ctypes.c_uint8 * n)()
+        assert lib.crx_huffman_lengths(c, n, out) == 0
+        assert list(out) == oracle.huffman_lengths(counts), k
+
+
 def test_caller_mistakes_raise_before_device_work():
     from crukx_sync_b200 import CorruptUpdate, apply_update, encode_update
     a, b = cases.rl_pair(1000)
