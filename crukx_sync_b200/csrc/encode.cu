@@ -1368,6 +1368,7 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     // ---- one Huffman table per exponent over the whole update (codec.py:369-392); a global
     //      update sums the histogram over its ranks first
     std::vector<std::pair<uint64_t, uint64_t>> rare_pairs;
+    rare_pairs.reserve(rare_total);
     for (int e = 0; e < 256; ++e)
         for (uint32_t k = 0; k < hrc[size_t(e)]; ++k) {
             const uint64_t v = hrare[size_t(hrb[size_t(e)] + k)];
@@ -1400,6 +1401,7 @@ Status encode_impl(Ctx& C, int nT, const int16_t* const* prev, const int16_t* co
     // ---- upload rice, block starts, code tables
     std::vector<uint32_t> dense_code(256 * DENSE_SYM, 0);
     std::vector<uint64_t> rare_codes;
+    rare_codes.reserve(rare_pairs.size());
     for (int e = 0; e < 256; ++e) {
         for (size_t k = 0; k < tabs.sym[e].size(); ++k) {
             const uint32_t z = tabs.sym[e][k];
