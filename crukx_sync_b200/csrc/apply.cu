@@ -13,10 +13,13 @@
 //                  in-block running sum (codec.py:640-642), range checks (codec.py:696-697).
 //   k_map          per super-tile: per-lane masks of the old exponents over a 16-exponent window,
 //                  then every change is placed by (exponent, local rank) -> position through
-//                  selection on the masks' counts (codec.py:654-694), the new value staged and the
+//                  selection on the masks' counts (codec.py:654-694) and written in place (device
+//                  weights; its old value kept in the commit list) or staged (host weights), the
 //                  checksum delta accumulated (codec.py:698-700).
-//   host verdict   one synchronisation: decode/range flags and per-tensor checksums.
-//   k_commit       scatter of the staged values, only after the verdict (codec.py:713-714).
+//   host verdict   one synchronisation: decode/range flags and per-tensor checksums; a failed one
+//                  has k_commit write the old values back, so nothing is left written.
+//   k_commit       scatter of the list's values at its positions (codec.py:713-714): the undo
+//                  above, or the new values into the device copies of host weights.
 #include <algorithm>
 #include <cstring>
 #include <string>
@@ -390,9 +393,9 @@ __global__ void __launch_bounds__(256) k_locals(const uint64_t* __restrict__ bsc
 // sub-tile's elements of exponent e is then found by selection: the warp whose exclusive base is
 // the last <= r, the lane likewise, and the r-th set bit of that lane's mask.  Elements outside the
 // window (zeros, tiny or huge weights) are few: their positions are listed in (exponent, index)
-// order by warp matching, into the super-tile's slot of a global scratch list.  New values are
-// staged in position order (per warp span), which keeps the commit's scattered writes of one
-// region together.
+// order by warp matching, into the super-tile's slot of a global scratch list.  Changes are
+// written (and listed) in position order per warp span, which keeps the scattered 2-byte writes of
+// one region together in L2.
 
 constexpr int MP_THREADS = 256;
 constexpr int MP_WARPS = MP_THREADS / 32;
