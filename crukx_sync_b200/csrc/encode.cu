@@ -1,7 +1,8 @@
 // Encoder: bf16 prev/cur -> crukx-sync update bytes (wire format version 2), byte-identical to
 // the reference's encode_update (src/crukx_sync/codec.py:278-420, wire.py:64-89).
 //
-// Pipeline (one CUDA stream, three small host round trips):
+// Pipeline (one CUDA stream, four small host round trips: the record count, the group table,
+// the statistics and the block lengths; a device result is then returned without waiting):
 //   k_enc_rank     one pass over prev+cur.  Per super-tile: old-exponent histogram and changed
 //                  count per exponent; every changed element becomes a record holding its rank
 //                  among same-exponent elements and among same-exponent changes, both local to
